@@ -1,0 +1,192 @@
+/*
+ * senmoe.h -- C ABI of the B200 (sm_100a) mixture-of-experts block.
+ *
+ * Drop-in boundary for sen-mlx's MoE hot path.  Every entry point is plain C:
+ * device pointers, sizes and a cudaStream_t, an int status (0 = ok) and a
+ * thread-local message from senmoe_last_error().  No entry point aborts,
+ * traps or allocates on the forward path.
+ *
+ * Reference interfaces replaced (paths inside the sen-mlx project):
+ *   senmoe_gather_qmm       <- gather_qmm / mlx_sys::mlx_gather_qmm
+ *                              src/engine/mlx_lm/utils/moe.rs:33-77
+ *   senmoe_layer_create     <- DeepseekMoe::new + SwitchGlu/SwitchLinear weight slots
+ *                              src/engine/mlx_lm/models/deepseek_v2.rs:400-428, 485-518
+ *   senmoe_layer_forward    <- DeepseekMoe::forward(&mut self, x: &Array) -> Result<Array>
+ *                              src/engine/mlx_lm/models/deepseek_v2.rs:520-553
+ *   senmoe_router           <- the router half of DeepseekMoe::forward, :526-543
+ *   senmoe_dispatch         <- (no counterpart: the reference gathers per (token, slot)
+ *                              with sorted_indices=false, deepseek_v2.rs:441; this is the
+ *                              build's expert-contiguous permutation)
+ *   senmoe_layer_destroy    <- Drop of the MLX Param<Array>s (deepseek_v2.rs:408-413)
+ *   senmoe_last_error       <- Exception::custom(...) text, utils/moe.rs:66-74
+ *
+ * Weight layout is MLX's affine-quantized layout, unchanged
+ * (src/engine/mlx_native.rs:3381-3389, 3473-3477): for a [E, out, in]
+ * projection, weight is uint32 [E, out, in*bits/32] with 32/bits codes per
+ * word (lower columns in lower bits), scales and biases are bf16
+ * [E, out, in/group]; w = q * scale + bias.  bits is 4 or 8, group is 64.
+ *
+ * Numerics: fp32 accumulation; bf16 rounding at the points where the MLX
+ * graph rounds (logits, softmax scores, gate/up, silu, silu*up, down);
+ * router weights and the weighted combine in fp32; y is bf16.
+ */
+#ifndef SENMOE_H_
+#define SENMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SENMOE_ABI_VERSION 1
+
+typedef struct CUstream_st* senmoe_stream_t; /* == cudaStream_t */
+
+typedef enum SenMoeStatus {
+  SENMOE_OK = 0,
+  SENMOE_ERR_BAD_ARG = 1,     /* shape, alignment or index rejected on the host */
+  SENMOE_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+  SENMOE_ERR_NCCL = 3,        /* an NCCL call failed (expert parallelism) */
+  SENMOE_ERR_TIMEOUT = 4,     /* a bounded device- or host-side wait ran out */
+  SENMOE_ERR_UNSUPPORTED = 5, /* valid in MLX, not supported by this build */
+  SENMOE_ERR_NO_MEMORY = 6,   /* scratch allocation at create time failed */
+  SENMOE_ERR_DEVICE = 7       /* a kernel reported bad data (expert index out of range) */
+} SenMoeStatus;
+
+typedef enum SenMoeRouter {
+  SENMOE_ROUTER_SOFTMAX_TOPK = 0 /* DeepSeek/Qwen: softmax over E, top-k, optional renorm */
+} SenMoeRouter;
+
+typedef enum SenMoeActivation {
+  SENMOE_ACT_SWIGLU = 0, /* silu(gate) * up   (deepseek_v2.rs:472-474) */
+  SENMOE_ACT_GEGLU = 1   /* gelu_approx(gate) * up (gemma4.rs:817-819) */
+} SenMoeActivation;
+
+/* Field names follow the reference's config.json / ModelArgs
+ * (deepseek_v2.rs:103-118). */
+typedef struct SenMoeConfig {
+  int32_t hidden_size;             /* H */
+  int32_t moe_intermediate_size;   /* I */
+  int32_t n_routed_experts;        /* E (global expert count) */
+  int32_t num_experts_per_tok;     /* K */
+  int32_t bits;                    /* 4 or 8 */
+  int32_t group_size;              /* 64 */
+  int32_t router_kind;             /* SenMoeRouter */
+  int32_t activation;              /* SenMoeActivation */
+  int32_t norm_topk_prob;          /* 0/1 */
+  float routed_scaling_factor;     /* 1.0 = off */
+  int32_t shared_intermediate;     /* moe_intermediate_size * n_shared_experts; 0 = none */
+  int32_t shared_gate;             /* 1: y += sigmoid(x . shared_gate_w) * shared(x) */
+  int32_t max_tokens;              /* T_max: scratch is sized for this at create time */
+  int32_t expert_begin;            /* first expert held by this rank (0 on one GPU) */
+  int32_t expert_end;              /* one past the last local expert (E on one GPU) */
+  int32_t reserved[3];
+} SenMoeConfig;
+
+/* Device pointers, caller-owned, valid for the layer's lifetime.  Expert
+ * tensors hold experts [expert_begin, expert_end) only. */
+typedef struct SenMoeWeights {
+  const void* router_weight;      /* bf16 [E, H]  (mlp.gate.weight, unquantized) */
+  const uint32_t* gate_weight;    /* u32 [E_local, I, H*bits/32] (switch_mlp.gate_proj) */
+  const void* gate_scales;        /* bf16 [E_local, I, H/group] */
+  const void* gate_biases;
+  const uint32_t* up_weight;      /* switch_mlp.up_proj, same shapes as gate */
+  const void* up_scales;
+  const void* up_biases;
+  const uint32_t* down_weight;    /* u32 [E_local, H, I*bits/32] (switch_mlp.down_proj) */
+  const void* down_scales;        /* bf16 [E_local, H, I/group] */
+  const void* down_biases;
+  const uint32_t* shared_gate_weight; /* shared_experts.gate_proj: u32 [Is, H*bits/32] */
+  const void* shared_gate_scales;
+  const void* shared_gate_biases;
+  const uint32_t* shared_up_weight;
+  const void* shared_up_scales;
+  const void* shared_up_biases;
+  const uint32_t* shared_down_weight; /* u32 [H, Is*bits/32] */
+  const void* shared_down_scales;
+  const void* shared_down_biases;
+  const void* shared_gate_vector;     /* bf16 [H], only when shared_gate */
+} SenMoeWeights;
+
+/* Optional device outputs of one forward (any field may be NULL). */
+typedef struct SenMoeDebug {
+  int32_t* topk_ids;      /* [T, K] expert ids, slot order = score desc, id asc */
+  float* topk_weights;    /* [T, K] fp32 router weights after renorm/scaling */
+  int32_t* perm;          /* [T*K] pair index (t*K + j) of each expert-sorted slot */
+  int32_t* offsets;       /* [E + 1] slot range of each expert */
+} SenMoeDebug;
+
+typedef struct SenMoeLayer SenMoeLayer;
+
+/* Message of the last failing call on this thread ("" when none). */
+const char* senmoe_last_error(void);
+/* "senmoe <abi> sm_100a" */
+const char* senmoe_version(void);
+
+/* Layer life cycle.  create validates the config, checks pointer alignment,
+ * and allocates the layer's scratch on `device` for config->max_tokens. */
+int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights, int device,
+                        SenMoeLayer** out_layer);
+int senmoe_layer_destroy(SenMoeLayer* layer);
+
+/* y[T, H] = DeepseekMoe::forward(x[T, H]), bf16, stream-ordered, no host
+ * synchronisation and no allocation; 0 <= T <= max_tokens. */
+int senmoe_layer_forward(SenMoeLayer* layer, const void* x, int64_t num_tokens, void* y,
+                         const SenMoeDebug* debug, senmoe_stream_t stream);
+
+/* h_out[T, H] = bf16(x + DeepseekMoe::forward(x)): the residual add of
+ * DecoderLayer::forward (deepseek_v2.rs:613-620, `h.add(&r)`) fused into
+ * the combine, so a decoder stack chains layers without an extra pass. */
+int senmoe_layer_forward_residual(SenMoeLayer* layer, const void* x, int64_t num_tokens, void* h_out,
+                                  senmoe_stream_t stream);
+
+/* Per-stage timing (the build's counterpart of the reference's tracing of
+ * prefill/decode rates, src/engine/mlx_native.rs:916-936).  When enabled,
+ * forward records CUDA events between its stages on the stream (also inside
+ * a CUDA-graph capture).  senmoe_layer_stage_times waits for the last
+ * forward's final event and writes that forward's per-stage milliseconds to
+ * ms[0 .. n): router, dispatch, gate/up, down, shared expert, combine.
+ * Returns the number of stages written (or a negative status). */
+#define SENMOE_NUM_STAGES 6
+int senmoe_layer_set_profiling(SenMoeLayer* layer, int enable);
+int senmoe_layer_stage_times(SenMoeLayer* layer, float* ms, int n);
+
+/* Synchronises `stream` and reports any error a kernel recorded on the
+ * device since the previous check (bad expert index, timed-out wait). */
+int senmoe_layer_check(SenMoeLayer* layer, senmoe_stream_t stream);
+
+/* Router alone: ids/weights [T, K] for x [T, H] (bf16), router weight
+ * [E, H] (bf16).  Same rounding and slot order as the layer. */
+int senmoe_router(const void* x, int64_t num_tokens, const void* router_weight, int32_t hidden,
+                  int32_t num_experts, int32_t top_k, int32_t norm_topk_prob, float routed_scaling_factor,
+                  float* logits_scratch /* [T, E] fp32 device */, int32_t* topk_ids, float* topk_weights,
+                  senmoe_stream_t stream);
+
+/* Dispatch alone: stable counting sort of the T*K pairs by expert.
+ * perm [T*K], inverse [T*K] (slot of each pair), offsets [E + 1]; scratch is
+ * int32 [E + 2] device memory: scratch[0 .. n) lists the experts that
+ * received pairs (ascending), scratch[E] = n, scratch[E + 1] = nonzero if an
+ * id was outside [0, E) (the caller zeroes it before the call).  E <= 1024. */
+int senmoe_dispatch(const int32_t* topk_ids, int64_t num_tokens, int32_t top_k, int32_t num_experts,
+                    int32_t* perm, int32_t* inverse, int32_t* offsets, int32_t* scratch, senmoe_stream_t stream);
+
+/* gather_qmm, transpose=true (utils/moe.rs:33-43):
+ *   out[i, :] = bf16( x[i / (n_indices / x_rows), :] @ dequant(w[rhs_indices[i]])^T )
+ * x bf16 [x_rows, in_features]; w u32 [num_experts, out_features, in*bits/32];
+ * scales/biases bf16 [num_experts, out_features, in/group]; out bf16
+ * [n_indices, out_features].  n_indices must be a multiple of x_rows (x
+ * broadcasts over the trailing index dim, the SwitchGlu gate/up form) or equal
+ * to it (the down form).  transpose == 0 returns SENMOE_ERR_UNSUPPORTED (the
+ * reference only calls the transposed form, moe.rs:43, deepseek_v2.rs:437).
+ * sorted_indices is accepted and ignored (it is a performance hint in MLX). */
+int senmoe_gather_qmm(const void* x, int64_t x_rows, const uint32_t* w, const void* scales, const void* biases,
+                      const uint32_t* rhs_indices, int64_t n_indices, int64_t in_features, int64_t out_features,
+                      int32_t num_experts, int32_t transpose, int32_t group_size, int32_t bits,
+                      int32_t sorted_indices, void* out, senmoe_stream_t stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+#endif /* SENMOE_H_ */

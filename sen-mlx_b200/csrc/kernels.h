@@ -1,0 +1,104 @@
+// kernels.h -- internal launch interfaces of the senmoe CUDA kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace senmoe {
+
+// Device-side error codes written to an error word (first writer wins).
+enum DeviceError : int {
+  kDevOk = 0,
+  kDevBadExpert = 1,    // an expert id outside [0, E)
+  kDevWaitTimeout = 2,  // a bounded mbarrier wait ran out
+};
+
+// ---------------------------------------------------------------- router
+struct RouterArgs {
+  const uint16_t* x;        // bf16 [T, H]
+  const uint16_t* weight;   // bf16 [E, H]
+  float* logits;            // fp32 [T, E] (bf16-rounded values unless raw)
+  int32_t* topk_ids;        // [T, K]
+  float* topk_weights;      // [T, K]
+  int num_tokens, hidden, num_experts, top_k;
+  int norm_topk_prob;
+  float routed_scaling_factor;
+  int round_logits;         // 1: logits rounded to bf16 (nn::Linear output dtype)
+};
+cudaError_t launch_router_logits(const RouterArgs& a, cudaStream_t st);
+cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st);
+bool router_supported(int hidden, int num_experts, int top_k);
+
+// -------------------------------------------------------------- dispatch
+struct DispatchArgs {
+  const int32_t* topk_ids;  // [P] = [T*K]
+  int num_pairs, num_experts;
+  int expert_begin, expert_end;  // experts whose slots count as local
+  int32_t* perm;            // [P] pair index of each expert-sorted slot
+  int32_t* inverse;         // [P] slot of each pair (-1 for non-local experts)
+  int32_t* offsets;         // [E + 1]
+  int32_t* active;          // [E] local experts with tokens, ascending
+  int32_t* active_count;    // [1]
+  int32_t* chunk_hist;      // [nchunks, E] scratch (large dispatch only)
+  int* err;
+};
+constexpr int kDispatchChunk = 1024;
+cudaError_t launch_dispatch(const DispatchArgs& a, cudaStream_t st);
+size_t dispatch_smem_bytes(int num_experts);
+
+// ------------------------------------------------------------ expert GEMV
+enum ItemMode : int { kItemsGrouped = 0, kItemsGather = 1 };
+struct QGemvArgs {
+  const uint16_t* x;        // bf16 [tokens, kdim]
+  const uint32_t* w[2];     // per projection: u32 [E_local, rows, kdim*bits/32]
+  const uint16_t* s[2];     // bf16 [E_local, rows, kdim/64]
+  const uint16_t* b[2];
+  int kdim, rows, rows_per_cta;
+  int mode;                 // ItemMode
+  // grouped items: CTA x-index i serves active[i]'s slots offsets[e]..offsets[e+1]
+  const int32_t* active;
+  const int32_t* active_count;
+  const int32_t* offsets;
+  const int32_t* perm;
+  int k_div;                // token of slot s = perm[s] / k_div
+  int x_by_slot;            // 1: x row of slot s is s itself (the down projection)
+  int expert_begin;
+  // gather items: CTA x-index i serves index i, token i / rep, expert gather_idx[i]
+  const uint32_t* gather_idx;
+  long long rep;
+  int num_experts;
+  uint16_t* out;            // bf16 [slots, out_stride], row r of slot s at out[s*out_stride + r]
+  long long out_stride;
+  int act;                  // 0 SwiGLU, 1 GeGLU (two-projection form only)
+  int* err;
+};
+size_t qgemv_smem_bytes(int nproj, int rows_per_cta, int kdim, int bits);
+// grid: x = items (active experts or indices), y = row blocks.
+cudaError_t launch_qgemv(const QGemvArgs& a, int nproj, int bits, int num_items, cudaStream_t st);
+bool qgemv_supported(int kdim, int bits);
+
+// --------------------------------------------------------------- combine
+struct CombineArgs {
+  const uint16_t* d;        // bf16 [P, H] expert outputs in slot order
+  const int32_t* inverse;   // [T*K]
+  const float* weights;     // [T*K]
+  const uint16_t* shared_out;  // bf16 [T, H] or null
+  const float* shared_gate;    // fp32 [T] gate per token (already sigmoid) or null
+  const uint16_t* residual;    // bf16 [T, H] added before rounding (fused residual) or null
+  uint16_t* y;              // bf16 [T, H]
+  float* y_f32;             // optional fp32 copy
+  int hidden, top_k;
+};
+cudaError_t launch_combine(const CombineArgs& a, int num_tokens, cudaStream_t st);
+
+// Raises a kernel's dynamic shared-memory limit to at least `bytes` on the
+// current device.  Only the first call per (kernel, device, size) reaches the
+// driver, so launches inside a CUDA-graph capture after a warm-up call make
+// no attribute calls.
+cudaError_t ensure_dynamic_smem(const void* kernel, size_t bytes);
+
+// sigmoid of a per-token logit, in place.
+cudaError_t launch_sigmoid_inplace(float* v, int n, cudaStream_t st);
+
+}  // namespace senmoe

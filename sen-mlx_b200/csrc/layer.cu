@@ -1,0 +1,587 @@
+// layer.cu -- the C ABI (include/senmoe.h): layer life cycle, forward, and
+// the stand-alone router / dispatch / gather_qmm entry points.
+//
+// SenMoeLayer mirrors DeepseekMoe (src/engine/mlx_lm/models/deepseek_v2.rs:485-553):
+// it borrows the caller's device weights in MLX layout and owns only its
+// scratch, allocated once at create time for config.max_tokens.  forward is
+// stream-ordered, allocation-free and never synchronises the host.
+
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <map>
+#include <mutex>
+#include <utility>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "../../include/senmoe.h"
+#include "kernels.h"
+
+using namespace senmoe;
+
+namespace senmoe {
+cudaError_t ensure_dynamic_smem(const void* kernel, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  size_t& cur = done[{kernel, dev}];
+  if (bytes <= cur) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e == cudaSuccess) cur = bytes;
+  return e;
+}
+}  // namespace senmoe
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+#define SENMOE_CUDA(call)                                                                            \
+  do {                                                                                               \
+    cudaError_t e_ = (call);                                                                         \
+    if (e_ != cudaSuccess)                                                                           \
+      return fail(e_ == cudaErrorNotSupported ? SENMOE_ERR_UNSUPPORTED : SENMOE_ERR_CUDA, "%s: %s (%s:%d)", \
+                  #call, cudaGetErrorString(e_), __FILE__, __LINE__);                                \
+  } while (0)
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Rows of one CTA for the grouped GEMV: gate/up rows (two projections) and
+// down rows.  Both keep one CTA's slice under ~70 KB of shared memory.
+constexpr int kGateUpRows = 16;
+constexpr int kDownRows = 64;
+
+}  // namespace
+
+struct SenMoeLayer {
+  SenMoeConfig cfg{};
+  SenMoeWeights w{};
+  int device = 0;
+  int max_pairs = 0;
+  int nchunks_max = 0;
+  // scratch (one allocation, carved)
+  void* arena = nullptr;
+  float* logits = nullptr;       // [Tmax, E]
+  int32_t* ids = nullptr;        // [Tmax*K]
+  float* wts = nullptr;          // [Tmax*K]
+  int32_t* perm = nullptr;       // [Tmax*K]
+  int32_t* inv = nullptr;        // [Tmax*K]
+  int32_t* offsets = nullptr;    // [E+1]
+  int32_t* active = nullptr;     // [E]
+  int32_t* active_count = nullptr;
+  int* err = nullptr;
+  int32_t* chunk_hist = nullptr; // [nchunks, E]
+  uint16_t* h = nullptr;         // [Tmax*K, I]
+  uint16_t* d = nullptr;         // [Tmax*K, H]
+  uint16_t* sh_h = nullptr;      // [Tmax, Is]
+  uint16_t* sh_out = nullptr;    // [Tmax, H]
+  float* sh_gate = nullptr;      // [Tmax]
+  uint32_t* zeros_idx = nullptr; // [Tmax] expert 0 for the shared expert
+  // per-stage timing
+  bool profiling = false;
+  bool profiled_once = false;
+  cudaEvent_t ev[SENMOE_NUM_STAGES + 1] = {};
+};
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+static int validate_config(const SenMoeConfig* c) {
+  if (!c) return fail(SENMOE_ERR_BAD_ARG, "config is NULL");
+  const int H = c->hidden_size, I = c->moe_intermediate_size, E = c->n_routed_experts, K = c->num_experts_per_tok;
+  if (H <= 0 || I <= 0 || E <= 0 || K <= 0 || K > E)
+    return fail(SENMOE_ERR_BAD_ARG, "bad sizes H=%d I=%d E=%d K=%d", H, I, E, K);
+  if (c->bits != 4 && c->bits != 8)
+    return fail(SENMOE_ERR_UNSUPPORTED, "bits=%d: only 4- and 8-bit affine quantization is supported", c->bits);
+  if (c->group_size != 64)
+    return fail(SENMOE_ERR_UNSUPPORTED, "group_size=%d: only 64 is supported", c->group_size);
+  if (c->router_kind != SENMOE_ROUTER_SOFTMAX_TOPK)
+    return fail(SENMOE_ERR_UNSUPPORTED, "router_kind=%d not supported", c->router_kind);
+  if (c->activation != SENMOE_ACT_SWIGLU && c->activation != SENMOE_ACT_GEGLU)
+    return fail(SENMOE_ERR_BAD_ARG, "activation=%d", c->activation);
+  if (!router_supported(H, E, K))
+    return fail(SENMOE_ERR_UNSUPPORTED, "router: need H %% 256 == 0, H <= 4096, E <= 512, K <= 16 (H=%d E=%d K=%d)",
+                H, E, K);
+  if (!qgemv_supported(H, c->bits) || !qgemv_supported(I, c->bits))
+    return fail(SENMOE_ERR_UNSUPPORTED, "expert GEMV: H=%d / I=%d not supported at %d bits", H, I, c->bits);
+  if (c->shared_intermediate < 0 || (c->shared_intermediate > 0 && !qgemv_supported(c->shared_intermediate, c->bits)))
+    return fail(SENMOE_ERR_UNSUPPORTED, "shared_intermediate=%d not supported", c->shared_intermediate);
+  if (c->max_tokens <= 0) return fail(SENMOE_ERR_BAD_ARG, "max_tokens=%d", c->max_tokens);
+  if ((long long)c->max_tokens * K > (1ll << 30)) return fail(SENMOE_ERR_BAD_ARG, "max_tokens*K too large");
+  if (c->expert_begin < 0 || c->expert_end > E || c->expert_begin >= c->expert_end)
+    return fail(SENMOE_ERR_BAD_ARG, "local expert range [%d, %d) outside [0, %d)", c->expert_begin, c->expert_end, E);
+  return SENMOE_OK;
+}
+
+static int validate_weights(const SenMoeConfig* c, const SenMoeWeights* w) {
+  if (!w) return fail(SENMOE_ERR_BAD_ARG, "weights is NULL");
+  const void* req[] = {w->router_weight, w->gate_weight, w->gate_scales, w->gate_biases, w->up_weight,
+                       w->up_scales,     w->up_biases,   w->down_weight, w->down_scales, w->down_biases};
+  for (const void* p : req) {
+    if (!p) return fail(SENMOE_ERR_BAD_ARG, "a required weight pointer is NULL");
+    if (!aligned16(p)) return fail(SENMOE_ERR_BAD_ARG, "weight pointer %p is not 16-byte aligned", p);
+  }
+  if (c->shared_intermediate > 0) {
+    const void* sh[] = {w->shared_gate_weight, w->shared_gate_scales, w->shared_gate_biases,
+                        w->shared_up_weight,   w->shared_up_scales,   w->shared_up_biases,
+                        w->shared_down_weight, w->shared_down_scales, w->shared_down_biases};
+    for (const void* p : sh) {
+      if (!p) return fail(SENMOE_ERR_BAD_ARG, "a shared-expert weight pointer is NULL");
+      if (!aligned16(p)) return fail(SENMOE_ERR_BAD_ARG, "shared-expert pointer %p is not 16-byte aligned", p);
+    }
+    if (c->shared_gate && !w->shared_gate_vector)
+      return fail(SENMOE_ERR_BAD_ARG, "shared_gate set but shared_gate_vector is NULL");
+  }
+  // Bulk copies move whole row blocks: the scale/bias rows of a block must be
+  // 16-byte multiples.
+  // Every block start (expert stride, full blocks) and the ragged last block
+  // must be 16-byte multiples.
+  auto blocks_ok = [](long long rows, long long kdim, long long rows_per_cta) {
+    const long long g2 = kdim / 64 * 2;
+    return (rows * g2) % 16 == 0 && (rows_per_cta * g2) % 16 == 0 && ((rows % rows_per_cta) * g2) % 16 == 0;
+  };
+  const int H = c->hidden_size, I = c->moe_intermediate_size, Is = c->shared_intermediate;
+  if (!blocks_ok(I, H, kGateUpRows) || !blocks_ok(H, I, kDownRows) ||
+      (Is > 0 && (!blocks_ok(Is, H, kGateUpRows) || !blocks_ok(H, Is, kDownRows))))
+    return fail(SENMOE_ERR_UNSUPPORTED, "scale/bias blocks of H=%d I=%d Is=%d are not 16-byte multiples", H, I, Is);
+  return SENMOE_OK;
+}
+
+extern "C" {
+
+const char* senmoe_last_error(void) { return g_last_error.c_str(); }
+
+const char* senmoe_version(void) { return "senmoe 1 sm_100a"; }
+
+int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights, int device,
+                        SenMoeLayer** out_layer) {
+  g_last_error.clear();
+  if (!out_layer) return fail(SENMOE_ERR_BAD_ARG, "out_layer is NULL");
+  *out_layer = nullptr;
+  int rc = validate_config(config);
+  if (rc) return rc;
+  if ((rc = validate_weights(config, weights))) return rc;
+  int cur = 0;
+  SENMOE_CUDA(cudaGetDevice(&cur));
+  SENMOE_CUDA(cudaSetDevice(device));
+
+  SenMoeLayer* L = new (std::nothrow) SenMoeLayer();
+  if (!L) return fail(SENMOE_ERR_NO_MEMORY, "host allocation failed");
+  L->cfg = *config;
+  L->w = *weights;
+  L->device = device;
+  const SenMoeConfig& c = L->cfg;
+  const size_t T = c.max_tokens, K = c.num_experts_per_tok, E = c.n_routed_experts;
+  const size_t H = c.hidden_size, I = c.moe_intermediate_size, Is = c.shared_intermediate;
+  const size_t P = T * K;
+  L->max_pairs = static_cast<int>(P);
+  L->nchunks_max = static_cast<int>((P + kDispatchChunk - 1) / kDispatchChunk);
+
+  // carve one arena (256-byte aligned pieces)
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
+  const size_t o_logits = take(T * E * 4), o_ids = take(P * 4), o_wts = take(P * 4), o_perm = take(P * 4),
+               o_inv = take(P * 4), o_offs = take((E + 1) * 4), o_act = take(E * 4), o_cnt = take(4),
+               o_err = take(4), o_hist = take(size_t(L->nchunks_max) * E * 4), o_h = take(P * I * 2),
+               o_d = take(P * H * 2), o_shh = take(Is ? T * Is * 2 : 0), o_sho = take(Is ? T * H * 2 : 0),
+               o_shg = take(Is ? T * 4 : 0), o_zero = take(Is ? T * 4 : 0);
+  cudaError_t e = cudaMalloc(&L->arena, off);
+  if (e != cudaSuccess) {
+    delete L;
+    cudaSetDevice(cur);
+    return fail(SENMOE_ERR_NO_MEMORY, "cudaMalloc(%zu) for layer scratch failed: %s", off, cudaGetErrorString(e));
+  }
+  char* base = static_cast<char*>(L->arena);
+  L->logits = reinterpret_cast<float*>(base + o_logits);
+  L->ids = reinterpret_cast<int32_t*>(base + o_ids);
+  L->wts = reinterpret_cast<float*>(base + o_wts);
+  L->perm = reinterpret_cast<int32_t*>(base + o_perm);
+  L->inv = reinterpret_cast<int32_t*>(base + o_inv);
+  L->offsets = reinterpret_cast<int32_t*>(base + o_offs);
+  L->active = reinterpret_cast<int32_t*>(base + o_act);
+  L->active_count = reinterpret_cast<int32_t*>(base + o_cnt);
+  L->err = reinterpret_cast<int*>(base + o_err);
+  L->chunk_hist = reinterpret_cast<int32_t*>(base + o_hist);
+  L->h = reinterpret_cast<uint16_t*>(base + o_h);
+  L->d = reinterpret_cast<uint16_t*>(base + o_d);
+  if (Is) {
+    L->sh_h = reinterpret_cast<uint16_t*>(base + o_shh);
+    L->sh_out = reinterpret_cast<uint16_t*>(base + o_sho);
+    L->sh_gate = reinterpret_cast<float*>(base + o_shg);
+    L->zeros_idx = reinterpret_cast<uint32_t*>(base + o_zero);
+  }
+  e = cudaMemset(L->arena, 0, off);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaSetDevice(cur);
+  if (e != cudaSuccess) {
+    cudaFree(L->arena);
+    delete L;
+    return fail(SENMOE_ERR_CUDA, "scratch initialisation failed: %s", cudaGetErrorString(e));
+  }
+  *out_layer = L;
+  return SENMOE_OK;
+}
+
+int senmoe_layer_destroy(SenMoeLayer* layer) {
+  g_last_error.clear();
+  if (!layer) return SENMOE_OK;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  cudaSetDevice(layer->device);
+  for (auto& ev : layer->ev)
+    if (ev) cudaEventDestroy(ev);
+  cudaError_t e = cudaFree(layer->arena);
+  cudaSetDevice(cur);
+  delete layer;
+  if (e != cudaSuccess) return fail(SENMOE_ERR_CUDA, "cudaFree: %s", cudaGetErrorString(e));
+  return SENMOE_OK;
+}
+
+static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void* y, const SenMoeDebug* debug,
+                         bool residual, senmoe_stream_t stream) {
+  g_last_error.clear();
+  if (!L) return fail(SENMOE_ERR_BAD_ARG, "layer is NULL");
+  const SenMoeConfig& c = L->cfg;
+  if (num_tokens < 0 || num_tokens > c.max_tokens)
+    return fail(SENMOE_ERR_BAD_ARG, "num_tokens=%lld outside [0, max_tokens=%d]", (long long)num_tokens, c.max_tokens);
+  if (num_tokens == 0) return SENMOE_OK;
+  if (!x || !y) return fail(SENMOE_ERR_BAD_ARG, "x or y is NULL");
+  if (!aligned16(x) || !aligned16(y)) return fail(SENMOE_ERR_BAD_ARG, "x and y must be 16-byte aligned");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int T = static_cast<int>(num_tokens), K = c.num_experts_per_tok, E = c.n_routed_experts;
+  const int H = c.hidden_size, I = c.moe_intermediate_size, Is = c.shared_intermediate;
+  const int P = T * K;
+  auto mark = [&](int stage) -> cudaError_t {
+    return L->profiling ? cudaEventRecord(L->ev[stage], st) : cudaSuccess;
+  };
+  SENMOE_CUDA(mark(0));
+
+  // 1. router (deepseek_v2.rs:528-543)
+  RouterArgs ra{};
+  ra.x = static_cast<const uint16_t*>(x);
+  ra.weight = static_cast<const uint16_t*>(L->w.router_weight);
+  ra.logits = L->logits;
+  ra.topk_ids = L->ids;
+  ra.topk_weights = L->wts;
+  ra.num_tokens = T;
+  ra.hidden = H;
+  ra.num_experts = E;
+  ra.top_k = K;
+  ra.norm_topk_prob = c.norm_topk_prob;
+  ra.routed_scaling_factor = c.routed_scaling_factor;
+  ra.round_logits = 1;
+  SENMOE_CUDA(launch_router_logits(ra, st));
+  SENMOE_CUDA(launch_router_topk(ra, st));
+  SENMOE_CUDA(mark(1));
+
+  // 2. dispatch
+  DispatchArgs da{};
+  da.topk_ids = L->ids;
+  da.num_pairs = P;
+  da.num_experts = E;
+  da.expert_begin = c.expert_begin;
+  da.expert_end = c.expert_end;
+  da.perm = L->perm;
+  da.inverse = L->inv;
+  da.offsets = L->offsets;
+  da.active = L->active;
+  da.active_count = L->active_count;
+  da.chunk_hist = L->chunk_hist;
+  da.err = L->err;
+  SENMOE_CUDA(launch_dispatch(da, st));
+  SENMOE_CUDA(mark(2));
+
+  // 3. gate/up + activation over the touched local experts -> h [P, I]
+  const int max_items = P < (c.expert_end - c.expert_begin) ? P : (c.expert_end - c.expert_begin);
+  QGemvArgs g{};
+  g.x = static_cast<const uint16_t*>(x);
+  g.w[0] = L->w.gate_weight;
+  g.s[0] = static_cast<const uint16_t*>(L->w.gate_scales);
+  g.b[0] = static_cast<const uint16_t*>(L->w.gate_biases);
+  g.w[1] = L->w.up_weight;
+  g.s[1] = static_cast<const uint16_t*>(L->w.up_scales);
+  g.b[1] = static_cast<const uint16_t*>(L->w.up_biases);
+  g.kdim = H;
+  g.rows = I;
+  g.rows_per_cta = kGateUpRows;
+  g.mode = kItemsGrouped;
+  g.active = L->active;
+  g.active_count = L->active_count;
+  g.offsets = L->offsets;
+  g.perm = L->perm;
+  g.k_div = K;
+  g.x_by_slot = 0;
+  g.expert_begin = c.expert_begin;
+  g.out = L->h;
+  g.out_stride = I;
+  g.act = c.activation;
+  g.err = L->err;
+  SENMOE_CUDA(launch_qgemv(g, 2, c.bits, max_items, st));
+  SENMOE_CUDA(mark(3));
+
+  // 4. down -> d [P, H]
+  QGemvArgs dn = g;
+  dn.x = L->h;
+  dn.w[0] = L->w.down_weight;
+  dn.s[0] = static_cast<const uint16_t*>(L->w.down_scales);
+  dn.b[0] = static_cast<const uint16_t*>(L->w.down_biases);
+  dn.kdim = I;
+  dn.rows = H;
+  dn.rows_per_cta = kDownRows;
+  dn.x_by_slot = 1;
+  dn.out = L->d;
+  dn.out_stride = H;
+  SENMOE_CUDA(launch_qgemv(dn, 1, c.bits, max_items, st));
+  SENMOE_CUDA(mark(4));
+
+  // 5. shared expert (deepseek_v2.rs:550-552), optionally sigmoid-gated
+  if (Is > 0) {
+    QGemvArgs sg{};
+    sg.x = static_cast<const uint16_t*>(x);
+    sg.w[0] = L->w.shared_gate_weight;
+    sg.s[0] = static_cast<const uint16_t*>(L->w.shared_gate_scales);
+    sg.b[0] = static_cast<const uint16_t*>(L->w.shared_gate_biases);
+    sg.w[1] = L->w.shared_up_weight;
+    sg.s[1] = static_cast<const uint16_t*>(L->w.shared_up_scales);
+    sg.b[1] = static_cast<const uint16_t*>(L->w.shared_up_biases);
+    sg.kdim = H;
+    sg.rows = Is;
+    sg.rows_per_cta = kGateUpRows;
+    sg.mode = kItemsGather;
+    sg.gather_idx = L->zeros_idx;
+    sg.rep = 1;
+    sg.num_experts = 1;
+    sg.out = L->sh_h;
+    sg.out_stride = Is;
+    sg.act = c.activation;
+    sg.err = L->err;
+    SENMOE_CUDA(launch_qgemv(sg, 2, c.bits, T, st));
+    QGemvArgs sd = sg;
+    sd.x = L->sh_h;
+    sd.w[0] = L->w.shared_down_weight;
+    sd.s[0] = static_cast<const uint16_t*>(L->w.shared_down_scales);
+    sd.b[0] = static_cast<const uint16_t*>(L->w.shared_down_biases);
+    sd.kdim = Is;
+    sd.rows = H;
+    sd.rows_per_cta = kDownRows;
+    sd.out = L->sh_out;
+    sd.out_stride = H;
+    SENMOE_CUDA(launch_qgemv(sd, 1, c.bits, T, st));
+    if (c.shared_gate) {
+      RouterArgs gr = ra;
+      gr.weight = static_cast<const uint16_t*>(L->w.shared_gate_vector);
+      gr.logits = L->sh_gate;
+      gr.num_experts = 1;
+      gr.round_logits = 0;
+      SENMOE_CUDA(launch_router_logits(gr, st));
+      SENMOE_CUDA(launch_sigmoid_inplace(L->sh_gate, T, st));
+    }
+  }
+
+  SENMOE_CUDA(mark(5));
+
+  // 6. weighted combine (deepseek_v2.rs:546-548) -> y
+  CombineArgs ca{};
+  ca.d = L->d;
+  ca.inverse = L->inv;
+  ca.weights = L->wts;
+  ca.shared_out = Is > 0 ? L->sh_out : nullptr;
+  ca.shared_gate = (Is > 0 && c.shared_gate) ? L->sh_gate : nullptr;
+  ca.y = static_cast<uint16_t*>(y);
+  ca.residual = residual ? static_cast<const uint16_t*>(x) : nullptr;
+  ca.y_f32 = nullptr;
+  ca.hidden = H;
+  ca.top_k = K;
+  SENMOE_CUDA(launch_combine(ca, T, st));
+  SENMOE_CUDA(mark(6));
+  if (L->profiling) L->profiled_once = true;
+
+  if (debug) {
+    if (debug->topk_ids)
+      SENMOE_CUDA(cudaMemcpyAsync(debug->topk_ids, L->ids, size_t(P) * 4, cudaMemcpyDeviceToDevice, st));
+    if (debug->topk_weights)
+      SENMOE_CUDA(cudaMemcpyAsync(debug->topk_weights, L->wts, size_t(P) * 4, cudaMemcpyDeviceToDevice, st));
+    if (debug->perm) SENMOE_CUDA(cudaMemcpyAsync(debug->perm, L->perm, size_t(P) * 4, cudaMemcpyDeviceToDevice, st));
+    if (debug->offsets)
+      SENMOE_CUDA(cudaMemcpyAsync(debug->offsets, L->offsets, size_t(E + 1) * 4, cudaMemcpyDeviceToDevice, st));
+  }
+  return SENMOE_OK;
+}
+
+int senmoe_layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void* y, const SenMoeDebug* debug,
+                         senmoe_stream_t stream) {
+  return layer_forward(L, x, num_tokens, y, debug, false, stream);
+}
+
+int senmoe_layer_forward_residual(SenMoeLayer* L, const void* x, int64_t num_tokens, void* h_out,
+                                  senmoe_stream_t stream) {
+  return layer_forward(L, x, num_tokens, h_out, nullptr, true, stream);
+}
+
+int senmoe_layer_set_profiling(SenMoeLayer* L, int enable) {
+  g_last_error.clear();
+  if (!L) return fail(SENMOE_ERR_BAD_ARG, "layer is NULL");
+  int cur = 0;
+  SENMOE_CUDA(cudaGetDevice(&cur));
+  SENMOE_CUDA(cudaSetDevice(L->device));
+  if (enable && !L->ev[0]) {
+    for (auto& e : L->ev) SENMOE_CUDA(cudaEventCreate(&e));
+  }
+  L->profiling = enable != 0;
+  L->profiled_once = false;
+  SENMOE_CUDA(cudaSetDevice(cur));
+  return SENMOE_OK;
+}
+
+int senmoe_layer_stage_times(SenMoeLayer* L, float* ms, int n) {
+  g_last_error.clear();
+  if (!L || !ms || n < 0) return -fail(SENMOE_ERR_BAD_ARG, "bad arguments");
+  if (!L->profiled_once) return -fail(SENMOE_ERR_BAD_ARG, "no profiled forward since profiling was enabled");
+  cudaError_t e = cudaEventSynchronize(L->ev[SENMOE_NUM_STAGES]);
+  if (e != cudaSuccess) return -fail(SENMOE_ERR_CUDA, "cudaEventSynchronize: %s", cudaGetErrorString(e));
+  const int m = n < SENMOE_NUM_STAGES ? n : SENMOE_NUM_STAGES;
+  for (int i = 0; i < m; ++i) {
+    e = cudaEventElapsedTime(&ms[i], L->ev[i], L->ev[i + 1]);
+    if (e != cudaSuccess) return -fail(SENMOE_ERR_CUDA, "cudaEventElapsedTime: %s", cudaGetErrorString(e));
+  }
+  return m;
+}
+
+int senmoe_layer_check(SenMoeLayer* L, senmoe_stream_t stream) {
+  g_last_error.clear();
+  if (!L) return fail(SENMOE_ERR_BAD_ARG, "layer is NULL");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int host_err = 0;
+  SENMOE_CUDA(cudaMemcpyAsync(&host_err, L->err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  SENMOE_CUDA(cudaStreamSynchronize(st));
+  if (host_err) {
+    SENMOE_CUDA(cudaMemsetAsync(L->err, 0, sizeof(int), st));
+    SENMOE_CUDA(cudaStreamSynchronize(st));
+    if (host_err == kDevBadExpert) return fail(SENMOE_ERR_DEVICE, "a kernel saw an expert id outside [0, E)");
+    if (host_err == kDevWaitTimeout) return fail(SENMOE_ERR_TIMEOUT, "a bounded device-side wait ran out");
+    return fail(SENMOE_ERR_DEVICE, "device error code %d", host_err);
+  }
+  return SENMOE_OK;
+}
+
+int senmoe_router(const void* x, int64_t num_tokens, const void* router_weight, int32_t hidden, int32_t num_experts,
+                  int32_t top_k, int32_t norm_topk_prob, float routed_scaling_factor, float* logits_scratch,
+                  int32_t* topk_ids, float* topk_weights, senmoe_stream_t stream) {
+  g_last_error.clear();
+  if (num_tokens < 0 || num_tokens > (1ll << 28)) return fail(SENMOE_ERR_BAD_ARG, "num_tokens=%lld", (long long)num_tokens);
+  if (!router_supported(hidden, num_experts, top_k))
+    return fail(SENMOE_ERR_UNSUPPORTED, "router: H=%d E=%d K=%d unsupported", hidden, num_experts, top_k);
+  if (num_tokens == 0) return SENMOE_OK;
+  if (!x || !router_weight || !logits_scratch || !topk_ids || !topk_weights)
+    return fail(SENMOE_ERR_BAD_ARG, "NULL pointer");
+  if (!aligned16(x) || !aligned16(router_weight)) return fail(SENMOE_ERR_BAD_ARG, "x / router_weight not 16-byte aligned");
+  RouterArgs ra{};
+  ra.x = static_cast<const uint16_t*>(x);
+  ra.weight = static_cast<const uint16_t*>(router_weight);
+  ra.logits = logits_scratch;
+  ra.topk_ids = topk_ids;
+  ra.topk_weights = topk_weights;
+  ra.num_tokens = static_cast<int>(num_tokens);
+  ra.hidden = hidden;
+  ra.num_experts = num_experts;
+  ra.top_k = top_k;
+  ra.norm_topk_prob = norm_topk_prob;
+  ra.routed_scaling_factor = routed_scaling_factor;
+  ra.round_logits = 1;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  SENMOE_CUDA(launch_router_logits(ra, st));
+  SENMOE_CUDA(launch_router_topk(ra, st));
+  return SENMOE_OK;
+}
+
+int senmoe_dispatch(const int32_t* topk_ids, int64_t num_tokens, int32_t top_k, int32_t num_experts, int32_t* perm,
+                    int32_t* inverse, int32_t* offsets, int32_t* scratch, senmoe_stream_t stream) {
+  g_last_error.clear();
+  if (num_tokens < 0 || top_k <= 0 || num_experts <= 0 || num_experts > 1024 || num_tokens * top_k > (1ll << 30))
+    return fail(SENMOE_ERR_BAD_ARG, "bad sizes T=%lld K=%d E=%d", (long long)num_tokens, top_k, num_experts);
+  if (num_tokens == 0) return SENMOE_OK;
+  if (!topk_ids || !perm || !inverse || !offsets || !scratch) return fail(SENMOE_ERR_BAD_ARG, "NULL pointer");
+  DispatchArgs da{};
+  da.topk_ids = topk_ids;
+  da.num_pairs = static_cast<int>(num_tokens * top_k);
+  da.num_experts = num_experts;
+  da.expert_begin = 0;
+  da.expert_end = num_experts;
+  da.perm = perm;
+  da.inverse = inverse;
+  da.offsets = offsets;
+  da.active = scratch;
+  da.active_count = scratch + num_experts;
+  da.err = scratch + num_experts + 1;
+  da.chunk_hist = nullptr;  // single-CTA form
+  SENMOE_CUDA(launch_dispatch(da, reinterpret_cast<cudaStream_t>(stream)));
+  return SENMOE_OK;
+}
+
+int senmoe_gather_qmm(const void* x, int64_t x_rows, const uint32_t* w, const void* scales, const void* biases,
+                      const uint32_t* rhs_indices, int64_t n_indices, int64_t in_features, int64_t out_features,
+                      int32_t num_experts, int32_t transpose, int32_t group_size, int32_t bits,
+                      int32_t sorted_indices, void* out, senmoe_stream_t stream) {
+  (void)sorted_indices;
+  g_last_error.clear();
+  if (!transpose)
+    return fail(SENMOE_ERR_UNSUPPORTED, "gather_qmm: transpose=false is not supported (the reference only uses "
+                                        "transpose=true)");
+  if (bits != 4 && bits != 8) return fail(SENMOE_ERR_UNSUPPORTED, "gather_qmm: bits=%d", bits);
+  if (group_size != 64) return fail(SENMOE_ERR_UNSUPPORTED, "gather_qmm: group_size=%d", group_size);
+  if (x_rows <= 0 || n_indices < 0 || n_indices % x_rows || num_experts <= 0 || out_features <= 0 ||
+      n_indices > (1ll << 31) - 1)
+    return fail(SENMOE_ERR_BAD_ARG, "gather_qmm: x_rows=%lld n_indices=%lld (must be a multiple)", (long long)x_rows,
+                (long long)n_indices);
+  if (in_features <= 0 || in_features > (1 << 20) || !qgemv_supported(static_cast<int>(in_features), bits))
+    return fail(SENMOE_ERR_UNSUPPORTED, "gather_qmm: in_features=%lld unsupported at %d bits",
+                (long long)in_features, bits);
+  if (n_indices == 0) return SENMOE_OK;
+  if (!x || !w || !scales || !biases || !rhs_indices || !out) return fail(SENMOE_ERR_BAD_ARG, "NULL pointer");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(scales) || !aligned16(biases))
+    return fail(SENMOE_ERR_BAD_ARG, "gather_qmm: x / w / scales / biases must be 16-byte aligned");
+  // Bulk copies move [rows_per_cta, groups] scale blocks: every block start
+  // and size must be a 16-byte multiple.
+  const int groups = static_cast<int>(in_features / 64);
+  int rows_per_cta = 16;
+  while ((rows_per_cta * groups * 2) % 16) rows_per_cta *= 2;
+  if ((out_features * groups * 2) % 16 || ((out_features % rows_per_cta) * groups * 2) % 16)
+    return fail(SENMOE_ERR_UNSUPPORTED, "gather_qmm: out_features=%lld with in_features=%lld leaves scale rows "
+                "that are not 16-byte multiples", (long long)out_features, (long long)in_features);
+  QGemvArgs g{};
+  g.x = static_cast<const uint16_t*>(x);
+  g.w[0] = w;
+  g.s[0] = static_cast<const uint16_t*>(scales);
+  g.b[0] = static_cast<const uint16_t*>(biases);
+  g.kdim = static_cast<int>(in_features);
+  g.rows = static_cast<int>(out_features);
+  g.rows_per_cta = rows_per_cta;
+  g.mode = kItemsGather;
+  g.gather_idx = rhs_indices;
+  g.rep = n_indices / x_rows;
+  g.num_experts = num_experts;
+  g.out = static_cast<uint16_t*>(out);
+  g.out_stride = out_features;
+  g.err = nullptr;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  SENMOE_CUDA(launch_qgemv(g, 1, bits, static_cast<int>(n_indices), st));
+  return SENMOE_OK;
+}
+
+}  // extern "C"

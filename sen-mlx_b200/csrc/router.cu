@@ -1,0 +1,195 @@
+// router.cu -- the MoE router: gate GEMV/GEMM, softmax, top-k, renorm.
+//
+// Restates the router half of DeepseekMoe::forward
+// (src/engine/mlx_lm/models/deepseek_v2.rs:526-543):
+//   logits = bf16(x . Wg^T)                 nn::Linear on bf16 -> bf16
+//   scores = bf16(softmax_fp32(logits))     softmax_axis(.., precise=true)
+//   top-k over scores                       argpartition(-scores, k)[:k]
+//   w = scores[top-k]; if norm: w = f32(w) / (f32(bf16(sum w)) + 1e-20f)
+//   if routed_scaling_factor != 1: w *= routed_scaling_factor
+// MLX leaves the order inside the k unspecified; slots here are ordered by
+// score descending, then expert id ascending, which also fixes tie-breaking.
+
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace senmoe {
+
+namespace {
+constexpr int kRouterWarps = 4;        // experts per CTA (one per warp)
+constexpr int kRouterTokTile = 16;     // tokens per CTA (x tile in shared memory)
+constexpr int kTopkWarps = 4;          // tokens per CTA in the top-k kernel
+constexpr int kMaxTopK = 16;
+}  // namespace
+
+// Each warp owns one expert row (held in registers as packed bf16; lane l
+// holds columns 256 i + 8 l .. +8), each CTA a tile of tokens staged in shared
+// memory; one fp32 dot per (token, expert), reduced by warp shuffles.
+template <int VPL>  // 16-byte vectors per lane = H / 256
+__global__ void __launch_bounds__(kRouterWarps * 32) router_logits_kernel(RouterArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  uint4* xs = reinterpret_cast<uint4*>(smem);  // [tile][H/8]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int e = blockIdx.x * kRouterWarps + warp;
+  const int t0 = blockIdx.y * kRouterTokTile;
+  const int nt = min(kRouterTokTile, a.num_tokens - t0);
+  const int vec_per_row = a.hidden / 8;
+
+  for (int i = threadIdx.x; i < nt * vec_per_row; i += blockDim.x)
+    xs[i] = reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t0) * a.hidden)[i];
+  __syncthreads();
+  if (e >= a.num_experts) return;
+
+  float wv[VPL][8];
+  const uint4* wrow = reinterpret_cast<const uint4*>(a.weight + static_cast<size_t>(e) * a.hidden);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const uint4 v = wrow[32 * i + lane];
+    wv[i][0] = bf16_lo(v.x); wv[i][1] = bf16_hi(v.x); wv[i][2] = bf16_lo(v.y); wv[i][3] = bf16_hi(v.y);
+    wv[i][4] = bf16_lo(v.z); wv[i][5] = bf16_hi(v.z); wv[i][6] = bf16_lo(v.w); wv[i][7] = bf16_hi(v.w);
+  }
+  for (int t = 0; t < nt; ++t) {
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const uint4 v = xs[t * vec_per_row + 32 * i + lane];
+      acc = fmaf(bf16_lo(v.x), wv[i][0], acc); acc = fmaf(bf16_hi(v.x), wv[i][1], acc);
+      acc = fmaf(bf16_lo(v.y), wv[i][2], acc); acc = fmaf(bf16_hi(v.y), wv[i][3], acc);
+      acc = fmaf(bf16_lo(v.z), wv[i][4], acc); acc = fmaf(bf16_hi(v.z), wv[i][5], acc);
+      acc = fmaf(bf16_lo(v.w), wv[i][6], acc); acc = fmaf(bf16_hi(v.w), wv[i][7], acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0)
+      a.logits[static_cast<size_t>(t0 + t) * a.num_experts + e] = a.round_logits ? round_bf16(acc) : acc;
+  }
+}
+
+// One warp per token: softmax over E (fp32), scores rounded to bf16, K rounds
+// of warp arg-max (score desc, id asc), then renorm / scaling in fp32.
+template <int EPL>  // experts per lane = ceil(E / 32)
+__global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(RouterArgs a) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.x * kTopkWarps + warp;
+  if (t >= a.num_tokens) return;
+  const float* lg = a.logits + static_cast<size_t>(t) * a.num_experts;
+  float p[EPL];
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int e = lane + 32 * j;
+    p[j] = e < a.num_experts ? lg[e] : -INFINITY;
+    m = fmaxf(m, p[j]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int e = lane + 32 * j;
+    p[j] = e < a.num_experts ? expf(p[j] - m) : 0.f;
+    sum += p[j];
+  }
+  sum = warp_sum(sum);
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int e = lane + 32 * j;
+    p[j] = e < a.num_experts ? round_bf16(p[j] / sum) : -1.0f;
+  }
+
+  uint32_t taken = 0;
+  float sel_w[kMaxTopK];
+  int sel_e[kMaxTopK];
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k) {
+    if (k >= a.top_k) break;
+    float bv = -2.0f;
+    int be = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) {
+      const int e = lane + 32 * j;
+      if (!((taken >> j) & 1u) && (p[j] > bv || (p[j] == bv && e < be))) {
+        bv = p[j];
+        be = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+      if (ov > bv || (ov == bv && oe < be)) {
+        bv = ov;
+        be = oe;
+      }
+    }
+    if ((be & 31) == lane) taken |= 1u << (be >> 5);
+    sel_w[k] = bv;
+    sel_e[k] = be;
+  }
+  if (lane == 0) {
+    if (a.norm_topk_prob) {
+      float s = 0.f;
+      for (int k = 0; k < a.top_k; ++k) s += sel_w[k];
+      const float den = round_bf16(s) + 1e-20f;
+      for (int k = 0; k < a.top_k; ++k) sel_w[k] = sel_w[k] / den;
+    }
+    if (fabsf(a.routed_scaling_factor - 1.0f) > 1.1920929e-7f)
+      for (int k = 0; k < a.top_k; ++k) sel_w[k] *= a.routed_scaling_factor;
+    for (int k = 0; k < a.top_k; ++k) {
+      a.topk_ids[static_cast<size_t>(t) * a.top_k + k] = sel_e[k];
+      a.topk_weights[static_cast<size_t>(t) * a.top_k + k] = sel_w[k];
+    }
+  }
+}
+
+__global__ void sigmoid_inplace_kernel(float* v, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) v[i] = 1.0f / (1.0f + expf(-v[i]));
+}
+
+bool router_supported(int hidden, int num_experts, int top_k) {
+  const int vpl = hidden / 256;
+  const bool vpl_ok = vpl == 1 || vpl == 2 || vpl == 4 || vpl == 8 || vpl == 12 || vpl == 16;
+  return hidden % 256 == 0 && vpl_ok && num_experts >= 1 && num_experts <= 512 && top_k >= 1 &&
+         top_k <= kMaxTopK && top_k <= num_experts;
+}
+
+cudaError_t launch_router_logits(const RouterArgs& a, cudaStream_t st) {
+  if (a.num_tokens == 0) return cudaSuccess;
+  const int vpl = a.hidden / 256;
+  const size_t smem = static_cast<size_t>(kRouterTokTile) * a.hidden * 2;
+  dim3 grid((a.num_experts + kRouterWarps - 1) / kRouterWarps, (a.num_tokens + kRouterTokTile - 1) / kRouterTokTile);
+#define SENMOE_RL_CASE(V)                                                                                  \
+  if (vpl == V) {                                                                                          \
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(router_logits_kernel<V>), smem);      \
+    if (e != cudaSuccess) return e;                                                                        \
+    router_logits_kernel<V><<<grid, kRouterWarps * 32, smem, st>>>(a);                                     \
+    return cudaGetLastError();                                                                             \
+  }
+  SENMOE_RL_CASE(1) SENMOE_RL_CASE(2) SENMOE_RL_CASE(4) SENMOE_RL_CASE(8) SENMOE_RL_CASE(12) SENMOE_RL_CASE(16)
+#undef SENMOE_RL_CASE
+  return cudaErrorNotSupported;
+}
+
+cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st) {
+  if (a.num_tokens == 0) return cudaSuccess;
+  const int epl = (a.num_experts + 31) / 32;
+  dim3 grid((a.num_tokens + kTopkWarps - 1) / kTopkWarps);
+#define SENMOE_TK_CASE(V)                                        \
+  if (epl <= V) {                                                \
+    router_topk_kernel<V><<<grid, kTopkWarps * 32, 0, st>>>(a);  \
+    return cudaGetLastError();                                   \
+  }
+  SENMOE_TK_CASE(1) SENMOE_TK_CASE(2) SENMOE_TK_CASE(4) SENMOE_TK_CASE(8) SENMOE_TK_CASE(16)
+#undef SENMOE_TK_CASE
+  return cudaErrorNotSupported;
+}
+
+cudaError_t launch_sigmoid_inplace(float* v, int n, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  sigmoid_inplace_kernel<<<(n + 255) / 256, 256, 0, st>>>(v, n);
+  return cudaGetLastError();
+}
+
+}  // namespace senmoe

@@ -1,0 +1,181 @@
+"""GPU parity of the whole block (DeepseekMoe::forward,
+src/engine/mlx_lm/models/deepseek_v2.rs:520-553) with the oracle's MLX
+rounding mode, through the C ABI.
+
+Tolerances (bf16 block outputs): max abs error <= 2e-2 and relative L2 error
+<= 5e-3; top-k ids identical except at router ties; dispatch bit-exact."""
+import os
+
+import numpy as np
+import pytest
+
+from helpers import (MAX_ABS_TOL, REL_L2_TOL, bf16_np_to_f32, device_weights, moe_args, rel_l2, t_bf16,
+                     to_numpy_bf16, topk_match_except_ties)
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.fixture(scope="module")
+def senmoe():
+    import torch
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    import senmoe as s
+    s.lib()
+    return s
+
+
+def run_block(senmoe, cfg, mw, x_bits, max_tokens=None):
+    import torch
+    T = x_bits.shape[0]
+    blk = senmoe.DeepseekMoe(moe_args(cfg), device_weights(mw), max_tokens=max_tokens or max(T, 1))
+    dbg = dict(topk_ids=torch.empty((T, cfg.top_k), dtype=torch.int32, device="cuda"),
+               topk_weights=torch.empty((T, cfg.top_k), dtype=torch.float32, device="cuda"),
+               perm=torch.empty(T * cfg.top_k, dtype=torch.int32, device="cuda"),
+               offsets=torch.empty(cfg.num_experts + 1, dtype=torch.int32, device="cuda"))
+    y = blk.forward(t_bf16(x_bits), debug=dbg)
+    blk.check()
+    out = dict(y=bf16_np_to_f32(to_numpy_bf16(y)), **{k: v.cpu().numpy() for k, v in dbg.items()})
+    blk.close()
+    return out
+
+
+def check_against_oracle(cfg, mw, x, got):
+    ref = O.moe_forward(cfg, mw, x, mode=0)
+    _, _, scores = O.router(cfg, mw, x)
+    ok, ties = topk_match_except_ties(got["topk_ids"], ref["ids"], scores)
+    assert ok, "top-k ids differ beyond router ties"
+    same = (got["topk_ids"] == ref["ids"]).all(axis=1)
+    if ties == 0:
+        # dispatch is a pure function of the ids: bit-exact
+        np.testing.assert_array_equal(got["perm"], ref["perm"])
+        np.testing.assert_array_equal(got["offsets"], ref["offsets"])
+    y, yr = got["y"][same], ref["y_f32"][same]
+    err = np.abs(y - yr).max() if y.size else 0.0
+    r = rel_l2(y, yr) if y.size else 0.0
+    assert err <= MAX_ABS_TOL, f"max abs error {err}"
+    assert r <= REL_L2_TOL, f"relative L2 error {r}"
+    return err, r
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_small_block_vs_golden_fixture(senmoe, bits):
+    d = np.load(os.path.join(GOLD, f"moe_block_small_{bits}bit.npz"))
+    from test_oracle import _fixture_layer
+    cfg, mw = _fixture_layer(d)
+    got = run_block(senmoe, cfg, mw, d["x"])
+    np.testing.assert_array_equal(got["topk_ids"], d["ids"])
+    assert np.abs(got["y"] - d["y_f32"]).max() <= MAX_ABS_TOL
+    assert rel_l2(got["y"], d["y_f32"]) <= REL_L2_TOL
+
+
+@pytest.fixture(scope="module")
+def config0_layer():
+    """H=2048, E=128, K=8, I=768, 4-bit g64, seed 0."""
+    cfg = O.MoeConfig()
+    return cfg, O.make_layer(cfg, seed=0)
+
+
+@pytest.mark.parametrize("T", [1, 8, 16, 64])
+def test_config0_block_vs_oracle(senmoe, config0_layer, T):
+    cfg, mw = config0_layer
+    x = O.make_tokens(T, cfg.hidden, seed=T)
+    got = run_block(senmoe, cfg, mw, x)
+    check_against_oracle(cfg, mw, x, got)
+
+
+def test_block_8bit_shared_gated_large_e(senmoe):
+    """Config-3-like: E=512, K=10, I=512, sigmoid-gated shared expert (I_s=512)."""
+    cfg = O.MoeConfig(hidden=2048, intermediate=512, num_experts=512, top_k=10, bits=4,
+                      shared_intermediate=512, shared_gate=True)
+    mw = O.make_layer(cfg, seed=3)
+    x = O.make_tokens(24, cfg.hidden, seed=5)
+    got = run_block(senmoe, cfg, mw, x)
+    check_against_oracle(cfg, mw, x, got)
+
+
+def test_block_8bit_skewed(senmoe):
+    """Config-4-like: 8-bit weights, Zipf-biased router (many tokens on few experts)."""
+    cfg = O.MoeConfig(hidden=2048, intermediate=768, num_experts=128, top_k=8, bits=8)
+    mw = O.make_layer(cfg, seed=4)
+    bias = (1.0 / np.arange(1, 129) ** 1.2).astype(np.float32)
+    # fold a per-expert offset into the router: x gets a constant column, Wg that column's weight
+    rw = O.bf16_to_f32(mw.router_w)
+    rw[:, 0] += 3.0 * bias / max(bias.max(), 1e-9)
+    mw.router_w = O.f32_to_bf16(rw)
+    x = O.make_tokens(96, cfg.hidden, seed=8)
+    xf = O.bf16_to_f32(x)
+    xf[:, 0] = 4.0
+    x = O.f32_to_bf16(xf)
+    got = run_block(senmoe, cfg, mw, x)
+    counts = np.diff(got["offsets"])
+    assert counts.max() > 4 * counts[counts > 0].mean()  # skew present
+    check_against_oracle(cfg, mw, x, got)
+
+
+def test_many_tokens_multi_chunk_dispatch(senmoe):
+    """T*K > 2048 pairs takes the three-kernel dispatch; small H/I keep the oracle fast."""
+    cfg = O.MoeConfig(hidden=256, intermediate=128, num_experts=64, top_k=8, bits=4)
+    mw = O.make_layer(cfg, seed=6)
+    x = O.make_tokens(2000, cfg.hidden, seed=9)
+    got = run_block(senmoe, cfg, mw, x)
+    check_against_oracle(cfg, mw, x, got)
+
+
+def test_scaling_factor_and_geglu_free_path(senmoe):
+    cfg = O.MoeConfig(hidden=512, intermediate=256, num_experts=32, top_k=4, bits=4, norm_topk_prob=False,
+                      routed_scaling_factor=2.5)
+    mw = O.make_layer(cfg, seed=12)
+    x = O.make_tokens(40, cfg.hidden, seed=1)
+    got = run_block(senmoe, cfg, mw, x)
+    check_against_oracle(cfg, mw, x, got)
+
+
+def test_deterministic_and_stream_ordered(senmoe, config0_layer):
+    import torch
+    cfg, mw = config0_layer
+    blk = senmoe.DeepseekMoe(moe_args(cfg), device_weights(mw), max_tokens=64)
+    x = t_bf16(O.make_tokens(64, cfg.hidden, seed=3))
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        a = blk.forward(x, stream=s)
+        b = blk.forward(x, stream=s)
+    s.synchronize()
+    assert torch.equal(a, b)
+    blk.check()
+    blk.close()
+
+
+def test_zero_tokens_and_max_tokens(senmoe, config0_layer):
+    import torch
+    cfg, mw = config0_layer
+    blk = senmoe.DeepseekMoe(moe_args(cfg), device_weights(mw), max_tokens=4)
+    y = blk.forward(torch.empty(0, cfg.hidden, dtype=torch.bfloat16, device="cuda"))
+    assert y.shape == (0, cfg.hidden)
+    with pytest.raises(senmoe.SenMoeError):
+        blk.forward(torch.zeros(5, cfg.hidden, dtype=torch.bfloat16, device="cuda"))
+    blk.close()
+
+
+def test_cuda_graph_capture_of_forward(senmoe, config0_layer):
+    import torch
+    cfg, mw = config0_layer
+    blk = senmoe.DeepseekMoe(moe_args(cfg), device_weights(mw), max_tokens=8)
+    x = t_bf16(O.make_tokens(8, cfg.hidden, seed=21))
+    y = torch.empty_like(x)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        blk.forward(x, out=y, stream=s)  # warm-up (sets kernel attributes)
+    s.synchronize()
+    ref = y.clone()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        blk.forward(x, out=y, stream=s)
+    y.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y, ref)
+    del g
+    blk.close()
