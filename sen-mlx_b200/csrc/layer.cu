@@ -116,7 +116,7 @@ static int validate_config(const SenMoeConfig* c) {
   if (c->activation != SENMOE_ACT_SWIGLU && c->activation != SENMOE_ACT_GEGLU)
     return fail(SENMOE_ERR_BAD_ARG, "activation=%d", c->activation);
   if (!router_supported(H, E, K))
-    return fail(SENMOE_ERR_UNSUPPORTED, "router: need H %% 256 == 0, H <= 4096, E <= 512, K <= 16 (H=%d E=%d K=%d)",
+    return fail(SENMOE_ERR_UNSUPPORTED, "router: need H %% 8 == 0, H <= 4096, E <= 512, K <= 16 (H=%d E=%d K=%d)",
                 H, E, K);
   if (!qgemv_supported(H, c->bits) || !qgemv_supported(I, c->bits))
     return fail(SENMOE_ERR_UNSUPPORTED, "expert GEMV: H=%d / I=%d not supported at %d bits", H, I, c->bits);

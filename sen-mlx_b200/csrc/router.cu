@@ -27,7 +27,7 @@ constexpr int kMaxTopK = 16;
 // Each warp owns one expert row (held in registers as packed bf16; lane l
 // holds columns 256 i + 8 l .. +8), each CTA a tile of tokens staged in shared
 // memory; one fp32 dot per (token, expert), reduced by warp shuffles.
-template <int VPL>  // 16-byte vectors per lane = H / 256
+template <int VPL>  // 16-byte vectors per lane = ceil(H / 256)
 __global__ void __launch_bounds__(kRouterWarps * 32) router_logits_kernel(RouterArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   uint4* xs = reinterpret_cast<uint4*>(smem);  // [tile][H/8]
@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_logits_kernel(Router
   const uint4* wrow = reinterpret_cast<const uint4*>(a.weight + static_cast<size_t>(e) * a.hidden);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
-    const uint4 v = wrow[32 * i + lane];
+    const uint4 v = (32 * i + lane < vec_per_row) ? wrow[32 * i + lane] : make_uint4(0, 0, 0, 0);
     wv[i][0] = bf16_lo(v.x); wv[i][1] = bf16_hi(v.x); wv[i][2] = bf16_lo(v.y); wv[i][3] = bf16_hi(v.y);
     wv[i][4] = bf16_lo(v.z); wv[i][5] = bf16_hi(v.z); wv[i][6] = bf16_lo(v.w); wv[i][7] = bf16_hi(v.w);
   }
@@ -54,6 +54,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_logits_kernel(Router
     float acc = 0.f;
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
+      if (32 * i + lane >= vec_per_row) break;
       const uint4 v = xs[t * vec_per_row + 32 * i + lane];
       acc = fmaf(bf16_lo(v.x), wv[i][0], acc); acc = fmaf(bf16_hi(v.x), wv[i][1], acc);
       acc = fmaf(bf16_lo(v.y), wv[i][2], acc); acc = fmaf(bf16_hi(v.y), wv[i][3], acc);
@@ -149,15 +150,14 @@ __global__ void sigmoid_inplace_kernel(float* v, int n) {
 }
 
 bool router_supported(int hidden, int num_experts, int top_k) {
-  const int vpl = hidden / 256;
-  const bool vpl_ok = vpl == 1 || vpl == 2 || vpl == 4 || vpl == 8 || vpl == 12 || vpl == 16;
-  return hidden % 256 == 0 && vpl_ok && num_experts >= 1 && num_experts <= 512 && top_k >= 1 &&
-         top_k <= kMaxTopK && top_k <= num_experts;
+  return hidden > 0 && hidden % 8 == 0 && hidden <= 4096 && num_experts >= 1 && num_experts <= 512 &&
+         top_k >= 1 && top_k <= kMaxTopK && top_k <= num_experts;
 }
 
 cudaError_t launch_router_logits(const RouterArgs& a, cudaStream_t st) {
   if (a.num_tokens == 0) return cudaSuccess;
-  const int vpl = a.hidden / 256;
+  const int v = (a.hidden + 255) / 256;
+  const int vpl = v <= 2 ? v : v <= 4 ? 4 : v <= 8 ? 8 : v <= 12 ? 12 : 16;
   const size_t smem = static_cast<size_t>(kRouterTokTile) * a.hidden * 2;
   dim3 grid((a.num_experts + kRouterWarps - 1) / kRouterWarps, (a.num_tokens + kRouterTokTile - 1) / kRouterTokTile);
 #define SENMOE_RL_CASE(V)                                                                                  \

@@ -73,7 +73,7 @@ def _cfg(senmoe, **kw):
 
 @pytest.mark.parametrize("field,value,status", [
     ("bits", 3, 5), ("group_size", 32, 5), ("num_experts_per_tok", 0, 1), ("num_experts_per_tok", 200, 1),
-    ("max_tokens", 0, 1), ("expert_end", 129, 1), ("hidden_size", 2000, 5), ("router_kind", 7, 5),
+    ("max_tokens", 0, 1), ("expert_end", 129, 1), ("hidden_size", 2004, 5), ("router_kind", 7, 5),
 ])
 def test_layer_create_rejects_bad_config_on_host(senmoe, field, value, status):
     L = senmoe.lib()
