@@ -201,6 +201,9 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu", action="store_true",
+                    help="profiling mode: plain (non-graph) forwards of the workload, W warm-up + K steps, no "
+                         "timing or JSON; every step launches 6 kernels per layer in order")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -232,6 +235,16 @@ def main():
         t = torch.tensor([v], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    if args.ncu:
+        layers, _keep = make_stack(torch, senmoe, local, args.layers, args.batch, seed=rank)
+        x = torch.randn((args.batch, H), device=dev).to(torch.bfloat16)
+        for _ in range(args.warmup + args.steps):
+            h = x
+            for L in layers:
+                h = L.forward_residual(h)
+        torch.cuda.synchronize()
+        return
 
     batches = [args.batch] if args.no_sweep else sorted({1, 8, 32, args.batch})
     tmax = max(batches)
