@@ -186,6 +186,21 @@ int senmoe_gather_qmm(const void* x, int64_t x_rows, const uint32_t* w, const vo
                       int32_t num_experts, int32_t transpose, int32_t group_size, int32_t bits,
                       int32_t sorted_indices, void* out, senmoe_stream_t stream);
 
+/* Allocation-free forward (no counterpart in the reference; this build adds
+ * it for callers that cannot allocate device memory at call time: code inside
+ * an open CUDA stream capture, serving loops whose HBM another allocator has
+ * fully reserved, plugin hosts that forbid device allocation on the hot path).
+ * Same result as senmoe_layer_forward for the same config, weights and x,
+ * without a layer handle: all scratch lives in one fixed 4 MiB device array
+ * inside the library (held by every GPU that loads it until exit), so
+ * num_tokens is limited to what fits (config 0, H=2048 E=128 K=8 I=768: up to
+ * 64 tokens); larger calls return SENMOE_ERR_BAD_ARG.  The first call on a
+ * device resolves the array's address and should come before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race, so
+ * serialise them.  config->max_tokens bounds num_tokens as for a layer. */
+int senmoe_moe_forward_noalloc(const SenMoeConfig* config, const SenMoeWeights* weights, const void* x,
+                               int64_t num_tokens, void* y, senmoe_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

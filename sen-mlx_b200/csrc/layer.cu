@@ -585,3 +585,120 @@ int senmoe_gather_qmm(const void* x, int64_t x_rows, const uint32_t* w, const vo
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free forward.
+//
+// Some callers cannot allocate device memory when they need a MoE forward:
+// code that runs while a CUDA stream capture is open (cudaMalloc is illegal
+// there), serving loops whose HBM is fully reserved up front by another
+// allocator (a caching pool that owns all free memory), and plugin hosts that
+// forbid device allocation on their hot path.  senmoe_moe_forward_noalloc
+// serves them: it takes the config and weights directly (no layer handle, no
+// create-time allocation) and places all of its scratch in the file-scope
+// array below, which every GPU that loads this library holds until exit.
+//
+// Set-up: the first call on each device looks up the array's device address
+// with cudaGetSymbolAddress (a host-side use of the array's name is only a
+// stand-in, not a device address); make that first call before any stream
+// capture.  Every call shares the array and it keeps the last call's
+// contents, so calls whose work overlaps on the GPU (different streams, or
+// concurrent host threads) race with each other: serialise them.
+// ---------------------------------------------------------------------------
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Scratch bytes one forward of T tokens needs (same pieces as a layer's arena).
+size_t noalloc_bytes(const SenMoeConfig& c, size_t T, size_t* offs /* [16] */) {
+  const size_t K = c.num_experts_per_tok, E = c.n_routed_experts, H = c.hidden_size;
+  const size_t I = c.moe_intermediate_size, Is = c.shared_intermediate, P = T * K;
+  const size_t nchunks = (P + kDispatchChunk - 1) / kDispatchChunk;
+  const size_t sizes[16] = {T * E * 4, P * 4, P * 4, P * 4, P * 4, (E + 1) * 4, E * 4, 4, 4,
+                            nchunks * E * 4, P * I * 2, P * H * 2, Is ? T * Is * 2 : 0, Is ? T * H * 2 : 0,
+                            Is ? T * 4 : 0, Is ? T * 4 : 0};
+  size_t off = 0;
+  for (int i = 0; i < 16; ++i) {
+    offs[i] = off;
+    off = align_up(off + sizes[i], 256);
+  }
+  return off;
+}
+
+}  // namespace
+
+extern "C" int senmoe_moe_forward_noalloc(const SenMoeConfig* config, const SenMoeWeights* weights, const void* x,
+                                          int64_t num_tokens, void* y, senmoe_stream_t stream) {
+  g_last_error.clear();
+  int rc = validate_config(config);
+  if (rc) return rc;
+  if ((rc = validate_weights(config, weights))) return rc;
+  if (num_tokens < 0 || num_tokens > config->max_tokens)
+    return fail(SENMOE_ERR_BAD_ARG, "num_tokens=%lld outside [0, max_tokens=%d]", (long long)num_tokens,
+                config->max_tokens);
+  if (num_tokens == 0) return SENMOE_OK;
+  size_t offs[16];
+  const size_t need = noalloc_bytes(*config, static_cast<size_t>(num_tokens), offs);
+  if (need > kNoAllocScratchBytes)
+    return fail(SENMOE_ERR_BAD_ARG,
+                "senmoe_moe_forward_noalloc: %lld tokens need %zu bytes of scratch, above its fixed %zu-byte "
+                "array (use a layer handle for this size)",
+                (long long)num_tokens, need, kNoAllocScratchBytes);
+
+  int dev = 0;
+  SENMOE_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(SENMOE_ERR_UNSUPPORTED, "device %d out of range", dev);
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void* p = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (e != cudaSuccess || !p)
+        return fail(SENMOE_ERR_CUDA, "cudaGetSymbolAddress(g_noalloc_scratch) on device %d: %s", dev,
+                    cudaGetErrorString(e));
+      g_noalloc_ptr[dev] = p;
+    }
+    base = g_noalloc_ptr[dev];
+  }
+
+  // A stack-only layer view over the static array; the forward itself is the
+  // layer forward, unchanged.
+  SenMoeLayer L;
+  L.cfg = *config;
+  L.w = *weights;
+  L.device = dev;
+  L.max_pairs = static_cast<int>(num_tokens * config->num_experts_per_tok);
+  L.nchunks_max = (L.max_pairs + kDispatchChunk - 1) / kDispatchChunk;
+  char* b = static_cast<char*>(base);
+  L.logits = reinterpret_cast<float*>(b + offs[0]);
+  L.ids = reinterpret_cast<int32_t*>(b + offs[1]);
+  L.wts = reinterpret_cast<float*>(b + offs[2]);
+  L.perm = reinterpret_cast<int32_t*>(b + offs[3]);
+  L.inv = reinterpret_cast<int32_t*>(b + offs[4]);
+  L.offsets = reinterpret_cast<int32_t*>(b + offs[5]);
+  L.active = reinterpret_cast<int32_t*>(b + offs[6]);
+  L.active_count = reinterpret_cast<int32_t*>(b + offs[7]);
+  L.err = reinterpret_cast<int*>(b + offs[8]);
+  L.chunk_hist = reinterpret_cast<int32_t*>(b + offs[9]);
+  L.h = reinterpret_cast<uint16_t*>(b + offs[10]);
+  L.d = reinterpret_cast<uint16_t*>(b + offs[11]);
+  if (config->shared_intermediate > 0) {
+    L.sh_h = reinterpret_cast<uint16_t*>(b + offs[12]);
+    L.sh_out = reinterpret_cast<uint16_t*>(b + offs[13]);
+    L.sh_gate = reinterpret_cast<float*>(b + offs[14]);
+    L.zeros_idx = reinterpret_cast<uint32_t*>(b + offs[15]);
+  }
+  // The array keeps the previous call's bytes: clear what must start at zero
+  // (the device error word and the shared expert's all-zero index list).
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  SENMOE_CUDA(cudaMemsetAsync(L.err, 0, sizeof(int), st));
+  if (L.zeros_idx) SENMOE_CUDA(cudaMemsetAsync(L.zeros_idx, 0, size_t(num_tokens) * 4, st));
+  return layer_forward(&L, x, num_tokens, y, nullptr, false, stream);
+}

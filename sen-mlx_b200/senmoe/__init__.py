@@ -83,6 +83,7 @@ SIGNATURES = {
     "senmoe_dispatch": (C.c_int, [_P, _i64, _i32, _i32, _P, _P, _P, _P, _P]),
     "senmoe_gather_qmm": (C.c_int, [_P, _i64, _P, _P, _P, _P, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _P,
                                     _P]),
+    "senmoe_moe_forward_noalloc": (C.c_int, [C.POINTER(SenMoeConfig), C.POINTER(SenMoeWeights), _P, _i64, _P, _P]),
 }
 
 _lib = None
