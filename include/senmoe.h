@@ -82,7 +82,8 @@ typedef struct SenMoeConfig {
   int32_t max_tokens;              /* T_max: scratch is sized for this at create time */
   int32_t expert_begin;            /* first expert held by this rank (0 on one GPU) */
   int32_t expert_end;              /* one past the last local expert (E on one GPU) */
-  int32_t reserved[3];
+  int32_t reserved[3];             /* [0]: expert kernels, 0 auto, 1 CUDA-core GEMV, 2 tcgen05 GEMM;
+                                      [1], [2]: zero */
 } SenMoeConfig;
 
 /* Device pointers, caller-owned, valid for the layer's lifetime.  Expert

@@ -1,6 +1,7 @@
 // kernels.h -- internal launch interfaces of the senmoe CUDA kernels.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (types only; the encoder is fetched at run time)
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -12,6 +13,7 @@ enum DeviceError : int {
   kDevOk = 0,
   kDevBadExpert = 1,    // an expert id outside [0, E)
   kDevWaitTimeout = 2,  // a bounded mbarrier wait ran out
+  kDevFp16Range = 3,    // an activation outside fp16 range met the tensor-core path
 };
 
 // ---------------------------------------------------------------- router
@@ -91,6 +93,34 @@ struct CombineArgs {
   int hidden, top_k;
 };
 cudaError_t launch_combine(const CombineArgs& a, int num_tokens, cudaStream_t st);
+
+// -------------------------------------------------- tensor-core GEMM
+struct TcGemmArgs {
+  const uint16_t* s[2];     // bf16 scales per projection [E_local, rows, kdim/64]
+  const uint16_t* b[2];     // bf16 biases
+  int rows, kdim, m_tiles;  // rows = output features per expert (multiple of 128)
+  const int32_t* active;
+  const int32_t* active_count;
+  const int32_t* offsets;
+  int expert_begin;
+  uint16_t* out;            // [slots, out_stride]: fp16 (two-projection form) or bf16 (one)
+  long long out_stride;
+  int act;                  // 0 SwiGLU, 1 GeGLU (two-projection form)
+  int* err;
+};
+size_t tc_smem_bytes(int bits, int nproj, int bn, int kdim);
+bool tc_supported(int rows, int kdim, int bits, int nproj, int bn);
+// grid = an upper bound on the tile count; CTAs past the last tile exit.
+cudaError_t launch_tc_gemm(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
+                           const TcGemmArgs& a, int bits, int nproj, int bn, int grid, cudaStream_t st);
+// 2-D tiled tensor map (row-major [outer, inner], no interleave, zero OOB fill).
+cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t inner,
+                         uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                         bool swizzle128);
+// x_sorted[s, :] = fp16(x[perm[s] / k_div, :]) for s < num_slots (x bf16, rows of
+// `hidden`); a value outside fp16 range records kDevFp16Range in *err.
+cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
+                               int num_slots, int hidden, int* err, cudaStream_t st);
 
 // Raises a kernel's dynamic shared-memory limit to at least `bytes` on the
 // current device.  Only the first call per (kernel, device, size) reaches the

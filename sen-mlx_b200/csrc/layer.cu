@@ -68,6 +68,18 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 constexpr int kGateUpRows = 16;
 constexpr int kDownRows = 64;
 
+// Tensor-core path: token tiles (N) offered, and the average tokens per
+// touched expert from which the tensor cores beat the CUDA-core GEMV.
+constexpr int kTcTiles[5] = {16, 32, 64, 128, 256};
+constexpr double kTcMinTokensPerExpert = 3.0;
+enum ExpertPath { kPathAuto = 0, kPathGemv = 1, kPathTensorCore = 2 };
+
+int tc_tile_index(double tokens_per_expert) {
+  for (int i = 0; i < 4; ++i)
+    if (tokens_per_expert <= kTcTiles[i]) return i;
+  return 4;
+}
+
 }  // namespace
 
 struct SenMoeLayer {
@@ -94,6 +106,12 @@ struct SenMoeLayer {
   uint16_t* sh_out = nullptr;    // [Tmax, H]
   float* sh_gate = nullptr;      // [Tmax]
   uint32_t* zeros_idx = nullptr; // [Tmax] expert 0 for the shared expert
+  // tensor-core path
+  bool tc_ok = false;
+  uint16_t* xs = nullptr;        // fp16 [Tmax*K, H] activations gathered into slot order
+  uint16_t* h16 = nullptr;       // fp16 [Tmax*K, I] SwiGLU output (B operand of the down GEMM)
+  CUtensorMap tm_gate{}, tm_up{}, tm_down{};  // packed codes, [rows, words]
+  CUtensorMap tm_xs[5]{}, tm_h[5]{};          // activation tiles per token-tile width
   // per-stage timing
   bool profiling = false;
   bool profiled_once = false;
@@ -200,7 +218,8 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                o_inv = take(P * 4), o_offs = take((E + 1) * 4), o_act = take(E * 4), o_cnt = take(4),
                o_err = take(4), o_hist = take(size_t(L->nchunks_max) * E * 4), o_h = take(P * I * 2),
                o_d = take(P * H * 2), o_shh = take(Is ? T * Is * 2 : 0), o_sho = take(Is ? T * H * 2 : 0),
-               o_shg = take(Is ? T * 4 : 0), o_zero = take(Is ? T * 4 : 0);
+               o_shg = take(Is ? T * 4 : 0), o_zero = take(Is ? T * 4 : 0), o_xs = take(P * H * 2),
+               o_h16 = take(P * I * 2);
   cudaError_t e = cudaMalloc(&L->arena, off);
   if (e != cudaSuccess) {
     delete L;
@@ -225,6 +244,27 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
     L->sh_out = reinterpret_cast<uint16_t*>(base + o_sho);
     L->sh_gate = reinterpret_cast<float*>(base + o_shg);
     L->zeros_idx = reinterpret_cast<uint32_t*>(base + o_zero);
+  }
+  L->xs = reinterpret_cast<uint16_t*>(base + o_xs);
+  L->h16 = reinterpret_cast<uint16_t*>(base + o_h16);
+  {  // tensor maps for the tcgen05 path (host-side encoding only)
+    const int bits = c.bits, El = c.expert_end - c.expert_begin;
+    const uint32_t wk = 64u * bits / 32u;
+    const uint64_t gw = uint64_t(H) * bits / 32, dw = uint64_t(I) * bits / 32;
+    bool ok = tc_supported(int(I), int(H), bits, 2, 256) && tc_supported(int(H), int(I), bits, 1, 256);
+    ok = ok && make_tmap_2d(&L->tm_gate, L->w.gate_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, gw, uint64_t(El) * I,
+                            gw * 4, wk, 128, false) == cudaSuccess;
+    ok = ok && make_tmap_2d(&L->tm_up, L->w.up_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, gw, uint64_t(El) * I, gw * 4,
+                            wk, 128, false) == cudaSuccess;
+    ok = ok && make_tmap_2d(&L->tm_down, L->w.down_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, dw, uint64_t(El) * H,
+                            dw * 4, wk, 128, false) == cudaSuccess;
+    for (int i = 0; i < 5 && ok; ++i) {
+      ok = make_tmap_2d(&L->tm_xs[i], L->xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, H, P, H * 2, 64, kTcTiles[i], true) ==
+               cudaSuccess &&
+           make_tmap_2d(&L->tm_h[i], L->h16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, I, P, I * 2, 64, kTcTiles[i], true) ==
+               cudaSuccess;
+    }
+    L->tc_ok = ok;
   }
   e = cudaMemset(L->arena, 0, off);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -305,50 +345,92 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   da.chunk_hist = L->chunk_hist;
   da.err = L->err;
   SENMOE_CUDA(launch_dispatch(da, st));
-  SENMOE_CUDA(mark(2));
 
-  // 3. gate/up + activation over the touched local experts -> h [P, I]
-  const int max_items = P < (c.expert_end - c.expert_begin) ? P : (c.expert_end - c.expert_begin);
-  QGemvArgs g{};
-  g.x = static_cast<const uint16_t*>(x);
-  g.w[0] = L->w.gate_weight;
-  g.s[0] = static_cast<const uint16_t*>(L->w.gate_scales);
-  g.b[0] = static_cast<const uint16_t*>(L->w.gate_biases);
-  g.w[1] = L->w.up_weight;
-  g.s[1] = static_cast<const uint16_t*>(L->w.up_scales);
-  g.b[1] = static_cast<const uint16_t*>(L->w.up_biases);
-  g.kdim = H;
-  g.rows = I;
-  g.rows_per_cta = kGateUpRows;
-  g.mode = kItemsGrouped;
-  g.active = L->active;
-  g.active_count = L->active_count;
-  g.offsets = L->offsets;
-  g.perm = L->perm;
-  g.k_div = K;
-  g.x_by_slot = 0;
-  g.expert_begin = c.expert_begin;
-  g.out = L->h;
-  g.out_stride = I;
-  g.act = c.activation;
-  g.err = L->err;
-  SENMOE_CUDA(launch_qgemv(g, 2, c.bits, max_items, st));
-  SENMOE_CUDA(mark(3));
+  // 3-4. expert products over the touched local experts: h [P, I], d [P, H]
+  const int E_local = c.expert_end - c.expert_begin;
+  const int max_items = P < E_local ? P : E_local;
+  const double per_expert = double(P) / double(max_items);
+  const int path = c.reserved[0];
+  const bool use_tc =
+      L->tc_ok && (path == kPathTensorCore || (path == kPathAuto && per_expert >= kTcMinTokensPerExpert));
+  if (use_tc) {
+    const int ti = tc_tile_index(per_expert), bn = kTcTiles[ti];
+    SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st));
+    SENMOE_CUDA(mark(2));
+    TcGemmArgs ga{};
+    ga.s[0] = static_cast<const uint16_t*>(L->w.gate_scales);
+    ga.b[0] = static_cast<const uint16_t*>(L->w.gate_biases);
+    ga.s[1] = static_cast<const uint16_t*>(L->w.up_scales);
+    ga.b[1] = static_cast<const uint16_t*>(L->w.up_biases);
+    ga.rows = I;
+    ga.kdim = H;
+    ga.m_tiles = I / 128;
+    ga.active = L->active;
+    ga.active_count = L->active_count;
+    ga.offsets = L->offsets;
+    ga.expert_begin = c.expert_begin;
+    ga.out = L->h16;
+    ga.out_stride = I;
+    ga.act = c.activation;
+    ga.err = L->err;
+    SENMOE_CUDA(launch_tc_gemm(L->tm_gate, L->tm_up, L->tm_xs[ti], ga, c.bits, 2, bn,
+                               (P / bn + max_items) * ga.m_tiles, st));
+    SENMOE_CUDA(mark(3));
+    TcGemmArgs gd = ga;
+    gd.s[0] = static_cast<const uint16_t*>(L->w.down_scales);
+    gd.b[0] = static_cast<const uint16_t*>(L->w.down_biases);
+    gd.s[1] = gd.s[0];
+    gd.b[1] = gd.b[0];
+    gd.rows = H;
+    gd.kdim = I;
+    gd.m_tiles = H / 128;
+    gd.out = L->d;
+    gd.out_stride = H;
+    SENMOE_CUDA(launch_tc_gemm(L->tm_down, L->tm_down, L->tm_h[ti], gd, c.bits, 1, bn,
+                               (P / bn + max_items) * gd.m_tiles, st));
+    SENMOE_CUDA(mark(4));
+  } else {
+    SENMOE_CUDA(mark(2));
+    QGemvArgs g{};
+    g.x = static_cast<const uint16_t*>(x);
+    g.w[0] = L->w.gate_weight;
+    g.s[0] = static_cast<const uint16_t*>(L->w.gate_scales);
+    g.b[0] = static_cast<const uint16_t*>(L->w.gate_biases);
+    g.w[1] = L->w.up_weight;
+    g.s[1] = static_cast<const uint16_t*>(L->w.up_scales);
+    g.b[1] = static_cast<const uint16_t*>(L->w.up_biases);
+    g.kdim = H;
+    g.rows = I;
+    g.rows_per_cta = kGateUpRows;
+    g.mode = kItemsGrouped;
+    g.active = L->active;
+    g.active_count = L->active_count;
+    g.offsets = L->offsets;
+    g.perm = L->perm;
+    g.k_div = K;
+    g.x_by_slot = 0;
+    g.expert_begin = c.expert_begin;
+    g.out = L->h;
+    g.out_stride = I;
+    g.act = c.activation;
+    g.err = L->err;
+    SENMOE_CUDA(launch_qgemv(g, 2, c.bits, max_items, st));
+    SENMOE_CUDA(mark(3));
 
-  // 4. down -> d [P, H]
-  QGemvArgs dn = g;
-  dn.x = L->h;
-  dn.w[0] = L->w.down_weight;
-  dn.s[0] = static_cast<const uint16_t*>(L->w.down_scales);
-  dn.b[0] = static_cast<const uint16_t*>(L->w.down_biases);
-  dn.kdim = I;
-  dn.rows = H;
-  dn.rows_per_cta = kDownRows;
-  dn.x_by_slot = 1;
-  dn.out = L->d;
-  dn.out_stride = H;
-  SENMOE_CUDA(launch_qgemv(dn, 1, c.bits, max_items, st));
-  SENMOE_CUDA(mark(4));
+    QGemvArgs dn = g;
+    dn.x = L->h;
+    dn.w[0] = L->w.down_weight;
+    dn.s[0] = static_cast<const uint16_t*>(L->w.down_scales);
+    dn.b[0] = static_cast<const uint16_t*>(L->w.down_biases);
+    dn.kdim = I;
+    dn.rows = H;
+    dn.rows_per_cta = kDownRows;
+    dn.x_by_slot = 1;
+    dn.out = L->d;
+    dn.out_stride = H;
+    SENMOE_CUDA(launch_qgemv(dn, 1, c.bits, max_items, st));
+    SENMOE_CUDA(mark(4));
+  }
 
   // 5. shared expert (deepseek_v2.rs:550-552), optionally sigmoid-gated
   if (Is > 0) {
@@ -475,6 +557,9 @@ int senmoe_layer_check(SenMoeLayer* L, senmoe_stream_t stream) {
     SENMOE_CUDA(cudaStreamSynchronize(st));
     if (host_err == kDevBadExpert) return fail(SENMOE_ERR_DEVICE, "a kernel saw an expert id outside [0, E)");
     if (host_err == kDevWaitTimeout) return fail(SENMOE_ERR_TIMEOUT, "a bounded device-side wait ran out");
+    if (host_err == kDevFp16Range)
+      return fail(SENMOE_ERR_DEVICE, "an activation outside fp16 range reached the tensor-core path (use the "
+                                     "CUDA-core path, expert path 1, for such inputs)");
     return fail(SENMOE_ERR_DEVICE, "device error code %d", host_err);
   }
   return SENMOE_OK;

@@ -31,6 +31,7 @@ LIB_PATH = os.path.abspath(os.path.join(_HERE, "..", "lib", "libsenmoe.so"))
 OK, ERR_BAD_ARG, ERR_CUDA, ERR_NCCL, ERR_TIMEOUT, ERR_UNSUPPORTED, ERR_NO_MEMORY, ERR_DEVICE = range(8)
 ROUTER_SOFTMAX_TOPK = 0
 ACT_SWIGLU, ACT_GEGLU = 0, 1
+PATH_AUTO, PATH_GEMV, PATH_TENSOR_CORE = 0, 1, 2  # expert-product kernels (SenMoeConfig.reserved[0])
 
 
 class SenMoeError(RuntimeError):
@@ -175,6 +176,7 @@ class MoeArgs:
     group_size: int = 64
     activation: int = ACT_SWIGLU
     shared_gate: bool = False  # sigmoid-gated shared expert (no reference counterpart)
+    expert_path: int = PATH_AUTO  # AUTO picks tcgen05 GEMM once experts average >= 3 tokens
 
 
 @dataclass
@@ -228,6 +230,7 @@ class DeepseekMoe:
         cfg.shared_gate = int(args.shared_gate)
         cfg.max_tokens = int(max_tokens)
         cfg.expert_begin, cfg.expert_end = eb, ee
+        cfg.reserved[0] = int(args.expert_path)
         self._cfg = cfg
         wt = SenMoeWeights()
         wt.router_weight = _ptr(weights.router_weight)

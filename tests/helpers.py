@@ -55,10 +55,10 @@ def device_weights(mw, device="cuda"):
     return out
 
 
-def moe_args(cfg):
+def moe_args(cfg, expert_path=0):
     """oracle.MoeConfig -> senmoe.MoeArgs."""
     import senmoe
-    return senmoe.MoeArgs(hidden_size=cfg.hidden, moe_intermediate_size=cfg.intermediate,
+    return senmoe.MoeArgs(expert_path=expert_path, hidden_size=cfg.hidden, moe_intermediate_size=cfg.intermediate,
                           n_routed_experts=cfg.num_experts, num_experts_per_tok=cfg.top_k,
                           n_shared_experts=(cfg.shared_intermediate // cfg.intermediate) if cfg.shared_intermediate else 0,
                           norm_topk_prob=cfg.norm_topk_prob, routed_scaling_factor=cfg.routed_scaling_factor,

@@ -26,10 +26,13 @@ def senmoe():
     return s
 
 
-def run_block(senmoe, cfg, mw, x_bits, max_tokens=None):
+PATHS = {"gemv": 1, "tc": 2}
+
+
+def run_block(senmoe, cfg, mw, x_bits, max_tokens=None, path=0):
     import torch
     T = x_bits.shape[0]
-    blk = senmoe.DeepseekMoe(moe_args(cfg), device_weights(mw), max_tokens=max_tokens or max(T, 1))
+    blk = senmoe.DeepseekMoe(moe_args(cfg, path), device_weights(mw), max_tokens=max_tokens or max(T, 1))
     dbg = dict(topk_ids=torch.empty((T, cfg.top_k), dtype=torch.int32, device="cuda"),
                topk_weights=torch.empty((T, cfg.top_k), dtype=torch.float32, device="cuda"),
                perm=torch.empty(T * cfg.top_k, dtype=torch.int32, device="cuda"),
@@ -77,25 +80,49 @@ def config0_layer():
     return cfg, O.make_layer(cfg, seed=0)
 
 
+@pytest.mark.parametrize("path", ["gemv", "tc"])
 @pytest.mark.parametrize("T", [1, 8, 16, 64])
-def test_config0_block_vs_oracle(senmoe, config0_layer, T):
+def test_config0_block_vs_oracle(senmoe, config0_layer, T, path):
     cfg, mw = config0_layer
     x = O.make_tokens(T, cfg.hidden, seed=T)
-    got = run_block(senmoe, cfg, mw, x)
+    got = run_block(senmoe, cfg, mw, x, path=PATHS[path])
     check_against_oracle(cfg, mw, x, got)
 
 
-def test_block_8bit_shared_gated_large_e(senmoe):
+@pytest.mark.parametrize("T", [256, 1024])
+def test_config0_prefill_tensor_core_vs_oracle(senmoe, config0_layer, T):
+    """Prefill-size batches (32..64+ tokens per expert) on the tcgen05 path."""
+    cfg, mw = config0_layer
+    x = O.make_tokens(T, cfg.hidden, seed=100 + T)
+    got = run_block(senmoe, cfg, mw, x, path=PATHS["tc"])
+    check_against_oracle(cfg, mw, x, got)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("T", [3, 40, 600, 3000])
+def test_tensor_core_tiles_vs_oracle(senmoe, bits, T):
+    """Every token-tile width (16..256) and ragged expert groups, both code widths,
+    on a small layer so the oracle stays fast (H=256, I=128, E=16, K=4)."""
+    cfg = O.MoeConfig(hidden=256, intermediate=128, num_experts=16, top_k=4, bits=bits)
+    mw = O.make_layer(cfg, seed=20 + bits)
+    x = O.make_tokens(T, cfg.hidden, seed=T + bits)
+    got = run_block(senmoe, cfg, mw, x, path=PATHS["tc"])
+    check_against_oracle(cfg, mw, x, got)
+
+
+@pytest.mark.parametrize("path", ["gemv", "tc"])
+def test_block_8bit_shared_gated_large_e(senmoe, path):
     """Config-3-like: E=512, K=10, I=512, sigmoid-gated shared expert (I_s=512)."""
     cfg = O.MoeConfig(hidden=2048, intermediate=512, num_experts=512, top_k=10, bits=4,
                       shared_intermediate=512, shared_gate=True)
     mw = O.make_layer(cfg, seed=3)
     x = O.make_tokens(24, cfg.hidden, seed=5)
-    got = run_block(senmoe, cfg, mw, x)
+    got = run_block(senmoe, cfg, mw, x, path=PATHS[path])
     check_against_oracle(cfg, mw, x, got)
 
 
-def test_block_8bit_skewed(senmoe):
+@pytest.mark.parametrize("path", ["gemv", "tc"])
+def test_block_8bit_skewed(senmoe, path):
     """Config-4-like: 8-bit weights, Zipf-biased router (many tokens on few experts)."""
     cfg = O.MoeConfig(hidden=2048, intermediate=768, num_experts=128, top_k=8, bits=8)
     mw = O.make_layer(cfg, seed=4)
@@ -108,18 +135,19 @@ def test_block_8bit_skewed(senmoe):
     xf = O.bf16_to_f32(x)
     xf[:, 0] = 4.0
     x = O.f32_to_bf16(xf)
-    got = run_block(senmoe, cfg, mw, x)
+    got = run_block(senmoe, cfg, mw, x, path=PATHS[path])
     counts = np.diff(got["offsets"])
     assert counts.max() > 4 * counts[counts > 0].mean()  # skew present
     check_against_oracle(cfg, mw, x, got)
 
 
-def test_many_tokens_multi_chunk_dispatch(senmoe):
+@pytest.mark.parametrize("path", ["gemv", "tc"])
+def test_many_tokens_multi_chunk_dispatch(senmoe, path):
     """T*K > 2048 pairs takes the three-kernel dispatch; small H/I keep the oracle fast."""
     cfg = O.MoeConfig(hidden=256, intermediate=128, num_experts=64, top_k=8, bits=4)
     mw = O.make_layer(cfg, seed=6)
     x = O.make_tokens(2000, cfg.hidden, seed=9)
-    got = run_block(senmoe, cfg, mw, x)
+    got = run_block(senmoe, cfg, mw, x, path=PATHS[path])
     check_against_oracle(cfg, mw, x, got)
 
 
