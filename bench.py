@@ -53,6 +53,17 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def tensor_peak():
+    """Dense 16-bit tensor peak (TFLOP/s): the burst figure, as the expert GEMMs
+    are timed as individual launches."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
     """nvidia-smi clock / throttle sampling during the timed region."""
@@ -201,6 +212,8 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill-tokens", type=int, default=4096,
+                    help="config-2 prefill measurement (48 layers x this many tokens); 0 to skip")
     ap.add_argument("--ncu", action="store_true",
                     help="profiling mode: plain (non-graph) forwards of the workload, W warm-up + K steps, no "
                          "timing or JSON; every step launches 6 kernels per layer in order")
@@ -252,83 +265,119 @@ def main():
     stack = senmoe.MoeStack(layers, tmax, use_graph=True)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
-    x_all = torch.randn((tmax, H), generator=gen, device=dev).to(torch.bfloat16)
+    x_all = torch.randn((max(tmax, args.prefill_tokens), H), generator=gen, device=dev).to(torch.bfloat16)
 
-    def timed_steps(T, steps, warmup):
+    def timed_steps(stk, T, steps, warmup):
         """Device time of `steps` replays of the 48-layer chain, inputs resident."""
         x = x_all[:T]
         for _ in range(warmup):
-            stack.forward(x)
+            stk.forward(x)
         barrier()
-        s = stack.stream
+        s = stk.stream
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(s):
             e0.record(s)
             for _ in range(steps):
-                stack.bufs[0][:T].copy_(x, non_blocking=True)
-                stack._graph(T).replay()
+                stk.bufs[0][:T].copy_(x, non_blocking=True)
+                stk._graph(T).replay()
             e1.record(s)
         e1.synchronize()
         barrier()
         return max_over_ranks(e0.elapsed_time(e1) / 1e3)
 
-    # ---- touched experts per layer (algorithmic bytes), from the routing of the chain's inputs
-    def touched_per_layer(T):
+    def touched_per_layer(lays, T):
+        """Touched experts per layer for the chain's actual routing."""
         h = x_all[:T].clone()
         offs = torch.empty(E + 1, dtype=torch.int32, device=dev)
         counts = []
-        for L in layers:
+        for L in lays:
             L.forward(h, debug={"offsets": offs})
             counts.append(int((offs[1:] - offs[:-1] > 0).sum().item()))
             h = L.forward_residual(h)
         return counts
 
+    def stage_profile(lays, T, nrep):
+        """Per-stage milliseconds summed over nrep steps x layers, from CUDA
+        events between the stages of plain (non-graph) forwards; the host
+        enqueues a whole step long before the GPU finishes it, so the deltas
+        are kernel time."""
+        for L in lays:
+            L.set_profiling(True)
+        x = x_all[:T]
+        acc = {k: 0.0 for k in senmoe.DeepseekMoe.STAGES}
+        for _ in range(nrep):
+            h = x
+            for L in lays:
+                h = L.forward_residual(h)
+            torch.cuda.synchronize()
+            for L in lays:
+                for k, v in L.stage_times().items():
+                    acc[k] += v
+        for L in lays:
+            L.set_profiling(False)
+        return acc
+
+    hbm_peak, hbm_kind = peaks()
     results = {}
     clocks = None
     for T in batches:
-        touched = touched_per_layer(T)
+        touched = touched_per_layer(layers, T)
         if T == args.batch:
             with ClockSampler(local) as cs:
-                secs = timed_steps(T, args.steps, args.warmup)
+                secs = timed_steps(stack, T, args.steps, args.warmup)
             clocks = cs.summary()
         else:
-            secs = timed_steps(T, args.steps, args.warmup)
+            secs = timed_steps(stack, T, args.steps, args.warmup)
         step = secs / args.steps
         alg_bytes = sum(n * BYTES_EXPERT + E * H * 2 + 2 * T * H * 2 for n in touched)
         results[T] = {"tokens_per_s": world * T / step, "ms_per_step": step * 1e3,
+                      "expert_kernels": "tcgen05" if layers[0].expert_path(T) == senmoe.PATH_TENSOR_CORE else "gemv",
                       "touched_experts_per_layer": sum(touched) / len(touched),
-                      "hbm_gbs": alg_bytes / step / 1e9}
+                      "hbm_gbs": alg_bytes / step / 1e9, "hbm_frac": alg_bytes / step / 1e9 / hbm_peak}
         if rank == 0:
             print(f"[bench] batch {T}: {results[T]}", file=sys.stderr, flush=True)
 
-    # ---- per-stage times (dominant kernel) inside a graph with event records
+    # ---- dominant decode kernel (gate/up) from in-graph stage events
     T = args.batch
-    for L in layers:
-        L.set_profiling(True)
-    prof = senmoe.MoeStack(layers, T, use_graph=True)
-    x = x_all[:T]
-    prof.forward(x)  # capture
-    stage_ms = {k: 0.0 for k in senmoe.DeepseekMoe.STAGES}
-    touched = touched_per_layer(T)
     nrep = max(3, min(args.steps, 10))
-    for _ in range(nrep):
-        prof.forward(x)
-        torch.cuda.synchronize()
-        for L in layers:
-            for k, v in L.stage_times().items():
-                stage_ms[k] += v
-    prof.release()
-    for L in layers:
-        L.set_profiling(False)
+    stage_ms = stage_profile(layers, T, nrep)
+    touched = touched_per_layer(layers, T)
     launches = nrep * len(layers)
     gate_up_s = stage_ms["gate_up"] / 1e3 / launches
     gate_up_bytes = sum(n * BYTES_GATE_UP + T * K * (H + I) * 2 for n in touched) / len(touched)
-    hbm_peak, peak_kind = peaks()
     achieved = gate_up_bytes / gate_up_s / 1e9
     stage_share = {k: v / max(sum(stage_ms.values()), 1e-12) for k, v in stage_ms.items()}
     if rank == 0:
-        print(f"[bench] stage ms (sum over {nrep} steps x {len(layers)} layers): {stage_ms}", file=sys.stderr,
-              flush=True)
+        print(f"[bench] decode stage ms (sum over {nrep} steps x {len(layers)} layers): {stage_ms}",
+              file=sys.stderr, flush=True)
+
+    # ---- prefill (config 2): 48 layers x prefill_tokens, tensor-core roofline
+    prefill = None
+    if args.prefill_tokens > 0:
+        TP = args.prefill_tokens
+        pl = [senmoe.DeepseekMoe(L.args, L.weights, max_tokens=TP, device=local) for L in layers]
+        pstack = senmoe.MoeStack(pl, TP, use_graph=True)
+        psteps = max(2, min(args.steps, 5))
+        secs = timed_steps(pstack, TP, psteps, args.warmup)
+        step = secs / psteps
+        flops_layer = TP * K * 6 * H * I + 2 * TP * H * E
+        pst = stage_profile(pl, TP, 2)
+        gu_s = pst["gate_up"] / 1e3 / (2 * len(pl))
+        dn_s = pst["down"] / 1e3 / (2 * len(pl))
+        peak_t = tensor_peak()
+        prefill = {"tokens": TP, "tokens_per_s": world * TP / step, "ms_per_step": step * 1e3,
+                   "tflops": flops_layer * len(pl) / step / 1e12,
+                   "frac": flops_layer * len(pl) / step / 1e12 / peak_t[0],
+                   "gate_up_tflops": TP * K * 4 * H * I / gu_s / 1e12,
+                   "down_tflops": TP * K * 2 * H * I / dn_s / 1e12,
+                   "peak_tflops": peak_t[0], "peak_source": peak_t[1],
+                   "stage_share": {k: v / max(sum(pst.values()), 1e-12) for k, v in pst.items()}}
+        if rank == 0:
+            print(f"[bench] prefill: {prefill}", file=sys.stderr, flush=True)
+        pstack.release()
+        for L in pl:
+            L.close()
+        del pl
 
     # ---- e2e through the public API with host buffers
     x_host = x_all[:T].cpu().pin_memory()
@@ -358,12 +407,13 @@ def main():
                    "layers": args.layers, "parallelism": "replicas" if world > 1 else "single",
                    "l2": "weights 16.3 GB per step >> 126 MB L2 (no flush needed)", "cuda_graph": True},
         "sweep": {str(t): r for t, r in results.items()},
-        "roofline": {"bound": "hbm", "kernel": "qgemv gate/up (+SwiGLU)", "achieved": achieved, "peak": hbm_peak,
+        "roofline": {"bound": "hbm", "kernel": "expert gate/up (+SwiGLU)", "achieved": achieved, "peak": hbm_peak,
                      "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": None,
-                     "peak_source": peak_kind,
+                     "peak_source": hbm_kind,
                      "algorithmic_bytes_per_launch": gate_up_bytes, "avg_launch_ms": gate_up_s * 1e3,
                      "step_hbm_gbs": head["hbm_gbs"], "step_frac": head["hbm_gbs"] / hbm_peak},
         "stage_share": stage_share,
+        "prefill": prefill,
         "gpu_launches": launches_per_forward(args.batch) * args.layers * args.steps,
         "clocks": clocks,
         "e2e": {"value": world * args.batch / e2e_s, "unit": UNIT, "h2d_bytes_per_step": args.batch * H * 2,

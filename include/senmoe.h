@@ -151,8 +151,14 @@ int senmoe_layer_forward_residual(SenMoeLayer* layer, const void* x, int64_t num
  * ms[0 .. n): router, dispatch, gate/up, down, shared expert, combine.
  * Returns the number of stages written (or a negative status). */
 #define SENMOE_NUM_STAGES 6
+/* Events are recorded only by forwards issued outside a stream capture. */
 int senmoe_layer_set_profiling(SenMoeLayer* layer, int enable);
 int senmoe_layer_stage_times(SenMoeLayer* layer, float* ms, int n);
+
+/* Which expert-product kernels a forward of num_tokens tokens runs: 1 = the
+ * CUDA-core dequant-GEMV (decode-size batches), 2 = the tcgen05 grouped GEMM
+ * (prefill-size batches); SenMoeConfig.reserved[0] can force either. */
+int senmoe_layer_expert_path(const SenMoeLayer* layer, int64_t num_tokens);
 
 /* Synchronises `stream` and reports any error a kernel recorded on the
  * device since the previous check (bad expert index, timed-out wait). */

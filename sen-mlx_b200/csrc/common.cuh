@@ -13,8 +13,11 @@
 
 namespace senmoe {
 
-// Bounded waits: give up after this much wall time on the GPU's global timer.
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+// Bounded waits: give up after this many SM clock cycles (~2 s at <= 2 GHz).
+// The spin measures time with clock64 (an SM-local counter, cheap to read);
+// %globaltimer is a much slower read and would add its latency to every
+// handoff that is not ready on the first try.
+constexpr long long kWaitLimitCycles = 4000000000ll;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -68,13 +71,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Waits for the phase with the given parity to complete, for at most
-// kWaitLimitNs.  On timeout records kDevWaitTimeout and returns false.
+// kWaitLimitCycles.  On timeout records kDevWaitTimeout and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = global_timer_ns();
+  const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (clock64() - t0 > kWaitLimitCycles) {
       record_error(err, kDevWaitTimeout);
       return false;
     }

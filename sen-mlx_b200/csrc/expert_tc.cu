@@ -28,9 +28,13 @@
 //              multicast anywhere.
 //   warp 1     TMEM owner; one lane issues tcgen05.mma (kind::f16, bf16 x
 //              bf16 -> fp32, M=128, N=BN, K=16) and tcgen05.commit.
-//   warps 2-9  dequantise each 64-column k-block of codes to fp16
-//              (w = q * scale + bias, one rounding) into SWIZZLE_128B K-major
-//              tiles, then run the TMEM epilogue.
+//   warps 2-17 dequantise each 64-column k-block of codes to fp16
+//              (w = q * scale + bias, one rounding) straight into TMEM with
+//              tcgen05.st: the MMA reads its A operand from TMEM, so the
+//              8x-expanded fp16 weights never cross the shared-memory port
+//              (which would otherwise bound the kernel).
+//   warps 18-21 epilogue (TMEM accumulators -> global), warp 22 TMA of the
+//              activation tiles.
 // Every mbarrier wait is bounded; a timeout sets a CTA-wide abort flag, every
 // role drains and the CTA frees its TMEM and returns.
 
@@ -44,8 +48,7 @@
 namespace senmoe {
 namespace {
 
-constexpr int kTcThreads = 320;
-constexpr int kDqThreads = 256;
+constexpr int kDqWarps = 16;
 constexpr int BM = 128;  // weight rows per tile
 constexpr int BK = 64;   // one quantization group per k-block
 
@@ -71,15 +74,31 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
+// A from TMEM (row m in lane m, K pairs per 32-bit column), B from shared memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
       : "memory");
 }
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -100,13 +119,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Bounded wait that also gives up as soon as another role of the CTA has.
+// Warp-wide callers combine the result with __all_sync so that every lane
+// takes the same branch (they arrive per warp and issue .sync.aligned ops).
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = global_timer_ns();
+  const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (clock64() - t0 > kWaitLimitCycles) {
       *abort_flag = 1;
       record_error(err, kDevWaitTimeout);
       return false;
@@ -115,7 +136,17 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 }
 
 // ------------------------------------------------------- dequantisation
-// 8 consecutive 4-bit codes (one u32) -> 8 fp16 w = q * s + b, in order.
+// Within every aligned block of 8 k-columns both MMA operands are stored in
+// the order (0,4,1,5,2,6,3,7): it is the order in which the 4-bit codes of a
+// u32 unpack two at a time, and the contraction over k does not depend on it.
+// The activations are written in that order by gather_rows_kernel and by the
+// gate/up epilogue (kperm8).
+__device__ __forceinline__ int kperm8(int col) {
+  const int j = col & 7;
+  return (col & ~7) | (j < 4 ? 2 * j : 2 * (j - 4) + 1);
+}
+
+// 8 consecutive 4-bit codes (one u32) -> 8 fp16 w = q * s + b, k-permuted.
 __device__ __forceinline__ uint4 dequant8_u4(uint32_t w, __half2 s2, __half2 b2) {
   const __half2 k1024 = __floats2half2_rn(1024.0f, 1024.0f);
   uint32_t v[4];
@@ -130,106 +161,179 @@ __device__ __forceinline__ uint4 dequant8_u4(uint32_t w, __half2 s2, __half2 b2)
     __half2 r = __hfma2(q, s2, b2);                                 // one rounding
     o[i] = *reinterpret_cast<uint32_t*>(&r);
   }
-  // (0,4),(1,5),(2,6),(3,7) -> (0,1),(2,3),(4,5),(6,7)
-  return make_uint4(__byte_perm(o[0], o[1], 0x5410), __byte_perm(o[2], o[3], 0x5410),
-                    __byte_perm(o[0], o[1], 0x7632), __byte_perm(o[2], o[3], 0x7632));
+  return make_uint4(o[0], o[1], o[2], o[3]);  // (0,4),(1,5),(2,6),(3,7)
 }
 
-// 4 consecutive 8-bit codes (one u32) -> 4 fp16 (two u32), w = q * s + b.
-__device__ __forceinline__ uint2 dequant4_u8(uint32_t w, float s, float b) {
-  float f[4];
+// Same result through fp16 subnormals: (w << 6, << 2, >> 2, >> 6) & 0x03C003C0
+// puts code k (and k + 4) in mantissa bits 6-9, i.e. the fp16 value q * 2^-18,
+// and fma(q * 2^-18, s * 2^18, b) = q * s + b with one rounding.  s * 2^18 is
+// exact in fp16 for 2^-32 < |s| < 0.2498; callers use dequant8_u4 otherwise.
+__device__ __forceinline__ uint4 dequant8_u4_sub(uint32_t w, __half2 s18, __half2 b2) {
+  const uint32_t m = 0x03C003C0u;
+  const uint32_t v0 = (w << 6) & m, v1 = (w << 2) & m, v2 = (w >> 2) & m, v3 = (w >> 6) & m;
+  __half2 r0 = __hfma2(*reinterpret_cast<const __half2*>(&v0), s18, b2);
+  __half2 r1 = __hfma2(*reinterpret_cast<const __half2*>(&v1), s18, b2);
+  __half2 r2 = __hfma2(*reinterpret_cast<const __half2*>(&v2), s18, b2);
+  __half2 r3 = __hfma2(*reinterpret_cast<const __half2*>(&v3), s18, b2);
+  return make_uint4(*reinterpret_cast<uint32_t*>(&r0), *reinterpret_cast<uint32_t*>(&r1),
+                    *reinterpret_cast<uint32_t*>(&r2), *reinterpret_cast<uint32_t*>(&r3));
+}
+
+// 8 consecutive 8-bit codes (two u32) -> 8 fp16 w = q * s + b, k-permuted.
+__device__ __forceinline__ uint4 dequant8_u8(uint32_t w0, uint32_t w1, float s, float b) {
+  float f[8];
 #pragma unroll
-  for (int k = 0; k < 4; ++k)
-    f[k] = fmaf(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540 + k)) - 8388608.0f, s, b);
-  __half2 lo = __floats2half2_rn(f[0], f[1]);
-  __half2 hi = __floats2half2_rn(f[2], f[3]);
-  return make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+  for (int k = 0; k < 4; ++k) {
+    f[k] = fmaf(__uint_as_float(__byte_perm(w0, 0x4B000000u, 0x7540 + k)) - 8388608.0f, s, b);
+    f[k + 4] = fmaf(__uint_as_float(__byte_perm(w1, 0x4B000000u, 0x7540 + k)) - 8388608.0f, s, b);
+  }
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 h = __floats2half2_rn(f[i], f[i + 4]);
+    o[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// Shared-memory byte offset of 16-byte chunk `c` (0..7) of row `r` in a
-// [rows x 64] 16-bit SWIZZLE_128B K-major tile.
-__device__ __forceinline__ uint32_t sw128_offset(int r, int c) {
-  return static_cast<uint32_t>(r) * 128u + (static_cast<uint32_t>(c ^ (r & 7)) << 4);
-}
-
-// Stage counts per tile shape: activation (B) stages, packed-code stages.
-template <int BN> struct TcStages {
-  static constexpr int kB = BN >= 128 ? 2 : 4;
-  static constexpr int kP = BN >= 128 ? 4 : 6;
-  static constexpr int kA = 2;
+// Pipeline shape per instance.  A packed-code stage holds KP k-blocks so each
+// weight row contributes one full 128-byte line per load (KP = 4 at 4 bits,
+// 2 at 8 bits); it lands with SWIZZLE_128B so the dequant warps' reads are
+// bank-conflict free.  Decode-size token tiles get a third fp16 A stage so
+// dequantisation runs ahead of the MMA round trip; TMEM holds two
+// accumulators whenever they fit, so the epilogue of one tile overlaps the
+// MMAs of the next.
+template <int BITS, int NPROJ, int BN> struct TcShape {
+  static constexpr int KP = 512 / BITS / 32;                    // k-blocks per packed stage
+  // One pipeline step (an A stage and its activation stage) spans KA k-blocks
+  // so that each barrier wait and commit covers 16 MMAs: every wait costs a
+  // few hundred cycles even when its phase has already completed.
+  static constexpr int KA = NPROJ == 2 ? 2 : (KP < 4 ? KP : 4);
+  static constexpr int kACols = NPROJ * KA * 32;                // TMEM columns of one A stage
+  // TMEM (512 columns): ACC accumulators of NPROJ*BN columns, then kA A stages
+  // (128 rows x 64 k per k-block, two fp16 per column).
+  static constexpr int kAccCols = NPROJ * BN;
+  static constexpr int kAcc = 2 * kAccCols + 2 * kACols <= 512 ? 2 : 1;
+  static constexpr int kAFit = (512 - kAcc * kAccCols) / kACols;
+  static constexpr int kA = kAFit > 4 ? 4 : kAFit;              // TMEM A stages
+  static constexpr int kACol0 = kAcc * kAccCols;                // first A column
+  static constexpr int kCols = 512;
+  // activation stages (KA tiles each): refilled only after the MMAs that read
+  // them, so the ring covers an L2 round trip
+  static constexpr uint32_t kBTile = BN * 64 * 2;               // one k-block of activations
+  static constexpr uint32_t kBBytes = KA * kBTile;
+  static constexpr int kBFit = int(65536u / kBBytes);
+  static constexpr int kB = kBFit < 2 ? 2 : (kBFit > 8 ? 8 : kBFit);
+  static constexpr uint32_t kPBytes = 128 * 128;                // one projection's packed stage
+  // packed stages fill the rest of shared memory (at most 8)
+  static constexpr int kPFit = int((200u * 1024u - kB * kBBytes) / (NPROJ * kPBytes));
+  static constexpr int kP = kPFit > 8 ? 8 : kPFit;
+  static constexpr size_t kSmem = 1024 + size_t(kB) * kBBytes + size_t(kP) * NPROJ * kPBytes;
 };
+
+constexpr int kMaxTilesPerCta = 64;
+// warp 0: TMA of packed codes; warp 1: TMEM + MMA; warps 2-17: dequant;
+// warps 18-21: epilogue; warp 22: TMA of activation tiles.  The two TMA
+// streams live in separate warps so the weight prefetch never waits behind an
+// activation slot that only the MMA frees.  Dequantisation is the busiest
+// role (~12 instructions per 8 codes), so it gets 16 warps.
+constexpr int kEpiWarp0 = 2 + kDqWarps;
+constexpr int kBWarp = kEpiWarp0 + 4;
+constexpr int kTcThreadsP = (kBWarp + 1) * 32;
+
+// Scale/bias of k-block j (0 <= j < KP) from KP bf16 values held as packed u32s.
+template <int KP>
+__device__ __forceinline__ uint16_t pick_bf16(const uint32_t (&v)[KP / 2], int j) {
+  uint32_t w = v[0];
+#pragma unroll
+  for (int i = 1; i < KP / 2; ++i)
+    if (j / 2 == i) w = v[i];
+  return static_cast<uint16_t>(j & 1 ? w >> 16 : w & 0xffffu);
+}
+
+template <int KP>
+__device__ __forceinline__ void load_group_params(const uint16_t* p, uint32_t (&v)[KP / 2]) {
+  if constexpr (KP == 4) {
+    const uint2 t = __ldg(reinterpret_cast<const uint2*>(p));
+    v[0] = t.x;
+    v[1] = t.y;
+  } else {
+    v[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
+  }
+}
 
 }  // namespace
 
+// Persistent grouped GEMM: each CTA walks a strided list of (expert, 128-row
+// block, BN-slot block) tiles with one continuous pipeline across them.
 template <int BITS, int NPROJ, int BN>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreadsP, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                    const __grid_constant__ CUtensorMap tmB, TcGemmArgs a) {
-  constexpr int SA = TcStages<BN>::kA, SB = TcStages<BN>::kB, SP = TcStages<BN>::kP;
-  constexpr int WK = BK * BITS / 32;                 // packed words per row per k-block
-  constexpr uint32_t kABytes = BM * BK * 2;          // one fp16 A tile (16 KB)
-  constexpr uint32_t kBBytes = BN * BK * 2;          // one activation tile
-  constexpr uint32_t kPBytes = BM * WK * 4;          // one projection's packed k-block
-  constexpr int kCols = (NPROJ * BN) <= 32 ? 32 : (NPROJ * BN) <= 64 ? 64 : (NPROJ * BN) <= 128 ? 128
-                        : (NPROJ * BN) <= 256 ? 256 : 512;
+  using S = TcShape<BITS, NPROJ, BN>;
+  constexpr int SA = S::kA, SB = S::kB, SP = S::kP, KP = S::KP, KA = S::KA, ACC = S::kAcc;
+  constexpr uint32_t kBTile = S::kBTile, kBBytes = S::kBBytes, kPBytes = S::kPBytes;
   constexpr uint32_t kIdesc = idesc_f16_f32<BN>();
+  static_assert(S::kSmem + 2048 <= 227 * 1024, "shared memory budget");
+  static_assert(SA >= 2 && SP >= 2 && KP % KA == 0, "pipeline shape");
+  static_assert(S::kACol0 + SA * S::kACols <= S::kCols, "TMEM budget");
 
   extern __shared__ unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t bar_pfull[SP], bar_pempty[SP], bar_afull[SA], bar_aempty[SA], bar_bfull[SB],
-      bar_bempty[SB], bar_sb, bar_acc, bar_drain;
+      bar_bempty[SB], bar_accfull[ACC], bar_accempty[ACC], bar_drain;
   __shared__ uint32_t s_tmem;
-  __shared__ int s_tile[4];  // local expert, first weight row, first slot, valid slots (-1: no tile)
+  __shared__ int4 s_tiles[kMaxTilesPerCta];  // local expert, first weight row, first slot, valid slots
+  __shared__ int s_ntiles;
   __shared__ volatile int s_abort;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int groups = a.kdim / BK, ktiles = a.kdim / BK;
+  const int nsteps = ktiles / KA;  // pipeline steps per tile
 
-  // ---- carve dynamic shared memory (1024-byte aligned for SWIZZLE_128B)
   const uint32_t raw = smem_u32(smem_raw);
   unsigned char* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  unsigned char* sA = base;                                   // [SA][NPROJ][16 KB]
-  unsigned char* sB = sA + SA * NPROJ * kABytes;              // [SB][BN*128]
-  unsigned char* sP = sB + SB * kBBytes;                      // [SP][NPROJ][kPBytes]
-  uint16_t* sSB = reinterpret_cast<uint16_t*>(sP + SP * NPROJ * kPBytes);  // [NPROJ][2][BM*groups]
+  unsigned char* sB = base;                       // [SB][KA][BN*128]
+  unsigned char* sP = sB + SB * kBBytes;          // [SP][NPROJ][16 KB]
 
-  // ---- which tile: walk the active experts (m-block fastest)
+  // ---- this CTA's tiles: global tile t (m-block fastest within an expert's
+  // slot block) belongs to CTA t % gridDim.x
   if (tid == 0) {
-    int t = blockIdx.x, found = 0;
+    int n = 0, t0 = 0;
+    const int G = gridDim.x, b = blockIdx.x;
     const int nact = *a.active_count;
-    for (int i = 0; i < nact && !found; ++i) {
+    for (int i = 0; i < nact; ++i) {
       const int e = a.active[i];
-      const int s0 = a.offsets[e], n = a.offsets[e + 1] - s0;
-      const int cnt = ((n + BN - 1) / BN) * a.m_tiles;
-      if (t < cnt) {
-        const int nt = t / a.m_tiles, mt = t % a.m_tiles;
-        s_tile[0] = e - a.expert_begin;
-        s_tile[1] = mt * BM;
-        s_tile[2] = s0 + nt * BN;
-        s_tile[3] = min(BN, n - nt * BN);
-        found = 1;
-      } else {
-        t -= cnt;
+      const int s0 = a.offsets[e], cnt = a.offsets[e + 1] - s0;
+      const int tiles_e = ((cnt + BN - 1) / BN) * a.m_tiles;
+      for (int t = t0 + ((b - t0 % G) % G + G) % G; t < t0 + tiles_e; t += G) {
+        if (n == kMaxTilesPerCta) {
+          record_error(a.err, kDevTileOverflow);
+          break;
+        }
+        const int local = t - t0, nt = local / a.m_tiles, mt = local % a.m_tiles;
+        s_tiles[n++] = make_int4(e - a.expert_begin, mt * BM, s0 + nt * BN, min(BN, cnt - nt * BN));
       }
+      t0 += tiles_e;
     }
-    if (!found) s_tile[3] = -1;
+    s_ntiles = n;
     s_abort = 0;
   }
   if (warp == 0 && lane == 0) {
-    for (int i = 0; i < SP; ++i) { mbar_init(&bar_pfull[i], 1); mbar_init(&bar_pempty[i], kDqThreads); }
-    for (int i = 0; i < SA; ++i) { mbar_init(&bar_afull[i], kDqThreads); mbar_init(&bar_aempty[i], 1); }
+    // consumer-side barriers count warps: each warp fences, syncs, and arrives once
+    for (int i = 0; i < SP; ++i) { mbar_init(&bar_pfull[i], 1); mbar_init(&bar_pempty[i], kDqWarps); }
+    for (int i = 0; i < SA; ++i) { mbar_init(&bar_afull[i], kDqWarps); mbar_init(&bar_aempty[i], 1); }
     for (int i = 0; i < SB; ++i) { mbar_init(&bar_bfull[i], 1); mbar_init(&bar_bempty[i], 1); }
-    mbar_init(&bar_sb, 1);
-    mbar_init(&bar_acc, 1);
+    for (int i = 0; i < ACC; ++i) { mbar_init(&bar_accfull[i], 1); mbar_init(&bar_accempty[i], 4); }
     mbar_init(&bar_drain, 1);
     fence_mbar_init();
   }
   __syncthreads();
-  if (s_tile[3] <= 0) return;  // no tile for this CTA (uniform exit before TMEM use)
-  const int e_local = s_tile[0], m0 = s_tile[1], slot0 = s_tile[2], nvalid = s_tile[3];
+  const int ntiles = s_ntiles;
+  if (ntiles == 0) return;  // uniform exit before any TMEM use
 
-  if (warp == 1) {  // TMEM allocation (whole warp)
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                 "r"(kCols)
+                 "r"(S::kCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -237,43 +341,47 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
-  const int row_base = e_local * a.rows + m0;  // first packed row of this tile
 
-  if (warp == 0) {
-    // ================================================= TMA producer
+  if (warp == 0 || warp == kBWarp) {
+    // ================================================= TMA producers
     if (lane == 0) {
-      const uint32_t sb_bytes = BM * groups * 2;
-      mbar_arrive_expect_tx(&bar_sb, NPROJ * 2 * sb_bytes);
-      const uint64_t pol = policy_evict_first();
-#pragma unroll
-      for (int p = 0; p < NPROJ; ++p) {
-        bulk_g2s(sSB + (p * 2 + 0) * BM * groups, a.s[p] + static_cast<size_t>(row_base) * groups, sb_bytes, &bar_sb,
-                 pol);
-        bulk_g2s(sSB + (p * 2 + 1) * BM * groups, a.b[p] + static_cast<size_t>(row_base) * groups, sb_bytes, &bar_sb,
-                 pol);
-      }
-      int last_p[SP], last_b[SB];  // parity of the last load issued per stage (-1: none)
+      const bool packed = warp == 0;  // warp 0: packed codes, warp kBWarp: activation tiles
+      int last_p[SP], last_b[SB];     // parity of the last load issued per stage (-1: none)
 #pragma unroll
       for (int i = 0; i < SP; ++i) last_p[i] = -1;
 #pragma unroll
       for (int i = 0; i < SB; ++i) last_b[i] = -1;
       bool ok = true;
-      for (int kt = 0; kt < ktiles; ++kt) {
-        const int ps = kt % SP, pph = (kt / SP) & 1;
-        if (!(ok = wait_or_abort(&bar_pempty[ps], pph ^ 1, &s_abort, a.err))) break;
-        mbar_arrive_expect_tx(&bar_pfull[ps], NPROJ * kPBytes);
-        tma_load_2d(sP + (ps * NPROJ + 0) * kPBytes, &tmA0, kt * WK, row_base, &bar_pfull[ps]);
-        if constexpr (NPROJ == 2) tma_load_2d(sP + (ps * NPROJ + 1) * kPBytes, &tmA1, kt * WK, row_base, &bar_pfull[ps]);
-        last_p[ps] = pph;
-        const int bs = kt % SB, bph = (kt / SB) & 1;
-        if (!(ok = wait_or_abort(&bar_bempty[bs], bph ^ 1, &s_abort, a.err))) break;
-        mbar_arrive_expect_tx(&bar_bfull[bs], kBBytes);
-        tma_load_2d(sB + bs * kBBytes, &tmB, kt * BK, slot0, &bar_bfull[bs]);
-        last_b[bs] = bph;
+      int pi = 0, bi = 0;
+      for (int ti = 0; ti < ntiles && ok; ++ti) {
+        const int4 tl = s_tiles[ti];
+        const int row_base = tl.x * a.rows + tl.y;
+        if (packed) {
+          for (int kt = 0; kt < ktiles; kt += KP) {  // packed stage: k-blocks [kt, kt + KP)
+            const int ps = pi % SP, pph = (pi / SP) & 1;
+            if (!(ok = wait_or_abort(&bar_pempty[ps], pph ^ 1, &s_abort, a.err))) break;
+            mbar_arrive_expect_tx(&bar_pfull[ps], NPROJ * kPBytes);
+            tma_load_2d(sP + (ps * NPROJ + 0) * kPBytes, &tmA0, (kt / KP) * 32, row_base, &bar_pfull[ps]);
+            if constexpr (NPROJ == 2)
+              tma_load_2d(sP + (ps * NPROJ + 1) * kPBytes, &tmA1, (kt / KP) * 32, row_base, &bar_pfull[ps]);
+            last_p[ps] = pph;
+            ++pi;
+          }
+        } else {
+          for (int st = 0; st < nsteps; ++st) {  // activation stage: k-blocks [st*KA, st*KA + KA)
+            const int bs = bi % SB, bph = (bi / SB) & 1;
+            if (!(ok = wait_or_abort(&bar_bempty[bs], bph ^ 1, &s_abort, a.err))) break;
+            mbar_arrive_expect_tx(&bar_bfull[bs], kBBytes);
+#pragma unroll
+            for (int kk = 0; kk < KA; ++kk)
+              tma_load_2d(sB + bs * kBBytes + kk * kBTile, &tmB, (st * KA + kk) * BK, tl.z, &bar_bfull[bs]);
+            last_b[bs] = bph;
+            ++bi;
+          }
+        }
       }
       if (!ok) {  // give the copies already issued a bounded chance to land before exit
         volatile int never = 0;
-        wait_or_abort(&bar_sb, 0, &never, nullptr);
 #pragma unroll
         for (int i = 0; i < SP; ++i)
           if (last_p[i] >= 0) wait_or_abort(&bar_pfull[i], last_p[i], &never, nullptr);
@@ -286,114 +394,188 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ================================================= MMA issuer
     if (lane == 0) {
       bool ok = true;
-      for (int kt = 0; kt < ktiles && ok; ++kt) {
-        const int as = kt % SA, aph = (kt / SA) & 1;
-        const int bs = kt % SB, bph = (kt / SB) & 1;
-        ok = wait_or_abort(&bar_afull[as], aph, &s_abort, a.err) &&
-             wait_or_abort(&bar_bfull[bs], bph, &s_abort, a.err);
-        if (!ok) break;
+      int ai = 0;  // pipeline steps issued (A and B stages advance together)
+      for (int ti = 0; ti < ntiles && ok; ++ti) {
+        const int ab = ti % ACC, accph = (ti / ACC) & 1;
+        if (!(ok = wait_or_abort(&bar_accempty[ab], accph ^ 1, &s_abort, a.err))) break;
         tc_fence_after();
-        const uint32_t b_addr = smem_u32(sB + bs * kBBytes);
+        const uint32_t d_base = tmem + ab * NPROJ * BN;
+        for (int st = 0; st < nsteps; ++st, ++ai) {
+          const int as = ai % SA, aph = (ai / SA) & 1;
+          const int bs = ai % SB, bph = (ai / SB) & 1;
+          ok = wait_or_abort(&bar_afull[as], aph, &s_abort, a.err) &&
+               wait_or_abort(&bar_bfull[bs], bph, &s_abort, a.err);
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t b_desc0 = sw128_kmajor_desc(smem_u32(sB + bs * kBBytes));
+          const uint32_t a_stage = tmem + S::kACol0 + as * S::kACols;
 #pragma unroll
-        for (int p = 0; p < NPROJ; ++p) {
-          const uint32_t a_addr = smem_u32(sA + (as * NPROJ + p) * kABytes);
+          for (int p = 0; p < NPROJ; ++p)
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            umma_f16(tmem + p * BN, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32),
-                      kIdesc, (kt | k) != 0);
+            for (int kk = 0; kk < KA; ++kk)
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k)  // K = 16 per MMA: 8 TMEM columns of A, 32 bytes of B
+                umma_f16_ts(d_base + p * BN, a_stage + (p * KA + kk) * 32 + k * 8,
+                            b_desc0 + ((kk * kBTile + k * 32) >> 4), kIdesc, (st | kk | k) != 0);
+          umma_commit(&bar_aempty[as]);
+          umma_commit(&bar_bempty[bs]);
         }
-        umma_commit(&bar_aempty[as]);
-        umma_commit(&bar_bempty[bs]);
+        if (ok) umma_commit(&bar_accfull[ab]);
       }
-      umma_commit(ok ? &bar_acc : &bar_drain);
-      if (!ok) {  // let issued MMAs finish before TMEM is released
-        volatile int never = 0;
-        wait_or_abort(&bar_drain, 0, &never, nullptr);
+      umma_commit(&bar_drain);  // all MMAs issued by this thread have completed once it fires
+      volatile int never = 0;
+      wait_or_abort(&bar_drain, 0, &never, nullptr);
+    }
+  } else if (warp < kEpiWarp0) {
+    // ================================================= dequantisation -> TMEM
+    // A warp may only touch its TMEM lane quarter q = warp % 4, so lane l of
+    // warp w dequantises row 32 q + l.  The four warps of a quarter split the
+    // row's NPROJ x 64 codes of a k-block into slices j = (w - 2) / 4 of
+    // WPT packed words, stored as CPT TMEM columns (two fp16 per column).
+    constexpr int W = BK * BITS / 32;           // packed words per row per k-block (8 or 16)
+    constexpr int WPT = NPROJ * W / 4;          // words per slice
+    constexpr int CPT = 16 * NPROJ / 2;         // TMEM columns per slice (16 or 8)
+    const int q = warp & 3, j = (warp - 2) >> 2;
+    const int row = q * 32 + lane;
+    const int proj = NPROJ == 2 ? j >> 1 : 0;
+    const int slice = NPROJ == 2 ? j & 1 : j;   // slice within the projection's row
+    const uint32_t lane_base =
+        tmem + (static_cast<uint32_t>(q * 32) << 16) + S::kACol0 + proj * KA * 32 + slice * CPT;
+    bool ok = true;
+    int pi = 0, ai = 0;
+    // scales / biases of the next packed stage, prefetched one stage ahead,
+    // across tile boundaries too
+    uint32_t sv[KP / 2], bv[KP / 2], sn[KP / 2], bn[KP / 2];
+    auto group_ptr = [&](int ti, const uint16_t* base_ptr) {
+      const int4 t = s_tiles[ti];
+      return base_ptr + static_cast<size_t>(t.x * a.rows + t.y + row) * groups;
+    };
+    load_group_params<KP>(group_ptr(0, a.s[proj]), sn);
+    load_group_params<KP>(group_ptr(0, a.b[proj]), bn);
+    for (int ti = 0; ti < ntiles && ok; ++ti) {
+      int ps = 0;
+      for (int st = 0; st < nsteps; ++st, ++ai) {
+        const int kt0 = st * KA;
+        if (kt0 % KP == 0) {
+          ps = pi % SP;
+          const int pph = (pi / SP) & 1;
+          ok = __all_sync(0xffffffffu, wait_or_abort(&bar_pfull[ps], pph, &s_abort, a.err));
+          if (!ok) break;
+#pragma unroll
+          for (int i = 0; i < KP / 2; ++i) {
+            sv[i] = sn[i];
+            bv[i] = bn[i];
+          }
+          if (kt0 + KP < ktiles) {
+            load_group_params<KP>(group_ptr(ti, a.s[proj]) + kt0 + KP, sn);
+            load_group_params<KP>(group_ptr(ti, a.b[proj]) + kt0 + KP, bn);
+          } else if (ti + 1 < ntiles) {
+            load_group_params<KP>(group_ptr(ti + 1, a.s[proj]), sn);
+            load_group_params<KP>(group_ptr(ti + 1, a.b[proj]), bn);
+          }
+        }
+        const int as = ai % SA, aph = (ai / SA) & 1;
+        ok = __all_sync(0xffffffffu, wait_or_abort(&bar_aempty[as], aph ^ 1, &s_abort, a.err));
+        if (!ok) break;
+        tc_fence_after();  // the MMAs that read this A stage have completed
+        const unsigned char* prow = sP + (ps * NPROJ + proj) * kPBytes + row * 128;
+#pragma unroll
+        for (int kk = 0; kk < KA; ++kk) {
+          const int kt = kt0 + kk;
+          const uint16_t sb = pick_bf16<KP>(sv, kt % KP), bb = pick_bf16<KP>(bv, kt % KP);
+          // this thread's words start at word (kt % KP) * W + slice * WPT of the
+          // row's 128-byte packed line, whose 16-byte chunks sit at (c ^ (row & 7))
+          const int w0 = (kt % KP) * W + slice * WPT;
+          uint32_t wd[WPT];
+#pragma unroll
+          for (int i = 0; i < WPT; i += (WPT >= 4 ? 4 : 2)) {
+            const int wi = w0 + i;
+            const unsigned char* src = prow + (((wi >> 2) ^ (row & 7)) << 4) + (wi & 3) * 4;
+            if constexpr (WPT >= 4) {
+              const uint4 v = *reinterpret_cast<const uint4*>(src);
+              wd[i] = v.x; wd[i + 1] = v.y; wd[i + 2] = v.z; wd[i + 3] = v.w;
+            } else {
+              const uint2 v = *reinterpret_cast<const uint2*>(src);
+              wd[i] = v.x; wd[i + 1] = v.y;
+            }
+          }
+          uint32_t out[CPT];
+          if constexpr (BITS == 4) {  // one word (8 codes) -> four columns
+            const float sf = bf16_bits_to_f32(sb);
+            const __half2 b2 = __float2half2_rn(bf16_bits_to_f32(bb));
+            if (fabsf(sf) < 0.2498f) {
+              const __half2 s18 = __float2half2_rn(sf * 262144.0f);
+#pragma unroll
+              for (int i = 0; i < WPT; ++i) {
+                const uint4 v = dequant8_u4_sub(wd[i], s18, b2);
+                out[4 * i] = v.x; out[4 * i + 1] = v.y; out[4 * i + 2] = v.z; out[4 * i + 3] = v.w;
+              }
+            } else {
+              const __half2 s2 = __float2half2_rn(sf);
+#pragma unroll
+              for (int i = 0; i < WPT; ++i) {
+                const uint4 v = dequant8_u4(wd[i], s2, b2);
+                out[4 * i] = v.x; out[4 * i + 1] = v.y; out[4 * i + 2] = v.z; out[4 * i + 3] = v.w;
+              }
+            }
+          } else {  // two words (8 codes) -> four columns
+            const float sf = bf16_bits_to_f32(sb), bf = bf16_bits_to_f32(bb);
+#pragma unroll
+            for (int i = 0; i < WPT; i += 2) {
+              const uint4 v = dequant8_u8(wd[i], wd[i + 1], sf, bf);
+              out[2 * i] = v.x; out[2 * i + 1] = v.y; out[2 * i + 2] = v.z; out[2 * i + 3] = v.w;
+            }
+          }
+          const uint32_t taddr = lane_base + as * S::kACols + kk * 32;
+          if constexpr (CPT == 16) tmem_st16(taddr, out);
+          else tmem_st8(taddr, out);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_afull[as]);
+        if ((kt0 + KA) % KP == 0) {  // this step finished its packed stage
+          if (lane == 0) mbar_arrive(&bar_pempty[ps]);
+          ++pi;
+        }
       }
     }
-  } else {
-    // ================================================= dequant + epilogue
-    const int d = tid - 64;  // 0..255
-    // Per k-block: NPROJ x 128 rows x 64 codes over 256 threads.
-    // NPROJ == 2: thread -> (projection d / 128, row d % 128, all 64 codes)
-    // NPROJ == 1: thread -> (row d / 2, codes [32 * (d % 2), +32))
-    const int proj = NPROJ == 2 ? d / 128 : 0;
-    const int row = NPROJ == 2 ? d % 128 : d / 2;
-    const int half = NPROJ == 2 ? 0 : d % 2;
-    constexpr int kChunks = NPROJ == 2 ? 8 : 4;  // 16-byte output chunks per thread
-    bool ok = wait_or_abort(&bar_sb, 0, &s_abort, a.err);
-    const uint16_t* srow = sSB + (proj * 2 + 0) * BM * groups + row * groups;
-    const uint16_t* brow = sSB + (proj * 2 + 1) * BM * groups + row * groups;
-    for (int kt = 0; kt < ktiles && ok; ++kt) {
-      const int ps = kt % SP, pph = (kt / SP) & 1;
-      const int as = kt % SA, aph = (kt / SA) & 1;
-      ok = wait_or_abort(&bar_pfull[ps], pph, &s_abort, a.err) &&
-           wait_or_abort(&bar_aempty[as], aph ^ 1, &s_abort, a.err);
-      if (!ok) break;
-      const uint16_t sb = srow[kt], bb = brow[kt];
-      const uint32_t* src = reinterpret_cast<const uint32_t*>(sP + (ps * NPROJ + proj) * kPBytes) + row * WK;
-      unsigned char* dst = sA + (as * NPROJ + proj) * kABytes;
-      if constexpr (BITS == 4) {
-        const __half2 s2 = __float2half2_rn(bf16_bits_to_f32(sb));
-        const __half2 b2 = __float2half2_rn(bf16_bits_to_f32(bb));
-        const uint4* src4 = reinterpret_cast<const uint4*>(src + half * 4);
-#pragma unroll
-        for (int q = 0; q < kChunks / 4; ++q) {
-          const uint4 w = src4[q];
-          const int c = half * 4 + q * 4;
-          *reinterpret_cast<uint4*>(dst + sw128_offset(row, c + 0)) = dequant8_u4(w.x, s2, b2);
-          *reinterpret_cast<uint4*>(dst + sw128_offset(row, c + 1)) = dequant8_u4(w.y, s2, b2);
-          *reinterpret_cast<uint4*>(dst + sw128_offset(row, c + 2)) = dequant8_u4(w.z, s2, b2);
-          *reinterpret_cast<uint4*>(dst + sw128_offset(row, c + 3)) = dequant8_u4(w.w, s2, b2);
-        }
-      } else {
-        const float sf = bf16_bits_to_f32(sb), bf = bf16_bits_to_f32(bb);
-        const uint4* src4 = reinterpret_cast<const uint4*>(src + half * 8);
-#pragma unroll
-        for (int q = 0; q < kChunks / 2; ++q) {
-          const uint4 w = src4[q];  // 16 codes = 2 output chunks
-          const uint2 l0 = dequant4_u8(w.x, sf, bf), l1 = dequant4_u8(w.y, sf, bf);
-          const uint2 h0 = dequant4_u8(w.z, sf, bf), h1 = dequant4_u8(w.w, sf, bf);
-          const int c = half * 4 + q * 2;
-          *reinterpret_cast<uint4*>(dst + sw128_offset(row, c + 0)) = make_uint4(l0.x, l0.y, l1.x, l1.y);
-          *reinterpret_cast<uint4*>(dst + sw128_offset(row, c + 1)) = make_uint4(h0.x, h0.y, h1.x, h1.y);
-        }
-      }
-      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
-      mbar_arrive(&bar_afull[as]);
-      mbar_arrive(&bar_pempty[ps]);
-    }
-
-    // ---- epilogue: TMEM -> registers -> global (slot-major output)
-    if (ok && wait_or_abort(&bar_acc, 0, &s_abort, a.err)) {
+  } else if (warp < kBWarp) {
+    // ================================================= epilogue (TMEM -> global)
+    const int q = warp & 3;  // TMEM lane quarter this warp may read (warps 18..21 -> 2, 3, 0, 1)
+    for (int ti = 0; ti < ntiles; ++ti) {
+      const int ab = ti % ACC, accph = (ti / ACC) & 1;
+      if (!__all_sync(0xffffffffu, wait_or_abort(&bar_accfull[ab], accph, &s_abort, a.err))) break;
       tc_fence_after();
-      const int q = warp & 3;                    // TMEM lane quarter this warp may read
-      const int colhalf = (warp - 2) >> 2;       // two warps per quarter split the columns
-      const int r = m0 + q * 32 + lane;          // output row of this thread
-      const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
-      constexpr int kHalf = BN / 2 < 16 ? 16 : BN / 2;
-      const int c_begin = colhalf * kHalf;
-      for (int c0 = c_begin; c0 < c_begin + kHalf && c0 < BN; c0 += 16) {
-        if (c0 >= nvalid) break;  // uniform across the warp
+      const int4 tl = s_tiles[ti];
+      const int r = tl.y + q * 32 + lane;  // output row of this thread
+      const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ab * NPROJ * BN;
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        if (c0 >= tl.w) break;  // uniform across the warp
         uint32_t g[16], u[16];
         tmem_ld16(lane_addr + c0, g);
         if constexpr (NPROJ == 2) tmem_ld16(lane_addr + BN + c0, u);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (c0 + j >= nvalid) break;
+        for (int jj = 0; jj < 16; ++jj) {
+          if (c0 + jj >= tl.w) break;
           uint16_t bits;
-          if constexpr (NPROJ == 2) {  // h = act(bf16(g), bf16(u)) (bf16 value), stored as fp16
-            const float gg = round_bf16(__uint_as_float(g[j])), uu = round_bf16(__uint_as_float(u[j]));
+          if constexpr (NPROJ == 2) {  // h = act(bf16(g), bf16(u)) (a bf16 value), stored as fp16
+            const float gg = round_bf16(__uint_as_float(g[jj])), uu = round_bf16(__uint_as_float(u[jj]));
             const float v = a.act == 0 ? act_swiglu_mlx(gg, uu) : act_geglu_mlx(gg, uu);
             if (!(fabsf(v) < 65504.0f)) record_error(a.err, kDevFp16Range);
             bits = __half_as_ushort(__float2half_rn(v));
           } else {
-            bits = f32_to_bf16_bits(__uint_as_float(g[j]));
+            bits = f32_to_bf16_bits(__uint_as_float(g[jj]));
           }
-          a.out[static_cast<size_t>(slot0 + c0 + j) * a.out_stride + r] = bits;
+          // h feeds the down GEMM as its k dimension: store it k-permuted like x
+          const int col = NPROJ == 2 ? kperm8(r) : r;
+          a.out[static_cast<size_t>(tl.z + c0 + jj) * a.out_stride + col] = bits;
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_accempty[ab]);
     }
   }
 
@@ -402,43 +584,61 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::kCols) : "memory");
   }
 }
 
 // ------------------------------------------------------------- host side
 size_t tc_smem_bytes(int bits, int nproj, int bn, int kdim) {
-  const int groups = kdim / BK;
-  const int wk = BK * bits / 32;
-  const int sb = bn >= 128 ? 2 : 4, sp = bn >= 128 ? 4 : 6, sa = 2;
-  return 1024 + static_cast<size_t>(sa) * nproj * BM * BK * 2 + static_cast<size_t>(sb) * bn * BK * 2 +
-         static_cast<size_t>(sp) * nproj * BM * wk * 4 + static_cast<size_t>(nproj) * 2 * BM * groups * 2;
+  (void)kdim;
+#define SENMOE_TC_SMEM(B, P, N) \
+  if (bits == B && nproj == P && bn == N) return TcShape<B, P, N>::kSmem;
+#define SENMOE_TC_SMEM_BN(B, P) \
+  SENMOE_TC_SMEM(B, P, 16) SENMOE_TC_SMEM(B, P, 32) SENMOE_TC_SMEM(B, P, 64) SENMOE_TC_SMEM(B, P, 128)
+  SENMOE_TC_SMEM_BN(4, 1) SENMOE_TC_SMEM_BN(4, 2) SENMOE_TC_SMEM_BN(8, 1) SENMOE_TC_SMEM_BN(8, 2)
+#undef SENMOE_TC_SMEM_BN
+#undef SENMOE_TC_SMEM
+  return ~size_t(0);
 }
 
 bool tc_supported(int rows, int kdim, int bits, int nproj, int bn) {
-  return rows % BM == 0 && kdim % BK == 0 && kdim >= BK && (bits == 4 || bits == 8) &&
-         tc_smem_bytes(bits, nproj, bn, kdim) <= 227 * 1024;
+  const int kp = 512 / bits / 32;  // k-blocks per packed stage
+  return rows % BM == 0 && kdim % (BK * kp) == 0 && (bits == 4 || bits == 8) &&
+         tc_smem_bytes(bits, nproj, bn, kdim) + 2048 <= 227 * 1024;
+}
+
+static int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+  }
+  return n;
 }
 
 template <int BITS, int NPROJ, int BN>
 static cudaError_t launch_tc_t(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
-                               const TcGemmArgs& a, int grid, cudaStream_t st) {
-  const size_t smem = tc_smem_bytes(BITS, NPROJ, BN, a.kdim);
+                               const TcGemmArgs& a, int tiles_upper, cudaStream_t st) {
+  const size_t smem = TcShape<BITS, NPROJ, BN>::kSmem;
   auto kern = tc_gemm_kernel<BITS, NPROJ, BN>;
   cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kTcThreads, smem, st>>>(tA0, tA1, tB, a);
+  // one persistent CTA per SM, enough CTAs that none owns more than kMaxTilesPerCta tiles
+  int grid = tiles_upper < sm_count() ? tiles_upper : sm_count();
+  if ((tiles_upper + grid - 1) / grid > kMaxTilesPerCta) grid = (tiles_upper + kMaxTilesPerCta - 1) / kMaxTilesPerCta;
+  kern<<<grid, kTcThreadsP, smem, st>>>(tA0, tA1, tB, a);
   return cudaGetLastError();
 }
 
 cudaError_t launch_tc_gemm(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
-                           const TcGemmArgs& a, int bits, int nproj, int bn, int grid, cudaStream_t st) {
-  if (grid <= 0) return cudaSuccess;
+                           const TcGemmArgs& a, int bits, int nproj, int bn, int tiles_upper, cudaStream_t st) {
+  if (tiles_upper <= 0) return cudaSuccess;
 #define SENMOE_TC_CASE(B, P, N) \
-  if (bits == B && nproj == P && bn == N) return launch_tc_t<B, P, N>(tA0, tA1, tB, a, grid, st);
+  if (bits == B && nproj == P && bn == N) return launch_tc_t<B, P, N>(tA0, tA1, tB, a, tiles_upper, st);
 #define SENMOE_TC_BN(B, P) \
-  SENMOE_TC_CASE(B, P, 16) SENMOE_TC_CASE(B, P, 32) SENMOE_TC_CASE(B, P, 64) SENMOE_TC_CASE(B, P, 128) \
-  SENMOE_TC_CASE(B, P, 256)
+  SENMOE_TC_CASE(B, P, 16) SENMOE_TC_CASE(B, P, 32) SENMOE_TC_CASE(B, P, 64) SENMOE_TC_CASE(B, P, 128)
   SENMOE_TC_BN(4, 1) SENMOE_TC_BN(4, 2) SENMOE_TC_BN(8, 1) SENMOE_TC_BN(8, 2)
 #undef SENMOE_TC_BN
 #undef SENMOE_TC_CASE
@@ -483,7 +683,8 @@ cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-// Slot-ordered fp16 copy of the token rows (bf16 -> fp16 is exact in range).
+// Slot-ordered fp16 copy of the token rows (bf16 -> fp16 is exact in range),
+// k-permuted within each block of 8 columns like the dequantised weights.
 __global__ void gather_rows_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ perm, int k_div,
                                    uint16_t* __restrict__ out, int hidden, int* err) {
   const int s = blockIdx.x;
@@ -494,12 +695,17 @@ __global__ void gather_rows_kernel(const uint16_t* __restrict__ x, const int32_t
   for (int i = threadIdx.x; i < hidden / 8; i += blockDim.x) {
     const uint4 v = src[i];
     const uint32_t in[4] = {v.x, v.y, v.z, v.w};
-    uint32_t o[4];
+    float f[8];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const float lo = bf16_lo(in[k]), hi = bf16_hi(in[k]);
-      range_ok &= fabsf(lo) < 65504.0f && fabsf(hi) < 65504.0f;
-      const __half2 h = __floats2half2_rn(lo, hi);
+      f[2 * k] = bf16_lo(in[k]);
+      f[2 * k + 1] = bf16_hi(in[k]);
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {  // k-permuted pairs (k, k + 4), see kperm8
+      range_ok &= fabsf(f[k]) < 65504.0f && fabsf(f[k + 4]) < 65504.0f;
+      const __half2 h = __floats2half2_rn(f[k], f[k + 4]);
       o[k] = *reinterpret_cast<const uint32_t*>(&h);
     }
     dst[i] = make_uint4(o[0], o[1], o[2], o[3]);

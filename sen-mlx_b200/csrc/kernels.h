@@ -14,6 +14,7 @@ enum DeviceError : int {
   kDevBadExpert = 1,    // an expert id outside [0, E)
   kDevWaitTimeout = 2,  // a bounded mbarrier wait ran out
   kDevFp16Range = 3,    // an activation outside fp16 range met the tensor-core path
+  kDevTileOverflow = 4, // a persistent CTA was handed more tiles than it can list
 };
 
 // ---------------------------------------------------------------- router
@@ -110,9 +111,9 @@ struct TcGemmArgs {
 };
 size_t tc_smem_bytes(int bits, int nproj, int bn, int kdim);
 bool tc_supported(int rows, int kdim, int bits, int nproj, int bn);
-// grid = an upper bound on the tile count; CTAs past the last tile exit.
+// tiles_upper: an upper bound on the tile count (the grid is sized from it).
 cudaError_t launch_tc_gemm(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
-                           const TcGemmArgs& a, int bits, int nproj, int bn, int grid, cudaStream_t st);
+                           const TcGemmArgs& a, int bits, int nproj, int bn, int tiles_upper, cudaStream_t st);
 // 2-D tiled tensor map (row-major [outer, inner], no interleave, zero OOB fill).
 cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t inner,
                          uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,

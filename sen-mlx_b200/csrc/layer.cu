@@ -69,15 +69,18 @@ constexpr int kGateUpRows = 16;
 constexpr int kDownRows = 64;
 
 // Tensor-core path: token tiles (N) offered, and the average tokens per
-// touched expert from which the tensor cores beat the CUDA-core GEMV.
-constexpr int kTcTiles[5] = {16, 32, 64, 128, 256};
+// touched expert from which the tensor cores beat the CUDA-core GEMV.  Tiles
+// stop at 128 tokens: TMEM also holds the dequantised A stages, and a
+// 256-token tile of gate and up would fill it with accumulators alone.
+constexpr int kTcTiles[4] = {16, 32, 64, 128};
+constexpr int kTcMaxTile = 3;  // index of the widest tile
 constexpr double kTcMinTokensPerExpert = 3.0;
 enum ExpertPath { kPathAuto = 0, kPathGemv = 1, kPathTensorCore = 2 };
 
 int tc_tile_index(double tokens_per_expert) {
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < kTcMaxTile; ++i)
     if (tokens_per_expert <= kTcTiles[i]) return i;
-  return 4;
+  return kTcMaxTile;
 }
 
 }  // namespace
@@ -111,7 +114,7 @@ struct SenMoeLayer {
   uint16_t* xs = nullptr;        // fp16 [Tmax*K, H] activations gathered into slot order
   uint16_t* h16 = nullptr;       // fp16 [Tmax*K, I] SwiGLU output (B operand of the down GEMM)
   CUtensorMap tm_gate{}, tm_up{}, tm_down{};  // packed codes, [rows, words]
-  CUtensorMap tm_xs[5]{}, tm_h[5]{};          // activation tiles per token-tile width
+  CUtensorMap tm_xs[4]{}, tm_h[4]{};          // activation tiles per token-tile width
   // per-stage timing
   bool profiling = false;
   bool profiled_once = false;
@@ -249,16 +252,18 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
   L->h16 = reinterpret_cast<uint16_t*>(base + o_h16);
   {  // tensor maps for the tcgen05 path (host-side encoding only)
     const int bits = c.bits, El = c.expert_end - c.expert_begin;
-    const uint32_t wk = 64u * bits / 32u;
     const uint64_t gw = uint64_t(H) * bits / 32, dw = uint64_t(I) * bits / 32;
-    bool ok = tc_supported(int(I), int(H), bits, 2, 256) && tc_supported(int(H), int(I), bits, 1, 256);
+    bool ok = tc_supported(int(I), int(H), bits, 2, 128) && tc_supported(int(H), int(I), bits, 1, 128);
+    // packed codes: 128-row x 128-byte boxes (32 words), SWIZZLE_128B; a
+    // row shorter than a box would need a box wider than the tensor
+    ok = ok && gw >= 32 && dw >= 32;
     ok = ok && make_tmap_2d(&L->tm_gate, L->w.gate_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, gw, uint64_t(El) * I,
-                            gw * 4, wk, 128, false) == cudaSuccess;
+                            gw * 4, 32, 128, true) == cudaSuccess;
     ok = ok && make_tmap_2d(&L->tm_up, L->w.up_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, gw, uint64_t(El) * I, gw * 4,
-                            wk, 128, false) == cudaSuccess;
+                            32, 128, true) == cudaSuccess;
     ok = ok && make_tmap_2d(&L->tm_down, L->w.down_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, dw, uint64_t(El) * H,
-                            dw * 4, wk, 128, false) == cudaSuccess;
-    for (int i = 0; i < 5 && ok; ++i) {
+                            dw * 4, 32, 128, true) == cudaSuccess;
+    for (int i = 0; i < 4 && ok; ++i) {
       ok = make_tmap_2d(&L->tm_xs[i], L->xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, H, P, H * 2, 64, kTcTiles[i], true) ==
                cudaSuccess &&
            make_tmap_2d(&L->tm_h[i], L->h16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, I, P, I * 2, 64, kTcTiles[i], true) ==
@@ -293,6 +298,15 @@ int senmoe_layer_destroy(SenMoeLayer* layer) {
   return SENMOE_OK;
 }
 
+// Expert-product kernels one forward of `pairs` (token, slot) pairs takes.
+static bool uses_tensor_cores(const SenMoeLayer* L, int64_t pairs) {
+  const SenMoeConfig& c = L->cfg;
+  const int64_t e_local = c.expert_end - c.expert_begin;
+  const double per_expert = double(pairs) / double(pairs < e_local ? pairs : e_local);
+  const int path = c.reserved[0];
+  return L->tc_ok && (path == kPathTensorCore || (path == kPathAuto && per_expert >= kTcMinTokensPerExpert));
+}
+
 static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void* y, const SenMoeDebug* debug,
                          bool residual, senmoe_stream_t stream) {
   g_last_error.clear();
@@ -307,9 +321,15 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   const int T = static_cast<int>(num_tokens), K = c.num_experts_per_tok, E = c.n_routed_experts;
   const int H = c.hidden_size, I = c.moe_intermediate_size, Is = c.shared_intermediate;
   const int P = T * K;
-  auto mark = [&](int stage) -> cudaError_t {
-    return L->profiling ? cudaEventRecord(L->ev[stage], st) : cudaSuccess;
-  };
+  // Stage events are recorded only outside a stream capture (inside one a
+  // plain record only links the capture's streams).
+  bool profile = L->profiling;
+  if (profile) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    SENMOE_CUDA(cudaStreamIsCapturing(st, &cs));
+    profile = cs == cudaStreamCaptureStatusNone;
+  }
+  auto mark = [&](int stage) -> cudaError_t { return profile ? cudaEventRecord(L->ev[stage], st) : cudaSuccess; };
   SENMOE_CUDA(mark(0));
 
   // 1. router (deepseek_v2.rs:528-543)
@@ -350,9 +370,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   const int E_local = c.expert_end - c.expert_begin;
   const int max_items = P < E_local ? P : E_local;
   const double per_expert = double(P) / double(max_items);
-  const int path = c.reserved[0];
-  const bool use_tc =
-      L->tc_ok && (path == kPathTensorCore || (path == kPathAuto && per_expert >= kTcMinTokensPerExpert));
+  const bool use_tc = uses_tensor_cores(L, P);
   if (use_tc) {
     const int ti = tc_tile_index(per_expert), bn = kTcTiles[ti];
     SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st));
@@ -492,7 +510,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   ca.top_k = K;
   SENMOE_CUDA(launch_combine(ca, T, st));
   SENMOE_CUDA(mark(6));
-  if (L->profiling) L->profiled_once = true;
+  if (profile) L->profiled_once = true;
 
   if (debug) {
     if (debug->topk_ids)
@@ -514,6 +532,13 @@ int senmoe_layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
 int senmoe_layer_forward_residual(SenMoeLayer* L, const void* x, int64_t num_tokens, void* h_out,
                                   senmoe_stream_t stream) {
   return layer_forward(L, x, num_tokens, h_out, nullptr, true, stream);
+}
+
+int senmoe_layer_expert_path(const SenMoeLayer* L, int64_t num_tokens) {
+  g_last_error.clear();
+  if (!L) return -fail(SENMOE_ERR_BAD_ARG, "layer is NULL");
+  if (num_tokens <= 0) return kPathGemv;
+  return uses_tensor_cores(L, num_tokens * L->cfg.num_experts_per_tok) ? kPathTensorCore : kPathGemv;
 }
 
 int senmoe_layer_set_profiling(SenMoeLayer* L, int enable) {

@@ -79,6 +79,7 @@ SIGNATURES = {
     "senmoe_layer_check": (C.c_int, [_P, _P]),
     "senmoe_layer_forward_residual": (C.c_int, [_P, _P, _i64, _P, _P]),
     "senmoe_layer_set_profiling": (C.c_int, [_P, C.c_int]),
+    "senmoe_layer_expert_path": (C.c_int, [_P, _i64]),
     "senmoe_layer_stage_times": (C.c_int, [_P, C.POINTER(C.c_float), C.c_int]),
     "senmoe_router": (C.c_int, [_P, _i64, _P, _i32, _i32, _i32, _i32, _f32, _P, _P, _P, _P]),
     "senmoe_dispatch": (C.c_int, [_P, _i64, _i32, _i32, _P, _P, _P, _P, _P]),
@@ -280,6 +281,13 @@ class DeepseekMoe:
         _check(lib().senmoe_layer_forward_residual(self._handle, _ptr(xc), xc.numel() // self.args.hidden_size,
                                                    _ptr(h), _stream(stream)))
         return h
+
+    def expert_path(self, num_tokens: int) -> int:
+        """PATH_GEMV or PATH_TENSOR_CORE: the expert kernels a forward of num_tokens runs."""
+        r = lib().senmoe_layer_expert_path(self._handle, int(num_tokens))
+        if r < 0:
+            _check(-r)
+        return r
 
     STAGES = ("router", "dispatch", "gate_up", "down", "shared", "combine")
 

@@ -33,6 +33,8 @@ def run_block(senmoe, cfg, mw, x_bits, max_tokens=None, path=0):
     import torch
     T = x_bits.shape[0]
     blk = senmoe.DeepseekMoe(moe_args(cfg, path), device_weights(mw), max_tokens=max_tokens or max(T, 1))
+    if path:
+        assert blk.expert_path(T) == path, "the forced expert path is not the one that runs"
     dbg = dict(topk_ids=torch.empty((T, cfg.top_k), dtype=torch.int32, device="cuda"),
                topk_weights=torch.empty((T, cfg.top_k), dtype=torch.float32, device="cuda"),
                perm=torch.empty(T * cfg.top_k, dtype=torch.int32, device="cuda"),
@@ -102,8 +104,8 @@ def test_config0_prefill_tensor_core_vs_oracle(senmoe, config0_layer, T):
 @pytest.mark.parametrize("T", [3, 40, 600, 3000])
 def test_tensor_core_tiles_vs_oracle(senmoe, bits, T):
     """Every token-tile width (16..256) and ragged expert groups, both code widths,
-    on a small layer so the oracle stays fast (H=256, I=128, E=16, K=4)."""
-    cfg = O.MoeConfig(hidden=256, intermediate=128, num_experts=16, top_k=4, bits=bits)
+    on a small layer so the oracle stays fast (H=256, I=256, E=16, K=4)."""
+    cfg = O.MoeConfig(hidden=256, intermediate=256, num_experts=16, top_k=4, bits=bits)
     mw = O.make_layer(cfg, seed=20 + bits)
     x = O.make_tokens(T, cfg.hidden, seed=T + bits)
     got = run_block(senmoe, cfg, mw, x, path=PATHS["tc"])
@@ -144,7 +146,7 @@ def test_block_8bit_skewed(senmoe, path):
 @pytest.mark.parametrize("path", ["gemv", "tc"])
 def test_many_tokens_multi_chunk_dispatch(senmoe, path):
     """T*K > 2048 pairs takes the three-kernel dispatch; small H/I keep the oracle fast."""
-    cfg = O.MoeConfig(hidden=256, intermediate=128, num_experts=64, top_k=8, bits=4)
+    cfg = O.MoeConfig(hidden=256, intermediate=256, num_experts=64, top_k=8, bits=4)
     mw = O.make_layer(cfg, seed=6)
     x = O.make_tokens(2000, cfg.hidden, seed=9)
     got = run_block(senmoe, cfg, mw, x, path=PATHS[path])
