@@ -330,8 +330,11 @@ def main():
             secs = timed_steps(stack, T, args.steps, args.warmup)
         step = secs / args.steps
         alg_bytes = sum(n * BYTES_EXPERT + E * H * 2 + 2 * T * H * 2 for n in touched)
+        sp = stage_profile(layers, T, 3)
+        per_layer_us = {k: round(v / (3 * len(layers)) * 1e3, 2) for k, v in sp.items()}
         results[T] = {"tokens_per_s": world * T / step, "ms_per_step": step * 1e3,
                       "expert_kernels": "tcgen05" if layers[0].expert_path(T) == senmoe.PATH_TENSOR_CORE else "gemv",
+                      "stage_us_per_layer": per_layer_us,
                       "touched_experts_per_layer": sum(touched) / len(touched),
                       "hbm_gbs": alg_bytes / step / 1e9, "hbm_frac": alg_bytes / step / 1e9 / hbm_peak}
         if rank == 0:

@@ -122,6 +122,8 @@ __device__ void histogram_chunk(const DispatchArgs& a, int p_begin, int p_end, i
 
 // Whole dispatch in one CTA (num_pairs small).
 __global__ void __launch_bounds__(kThreads) dispatch_single_kernel(DispatchArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ int sm[];
   int* cnt = sm;                         // [E]
   int* whist = sm + a.num_experts;       // [kWarps * E]
@@ -138,6 +140,8 @@ __global__ void __launch_bounds__(kThreads) dispatch_single_kernel(DispatchArgs 
 
 // Phase 1 of the large dispatch: one histogram per chunk.
 __global__ void __launch_bounds__(kThreads) dispatch_hist_kernel(DispatchArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ int sm[];
   const int c = blockIdx.x;
   histogram_chunk(a, c * kThreads, min(a.num_pairs, (c + 1) * kThreads), sm);
@@ -146,11 +150,14 @@ __global__ void __launch_bounds__(kThreads) dispatch_hist_kernel(DispatchArgs a)
 
 // Phase 2: totals, offsets, active list; chunk_hist becomes per-chunk bases.
 __global__ void __launch_bounds__(kThreads) dispatch_scan_kernel(DispatchArgs a, int nchunks) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ int sm[];
   __shared__ int warp_tot[32];
   __shared__ int total;
   for (int e = threadIdx.x; e < a.num_experts; e += kThreads) {
     int s = 0;  // NOLINT
+#pragma unroll 16
     for (int c = 0; c < nchunks; ++c) s += a.chunk_hist[static_cast<size_t>(c) * a.num_experts + e];
     sm[e] = s;
   }
@@ -158,17 +165,25 @@ __global__ void __launch_bounds__(kThreads) dispatch_scan_kernel(DispatchArgs a,
   scan_counts(sm, a, warp_tot, &total);
   for (int e = threadIdx.x; e < a.num_experts; e += kThreads) {
     int run = a.offsets[e];
-    for (int c = 0; c < nchunks; ++c) {
-      int* h = a.chunk_hist + static_cast<size_t>(c) * a.num_experts + e;
-      const int n = *h;
-      *h = run;
-      run += n;
+    // 16 chunk counts per batch of independent loads, then their prefix
+    for (int c0 = 0; c0 < nchunks; c0 += 16) {
+      int n[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        n[i] = c0 + i < nchunks ? a.chunk_hist[static_cast<size_t>(c0 + i) * a.num_experts + e] : 0;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if (c0 + i < nchunks) a.chunk_hist[static_cast<size_t>(c0 + i) * a.num_experts + e] = run;
+        run += n[i];
+      }
     }
   }
 }
 
 // Phase 3: per-chunk stable placement from the chunk's bases.
 __global__ void __launch_bounds__(kThreads) dispatch_place_kernel(DispatchArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ int sm[];
   int* cursor = sm;
   int* whist = sm + a.num_experts;
@@ -190,15 +205,15 @@ cudaError_t launch_dispatch(const DispatchArgs& a, cudaStream_t st) {
   if (nchunks <= 2 || a.chunk_hist == nullptr) {
     e = ensure_dynamic_smem(reinterpret_cast<const void*>(dispatch_single_kernel), smem);
     if (e != cudaSuccess) return e;
-    dispatch_single_kernel<<<1, kThreads, smem, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(dispatch_single_kernel, dim3(1), dim3(kThreads), smem, st, a);
   }
   e = ensure_dynamic_smem(reinterpret_cast<const void*>(dispatch_place_kernel), smem);
   if (e != cudaSuccess) return e;
-  dispatch_hist_kernel<<<nchunks, kThreads, a.num_experts * sizeof(int), st>>>(a);
-  dispatch_scan_kernel<<<1, kThreads, a.num_experts * sizeof(int), st>>>(a, nchunks);
-  dispatch_place_kernel<<<nchunks, kThreads, smem, st>>>(a);
-  return cudaGetLastError();
+  e = launch_pdl(dispatch_hist_kernel, dim3(nchunks), dim3(kThreads), a.num_experts * sizeof(int), st, a);
+  if (e == cudaSuccess)
+    e = launch_pdl(dispatch_scan_kernel, dim3(1), dim3(kThreads), a.num_experts * sizeof(int), st, a, nchunks);
+  if (e == cudaSuccess) e = launch_pdl(dispatch_place_kernel, dim3(nchunks), dim3(kThreads), smem, st, a);
+  return e;
 }
 
 }  // namespace senmoe

@@ -135,6 +135,8 @@ __global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(QGemvArgs a) {
   const int words_per_row = a.kdim * BITS / 32;  // <= WPL * 32
   const int groups = a.kdim / 64;
 
+  pdl_wait();  // the active list / offsets come from the dispatch kernel
+  pdl_launch_dependents();
   // ---- which expert / slots does this CTA serve?
   int expert, s_begin, s_end;
   if (a.mode == kItemsGrouped) {
@@ -218,19 +220,39 @@ __global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(QGemvArgs a) {
 // y[t, :] = bf16( sum_j f32(d[inv[t*K + j], :]) * w[t, j]  (+ gate_t * shared[t, :]) )
 // in slot order j = 0..K-1 with fp32 accumulation (deepseek_v2.rs:546-552).
 __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int t = blockIdx.y;
   const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (col >= a.hidden) return;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int j = 0; j < a.top_k; ++j) {
-    const int slot = a.inverse[t * a.top_k + j];
-    const float w = a.weights[t * a.top_k + j];
-    if (slot < 0) continue;  // expert held by another rank
-    const uint4 v = *reinterpret_cast<const uint4*>(a.d + static_cast<size_t>(slot) * a.hidden + col);
-    acc[0] += bf16_lo(v.x) * w; acc[1] += bf16_hi(v.x) * w;
-    acc[2] += bf16_lo(v.y) * w; acc[3] += bf16_hi(v.y) * w;
-    acc[4] += bf16_lo(v.z) * w; acc[5] += bf16_hi(v.z) * w;
-    acc[6] += bf16_lo(v.w) * w; acc[7] += bf16_hi(v.w) * w;
+  // all slot indices and weights first, then all rows, so the loads overlap;
+  // the sum still runs in slot order j = 0..K-1
+  constexpr int kMaxK = 16;
+  int slot[kMaxK];
+  float wj[kMaxK];
+#pragma unroll
+  for (int j = 0; j < kMaxK; ++j) {
+    if (j < a.top_k) {
+      slot[j] = a.inverse[t * a.top_k + j];
+      wj[j] = a.weights[t * a.top_k + j];
+    }
+  }
+  uint4 rows[kMaxK];
+#pragma unroll
+  for (int j = 0; j < kMaxK; ++j)
+    if (j < a.top_k && slot[j] >= 0)  // slot < 0: expert held by another rank
+      rows[j] = *reinterpret_cast<const uint4*>(a.d + static_cast<size_t>(slot[j]) * a.hidden + col);
+#pragma unroll
+  for (int j = 0; j < kMaxK; ++j) {
+    if (j < a.top_k && slot[j] >= 0) {
+      const uint4 v = rows[j];
+      const float w = wj[j];
+      acc[0] += bf16_lo(v.x) * w; acc[1] += bf16_hi(v.x) * w;
+      acc[2] += bf16_lo(v.y) * w; acc[3] += bf16_hi(v.y) * w;
+      acc[4] += bf16_lo(v.z) * w; acc[5] += bf16_hi(v.z) * w;
+      acc[6] += bf16_lo(v.w) * w; acc[7] += bf16_hi(v.w) * w;
+    }
   }
   if (a.shared_out) {
     const float g = a.shared_gate ? a.shared_gate[t] : 1.0f;
@@ -273,8 +295,7 @@ static cudaError_t launch_qgemv_t(const QGemvArgs& a, int num_items, cudaStream_
   if (e != cudaSuccess) return e;
   if (num_items == 0) return cudaSuccess;
   dim3 grid(num_items, (a.rows + a.rows_per_cta - 1) / a.rows_per_cta);
-  kern<<<grid, kGemvThreads, smem, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(kern, grid, dim3(kGemvThreads), smem, st, a);
 }
 
 // Words per lane WPL = ceil(kdim * bits / 32 / 32) selects the instance;
@@ -310,8 +331,7 @@ cudaError_t launch_combine(const CombineArgs& a, int num_tokens, cudaStream_t st
   if (num_tokens == 0) return cudaSuccess;
   const int threads = 256;
   dim3 grid((a.hidden / 8 + threads - 1) / threads, num_tokens);
-  combine_kernel<<<grid, threads, 0, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(combine_kernel, grid, dim3(threads), 0, st, a);
 }
 
 }  // namespace senmoe

@@ -210,9 +210,10 @@ template <int BITS, int NPROJ, int BN> struct TcShape {
   // few hundred cycles even when its phase has already completed.
   static constexpr int KA = NPROJ == 2 ? 2 : (KP < 4 ? KP : 4);
   static constexpr int kACols = NPROJ * KA * 32;                // TMEM columns of one A stage
-  // TMEM (512 columns): ACC accumulators of NPROJ*BN columns, then kA A stages
-  // (128 rows x 64 k per k-block, two fp16 per column).
-  static constexpr int kAccCols = NPROJ * BN;
+  // TMEM (512 columns): ACC accumulator sets of 2*BN columns (gate and up, or
+  // the down projection's two partial sums, one per MMA issuer), then kA A
+  // stages (128 rows x 64 k per k-block, two fp16 per column).
+  static constexpr int kAccCols = 2 * BN;
   static constexpr int kAcc = 2 * kAccCols + 2 * kACols <= 512 ? 2 : 1;
   static constexpr int kAFit = (512 - kAcc * kAccCols) / kACols;
   static constexpr int kA = kAFit > 4 ? 4 : kAFit;              // TMEM A stages
@@ -232,14 +233,20 @@ template <int BITS, int NPROJ, int BN> struct TcShape {
 };
 
 constexpr int kMaxTilesPerCta = 64;
-// warp 0: TMA of packed codes; warp 1: TMEM + MMA; warps 2-17: dequant;
-// warps 18-21: epilogue; warp 22: TMA of activation tiles.  The two TMA
-// streams live in separate warps so the weight prefetch never waits behind an
-// activation slot that only the MMA frees.  Dequantisation is the busiest
-// role (~12 instructions per 8 codes), so it gets 16 warps.
+// warp 0: TMA of packed codes; warp 1: TMEM + MMA issuer 0; warps 2-17:
+// dequant; warps 18-21: epilogue; warp 22: TMA of activation tiles; warp 23:
+// MMA issuer 1.  The two TMA streams live in separate warps so the weight
+// prefetch never waits behind an activation slot that only the MMA frees.
+// Small-N tcgen05.mma issue is latency-bound per issuing thread, and a second
+// issuer (in another warp, into its own accumulator) doubles the rate:
+// issuer p takes projection p (gate/up), or alternate K steps of the down
+// projection into partial sums the epilogue adds.  Dequantisation is the
+// busiest role (~12 instructions per 8 codes), so it gets 16 warps.
 constexpr int kEpiWarp0 = 2 + kDqWarps;
 constexpr int kBWarp = kEpiWarp0 + 4;
-constexpr int kTcThreadsP = (kBWarp + 1) * 32;
+constexpr int kMma1Warp = kBWarp + 1;
+constexpr int kIssuers = 2;
+constexpr int kTcThreadsP = (kMma1Warp + 1) * 32;
 
 // Scale/bias of k-block j (0 <= j < KP) from KP bf16 values held as packed u32s.
 template <int KP>
@@ -280,7 +287,7 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
 
   extern __shared__ unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t bar_pfull[SP], bar_pempty[SP], bar_afull[SA], bar_aempty[SA], bar_bfull[SB],
-      bar_bempty[SB], bar_accfull[ACC], bar_accempty[ACC], bar_drain;
+      bar_bempty[SB], bar_accfull[ACC], bar_accempty[ACC], bar_drain[kIssuers];
   __shared__ uint32_t s_tmem;
   __shared__ int4 s_tiles[kMaxTilesPerCta];  // local expert, first weight row, first slot, valid slots
   __shared__ int s_ntiles;
@@ -294,6 +301,25 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
   unsigned char* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   unsigned char* sB = base;                       // [SB][KA][BN*128]
   unsigned char* sP = sB + SB * kBBytes;          // [SP][NPROJ][16 KB]
+
+  // ---- barriers and TMEM first: they do not depend on the previous kernel
+  if (warp == 0 && lane == 0) {
+    // consumer-side barriers count warps: each warp fences, syncs, and arrives once
+    for (int i = 0; i < SP; ++i) { mbar_init(&bar_pfull[i], 1); mbar_init(&bar_pempty[i], kDqWarps); }
+    for (int i = 0; i < SA; ++i) { mbar_init(&bar_afull[i], kDqWarps); mbar_init(&bar_aempty[i], kIssuers); }
+    for (int i = 0; i < SB; ++i) { mbar_init(&bar_bfull[i], 1); mbar_init(&bar_bempty[i], kIssuers); }
+    for (int i = 0; i < ACC; ++i) { mbar_init(&bar_accfull[i], kIssuers); mbar_init(&bar_accempty[i], 4); }
+    for (int i = 0; i < kIssuers; ++i) mbar_init(&bar_drain[i], 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(S::kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  pdl_wait();  // the tile list comes from the dispatch kernel's active list / offsets
+  pdl_launch_dependents();
 
   // ---- this CTA's tiles: global tile t (m-block fastest within an expert's
   // slot block) belongs to CTA t % gridDim.x
@@ -318,29 +344,16 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
     s_ntiles = n;
     s_abort = 0;
   }
-  if (warp == 0 && lane == 0) {
-    // consumer-side barriers count warps: each warp fences, syncs, and arrives once
-    for (int i = 0; i < SP; ++i) { mbar_init(&bar_pfull[i], 1); mbar_init(&bar_pempty[i], kDqWarps); }
-    for (int i = 0; i < SA; ++i) { mbar_init(&bar_afull[i], kDqWarps); mbar_init(&bar_aempty[i], 1); }
-    for (int i = 0; i < SB; ++i) { mbar_init(&bar_bfull[i], 1); mbar_init(&bar_bempty[i], 1); }
-    for (int i = 0; i < ACC; ++i) { mbar_init(&bar_accfull[i], 1); mbar_init(&bar_accempty[i], 4); }
-    mbar_init(&bar_drain, 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  const int ntiles = s_ntiles;
-  if (ntiles == 0) return;  // uniform exit before any TMEM use
-
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                 "r"(S::kCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
+  const int ntiles = s_ntiles;
+  if (ntiles == 0) {  // no tile for this CTA: release TMEM and leave
+    if (warp == 1)
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::kCols) : "memory");
+    return;
+  }
 
   if (warp == 0 || warp == kBWarp) {
     // ================================================= TMA producers
@@ -390,16 +403,17 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
           if (last_b[i] >= 0) wait_or_abort(&bar_bfull[i], last_b[i], &never, nullptr);
       }
     }
-  } else if (warp == 1) {
-    // ================================================= MMA issuer
+  } else if (warp == 1 || warp == kMma1Warp) {
+    // ================================================= MMA issuers
     if (lane == 0) {
+      const int iss = warp == 1 ? 0 : 1;
       bool ok = true;
       int ai = 0;  // pipeline steps issued (A and B stages advance together)
       for (int ti = 0; ti < ntiles && ok; ++ti) {
         const int ab = ti % ACC, accph = (ti / ACC) & 1;
         if (!(ok = wait_or_abort(&bar_accempty[ab], accph ^ 1, &s_abort, a.err))) break;
         tc_fence_after();
-        const uint32_t d_base = tmem + ab * NPROJ * BN;
+        const uint32_t d = tmem + ab * S::kAccCols + iss * BN;  // this issuer's accumulator
         for (int st = 0; st < nsteps; ++st, ++ai) {
           const int as = ai % SA, aph = (ai / SA) & 1;
           const int bs = ai % SB, bph = (ai / SB) & 1;
@@ -409,22 +423,29 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
           tc_fence_after();
           const uint64_t b_desc0 = sw128_kmajor_desc(smem_u32(sB + bs * kBBytes));
           const uint32_t a_stage = tmem + S::kACol0 + as * S::kACols;
-#pragma unroll
-          for (int p = 0; p < NPROJ; ++p)
+          if constexpr (NPROJ == 2) {  // projection iss, all K steps
 #pragma unroll
             for (int kk = 0; kk < KA; ++kk)
 #pragma unroll
               for (int k = 0; k < BK / 16; ++k)  // K = 16 per MMA: 8 TMEM columns of A, 32 bytes of B
-                umma_f16_ts(d_base + p * BN, a_stage + (p * KA + kk) * 32 + k * 8,
-                            b_desc0 + ((kk * kBTile + k * 32) >> 4), kIdesc, (st | kk | k) != 0);
+                umma_f16_ts(d, a_stage + (iss * KA + kk) * 32 + k * 8, b_desc0 + ((kk * kBTile + k * 32) >> 4),
+                            kIdesc, (st | kk | k) != 0);
+          } else {  // K steps of parity iss into this issuer's partial sum
+#pragma unroll
+            for (int kk = 0; kk < KA; ++kk)
+#pragma unroll
+              for (int k = iss; k < BK / 16; k += 2)
+                umma_f16_ts(d, a_stage + kk * 32 + k * 8, b_desc0 + ((kk * kBTile + k * 32) >> 4), kIdesc,
+                            (st | kk | (k - iss)) != 0);
+          }
           umma_commit(&bar_aempty[as]);
           umma_commit(&bar_bempty[bs]);
         }
         if (ok) umma_commit(&bar_accfull[ab]);
       }
-      umma_commit(&bar_drain);  // all MMAs issued by this thread have completed once it fires
+      umma_commit(&bar_drain[iss]);  // all MMAs issued by this thread have completed once it fires
       volatile int never = 0;
-      wait_or_abort(&bar_drain, 0, &never, nullptr);
+      wait_or_abort(&bar_drain[iss], 0, &never, nullptr);
     }
   } else if (warp < kEpiWarp0) {
     // ================================================= dequantisation -> TMEM
@@ -549,12 +570,12 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
       tc_fence_after();
       const int4 tl = s_tiles[ti];
       const int r = tl.y + q * 32 + lane;  // output row of this thread
-      const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ab * NPROJ * BN;
+      const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ab * S::kAccCols;
       for (int c0 = 0; c0 < BN; c0 += 16) {
         if (c0 >= tl.w) break;  // uniform across the warp
-        uint32_t g[16], u[16];
+        uint32_t g[16], u[16];  // gate / up, or the two partial sums of down
         tmem_ld16(lane_addr + c0, g);
-        if constexpr (NPROJ == 2) tmem_ld16(lane_addr + BN + c0, u);
+        tmem_ld16(lane_addr + BN + c0, u);
         tmem_ld_wait();
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) {
@@ -566,7 +587,7 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
             if (!(fabsf(v) < 65504.0f)) record_error(a.err, kDevFp16Range);
             bits = __half_as_ushort(__float2half_rn(v));
           } else {
-            bits = f32_to_bf16_bits(__uint_as_float(g[jj]));
+            bits = f32_to_bf16_bits(__uint_as_float(g[jj]) + __uint_as_float(u[jj]));
           }
           // h feeds the down GEMM as its k dimension: store it k-permuted like x
           const int col = NPROJ == 2 ? kperm8(r) : r;
@@ -628,8 +649,7 @@ static cudaError_t launch_tc_t(const CUtensorMap& tA0, const CUtensorMap& tA1, c
   // one persistent CTA per SM, enough CTAs that none owns more than kMaxTilesPerCta tiles
   int grid = tiles_upper < sm_count() ? tiles_upper : sm_count();
   if ((tiles_upper + grid - 1) / grid > kMaxTilesPerCta) grid = (tiles_upper + kMaxTilesPerCta - 1) / kMaxTilesPerCta;
-  kern<<<grid, kTcThreadsP, smem, st>>>(tA0, tA1, tB, a);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(kTcThreadsP), smem, st, tA0, tA1, tB, a);
 }
 
 cudaError_t launch_tc_gemm(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
@@ -687,6 +707,8 @@ cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
 // k-permuted within each block of 8 columns like the dequantised weights.
 __global__ void gather_rows_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ perm, int k_div,
                                    uint16_t* __restrict__ out, int hidden, int* err) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int s = blockIdx.x;
   const int token = perm[s] / k_div;
   const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(token) * hidden);
@@ -717,8 +739,7 @@ cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div
                                int num_slots, int hidden, int* err, cudaStream_t st) {
   if (num_slots <= 0) return cudaSuccess;
   const int threads = hidden / 8 < 256 ? ((hidden / 8 + 31) / 32) * 32 : 256;
-  gather_rows_kernel<<<num_slots, threads, 0, st>>>(x, perm, k_div, x_sorted, hidden, err);
-  return cudaGetLastError();
+  return launch_pdl(gather_rows_kernel, dim3(num_slots), dim3(threads), 0, st, x, perm, k_div, x_sorted, hidden, err);
 }
 
 }  // namespace senmoe

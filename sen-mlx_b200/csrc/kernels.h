@@ -123,6 +123,26 @@ cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
                                int num_slots, int hidden, int* err, cudaStream_t st);
 
+// Launch with programmatic dependent launch enabled: the kernel may start
+// while its predecessor in the stream is still running; it must call
+// pdl_wait() (griddepcontrol.wait) before touching the predecessor's output.
+// Works the same inside a CUDA-graph capture.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // Raises a kernel's dynamic shared-memory limit to at least `bytes` on the
 // current device.  Only the first call per (kernel, device, size) reaches the
 // driver, so launches inside a CUDA-graph capture after a warm-up call make

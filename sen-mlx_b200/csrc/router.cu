@@ -30,6 +30,7 @@ constexpr int kMaxTopK = 16;
 template <int VPL>  // 16-byte vectors per lane = ceil(H / 256)
 __global__ void __launch_bounds__(kRouterWarps * 32) router_logits_kernel(RouterArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ __align__(8) uint64_t bar;
   uint4* xs = reinterpret_cast<uint4*>(smem);  // [tile][H/8]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int e = blockIdx.x * kRouterWarps + warp;
@@ -37,19 +38,32 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_logits_kernel(Router
   const int nt = min(kRouterTokTile, a.num_tokens - t0);
   const int vec_per_row = a.hidden / 8;
 
-  for (int i = threadIdx.x; i < nt * vec_per_row; i += blockDim.x)
-    xs[i] = reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t0) * a.hidden)[i];
-  __syncthreads();
-  if (e >= a.num_experts) return;
-
+  // The router weights do not depend on the previous kernel: load them before
+  // waiting for it (programmatic dependent launch).
   float wv[VPL][8];
-  const uint4* wrow = reinterpret_cast<const uint4*>(a.weight + static_cast<size_t>(e) * a.hidden);
+  const uint4* wrow = reinterpret_cast<const uint4*>(a.weight + static_cast<size_t>(e < a.num_experts ? e : 0) *
+                                                                    a.hidden);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const uint4 v = (32 * i + lane < vec_per_row) ? wrow[32 * i + lane] : make_uint4(0, 0, 0, 0);
     wv[i][0] = bf16_lo(v.x); wv[i][1] = bf16_hi(v.x); wv[i][2] = bf16_lo(v.y); wv[i][3] = bf16_hi(v.y);
     wv[i][4] = bf16_lo(v.z); wv[i][5] = bf16_hi(v.z); wv[i][6] = bf16_lo(v.w); wv[i][7] = bf16_hi(v.w);
   }
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_launch_dependents();
+  // the token tile is one contiguous range of x: a single bulk copy
+  if (threadIdx.x == 0) {
+    const uint32_t bytes = static_cast<uint32_t>(nt) * a.hidden * 2;
+    mbar_arrive_expect_tx(&bar, bytes);
+    bulk_g2s(xs, a.x + static_cast<size_t>(t0) * a.hidden, bytes, &bar, policy_evict_last());
+  }
+  if (!mbar_wait(&bar, 0, nullptr)) return;
+  if (e >= a.num_experts) return;
   for (int t = 0; t < nt; ++t) {
     float acc = 0.f;
 #pragma unroll
@@ -73,6 +87,8 @@ template <int EPL>  // experts per lane = ceil(E / 32)
 __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(RouterArgs a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t = blockIdx.x * kTopkWarps + warp;
+  pdl_wait();
+  pdl_launch_dependents();
   if (t >= a.num_tokens) return;
   const float* lg = a.logits + static_cast<size_t>(t) * a.num_experts;
   float p[EPL];
@@ -99,33 +115,30 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(RouterArgs
     p[j] = e < a.num_experts ? round_bf16(p[j] / sum) : -1.0f;
   }
 
-  uint32_t taken = 0;
+  // K rounds of a warp-wide max over packed keys: bf16 score bits (scores are
+  // non-negative, so their bit patterns order like the values) above the
+  // inverted expert id, so the max picks the highest score and, on ties, the
+  // lowest id -- one redux.sync per round.
+  uint32_t key[EPL];
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int e = lane + 32 * j;
+    key[j] = e < a.num_experts ? (static_cast<uint32_t>(f32_to_bf16_bits(p[j])) << 16) | (0xffffu - e) : 0u;
+  }
   float sel_w[kMaxTopK];
   int sel_e[kMaxTopK];
 #pragma unroll
   for (int k = 0; k < kMaxTopK; ++k) {
     if (k >= a.top_k) break;
-    float bv = -2.0f;
-    int be = 0x7fffffff;
+    uint32_t best = 0;
 #pragma unroll
-    for (int j = 0; j < EPL; ++j) {
-      const int e = lane + 32 * j;
-      if (!((taken >> j) & 1u) && (p[j] > bv || (p[j] == bv && e < be))) {
-        bv = p[j];
-        be = e;
-      }
-    }
+    for (int j = 0; j < EPL; ++j) best = max(best, key[j]);
+    best = __reduce_max_sync(0xffffffffu, best);
+    const int be = 0xffff - static_cast<int>(best & 0xffffu);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-      if (ov > bv || (ov == bv && oe < be)) {
-        bv = ov;
-        be = oe;
-      }
-    }
-    if ((be & 31) == lane) taken |= 1u << (be >> 5);
-    sel_w[k] = bv;
+    for (int j = 0; j < EPL; ++j)
+      if (key[j] == best) key[j] = 0u;  // unique: the id is part of the key
+    sel_w[k] = bf16_bits_to_f32(static_cast<uint16_t>(best >> 16));
     sel_e[k] = be;
   }
   if (lane == 0) {
@@ -145,6 +158,8 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(RouterArgs
 }
 
 __global__ void sigmoid_inplace_kernel(float* v, int n) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) v[i] = 1.0f / (1.0f + expf(-v[i]));
 }
@@ -164,8 +179,7 @@ cudaError_t launch_router_logits(const RouterArgs& a, cudaStream_t st) {
   if (vpl == V) {                                                                                          \
     cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(router_logits_kernel<V>), smem);      \
     if (e != cudaSuccess) return e;                                                                        \
-    router_logits_kernel<V><<<grid, kRouterWarps * 32, smem, st>>>(a);                                     \
-    return cudaGetLastError();                                                                             \
+    return launch_pdl(router_logits_kernel<V>, grid, dim3(kRouterWarps * 32), smem, st, a);               \
   }
   SENMOE_RL_CASE(1) SENMOE_RL_CASE(2) SENMOE_RL_CASE(4) SENMOE_RL_CASE(8) SENMOE_RL_CASE(12) SENMOE_RL_CASE(16)
 #undef SENMOE_RL_CASE
@@ -176,11 +190,8 @@ cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st) {
   if (a.num_tokens == 0) return cudaSuccess;
   const int epl = (a.num_experts + 31) / 32;
   dim3 grid((a.num_tokens + kTopkWarps - 1) / kTopkWarps);
-#define SENMOE_TK_CASE(V)                                        \
-  if (epl <= V) {                                                \
-    router_topk_kernel<V><<<grid, kTopkWarps * 32, 0, st>>>(a);  \
-    return cudaGetLastError();                                   \
-  }
+#define SENMOE_TK_CASE(V) \
+  if (epl <= V) return launch_pdl(router_topk_kernel<V>, grid, dim3(kTopkWarps * 32), 0, st, a);
   SENMOE_TK_CASE(1) SENMOE_TK_CASE(2) SENMOE_TK_CASE(4) SENMOE_TK_CASE(8) SENMOE_TK_CASE(16)
 #undef SENMOE_TK_CASE
   return cudaErrorNotSupported;
@@ -188,8 +199,7 @@ cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st) {
 
 cudaError_t launch_sigmoid_inplace(float* v, int n, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  sigmoid_inplace_kernel<<<(n + 255) / 256, 256, 0, st>>>(v, n);
-  return cudaGetLastError();
+  return launch_pdl(sigmoid_inplace_kernel, dim3((n + 255) / 256), dim3(256), 0, st, v, n);
 }
 
 }  // namespace senmoe
