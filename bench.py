@@ -11,6 +11,12 @@ spanning the range of N(0, 0.02) weights), router N(0, 1/sqrt(H)) so logits
 are ~N(0, 1), tokens x ~ N(0, 1): 16.3 GB of packed weights, far larger than
 L2, so every step streams them from HBM (no L2 flush needed).
 
+On N GPUs (torchrun, one rank per GPU) the same 48-layer stack runs expert
+parallel: rank r holds experts [r*128/N, (r+1)*128/N) of every layer, every
+rank takes the same batch, and each layer's combine reads the other ranks'
+expert rows over NVLink (senmoe.ep).  Total work per step is fixed as N grows
+(strong scaling); `value` is the batch's tokens/s.
+
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl senmoe|reference]
 
 `--impl reference` times the CPU restatement of the reference block
@@ -115,20 +121,33 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------- weights
-def make_stack(torch, senmoe, device, layers, max_tokens, seed=0):
-    """Synthetic 48-layer stack in MLX layout on the device."""
+EXPERT_CHUNK = 16  # experts generated per seed: the model is the same for N = 1, 2, 4, 8
+
+
+def make_stack(torch, senmoe, device, layers, max_tokens, seed=0, rank=0, world=1):
+    """Synthetic 48-layer stack in MLX layout on the device: this rank's
+    experts of every layer (all of them on one GPU), the router whole."""
+    from senmoe import ep
     gen = torch.Generator(device=device)
     blocks, keep = [], []
     args = senmoe.MoeArgs(hidden_size=H, moe_intermediate_size=I, n_routed_experts=E, num_experts_per_tok=K,
                           bits=BITS, group_size=G)
+    bnd = ep.expert_bounds(E, world)
+    eb, ee = bnd[rank], bnd[rank + 1]
+    chunk = EXPERT_CHUNK if eb % EXPERT_CHUNK == 0 and ee % EXPERT_CHUNK == 0 else 1
 
-    def proj(rows, cols, gain=1.0):
-        w = torch.randint(-2**31, 2**31 - 1, (E, rows, cols * BITS // 32), generator=gen, device=device,
-                          dtype=torch.int32)
-        # groups of N(0, 0.02) values span about +-0.05: scale ~ 0.1/15, bias ~ -7.5 scale
-        s = (torch.rand((E, rows, cols // G), generator=gen, device=device) * 0.002 + 0.006) * gain
-        b = -(s * 7.5) + torch.randn((E, rows, cols // G), generator=gen, device=device) * (1e-3 * gain)
-        return senmoe.SwitchLinear(w, s.to(torch.bfloat16), b.to(torch.bfloat16))
+    def proj(l, which, rows, cols, gain=1.0):
+        ws, ss, bs = [], [], []
+        for c0 in range(eb, ee, chunk):
+            gen.manual_seed(((seed * 1000 + l) * 4 + which) * 4096 + c0 // chunk)
+            ws.append(torch.randint(-2**31, 2**31 - 1, (chunk, rows, cols * BITS // 32), generator=gen,
+                                    device=device, dtype=torch.int32))
+            # groups of N(0, 0.02) values span about +-0.05: scale ~ 0.1/15, bias ~ -7.5 scale
+            s = (torch.rand((chunk, rows, cols // G), generator=gen, device=device) * 0.002 + 0.006) * gain
+            b = -(s * 7.5) + torch.randn((chunk, rows, cols // G), generator=gen, device=device) * (1e-3 * gain)
+            ss.append(s.to(torch.bfloat16))
+            bs.append(b.to(torch.bfloat16))
+        return senmoe.SwitchLinear(torch.cat(ws), torch.cat(ss), torch.cat(bs))
 
     for l in range(layers):
         gen.manual_seed(seed * 1000 + l)
@@ -136,18 +155,21 @@ def make_stack(torch, senmoe, device, layers, max_tokens, seed=0):
         # The stack has no RMSNorm between blocks (that is the caller's), so the
         # down projection is scaled to keep each block's output small next to
         # the residual stream; routing inputs then stay ~N(0, 1) at every layer.
-        wt = senmoe.MoeWeights(router_weight=rw, gate_proj=proj(I, H), up_proj=proj(I, H),
-                               down_proj=proj(H, I, gain=0.01))
+        wt = senmoe.MoeWeights(router_weight=rw, gate_proj=proj(l, 0, I, H), up_proj=proj(l, 1, I, H),
+                               down_proj=proj(l, 2, H, I, gain=0.01))
         keep.append(wt)
-        blocks.append(senmoe.DeepseekMoe(args, wt, max_tokens=max_tokens, device=device))
+        blocks.append(senmoe.DeepseekMoe(args, wt, max_tokens=max_tokens, device=device, expert_range=(eb, ee)))
+    if world > 1:
+        ep.connect(blocks)
     return blocks, keep
 
 
-def launches_per_forward(T):
-    """Kernels one decode forward launches (router logits + top-k, dispatch,
-    gate/up, down, combine)."""
+def launches_per_forward(T, tensor_cores, world):
+    """Kernels one forward launches: router logits + top-k, dispatch (one
+    kernel up to 2048 pairs, else three), the expert-parallel fence, the
+    gathered-activation copy (tensor-core path), gate/up, down, combine."""
     disp = 1 if (T * K + 1023) // 1024 <= 2 else 3
-    return 2 + disp + 3
+    return 2 + disp + (1 if world > 1 else 0) + (1 if tensor_cores else 0) + 3
 
 
 # --------------------------------------------------------- CPU baseline
@@ -189,7 +211,7 @@ def run_reference(args):
     dt = (time.perf_counter() - t0) / args.steps  # one layer per step
     value = args.batch / (dt * LAYERS)
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": dt * LAYERS * 1e3, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": dt * LAYERS * 1e3, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "u4/bf16 (fp32 accumulate)", "data": "synthetic",
             "impl": "reference",
             "config": {"workload": WORKLOAD, "global_batch": args.batch, "layers": LAYERS},
@@ -231,6 +253,7 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")  # stdout carries only the JSON line
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -250,7 +273,7 @@ def main():
         return float(t.item())
 
     if args.ncu:
-        layers, _keep = make_stack(torch, senmoe, local, args.layers, args.batch, seed=rank)
+        layers, _keep = make_stack(torch, senmoe, local, args.layers, args.batch, rank=rank, world=world)
         x = torch.randn((args.batch, H), device=dev).to(torch.bfloat16)
         for _ in range(args.warmup + args.steps):
             h = x
@@ -261,10 +284,10 @@ def main():
 
     batches = [args.batch] if args.no_sweep else sorted({1, 8, 32, args.batch})
     tmax = max(batches)
-    layers, _keep = make_stack(torch, senmoe, local, args.layers, tmax, seed=rank)
+    layers, _keep = make_stack(torch, senmoe, local, args.layers, tmax, rank=rank, world=world)
     stack = senmoe.MoeStack(layers, tmax, use_graph=True)
     gen = torch.Generator(device=dev)
-    gen.manual_seed(1234 + rank)
+    gen.manual_seed(1234)  # the same tokens on every rank
     x_all = torch.randn((max(tmax, args.prefill_tokens), H), generator=gen, device=dev).to(torch.bfloat16)
 
     def timed_steps(stk, T, steps, warmup):
@@ -332,11 +355,11 @@ def main():
         alg_bytes = sum(n * BYTES_EXPERT + E * H * 2 + 2 * T * H * 2 for n in touched)
         sp = stage_profile(layers, T, 3)
         per_layer_us = {k: round(v / (3 * len(layers)) * 1e3, 2) for k, v in sp.items()}
-        results[T] = {"tokens_per_s": world * T / step, "ms_per_step": step * 1e3,
+        results[T] = {"tokens_per_s": T / step, "ms_per_step": step * 1e3,
                       "expert_kernels": "tcgen05" if layers[0].expert_path(T) == senmoe.PATH_TENSOR_CORE else "gemv",
                       "stage_us_per_layer": per_layer_us,
                       "touched_experts_per_layer": sum(touched) / len(touched),
-                      "hbm_gbs": alg_bytes / step / 1e9, "hbm_frac": alg_bytes / step / 1e9 / hbm_peak}
+                      "hbm_gbs": alg_bytes / step / 1e9, "hbm_frac": alg_bytes / step / 1e9 / (world * hbm_peak)}
         if rank == 0:
             print(f"[bench] batch {T}: {results[T]}", file=sys.stderr, flush=True)
 
@@ -347,7 +370,8 @@ def main():
     touched = touched_per_layer(layers, T)
     launches = nrep * len(layers)
     gate_up_s = stage_ms["gate_up"] / 1e3 / launches
-    gate_up_bytes = sum(n * BYTES_GATE_UP + T * K * (H + I) * 2 for n in touched) / len(touched)
+    # this rank's share of the touched experts and pairs (all of them on one GPU)
+    gate_up_bytes = sum(n * BYTES_GATE_UP + T * K * (H + I) * 2 for n in touched) / len(touched) / world
     achieved = gate_up_bytes / gate_up_s / 1e9
     stage_share = {k: v / max(sum(stage_ms.values()), 1e-12) for k, v in stage_ms.items()}
     if rank == 0:
@@ -358,7 +382,11 @@ def main():
     prefill = None
     if args.prefill_tokens > 0:
         TP = args.prefill_tokens
-        pl = [senmoe.DeepseekMoe(L.args, L.weights, max_tokens=TP, device=local) for L in layers]
+        pl = [senmoe.DeepseekMoe(L.args, L.weights, max_tokens=TP, device=local, expert_range=L.expert_range)
+              for L in layers]
+        if world > 1:
+            from senmoe import ep
+            ep.connect(pl)
         pstack = senmoe.MoeStack(pl, TP, use_graph=True)
         psteps = max(2, min(args.steps, 5))
         secs = timed_steps(pstack, TP, psteps, args.warmup)
@@ -368,9 +396,9 @@ def main():
         gu_s = pst["gate_up"] / 1e3 / (2 * len(pl))
         dn_s = pst["down"] / 1e3 / (2 * len(pl))
         peak_t = tensor_peak()
-        prefill = {"tokens": TP, "tokens_per_s": world * TP / step, "ms_per_step": step * 1e3,
+        prefill = {"tokens": TP, "tokens_per_s": TP / step, "ms_per_step": step * 1e3,
                    "tflops": flops_layer * len(pl) / step / 1e12,
-                   "frac": flops_layer * len(pl) / step / 1e12 / peak_t[0],
+                   "frac": flops_layer * len(pl) / step / 1e12 / (world * peak_t[0]),
                    "gate_up_tflops": TP * K * 4 * H * I / gu_s / 1e12,
                    "down_tflops": TP * K * 2 * H * I / dn_s / 1e12,
                    "peak_tflops": peak_t[0], "peak_source": peak_t[1],
@@ -403,11 +431,12 @@ def main():
     head = results[args.batch]
     line = {
         "metric": METRIC, "value": head["tokens_per_s"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "u4 weights / bf16 activations (fp32 accumulate)",
         "data": "synthetic (random-init 4-bit MLX-layout weights, x ~ N(0,1))",
-        "config": {"workload": WORKLOAD, "global_batch": args.batch * world, "per_gpu_batch": args.batch,
-                   "layers": args.layers, "parallelism": "replicas" if world > 1 else "single",
+        "config": {"workload": WORKLOAD, "global_batch": args.batch, "layers": args.layers,
+                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "experts_per_gpu": E // world,
                    "l2": "weights 16.3 GB per step >> 126 MB L2 (no flush needed)", "cuda_graph": True},
         "sweep": {str(t): r for t, r in results.items()},
         "roofline": {"bound": "hbm", "kernel": "expert gate/up (+SwiGLU)", "achieved": achieved, "peak": hbm_peak,
@@ -417,9 +446,10 @@ def main():
                      "step_hbm_gbs": head["hbm_gbs"], "step_frac": head["hbm_gbs"] / hbm_peak},
         "stage_share": stage_share,
         "prefill": prefill,
-        "gpu_launches": launches_per_forward(args.batch) * args.layers * args.steps,
+        "gpu_launches": launches_per_forward(args.batch, head["expert_kernels"] == "tcgen05", world) * args.layers
+        * args.steps,
         "clocks": clocks,
-        "e2e": {"value": world * args.batch / e2e_s, "unit": UNIT, "h2d_bytes_per_step": args.batch * H * 2,
+        "e2e": {"value": args.batch / e2e_s, "unit": UNIT, "h2d_bytes_per_step": args.batch * H * 2,
                 "d2h_bytes_per_step": args.batch * H * 2, "api": "senmoe.MoeStack.forward(host tensor)"},
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

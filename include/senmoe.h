@@ -164,6 +164,42 @@ int senmoe_layer_expert_path(const SenMoeLayer* layer, int64_t num_tokens);
  * device since the previous check (bad expert index, timed-out wait). */
 int senmoe_layer_check(SenMoeLayer* layer, senmoe_stream_t stream);
 
+/* ---- Expert parallelism (no counterpart in the reference, which runs the
+ * block on one Apple GPU).  One process per GPU; rank r creates its layer with
+ * expert_begin/expert_end set to its contiguous block of experts (rank order
+ * = expert order) and weight tensors holding only those experts, all ranks
+ * with the same config otherwise.  Each rank publishes its SenMoePeerInfo,
+ * the host exchanges them (e.g. torch.distributed all_gather), and every rank
+ * connects with the full table.  After that, forward on every rank takes the
+ * SAME tokens x (replicated), and every rank returns the same y: each rank
+ * computes only its experts' rows and the combine reads every row from its
+ * owner over NVLink (CUDA IPC mappings), in slot order, with the one-GPU
+ * combine's arithmetic.  All ranks must run the same sequence of forwards
+ * (same num_tokens); a rank that does not shows up as SENMOE_ERR_TIMEOUT from
+ * senmoe_layer_check on the others (every cross-GPU wait is bounded). */
+#define SENMOE_MAX_RANKS 8
+
+typedef struct SenMoePeerInfo {
+  uint8_t ipc_handle[64];  /* cudaIpcMemHandle_t of the layer's scratch arena */
+  int64_t rows_offset;     /* byte offset of the expert-output rows in the arena */
+  int64_t flags_offset;    /* byte offset of the rank flag block in the arena */
+  int64_t arena_bytes;     /* arena size (must match on every rank) */
+  int32_t expert_begin;
+  int32_t expert_end;
+  int32_t device;          /* CUDA ordinal in the publishing process (diagnostics) */
+  int32_t reserved;
+} SenMoePeerInfo;
+
+/* This rank's table entry. */
+int senmoe_layer_peer_info(const SenMoeLayer* layer, SenMoePeerInfo* out);
+
+/* Opens the peers' arenas and switches forward to the expert-parallel form.
+ * peers[r] is rank r's entry, r < world_size <= SENMOE_MAX_RANKS; the expert
+ * ranges must tile [0, n_routed_experts) in rank order and peers[rank] must be
+ * this layer's own entry.  world_size == 1 is allowed (no peers).  Call once,
+ * with no forward of the layer in flight; the mappings close on destroy. */
+int senmoe_layer_connect_peers(SenMoeLayer* layer, int32_t rank, int32_t world_size, const SenMoePeerInfo* peers);
+
 /* Router alone: ids/weights [T, K] for x [T, H] (bf16), router weight
  * [E, H] (bf16).  Same rounding and slot order as the layer. */
 int senmoe_router(const void* x, int64_t num_tokens, const void* router_weight, int32_t hidden,

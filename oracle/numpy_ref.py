@@ -73,12 +73,16 @@ def gather_qmm(x_bits, wq, s, b, idx, group: int = 64, bits: int = 4) -> np.ndar
     return bf16_bits(out.astype(np.float32))
 
 
-def moe_forward(cfg, w, x_bits, mode: int = 0):
-    """cfg/w: oracle.MoeConfig / oracle.MoeWeights.  Same outputs as the C oracle."""
-    R = rbf if mode == 0 else (lambda a: np.asarray(a, dtype=np.float32))
-    H, E, K, I = cfg.hidden, cfg.num_experts, cfg.top_k, cfg.intermediate
-    x = bf16_val(x_bits).reshape(-1, H)
-    T = x.shape[0]
+def rounding(mode: int):
+    """The rounding applied at the MLX graph's bf16 points (mode 0) or none (mode 1)."""
+    return rbf if mode == 0 else (lambda a: np.asarray(a, dtype=np.float32))
+
+
+def route(cfg, w, x, mode: int = 0):
+    """Router of deepseek_v2.rs:526-543 for x [T, H] fp32 (bf16 values):
+    returns (ids [T, K] int32, weights [T, K] fp32)."""
+    R = rounding(mode)
+    E, K = cfg.num_experts, cfg.top_k
     logits = R((x.astype(np.float64) @ bf16_val(w.router_w).astype(np.float64).T).astype(np.float32))
     m = logits.max(-1, keepdims=True)
     ex = np.exp(logits - m).astype(np.float32)
@@ -91,32 +95,52 @@ def moe_forward(cfg, w, x_bits, mode: int = 0):
         wts = (wts / den).astype(np.float32)
     if abs(cfg.routed_scaling_factor - 1.0) > 1.1920929e-7:
         wts = (wts * np.float32(cfg.routed_scaling_factor)).astype(np.float32)
+    return ids, wts
+
+
+def expert_mlp(xr, gd, ud, dd, mode: int = 0) -> np.ndarray:
+    """One SwitchGlu expert on one token (deepseek_v2.rs:443-462): x row fp64,
+    dequantised gate/up/down fp64; returns the down output (bf16 values, fp32)."""
+    R = rounding(mode)
+    g = R((gd @ xr).astype(np.float32))
+    u = R((ud @ xr).astype(np.float32))
+    sg = R((1.0 / (1.0 + np.exp(-g.astype(np.float32)))).astype(np.float32))
+    h = R(R(g * sg) * u)
+    return R((dd @ h.astype(np.float64)).astype(np.float32))
+
+
+def shared_out(cfg, w, x, mode: int = 0) -> np.ndarray:
+    """gate_t * shared_mlp(x_t) per token (deepseek_v2.rs:550-552), fp32 [T, H]."""
+    sg_d = dequantize(w.sh_gate_w, w.sh_gate_s, w.sh_gate_b, cfg.group_size, cfg.bits).astype(np.float64)
+    su_d = dequantize(w.sh_up_w, w.sh_up_s, w.sh_up_b, cfg.group_size, cfg.bits).astype(np.float64)
+    sd_d = dequantize(w.sh_down_w, w.sh_down_s, w.sh_down_b, cfg.group_size, cfg.bits).astype(np.float64)
+    out = np.zeros((x.shape[0], cfg.hidden), dtype=np.float32)
+    for t in range(x.shape[0]):
+        gate = np.float32(1.0)
+        if cfg.shared_gate:
+            a = float(x[t].astype(np.float64) @ bf16_val(w.sh_gate_vec).astype(np.float64))
+            gate = np.float32(1.0 / (1.0 + np.exp(-np.float32(a))))
+        out[t] = gate * expert_mlp(x[t].astype(np.float64), sg_d, su_d, sd_d, mode)
+    return out
+
+
+def moe_forward(cfg, w, x_bits, mode: int = 0):
+    """cfg/w: oracle.MoeConfig / oracle.MoeWeights.  Same outputs as the C oracle."""
+    H, K = cfg.hidden, cfg.top_k
+    x = bf16_val(x_bits).reshape(-1, H)
+    T = x.shape[0]
+    ids, wts = route(cfg, w, x, mode)
     g_d = dequantize(w.gate_w, w.gate_s, w.gate_b, cfg.group_size, cfg.bits).astype(np.float64)
     u_d = dequantize(w.up_w, w.up_s, w.up_b, cfg.group_size, cfg.bits).astype(np.float64)
     d_d = dequantize(w.down_w, w.down_s, w.down_b, cfg.group_size, cfg.bits).astype(np.float64)
-
-    def mlp(xr, gd, ud, dd):
-        g = R((gd @ xr).astype(np.float32))
-        u = R((ud @ xr).astype(np.float32))
-        sg = R((1.0 / (1.0 + np.exp(-g.astype(np.float32)))).astype(np.float32))
-        h = R(R(g * sg) * u)
-        return R((dd @ h.astype(np.float64)).astype(np.float32))
-
     y = np.zeros((T, H), dtype=np.float32)
     for t in range(T):
         acc = np.zeros(H, dtype=np.float32)
         for j in range(K):
             e = ids[t, j]
-            acc = (acc + mlp(x[t].astype(np.float64), g_d[e], u_d[e], d_d[e]) * wts[t, j]).astype(np.float32)
+            acc = (acc + expert_mlp(x[t].astype(np.float64), g_d[e], u_d[e], d_d[e], mode) * wts[t, j]).astype(
+                np.float32)
         y[t] = acc
     if cfg.shared_intermediate:
-        sg_d = dequantize(w.sh_gate_w, w.sh_gate_s, w.sh_gate_b, cfg.group_size, cfg.bits).astype(np.float64)
-        su_d = dequantize(w.sh_up_w, w.sh_up_s, w.sh_up_b, cfg.group_size, cfg.bits).astype(np.float64)
-        sd_d = dequantize(w.sh_down_w, w.sh_down_s, w.sh_down_b, cfg.group_size, cfg.bits).astype(np.float64)
-        for t in range(T):
-            gate = np.float32(1.0)
-            if cfg.shared_gate:
-                a = float(x[t].astype(np.float64) @ bf16_val(w.sh_gate_vec).astype(np.float64))
-                gate = np.float32(1.0 / (1.0 + np.exp(-np.float32(a))))
-            y[t] = (y[t] + gate * mlp(x[t].astype(np.float64), sg_d, su_d, sd_d)).astype(np.float32)
+        y = (y + shared_out(cfg, w, x, mode)).astype(np.float32)
     return dict(y_f32=y, y_bf16=bf16_bits(y), ids=ids, weights=wts)

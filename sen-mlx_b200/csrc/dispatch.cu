@@ -6,7 +6,8 @@
 // of pair indices p = t*K + j by expert id, giving
 //   offsets[e] .. offsets[e+1]   the slots of expert e,
 //   perm[slot]                   the pair in that slot (ascending p within e),
-//   inverse[p]                   the slot of pair p (-1 if e is not local),
+//   inverse[p]                   the slot of pair p (-1 if e is not local,
+//                                unless keep_remote_slots is set),
 //   active[0 .. active_count)    local experts that received pairs, ascending.
 // The result depends only on topk_ids: counts are integer atomics (order-free)
 // and ranks inside a 1024-pair chunk come from warp match masks plus
@@ -101,7 +102,7 @@ __device__ void place_chunk(const DispatchArgs& a, int chunk, int* cursor, int* 
   if (e >= 0) {
     const int slot = whist[warp * E + e] + rank;
     a.perm[slot] = p;
-    a.inverse[p] = (e >= a.expert_begin && e < a.expert_end) ? slot : -1;
+    a.inverse[p] = (a.keep_remote_slots || (e >= a.expert_begin && e < a.expert_end)) ? slot : -1;
   } else if (p < a.num_pairs) {
     a.inverse[p] = -1;  // rejected id: the combine skips the pair
   }

@@ -1,0 +1,182 @@
+// ep.cu -- expert parallelism over NVLink peer memory.
+//
+// The reference runs the MoE block on one GPU (deepseek_v2.rs:520-553); here
+// its experts are split across the GPUs of one node, contiguous blocks of
+// experts per rank.  Every rank holds the same tokens, runs the router and
+// the full dispatch itself (both are deterministic, so every rank computes
+// the same global slot order), and runs the expert products of its own
+// experts only, writing their rows at their global slots of its `d` buffer.
+// The weighted combine then reads each (token, slot) pair's row from the
+// rank that owns the pair's expert, through CUDA IPC mappings of the peers'
+// buffers, and sums the slots in order exactly as the one-GPU combine does,
+// so every rank ends with the same y.
+//
+// Two rank flags per layer order the exchange, both in the flag block of
+// each rank's arena and both holding a call epoch:
+//   ready[r]  rank r's expert rows of epoch e are complete (written by r's
+//             combine kernel into every peer's block before it reads);
+//   done[r]   rank r has finished reading its peers' rows of epoch e (written
+//             by the last CTA of r's combine).
+// A rank waits for done[*] >= e - 1 before its expert kernels overwrite d
+// (ep_fence_kernel) and for ready[*] >= e before reading (ep_combine_kernel).
+// Every wait is bounded: on timeout the kernel records kDevPeerTimeout and
+// continues, so a missing peer turns into a status the host reads, never a
+// hung GPU.
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace senmoe {
+
+namespace {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Spins until *flag >= want (wrap-safe) or the cycle limit passes.  Once a
+// peer wait has run out (*err == kDevPeerTimeout) later waits give up at
+// once, so a missing rank costs one limit, not one per CTA and layer.
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t want, const int* err) {
+  const long long t0 = clock64();
+  while (static_cast<int32_t>(ld_acquire_sys(flag) - want) < 0) {
+    if (clock64() - t0 > kWaitLimitCycles || *reinterpret_cast<const volatile int*>(err) == kDevPeerTimeout)
+      return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+
+__global__ void ep_fence_kernel(EpArgs a) {
+  __shared__ uint32_t s_epoch;
+  if (threadIdx.x == 0) {
+    const uint32_t e = *a.epoch + 1u;
+    *a.epoch = e;
+    s_epoch = e;
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  const int r = threadIdx.x;
+  if (r < a.world && r != a.rank) {
+    if (!wait_flag(a.flags + kEpDoneOffset + r, s_epoch - 1u, a.err)) record_error(a.err, kDevPeerTimeout);
+  }
+  pdl_wait();  // the expert kernels after this one wait on it, and through it on dispatch
+}
+
+// Expert-rows owner of expert e: the rank r with bounds[r] <= e < bounds[r+1].
+__device__ __forceinline__ int owner_of(const EpArgs& a, int e) {
+  int r = 0;
+#pragma unroll
+  for (int i = 1; i < kEpMaxRanks; ++i) r += (i < a.world && e >= a.bounds[i]) ? 1 : 0;
+  return r;
+}
+
+// y[t, :] = bf16( sum_j f32(d_owner(j)[inv[t*K + j], :]) * w[t, j]  (+ gate_t * shared[t, :]) (+ residual) )
+// with the one-GPU combine's arithmetic and slot order.  Grid: x covers the
+// hidden columns (8 per thread), y strides over tokens.
+__global__ void __launch_bounds__(256) ep_combine_kernel(EpArgs a, CombineArgs c, int num_tokens) {
+  pdl_wait();  // d, ids, inverse and weights of this call are complete
+  pdl_launch_dependents();
+  const uint32_t epoch = *a.epoch;
+  const int r = threadIdx.x;
+  if (r < a.world) {
+    // announce this rank's rows (d is complete: the producing grids finished)
+    __threadfence_system();
+    st_release_sys(a.peer_flags[r] + kEpReadyOffset + a.rank, epoch);
+    if (!wait_flag(a.flags + kEpReadyOffset + r, epoch, a.err)) record_error(a.err, kDevPeerTimeout);
+  }
+  __syncthreads();
+
+  const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  constexpr int kMaxK = 16;
+  if (col < c.hidden) {
+    for (int t = blockIdx.y; t < num_tokens; t += gridDim.y) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      const uint16_t* src[kMaxK];
+      float wj[kMaxK];
+#pragma unroll
+      for (int j = 0; j < kMaxK; ++j) {
+        src[j] = nullptr;
+        if (j < c.top_k) {
+          const int p = t * c.top_k + j;
+          const int slot = c.inverse[p];
+          wj[j] = c.weights[p];
+          if (slot >= 0) {
+            const int e = a.topk_ids[p];
+            src[j] = a.peer_d[owner_of(a, e)] + static_cast<size_t>(slot) * c.hidden + col;
+          }
+        }
+      }
+      uint4 rows[kMaxK];
+#pragma unroll
+      for (int j = 0; j < kMaxK; ++j)
+        if (src[j]) rows[j] = __ldcg(reinterpret_cast<const uint4*>(src[j]));
+#pragma unroll
+      for (int j = 0; j < kMaxK; ++j) {
+        if (src[j]) {
+          const uint4 v = rows[j];
+          const float w = wj[j];
+          acc[0] += bf16_lo(v.x) * w; acc[1] += bf16_hi(v.x) * w;
+          acc[2] += bf16_lo(v.y) * w; acc[3] += bf16_hi(v.y) * w;
+          acc[4] += bf16_lo(v.z) * w; acc[5] += bf16_hi(v.z) * w;
+          acc[6] += bf16_lo(v.w) * w; acc[7] += bf16_hi(v.w) * w;
+        }
+      }
+      if (c.shared_out) {
+        const float g = c.shared_gate ? c.shared_gate[t] : 1.0f;
+        const uint4 v = *reinterpret_cast<const uint4*>(c.shared_out + static_cast<size_t>(t) * c.hidden + col);
+        acc[0] += g * bf16_lo(v.x); acc[1] += g * bf16_hi(v.x);
+        acc[2] += g * bf16_lo(v.y); acc[3] += g * bf16_hi(v.y);
+        acc[4] += g * bf16_lo(v.z); acc[5] += g * bf16_hi(v.z);
+        acc[6] += g * bf16_lo(v.w); acc[7] += g * bf16_hi(v.w);
+      }
+      if (c.residual) {
+        const uint4 v = *reinterpret_cast<const uint4*>(c.residual + static_cast<size_t>(t) * c.hidden + col);
+        acc[0] += bf16_lo(v.x); acc[1] += bf16_hi(v.x); acc[2] += bf16_lo(v.y); acc[3] += bf16_hi(v.y);
+        acc[4] += bf16_lo(v.z); acc[5] += bf16_hi(v.z); acc[6] += bf16_lo(v.w); acc[7] += bf16_hi(v.w);
+      }
+      uint4 o;
+      o.x = uint32_t(f32_to_bf16_bits(acc[0])) | (uint32_t(f32_to_bf16_bits(acc[1])) << 16);
+      o.y = uint32_t(f32_to_bf16_bits(acc[2])) | (uint32_t(f32_to_bf16_bits(acc[3])) << 16);
+      o.z = uint32_t(f32_to_bf16_bits(acc[4])) | (uint32_t(f32_to_bf16_bits(acc[5])) << 16);
+      o.w = uint32_t(f32_to_bf16_bits(acc[6])) | (uint32_t(f32_to_bf16_bits(acc[7])) << 16);
+      *reinterpret_cast<uint4*>(c.y + static_cast<size_t>(t) * c.hidden + col) = o;
+    }
+  }
+
+  // The last CTA to finish tells every peer that this rank is done reading.
+  __shared__ bool s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t total = gridDim.x * gridDim.y;
+    s_last = atomicAdd(a.finished, 1u) == total - 1u;
+  }
+  __syncthreads();
+  if (s_last) {
+    if (threadIdx.x == 0) *a.finished = 0u;
+    if (r < a.world) st_release_sys(a.peer_flags[r] + kEpDoneOffset + a.rank, epoch);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_ep_fence(const EpArgs& a, cudaStream_t st) {
+  return launch_pdl(ep_fence_kernel, dim3(1), dim3(32), 0, st, a);
+}
+
+cudaError_t launch_ep_combine(const EpArgs& a, const CombineArgs& c, int num_tokens, cudaStream_t st) {
+  const int threads = 256;
+  const int gx = (c.hidden / 8 + threads - 1) / threads;
+  // enough CTAs to cover the tokens of a decode batch in one wave; larger
+  // batches loop (each CTA announces and waits once)
+  const int gy = num_tokens < 1024 ? num_tokens : 1024;
+  return launch_pdl(ep_combine_kernel, dim3(gx, gy), dim3(threads), 0, st, a, c, num_tokens);
+}
+
+}  // namespace senmoe

@@ -706,10 +706,12 @@ cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
 // Slot-ordered fp16 copy of the token rows (bf16 -> fp16 is exact in range),
 // k-permuted within each block of 8 columns like the dequantised weights.
 __global__ void gather_rows_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ perm, int k_div,
-                                   uint16_t* __restrict__ out, int hidden, int* err) {
+                                   uint16_t* __restrict__ out, int hidden, int* err,
+                                   const int32_t* __restrict__ offsets, int eb, int ee) {
   pdl_wait();
   pdl_launch_dependents();
   const int s = blockIdx.x;
+  if (offsets && (s < offsets[eb] || s >= offsets[ee])) return;  // another rank's slot
   const int token = perm[s] / k_div;
   const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(token) * hidden);
   uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(s) * hidden);
@@ -736,10 +738,12 @@ __global__ void gather_rows_kernel(const uint16_t* __restrict__ x, const int32_t
 }
 
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
-                               int num_slots, int hidden, int* err, cudaStream_t st) {
+                               int num_slots, int hidden, int* err, cudaStream_t st,
+                               const int32_t* offsets, int eb, int ee) {
   if (num_slots <= 0) return cudaSuccess;
   const int threads = hidden / 8 < 256 ? ((hidden / 8 + 31) / 32) * 32 : 256;
-  return launch_pdl(gather_rows_kernel, dim3(num_slots), dim3(threads), 0, st, x, perm, k_div, x_sorted, hidden, err);
+  return launch_pdl(gather_rows_kernel, dim3(num_slots), dim3(threads), 0, st, x, perm, k_div, x_sorted, hidden, err,
+                    offsets, eb, ee);
 }
 
 }  // namespace senmoe

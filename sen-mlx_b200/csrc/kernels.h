@@ -15,6 +15,7 @@ enum DeviceError : int {
   kDevWaitTimeout = 2,  // a bounded mbarrier wait ran out
   kDevFp16Range = 3,    // an activation outside fp16 range met the tensor-core path
   kDevTileOverflow = 4, // a persistent CTA was handed more tiles than it can list
+  kDevPeerTimeout = 5,  // a bounded wait on another rank's flag ran out
 };
 
 // ---------------------------------------------------------------- router
@@ -45,6 +46,7 @@ struct DispatchArgs {
   int32_t* active_count;    // [1]
   int32_t* chunk_hist;      // [nchunks, E] scratch (large dispatch only)
   int* err;
+  int keep_remote_slots;    // 1: inverse keeps the slot of non-local experts too
 };
 constexpr int kDispatchChunk = 1024;
 cudaError_t launch_dispatch(const DispatchArgs& a, cudaStream_t st);
@@ -120,8 +122,34 @@ cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
                          bool swizzle128);
 // x_sorted[s, :] = fp16(x[perm[s] / k_div, :]) for s < num_slots (x bf16, rows of
 // `hidden`); a value outside fp16 range records kDevFp16Range in *err.
+// With `offsets` non-null only the slots of experts [eb, ee), i.e. slots
+// offsets[eb] .. offsets[ee], are gathered.
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
-                               int num_slots, int hidden, int* err, cudaStream_t st);
+                               int num_slots, int hidden, int* err, cudaStream_t st,
+                               const int32_t* offsets = nullptr, int eb = 0, int ee = 0);
+
+// ------------------------------------------------- expert parallelism
+constexpr int kEpMaxRanks = 8;
+constexpr int kEpReadyOffset = 0;   // u32 index of ready[0] in a rank's flag block
+constexpr int kEpDoneOffset = 8;    // u32 index of done[0]
+constexpr size_t kEpFlagBytes = 64; // ready[8], done[8]
+struct EpArgs {
+  int rank, world;
+  int bounds[kEpMaxRanks + 1];         // rank r owns experts [bounds[r], bounds[r+1])
+  const uint16_t* peer_d[kEpMaxRanks]; // expert rows [P, H] of each rank, mapped here (own included)
+  uint32_t* peer_flags[kEpMaxRanks];   // flag block of each rank, mapped here (own included)
+  uint32_t* flags;                     // this rank's flag block
+  uint32_t* epoch;                     // this rank's call counter
+  uint32_t* finished;                  // combine CTA completion counter
+  const int32_t* topk_ids;             // [T*K]
+  int* err;
+};
+// Waits (bounded) until every peer has finished reading this rank's rows of
+// the previous call; advances the call epoch.  Launch before the expert kernels.
+cudaError_t launch_ep_fence(const EpArgs& a, cudaStream_t st);
+// Announces this rank's rows, waits (bounded) for every peer's, and runs the
+// weighted combine reading each pair's row from its owner (CombineArgs.d unused).
+cudaError_t launch_ep_combine(const EpArgs& a, const CombineArgs& c, int num_tokens, cudaStream_t st);
 
 // Launch with programmatic dependent launch enabled: the kernel may start
 // while its predecessor in the stream is still running; it must call

@@ -115,6 +115,15 @@ struct SenMoeLayer {
   uint16_t* h16 = nullptr;       // fp16 [Tmax*K, I] SwiGLU output (B operand of the down GEMM)
   CUtensorMap tm_gate{}, tm_up{}, tm_down{};  // packed codes, [rows, words]
   CUtensorMap tm_xs[4]{}, tm_h[4]{};          // activation tiles per token-tile width
+  // expert parallelism (senmoe_layer_connect_peers)
+  size_t arena_bytes = 0, o_d = 0, o_flags = 0;
+  uint32_t* ep_flags = nullptr;  // ready[8], done[8]: written by peers
+  uint32_t* ep_local = nullptr;  // [0] call epoch, [1] combine CTA counter
+  int ep_world = 0, ep_rank = 0; // ep_world 0: not connected
+  int ep_bounds[kEpMaxRanks + 1] = {};
+  const uint16_t* ep_peer_d[kEpMaxRanks] = {};
+  uint32_t* ep_peer_flags[kEpMaxRanks] = {};
+  void* ep_opened[kEpMaxRanks] = {};  // IPC mappings to close
   // per-stage timing
   bool profiling = false;
   bool profiled_once = false;
@@ -222,7 +231,7 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                o_err = take(4), o_hist = take(size_t(L->nchunks_max) * E * 4), o_h = take(P * I * 2),
                o_d = take(P * H * 2), o_shh = take(Is ? T * Is * 2 : 0), o_sho = take(Is ? T * H * 2 : 0),
                o_shg = take(Is ? T * 4 : 0), o_zero = take(Is ? T * 4 : 0), o_xs = take(P * H * 2),
-               o_h16 = take(P * I * 2);
+               o_h16 = take(P * I * 2), o_flags = take(kEpFlagBytes), o_local = take(8);
   cudaError_t e = cudaMalloc(&L->arena, off);
   if (e != cudaSuccess) {
     delete L;
@@ -250,6 +259,11 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
   }
   L->xs = reinterpret_cast<uint16_t*>(base + o_xs);
   L->h16 = reinterpret_cast<uint16_t*>(base + o_h16);
+  L->ep_flags = reinterpret_cast<uint32_t*>(base + o_flags);
+  L->ep_local = reinterpret_cast<uint32_t*>(base + o_local);
+  L->arena_bytes = off;
+  L->o_d = o_d;
+  L->o_flags = o_flags;
   {  // tensor maps for the tcgen05 path (host-side encoding only)
     const int bits = c.bits, El = c.expert_end - c.expert_begin;
     const uint64_t gw = uint64_t(H) * bits / 32, dw = uint64_t(I) * bits / 32;
@@ -291,6 +305,8 @@ int senmoe_layer_destroy(SenMoeLayer* layer) {
   cudaSetDevice(layer->device);
   for (auto& ev : layer->ev)
     if (ev) cudaEventDestroy(ev);
+  for (void* p : layer->ep_opened)
+    if (p) cudaIpcCloseMemHandle(p);
   cudaError_t e = cudaFree(layer->arena);
   cudaSetDevice(cur);
   delete layer;
@@ -302,6 +318,9 @@ int senmoe_layer_destroy(SenMoeLayer* layer) {
 static bool uses_tensor_cores(const SenMoeLayer* L, int64_t pairs) {
   const SenMoeConfig& c = L->cfg;
   const int64_t e_local = c.expert_end - c.expert_begin;
+  // expert-parallel ranks see only their experts' share of the pairs
+  if (L->ep_world > 0) pairs = pairs * e_local / c.n_routed_experts;
+  if (pairs < 1) pairs = 1;
   const double per_expert = double(pairs) / double(pairs < e_local ? pairs : e_local);
   const int path = c.reserved[0];
   return L->tc_ok && (path == kPathTensorCore || (path == kPathAuto && per_expert >= kTcMinTokensPerExpert));
@@ -364,16 +383,38 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   da.active_count = L->active_count;
   da.chunk_hist = L->chunk_hist;
   da.err = L->err;
+  const bool ep = L->ep_world > 0;
+  da.keep_remote_slots = ep ? 1 : 0;  // the combine reads remote slots from their owners
   SENMOE_CUDA(launch_dispatch(da, st));
+  EpArgs ea{};
+  if (ep) {
+    ea.rank = L->ep_rank;
+    ea.world = L->ep_world;
+    for (int r = 0; r <= L->ep_world; ++r) ea.bounds[r] = L->ep_bounds[r];
+    for (int r = 0; r < L->ep_world; ++r) {
+      ea.peer_d[r] = L->ep_peer_d[r];
+      ea.peer_flags[r] = L->ep_peer_flags[r];
+    }
+    ea.flags = L->ep_flags;
+    ea.epoch = L->ep_local;
+    ea.finished = L->ep_local + 1;
+    ea.topk_ids = L->ids;
+    ea.err = L->err;
+    // d is about to be overwritten: wait until the peers have read the last call's rows
+    SENMOE_CUDA(launch_ep_fence(ea, st));
+  }
 
   // 3-4. expert products over the touched local experts: h [P, I], d [P, H]
   const int E_local = c.expert_end - c.expert_begin;
   const int max_items = P < E_local ? P : E_local;
-  const double per_expert = double(P) / double(max_items);
+  int64_t P_est = ep ? int64_t(P) * E_local / E : P;  // expected local pairs (as uses_tensor_cores)
+  if (P_est < 1) P_est = 1;
+  const double per_expert = double(P_est) / double(P_est < E_local ? P_est : E_local);
   const bool use_tc = uses_tensor_cores(L, P);
   if (use_tc) {
     const int ti = tc_tile_index(per_expert), bn = kTcTiles[ti];
-    SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st));
+    SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
+                                   ep ? L->offsets : nullptr, c.expert_begin, c.expert_end));
     SENMOE_CUDA(mark(2));
     TcGemmArgs ga{};
     ga.s[0] = static_cast<const uint16_t*>(L->w.gate_scales);
@@ -508,7 +549,10 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   ca.y_f32 = nullptr;
   ca.hidden = H;
   ca.top_k = K;
-  SENMOE_CUDA(launch_combine(ca, T, st));
+  if (ep)
+    SENMOE_CUDA(launch_ep_combine(ea, ca, T, st));
+  else
+    SENMOE_CUDA(launch_combine(ca, T, st));
   SENMOE_CUDA(mark(6));
   if (profile) L->profiled_once = true;
 
@@ -582,11 +626,91 @@ int senmoe_layer_check(SenMoeLayer* L, senmoe_stream_t stream) {
     SENMOE_CUDA(cudaStreamSynchronize(st));
     if (host_err == kDevBadExpert) return fail(SENMOE_ERR_DEVICE, "a kernel saw an expert id outside [0, E)");
     if (host_err == kDevWaitTimeout) return fail(SENMOE_ERR_TIMEOUT, "a bounded device-side wait ran out");
+    if (host_err == kDevPeerTimeout)
+      return fail(SENMOE_ERR_TIMEOUT, "a wait for another expert-parallel rank ran out (a rank missed a forward, "
+                                      "or ran a different sequence of forwards)");
     if (host_err == kDevFp16Range)
       return fail(SENMOE_ERR_DEVICE, "an activation outside fp16 range reached the tensor-core path (use the "
                                      "CUDA-core path, expert path 1, for such inputs)");
     return fail(SENMOE_ERR_DEVICE, "device error code %d", host_err);
   }
+  return SENMOE_OK;
+}
+
+int senmoe_layer_peer_info(const SenMoeLayer* L, SenMoePeerInfo* out) {
+  g_last_error.clear();
+  if (!L || !out) return fail(SENMOE_ERR_BAD_ARG, "layer or out is NULL");
+  static_assert(sizeof(cudaIpcMemHandle_t) == sizeof(out->ipc_handle), "IPC handle size");
+  int cur = 0;
+  SENMOE_CUDA(cudaGetDevice(&cur));
+  SENMOE_CUDA(cudaSetDevice(L->device));
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, L->arena);
+  cudaSetDevice(cur);
+  if (e != cudaSuccess) return fail(SENMOE_ERR_CUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  std::memset(out, 0, sizeof(*out));
+  std::memcpy(out->ipc_handle, &h, sizeof(h));
+  out->rows_offset = static_cast<int64_t>(L->o_d);
+  out->flags_offset = static_cast<int64_t>(L->o_flags);
+  out->arena_bytes = static_cast<int64_t>(L->arena_bytes);
+  out->expert_begin = L->cfg.expert_begin;
+  out->expert_end = L->cfg.expert_end;
+  out->device = L->device;
+  return SENMOE_OK;
+}
+
+int senmoe_layer_connect_peers(SenMoeLayer* L, int32_t rank, int32_t world_size, const SenMoePeerInfo* peers) {
+  g_last_error.clear();
+  if (!L || !peers) return fail(SENMOE_ERR_BAD_ARG, "layer or peers is NULL");
+  if (L->ep_world) return fail(SENMOE_ERR_BAD_ARG, "layer is already connected");
+  if (world_size < 1 || world_size > kEpMaxRanks || rank < 0 || rank >= world_size)
+    return fail(SENMOE_ERR_BAD_ARG, "rank %d / world_size %d (at most %d ranks)", rank, world_size, kEpMaxRanks);
+  const SenMoeConfig& c = L->cfg;
+  if (peers[0].expert_begin != 0 || peers[world_size - 1].expert_end != c.n_routed_experts)
+    return fail(SENMOE_ERR_BAD_ARG, "expert ranges must start at 0 and end at %d", c.n_routed_experts);
+  for (int r = 0; r < world_size; ++r) {
+    const SenMoePeerInfo& p = peers[r];
+    if (p.expert_begin >= p.expert_end || (r > 0 && p.expert_begin != peers[r - 1].expert_end))
+      return fail(SENMOE_ERR_BAD_ARG, "rank %d expert range [%d, %d) does not continue the previous one", r,
+                  p.expert_begin, p.expert_end);
+    if (p.arena_bytes != static_cast<int64_t>(L->arena_bytes) || p.rows_offset != static_cast<int64_t>(L->o_d) ||
+        p.flags_offset != static_cast<int64_t>(L->o_flags))
+      return fail(SENMOE_ERR_BAD_ARG, "rank %d arena layout differs (configs must match apart from the expert range)",
+                  r);
+  }
+  if (peers[rank].expert_begin != c.expert_begin || peers[rank].expert_end != c.expert_end)
+    return fail(SENMOE_ERR_BAD_ARG, "peers[%d] is not this layer's entry", rank);
+  int cur = 0;
+  SENMOE_CUDA(cudaGetDevice(&cur));
+  SENMOE_CUDA(cudaSetDevice(L->device));
+  char* bases[kEpMaxRanks] = {};
+  for (int r = 0; r < world_size; ++r) {
+    if (r == rank) {
+      bases[r] = static_cast<char*>(L->arena);
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, peers[r].ipc_handle, sizeof(h));
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int q = 0; q < r; ++q)
+        if (q != rank && bases[q]) cudaIpcCloseMemHandle(bases[q]);
+      cudaSetDevice(cur);
+      return fail(SENMOE_ERR_CUDA, "cudaIpcOpenMemHandle(rank %d): %s", r, cudaGetErrorString(e));
+    }
+    bases[r] = static_cast<char*>(p);
+  }
+  cudaSetDevice(cur);
+  for (int r = 0; r < world_size; ++r) {
+    L->ep_peer_d[r] = reinterpret_cast<const uint16_t*>(bases[r] + L->o_d);
+    L->ep_peer_flags[r] = reinterpret_cast<uint32_t*>(bases[r] + L->o_flags);
+    L->ep_opened[r] = r == rank ? nullptr : bases[r];
+    L->ep_bounds[r] = peers[r].expert_begin;
+  }
+  L->ep_bounds[world_size] = c.n_routed_experts;
+  L->ep_rank = rank;
+  L->ep_world = world_size;
   return SENMOE_OK;
 }
 

@@ -68,6 +68,15 @@ class SenMoeDebug(C.Structure):
     _fields_ = [("topk_ids", _P), ("topk_weights", _P), ("perm", _P), ("offsets", _P)]
 
 
+MAX_RANKS = 8  # SENMOE_MAX_RANKS
+
+
+class SenMoePeerInfo(C.Structure):
+    _fields_ = [("ipc_handle", C.c_uint8 * 64), ("rows_offset", C.c_int64), ("flags_offset", C.c_int64),
+                ("arena_bytes", C.c_int64), ("expert_begin", C.c_int32), ("expert_end", C.c_int32),
+                ("device", C.c_int32), ("reserved", C.c_int32)]
+
+
 # Every symbol include/senmoe.h declares, with its ctypes signature.
 _i64, _i32, _f32 = C.c_int64, C.c_int32, C.c_float
 SIGNATURES = {
@@ -77,6 +86,8 @@ SIGNATURES = {
     "senmoe_layer_destroy": (C.c_int, [_P]),
     "senmoe_layer_forward": (C.c_int, [_P, _P, _i64, _P, C.POINTER(SenMoeDebug), _P]),
     "senmoe_layer_check": (C.c_int, [_P, _P]),
+    "senmoe_layer_peer_info": (C.c_int, [_P, C.POINTER(SenMoePeerInfo)]),
+    "senmoe_layer_connect_peers": (C.c_int, [_P, _i32, _i32, C.POINTER(SenMoePeerInfo)]),
     "senmoe_layer_forward_residual": (C.c_int, [_P, _P, _i64, _P, _P]),
     "senmoe_layer_set_profiling": (C.c_int, [_P, C.c_int]),
     "senmoe_layer_expert_path": (C.c_int, [_P, _i64]),
@@ -305,6 +316,24 @@ class DeepseekMoe:
     def check(self, stream=None) -> None:
         """Synchronises and raises if a kernel recorded a device-side error."""
         _check(lib().senmoe_layer_check(self._handle, _stream(stream)))
+
+    def peer_info(self) -> bytes:
+        """This rank's expert-parallel table entry (an opaque, picklable blob)."""
+        info = SenMoePeerInfo()
+        _check(lib().senmoe_layer_peer_info(self._handle, C.byref(info)))
+        return bytes(info)
+
+    def connect_peers(self, rank: int, infos: list) -> None:
+        """Expert-parallel form: ``infos[r]`` is rank r's ``peer_info()``.
+        Afterwards every rank's forward takes the same tokens and returns the
+        same output, each rank computing only its own experts."""
+        n = len(infos)
+        arr = (SenMoePeerInfo * max(n, 1))()
+        for i, blob in enumerate(infos):
+            if len(blob) != C.sizeof(SenMoePeerInfo):
+                raise SenMoeError(ERR_BAD_ARG, f"peer info {i} has {len(blob)} bytes")
+            C.memmove(C.byref(arr, i * C.sizeof(SenMoePeerInfo)), blob, len(blob))
+        _check(lib().senmoe_layer_connect_peers(self._handle, int(rank), n, arr))
 
     def close(self) -> None:
         if getattr(self, "_handle", None):

@@ -1,0 +1,238 @@
+"""Rank bodies for the expert-parallel tests, run as spawned processes
+(one per rank) joined in a torch.distributed group on 127.0.0.1.
+
+CPU ranks use gloo; GPU ranks bind one GPU each and still use gloo for the
+host-side table exchange (the data path is the library's peer-memory combine).
+"""
+from __future__ import annotations
+
+import bisect
+import os
+import socket
+import traceback
+from datetime import timedelta
+
+import numpy as np
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _entry(rank, world, port, fn_name, args, q):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        try:
+            q.put((rank, "ok", globals()[fn_name](rank, world, *args)))
+        finally:
+            dist.destroy_process_group()
+    except BaseException:
+        q.put((rank, "err", traceback.format_exc()))
+
+
+def spawn_ranks(fn_name: str, world: int, *args, timeout: float = 240.0) -> list:
+    """Runs ``fn_name(rank, world, *args)`` on ``world`` spawned ranks and
+    returns their results in rank order; raises with a rank's traceback."""
+    import multiprocessing as mp
+    import queue
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_entry, args=(r, world, port, fn_name, args, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results, errors = {}, []
+    try:
+        for _ in range(world):
+            rank, status, val = q.get(timeout=timeout)
+            if status == "ok":
+                results[rank] = val
+            else:
+                errors.append(f"rank {rank}:\n{val}")
+    except queue.Empty:
+        errors.append(f"ranks timed out after {timeout} s (got {sorted(results)})")
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()  # this test's own child, by handle
+                p.join()
+    if errors:
+        raise AssertionError("\n".join(errors))
+    return [results[r] for r in range(world)]
+
+
+# ------------------------------------------------------------------ CPU ranks
+class FakeLayer:
+    """Stands in for DeepseekMoe in the table exchange: a blob per (rank, layer)."""
+
+    def __init__(self, rank: int, index: int):
+        self.rank, self.index, self.connected = rank, index, None
+
+    def peer_info(self) -> bytes:
+        return f"r{self.rank}l{self.index}".encode()
+
+    def connect_peers(self, rank: int, infos: list) -> None:
+        self.connected = (rank, [b.decode() for b in infos])
+
+
+def exchange(rank, world, n_layers, extra_on_rank=-1):
+    from senmoe import ep
+
+    layers = [FakeLayer(rank, i) for i in range(n_layers + (1 if rank == extra_on_rank else 0))]
+    ep.connect(layers)
+    return [L.connected for L in layers]
+
+
+def decomposition(rank, world, bits):
+    """The expert-parallel data flow on the CPU: every rank routes all tokens,
+    computes the rows of its own experts at their global slots, the rows are
+    all-gathered, and each rank combines every pair's row from its owner in
+    slot order.  Returns this rank's y (fp32)."""
+    import torch
+    import torch.distributed as dist
+
+    from helpers import fixture_layer
+    from oracle import numpy_ref as N
+    from senmoe import ep
+
+    d = np.load(os.path.join(GOLD, f"moe_block_small_{bits}bit.npz"))
+    cfg, w = fixture_layer(d)
+    H, E, K, g = cfg.hidden, cfg.num_experts, cfg.top_k, cfg.group_size
+    x = N.bf16_val(d["x"]).reshape(-1, H)
+    T, P = x.shape[0], x.shape[0] * K
+    ids, wts = N.route(cfg, w, x)
+    b = ep.expert_bounds(E, world)
+    eb, ee = b[rank], b[rank + 1]
+    # global slots: stable counting sort of the pairs by expert
+    order = np.argsort(ids.reshape(-1), kind="stable")
+    slot = np.empty(P, dtype=np.int64)
+    slot[order] = np.arange(P)
+    gd = N.dequantize(w.gate_w[eb:ee], w.gate_s[eb:ee], w.gate_b[eb:ee], g, cfg.bits).astype(np.float64)
+    ud = N.dequantize(w.up_w[eb:ee], w.up_s[eb:ee], w.up_b[eb:ee], g, cfg.bits).astype(np.float64)
+    dd = N.dequantize(w.down_w[eb:ee], w.down_s[eb:ee], w.down_b[eb:ee], g, cfg.bits).astype(np.float64)
+    rows = np.zeros((P, H), dtype=np.float32)
+    for p in range(P):
+        e = int(ids.reshape(-1)[p])
+        if eb <= e < ee:
+            rows[slot[p]] = N.expert_mlp(x[p // K].astype(np.float64), gd[e - eb], ud[e - eb], dd[e - eb])
+    gathered = [torch.zeros(P, H) for _ in range(world)]
+    dist.all_gather(gathered, torch.from_numpy(rows))
+    y = np.zeros((T, H), dtype=np.float32)
+    for t in range(T):
+        acc = np.zeros(H, dtype=np.float32)
+        for j in range(K):
+            p = t * K + j
+            owner = bisect.bisect_right(b, int(ids[t, j])) - 1
+            acc = (acc + gathered[owner][slot[p]].numpy() * wts[t, j]).astype(np.float32)
+        y[t] = acc
+    if cfg.shared_intermediate:
+        y = (y + N.shared_out(cfg, w, x)).astype(np.float32)
+    return y
+
+
+# ------------------------------------------------------------------ GPU ranks
+def _gpu_setup(rank, world, H, I, E, K, bits, T, shared, seed):
+    import torch
+
+    from helpers import device_weights, moe_args
+    from oracle import oracle as O
+
+    torch.cuda.set_device(rank)
+    cfg = O.MoeConfig(hidden=H, intermediate=I, num_experts=E, top_k=K, bits=bits,
+                      shared_intermediate=shared, shared_gate=bool(shared))
+    mw = O.make_layer(cfg, seed=seed, router_std=1.0 / np.sqrt(H))
+    x = O.make_tokens(T, H, seed=seed + 1)
+    return cfg, mw, x, moe_args(cfg), device_weights(mw, device=f"cuda:{rank}")
+
+
+def ep_forward(rank, world, H, I, E, K, bits, Ts, shared, seed, expert_path):
+    """EP layer vs the one-GPU layer on every rank, for several batch sizes
+    (also through a CUDA-graph stack).  Returns per-T (bit-exact?, max abs diff,
+    max abs diff vs the oracle)."""
+    import torch
+
+    import senmoe
+    from helpers import moe_args, t_bf16, to_numpy_bf16, bf16_np_to_f32
+    from oracle import oracle as O
+    from senmoe import ep
+
+    Tmax = max(Ts)
+    cfg, mw, x_np, args, wd = _gpu_setup(rank, world, H, I, E, K, bits, Tmax, shared, seed)
+    args = moe_args(cfg, expert_path)
+    full = senmoe.DeepseekMoe(args, wd, max_tokens=Tmax)
+    epl = ep.make_layer(args, wd, Tmax, rank, world)
+    ep.connect([epl])
+    x = t_bf16(x_np, device=f"cuda:{rank}")
+    out = {}
+    for T in Ts:
+        ref = full.forward(x[:T])
+        y = epl.forward(x[:T])
+        y2 = epl.forward(x[:T])  # a second call: the epoch/flag hand-over
+        epl.check()
+        full.check()
+        orc = O.moe_forward(cfg, mw, x_np[:T])
+        a, b2 = to_numpy_bf16(y), to_numpy_bf16(ref)
+        out[T] = dict(exact=bool(torch.equal(y, ref) and torch.equal(y2, ref)),
+                      max_abs=float(np.abs(bf16_np_to_f32(a) - bf16_np_to_f32(b2)).max()),
+                      max_abs_oracle=float(np.abs(bf16_np_to_f32(a) - orc["y_f32"]).max()),
+                      path=epl.expert_path(T))
+    # a graph-captured two-layer stack with the residual add (the decode step)
+    epl2 = ep.make_layer(args, wd, Tmax, rank, world)
+    ep.connect([epl2])
+    full2 = senmoe.DeepseekMoe(args, wd, max_tokens=Tmax)
+    stack = senmoe.MoeStack([epl, epl2], max_tokens=Tmax)
+    ref_stack = senmoe.MoeStack([full, full2], max_tokens=Tmax, use_graph=False)
+    T = Ts[0]
+    ys = [stack.forward(x[:T]).clone() for _ in range(3)]
+    yr = ref_stack.forward(x[:T])
+    epl.check()
+    epl2.check()
+    out["stack_exact"] = all(bool(torch.equal(v, yr)) for v in ys)
+    stack.release()
+    torch.cuda.synchronize()
+    import torch.distributed as dist
+    dist.barrier()  # no rank frees its rows while a peer may still read them
+    for L in (epl, epl2, full, full2):
+        L.close()
+    dist.barrier()
+    return out
+
+
+def ep_missing_rank(rank, world, H, I, E, K, bits, T, seed):
+    """Rank world-1 skips one forward: the other ranks' bounded waits run out
+    and their check() reports ERR_TIMEOUT; the skipping rank stays clean."""
+    import torch
+    import torch.distributed as dist
+
+    import senmoe
+    from helpers import moe_args, t_bf16
+    from senmoe import ep
+
+    cfg, mw, x_np, args, wd = _gpu_setup(rank, world, H, I, E, K, bits, T, 0, seed)
+    epl = ep.make_layer(moe_args(cfg), wd, T, rank, world)
+    ep.connect([epl])
+    x = t_bf16(x_np, device=f"cuda:{rank}")
+    epl.forward(x)
+    epl.check()  # one good call on every rank
+    dist.barrier()
+    status = "ok"
+    if rank != world - 1:
+        epl.forward(x)
+        try:
+            epl.check()
+        except senmoe.SenMoeError as e:
+            status = f"status {e.status}"
+    torch.cuda.synchronize()
+    dist.barrier()
+    epl.close()
+    dist.barrier()
+    return status

@@ -83,3 +83,20 @@ def topk_match_except_ties(ids_gpu, ids_ref, scores_ref, ulp_rel=2.0 ** -7):
             continue
         return False, ties
     return True, ties
+
+
+def fixture_layer(d):
+    """(oracle.MoeConfig, oracle.MoeWeights) of a tests/golden/moe_block_small_*.npz fixture."""
+    from oracle import oracle as O
+
+    H, I, E, K, bits, g, norm, shared, sgate = (int(v) for v in d["cfg"])
+    cfg = O.MoeConfig(hidden=H, intermediate=I, num_experts=E, top_k=K, bits=bits, group_size=g,
+                      norm_topk_prob=bool(norm), routed_scaling_factor=float(d["routed_scaling_factor"]),
+                      shared_intermediate=shared, shared_gate=bool(sgate))
+    w = O.MoeWeights(d["router_w"], d["gate_w"], d["gate_s"], d["gate_b"], d["up_w"], d["up_s"], d["up_b"],
+                     d["down_w"], d["down_s"], d["down_b"])
+    if shared:
+        for k in ("sh_gate_w", "sh_gate_s", "sh_gate_b", "sh_up_w", "sh_up_s", "sh_up_b", "sh_down_w",
+                  "sh_down_s", "sh_down_b", "sh_gate_vec"):
+            setattr(w, k, d[k])
+    return cfg, w

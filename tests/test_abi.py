@@ -42,8 +42,9 @@ def test_struct_layouts_match_ctypes(senmoe):
 #include <stddef.h>
 #include "senmoe.h"
 int main(void) {
-  printf("%zu %zu %zu %zu %zu\n", sizeof(SenMoeConfig), sizeof(SenMoeWeights), sizeof(SenMoeDebug),
-         offsetof(SenMoeConfig, max_tokens), offsetof(SenMoeWeights, shared_gate_vector));
+  printf("%zu %zu %zu %zu %zu %zu %zu %zu\n", sizeof(SenMoeConfig), sizeof(SenMoeWeights), sizeof(SenMoeDebug),
+         offsetof(SenMoeConfig, max_tokens), offsetof(SenMoeWeights, shared_gate_vector), sizeof(SenMoePeerInfo),
+         offsetof(SenMoePeerInfo, arena_bytes), offsetof(SenMoePeerInfo, device));
   return 0;
 }'''
     with tempfile.TemporaryDirectory() as d:
@@ -53,7 +54,9 @@ int main(void) {
         out = subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()
     got = [int(v) for v in out]
     want = [C.sizeof(senmoe.SenMoeConfig), C.sizeof(senmoe.SenMoeWeights), C.sizeof(senmoe.SenMoeDebug),
-            senmoe.SenMoeConfig.max_tokens.offset, senmoe.SenMoeWeights.shared_gate_vector.offset]
+            senmoe.SenMoeConfig.max_tokens.offset, senmoe.SenMoeWeights.shared_gate_vector.offset,
+            C.sizeof(senmoe.SenMoePeerInfo), senmoe.SenMoePeerInfo.arena_bytes.offset,
+            senmoe.SenMoePeerInfo.device.offset]
     assert got == want
 
 
@@ -116,6 +119,14 @@ def test_forward_rejects_null_layer_and_bad_token_count(senmoe):
     L = senmoe.lib()
     assert L.senmoe_layer_forward(None, None, 1, None, None, None) == senmoe.ERR_BAD_ARG
     assert L.senmoe_layer_destroy(None) == senmoe.OK
+
+
+def test_expert_parallel_entry_points_reject_null(senmoe):
+    L = senmoe.lib()
+    info = senmoe.SenMoePeerInfo()
+    assert L.senmoe_layer_peer_info(None, C.byref(info)) == senmoe.ERR_BAD_ARG
+    assert L.senmoe_layer_connect_peers(None, 0, 1, C.byref(info)) == senmoe.ERR_BAD_ARG
+    assert b"NULL" in L.senmoe_last_error()
 
 
 def test_python_gather_qmm_rejects_unsupported_broadcast(senmoe):

@@ -1,0 +1,47 @@
+"""Expert parallelism on 2 or more B200s of one box: one spawned process per
+GPU, experts split in contiguous blocks, the combine reading every row from
+its owner GPU.  The expert-parallel output must equal the one-GPU layer's
+bit for bit (same kernels, same rows, same slot order and fp32 sums) and stay
+within the parity tolerance of the oracle.  Skipped with fewer than 2 GPUs."""
+import pytest
+import torch
+
+from ep_workers import spawn_ranks
+from helpers import MAX_ABS_TOL
+
+pytestmark = pytest.mark.gpu
+
+
+def _ngpu() -> int:
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+CASES = {
+    # H, I, E, K, bits, Ts, shared, seed, expert_path
+    "config0": (2048, 768, 128, 8, 4, [1, 8, 64, 256], 0, 3, 0),
+    "shared8": (256, 256, 16, 4, 8, [3, 40, 600], 256, 5, 0),
+    "config0_tc": (2048, 768, 128, 8, 4, [16, 512], 0, 7, 2),
+}
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_expert_parallel_matches_one_gpu(world, case):
+    if _ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
+    H, I, E, K, bits, Ts, shared, seed, path = CASES[case]
+    res = spawn_ranks("ep_forward", world, H, I, E, K, bits, Ts, shared, seed, path, timeout=600)
+    for rank, out in enumerate(res):
+        assert out["stack_exact"], f"rank {rank}: graph-captured EP stack differs from the one-GPU stack"
+        for T in Ts:
+            r = out[T]
+            assert r["exact"], f"rank {rank} T={T}: EP output differs from one GPU (max abs {r['max_abs']})"
+            assert r["max_abs_oracle"] <= MAX_ABS_TOL, f"rank {rank} T={T}: {r['max_abs_oracle']} vs oracle"
+
+
+def test_missing_rank_times_out_with_status():
+    if _ngpu() < 2:
+        pytest.skip("needs 2 GPUs")
+    res = spawn_ranks("ep_missing_rank", 2, 256, 256, 16, 4, 4, 8, 11, timeout=300)
+    assert res[0] == "status 4", res  # SENMOE_ERR_TIMEOUT
+    assert res[1] == "ok", res

@@ -9,8 +9,8 @@ import os
 import numpy as np
 import pytest
 
-from helpers import (MAX_ABS_TOL, REL_L2_TOL, bf16_np_to_f32, device_weights, moe_args, rel_l2, t_bf16,
-                     to_numpy_bf16, topk_match_except_ties)
+from helpers import (MAX_ABS_TOL, REL_L2_TOL, bf16_np_to_f32, device_weights, fixture_layer, moe_args, rel_l2,
+                     t_bf16, to_numpy_bf16, topk_match_except_ties)
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -67,8 +67,7 @@ def check_against_oracle(cfg, mw, x, got):
 @pytest.mark.parametrize("bits", [4, 8])
 def test_small_block_vs_golden_fixture(senmoe, bits):
     d = np.load(os.path.join(GOLD, f"moe_block_small_{bits}bit.npz"))
-    from test_oracle import _fixture_layer
-    cfg, mw = _fixture_layer(d)
+    cfg, mw = fixture_layer(d)
     got = run_block(senmoe, cfg, mw, d["x"])
     np.testing.assert_array_equal(got["topk_ids"], d["ids"])
     assert np.abs(got["y"] - d["y_f32"]).max() <= MAX_ABS_TOL

@@ -12,7 +12,7 @@ import pytest
 
 from oracle import numpy_ref as N
 from oracle import oracle as O
-from helpers import bf16_np_to_f32
+from helpers import bf16_np_to_f32, fixture_layer
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -47,24 +47,10 @@ def test_kat_gather_qmm_matches_reference_check():
     np.testing.assert_allclose(ref, d["expected_f64"], rtol=0, atol=1e-12)
 
 
-def _fixture_layer(d):
-    H, I, E, K, bits, g, norm, shared, sgate = (int(v) for v in d["cfg"])
-    cfg = O.MoeConfig(hidden=H, intermediate=I, num_experts=E, top_k=K, bits=bits, group_size=g,
-                      norm_topk_prob=bool(norm), routed_scaling_factor=float(d["routed_scaling_factor"]),
-                      shared_intermediate=shared, shared_gate=bool(sgate))
-    w = O.MoeWeights(d["router_w"], d["gate_w"], d["gate_s"], d["gate_b"], d["up_w"], d["up_s"], d["up_b"],
-                     d["down_w"], d["down_s"], d["down_b"])
-    if shared:
-        for k in ("sh_gate_w", "sh_gate_s", "sh_gate_b", "sh_up_w", "sh_up_s", "sh_up_b", "sh_down_w",
-                  "sh_down_s", "sh_down_b", "sh_gate_vec"):
-            setattr(w, k, d[k])
-    return cfg, w
-
-
 @pytest.mark.parametrize("bits", [4, 8])
 def test_small_block_c_oracle_matches_fixture(bits):
     d = np.load(os.path.join(GOLD, f"moe_block_small_{bits}bit.npz"))
-    cfg, w = _fixture_layer(d)
+    cfg, w = fixture_layer(d)
     r = O.moe_forward(cfg, w, d["x"], mode=0)
     np.testing.assert_array_equal(r["ids"], d["ids"])
     np.testing.assert_allclose(r["weights"], d["weights"], rtol=1e-6, atol=0)
