@@ -167,7 +167,7 @@ def make_stack(torch, senmoe, device, layers, max_tokens, seed=0, rank=0, world=
 def launches_per_forward(T, tensor_cores, world):
     """Kernels one forward launches: router logits + top-k, dispatch (one
     kernel up to 2048 pairs, else three), the expert-parallel fence, the
-    gathered-activation copy (tensor-core path), gate/up, down, combine."""
+    gathered-activation copy (tensor-core paths), gate/up, down, combine."""
     disp = 1 if (T * K + 1023) // 1024 <= 2 else 3
     return 2 + disp + (1 if world > 1 else 0) + (1 if tensor_cores else 0) + 3
 
@@ -356,7 +356,7 @@ def main():
         sp = stage_profile(layers, T, 3)
         per_layer_us = {k: round(v / (3 * len(layers)) * 1e3, 2) for k, v in sp.items()}
         results[T] = {"tokens_per_s": T / step, "ms_per_step": step * 1e3,
-                      "expert_kernels": "tcgen05" if layers[0].expert_path(T) == senmoe.PATH_TENSOR_CORE else "gemv",
+                      "expert_kernels": senmoe.PATH_NAMES[layers[0].expert_path(T)],
                       "stage_us_per_layer": per_layer_us,
                       "touched_experts_per_layer": sum(touched) / len(touched),
                       "hbm_gbs": alg_bytes / step / 1e9, "hbm_frac": alg_bytes / step / 1e9 / (world * hbm_peak)}
@@ -446,7 +446,7 @@ def main():
                      "step_hbm_gbs": head["hbm_gbs"], "step_frac": head["hbm_gbs"] / hbm_peak},
         "stage_share": stage_share,
         "prefill": prefill,
-        "gpu_launches": launches_per_forward(args.batch, head["expert_kernels"] == "tcgen05", world) * args.layers
+        "gpu_launches": launches_per_forward(args.batch, head["expert_kernels"] != "gemv", world) * args.layers
         * args.steps,
         "clocks": clocks,
         "e2e": {"value": args.batch / e2e_s, "unit": UNIT, "h2d_bytes_per_step": args.batch * H * 2,

@@ -135,4 +135,32 @@ __device__ __forceinline__ float act_geglu_mlx(float g, float u) {
   return round_bf16(a * u);
 }
 
+
+// 2-D tiled TMA load (no multicast) completing on an mbarrier.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+
+// Bounded wait that also gives up as soon as another role of the CTA has.
+// Warp-wide callers combine the result with __all_sync so that every lane
+// takes the same branch (they arrive per warp and issue .sync.aligned ops).
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      *abort_flag = 1;
+      record_error(err, kDevWaitTimeout);
+      return false;
+    }
+  }
+}
+
 }  // namespace senmoe

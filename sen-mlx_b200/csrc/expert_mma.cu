@@ -1,0 +1,419 @@
+// expert_mma.cu -- grouped affine-quantized expert GEMM for decode batches
+// (a few tokens per expert), on warp-level tensor-core MMAs.
+//
+// Same contraction as the reference's SwitchGlu gather_qmm calls
+// (src/engine/mlx_lm/models/deepseek_v2.rs:466-478, utils/moe.rs:33-77), with
+// tokens grouped by expert (dispatch.cu).  With 1-16 tokens per expert the
+// block is bound by streaming the touched experts' packed weights from HBM;
+// what limits a kernel there is the instruction budget per packed word.  Here
+// every lane dequantises its own words straight into mma.sync A-fragment
+// registers (no shared-memory or TMEM round trip for the 4x-expanded fp16
+// weights) and every warp issues its own m16n8k16 MMAs, so no single issuing
+// thread or per-k-block handoff paces the pipeline.  (The tcgen05 kernel,
+// expert_tc.cu, takes over when experts hold enough tokens for its 128 x N
+// tiles to be worth the TMEM round trip.)
+//
+// Tile: one expert, 128 weight rows (gate and up together, or down), and up
+// to 8*NT of the expert's slots; k streams in 256-column stages.
+//   warp 16       TMA producer: per stage the packed codes (2-D tensor map,
+//                 128 rows x 128 B boxes, SWIZZLE_128B) and the activation
+//                 tile (fp16 [slots, k], 64-column x 8*NT-row boxes,
+//                 SWIZZLE_128B), into a ring of stages.  No multicast.
+//   warps 0-15    warp w computes rows 16*(w%8) .. +16 for the k-half w/8 of
+//                 every stage (blocks of 32 columns), then the two k-halves
+//                 are added through shared memory and warps 0-7 run the
+//                 epilogue (SwiGLU / GeGLU with MLX's bf16 rounding, or the
+//                 bf16 down output).
+// k order: inside each 32-column block the operands are stored in the order
+// that puts one packed word's code pairs (p, p+4) in the k-pairs of the
+// A fragment (kperm32); B (activations, written by gather_rows_kernel and by
+// the gate/up epilogue) uses the same order, and the contraction does not
+// depend on it.  Operands are fp16 (exact codes, q*s+b rounded once, bf16
+// activations exact), accumulation fp32, as on the tcgen05 path.
+// Every mbarrier wait is bounded; a timeout aborts the CTA cleanly.
+
+#include <cuda.h>
+
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "dequant.cuh"
+#include "kernels.h"
+#include "tiles.cuh"
+
+namespace senmoe {
+namespace {
+
+constexpr int kRows = 128;           // weight rows per tile
+constexpr int kStageCols = 256;      // k columns per stage
+constexpr int kComputeWarps = 16;    // 8 row groups x 2 k-halves
+constexpr int kThreads = (kComputeWarps + 1) * 32;
+constexpr int kMaxTiles = 128;       // per CTA
+constexpr int kSmemBudget = 226 * 1024;
+
+template <int BITS, int NPROJ, int NT>
+struct MmaShape {
+  static constexpr int kABoxes = BITS / 4;                   // 128-byte boxes per row per stage
+  static constexpr int kABox = kRows * 128;                  // 16 KB
+  static constexpr int kABytes = NPROJ * kABoxes * kABox;
+  static constexpr int kBRows = 8 * NT;
+  static constexpr int kBBox = kBRows * 128;                 // 64 fp16 columns x kBRows
+  static constexpr int kBBytes = 4 * kBBox;
+  static constexpr int kStageBytes = kABytes + kBBytes;      // multiple of 1024
+  static constexpr int kRedBytes = 8 * 32 * NPROJ * NT * 4 * 4;
+  static constexpr int kMisc = 4096;                         // barriers + tile list
+  static constexpr int kFit = (kSmemBudget - kRedBytes - kMisc - 1024) / kStageBytes;
+  static constexpr int kStages = kFit > 8 ? 8 : kFit;
+  static constexpr int kSmem = 1024 + kStages * kStageBytes + kRedBytes + kMisc;
+  static_assert(kStages >= 2, "pipeline needs two stages");
+  static_assert(kStageBytes % 1024 == 0, "stage alignment");
+};
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// Per (row, group) dequantisation constants.
+struct GroupConst {
+  __half2 s;    // scale (x 2^18 / 2^22 for the subnormal form)
+  __half2 b;    // bias
+  bool sub;     // subnormal form usable
+};
+
+template <int BITS>
+__device__ __forceinline__ GroupConst group_const(uint16_t sbits, uint16_t bbits) {
+  const float sf = bf16_bits_to_f32(sbits);
+  GroupConst c;
+  c.b = __float2half2_rn(bf16_bits_to_f32(bbits));
+  // 4-bit codes sit at mantissa bits 6-9 (q * 2^-18), 8-bit at bits 2-9 (q * 2^-22)
+  constexpr float kUp = BITS == 4 ? 262144.0f : 4194304.0f;
+  constexpr float kMax = BITS == 4 ? 0.2498f : 0.0156f;
+  c.sub = fabsf(sf) < kMax;
+  c.s = __float2half2_rn(c.sub ? sf * kUp : sf);
+  return c;
+}
+
+// Code pairs (p, p+4), p = 0..3, of the 8 codes a lane holds for one row of a
+// 32-column block, as fp16 q*s+b.  4-bit: one word; 8-bit: two words.
+template <int BITS>
+__device__ __forceinline__ uint4 dequant_pairs(uint32_t w0, uint32_t w1, const GroupConst& c, bool all_sub) {
+  if constexpr (BITS == 4) {
+    (void)w1;
+    return all_sub ? dequant8_u4_sub(w0, c.s, c.b) : (c.sub ? dequant8_u4_sub(w0, c.s, c.b) : dequant8_u4(w0, c.s, c.b));
+  } else {
+    uint32_t o[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      // bytes: [w0.p, w0.0, w1.p, w0.0]
+      const uint32_t t = __byte_perm(w0, w1, static_cast<uint32_t>(p | ((4 + p) << 8)));
+      __half2 r;
+      if (all_sub || c.sub) {
+        const uint32_t v = (t << 2) & 0x03FC03FCu;  // q * 2^-22 in each half
+        r = __hfma2(*reinterpret_cast<const __half2*>(&v), c.s, c.b);
+      } else {
+        const uint32_t v = (t & 0x00FF00FFu) | 0x64006400u;  // 1024 + q
+        const __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&v), __floats2half2_rn(1024.0f, 1024.0f));
+        r = __hfma2(q, c.s, c.b);
+      }
+      o[p] = *reinterpret_cast<const uint32_t*>(&r);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// Position of feature `col` in the kperm32 order (see the file comment):
+// within each 32-block, column 8t + p + 4h goes to 8p + 2t + h.
+__device__ __forceinline__ int kperm32(int col) {
+  const int c = col & 31, t = c >> 3, r = c & 7, p = r & 3, h = r >> 2;
+  return (col & ~31) | (p << 3) | (t << 1) | h;
+}
+
+template <int BITS, int NPROJ, int NT>
+__global__ void __launch_bounds__(kThreads, 1)
+    qmma_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ CUtensorMap tA1,
+                const __grid_constant__ CUtensorMap tB, TcGemmArgs a) {
+  using S = MmaShape<BITS, NPROJ, NT>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sStage = smem;
+  float* sRed = reinterpret_cast<float*>(smem + S::kStages * S::kStageBytes);
+  uint64_t* bar_full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes + S::kRedBytes);
+  uint64_t* bar_empty = bar_full + S::kStages;
+  uint64_t* bar_red_full = bar_empty + S::kStages;   // [8] partner k-half partials written
+  uint64_t* bar_red_empty = bar_red_full + 8;        // [8] partials consumed
+  int4* s_tiles = reinterpret_cast<int4*>(bar_red_empty + 8);
+  __shared__ int s_ntiles;
+  __shared__ int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S::kStages; ++i) {
+      mbar_init(&bar_full[i], 1);
+      mbar_init(&bar_empty[i], kComputeWarps);
+    }
+    for (int i = 0; i < 8; ++i) {
+      mbar_init(&bar_red_full[i], 1);
+      mbar_init(&bar_red_empty[i], 1);
+    }
+    fence_mbar_init();
+    s_abort = 0;
+  }
+  pdl_wait();  // active list / offsets (dispatch) and the activation rows (gather or gate/up)
+  pdl_launch_dependents();
+  // the stage ring is free until the producer starts: use it as scratch
+  const int nlisted = list_tiles(a.active, a.active_count, a.offsets, a.expert_begin, a.m_tiles, kRows, 8 * NT, false,
+                                 s_tiles, kMaxTiles, reinterpret_cast<int*>(sStage), a.err);
+  if (threadIdx.x == 0) s_ntiles = nlisted;
+  __syncthreads();
+  const int ntiles = s_ntiles;
+  const int nst = a.kdim / kStageCols;
+
+  if (warp == kComputeWarps) {
+    // ===================================================== TMA producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int ti = 0; ti < ntiles && ok; ++ti) {
+        const int4 tl = s_tiles[ti];
+        const int arow = tl.x * a.rows + tl.y;
+        for (int st = 0; st < nst; ++st, ++it) {
+          const int slot = it % S::kStages, ph = (it / S::kStages) & 1;
+          if (!(ok = wait_or_abort(&bar_empty[slot], ph ^ 1, &s_abort, a.err))) break;
+          unsigned char* base = sStage + slot * S::kStageBytes;
+          mbar_arrive_expect_tx(&bar_full[slot], S::kStageBytes);
+#pragma unroll
+          for (int p = 0; p < NPROJ; ++p)
+#pragma unroll
+            for (int bx = 0; bx < S::kABoxes; ++bx)
+              tma_load_2d(base + (p * S::kABoxes + bx) * S::kABox, p ? &tA1 : &tA0, (st * S::kABoxes + bx) * 32,
+                          arow, &bar_full[slot]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tma_load_2d(base + S::kABytes + j * S::kBBox, &tB, st * kStageCols + j * 64, tl.z, &bar_full[slot]);
+        }
+      }
+      // drain: the copies of the last stages must land before the CTA may
+      // exit, consumed or not (bounded; each slot's latest use only)
+      const int last = it;
+      int never = 0;
+      for (int k = (last > S::kStages ? last - S::kStages : 0); k < last; ++k)
+        wait_or_abort(&bar_full[k % S::kStages], (k / S::kStages) & 1, &never, nullptr);
+    }
+    return;
+  }
+
+  // ======================================================= compute warps
+  const int rg = warp & 7, kh = warp >> 3;
+  const int g = lane >> 2, t = lane & 3;
+  const int groups = a.kdim / 64;
+  int it = 0;
+  bool ok = true;
+  const uint32_t sStage_u32 = smem_u32(sStage);
+  const int rA = 16 * rg + g;  // tile row of this lane's first fragment row
+  // scales / biases of this lane's two rows for the two groups of its k-half
+  // of a stage: u32 = (group q0, group q0+1), prefetched one stage ahead,
+  // across tile boundaries too
+  uint32_t scur[NPROJ][2], bcur[NPROJ][2], snext[NPROJ][2], bnext[NPROJ][2];
+  auto load_sb = [&](int ti, int st) {
+    const int4 tn = s_tiles[ti];
+    const size_t row = static_cast<size_t>(tn.x * a.rows + tn.y + rA) * groups + static_cast<size_t>(st) * 4 + kh * 2;
+#pragma unroll
+    for (int p = 0; p < NPROJ; ++p) {
+      snext[p][0] = __ldg(reinterpret_cast<const uint32_t*>(a.s[p] + row));
+      snext[p][1] = __ldg(reinterpret_cast<const uint32_t*>(a.s[p] + row + 8 * groups));
+      bnext[p][0] = __ldg(reinterpret_cast<const uint32_t*>(a.b[p] + row));
+      bnext[p][1] = __ldg(reinterpret_cast<const uint32_t*>(a.b[p] + row + 8 * groups));
+    }
+  };
+  if (ntiles > 0) load_sb(0, 0);
+  for (int ti = 0; ti < ntiles && ok; ++ti) {
+    const int4 tl = s_tiles[ti];
+    float acc[NPROJ][NT][4];
+#pragma unroll
+    for (int p = 0; p < NPROJ; ++p)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[p][nt][i] = 0.f;
+    for (int st = 0; st < nst; ++st, ++it) {
+#pragma unroll
+      for (int p = 0; p < NPROJ; ++p) {
+        scur[p][0] = snext[p][0]; scur[p][1] = snext[p][1];
+        bcur[p][0] = bnext[p][0]; bcur[p][1] = bnext[p][1];
+      }
+      if (st + 1 < nst) load_sb(ti, st + 1);
+      else if (ti + 1 < ntiles) load_sb(ti + 1, 0);
+      const int slot = it % S::kStages, ph = (it / S::kStages) & 1;
+      ok = __all_sync(0xffffffffu, wait_or_abort(&bar_full[slot], ph, &s_abort, a.err));
+      if (!ok) break;
+      const unsigned char* base = sStage + slot * S::kStageBytes;
+      const uint32_t bbase = sStage_u32 + slot * S::kStageBytes + S::kABytes;
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {  // the two 64-column groups of this k-half
+        GroupConst gc[NPROJ][2];
+        bool all_sub = true;
+#pragma unroll
+        for (int p = 0; p < NPROJ; ++p)
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            gc[p][r] = group_const<BITS>(static_cast<uint16_t>(scur[p][r] >> (16 * q)),
+                                         static_cast<uint16_t>(bcur[p][r] >> (16 * q)));
+            all_sub = all_sub && gc[p][r].sub;
+          }
+        all_sub = __all_sync(0xffffffffu, all_sub);
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int j = kh * 4 + q * 2 + jj;  // 32-column block within the stage
+          // B fragments (all n-tiles) for the block's two k-steps
+          uint32_t bf[NT][4];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const int n = lane & 7, mi = lane >> 3;
+            const uint32_t addr = bbase + (j >> 1) * S::kBBox + (8 * nt + n) * 128 +
+                                  ((((j & 1) * 4 + mi) ^ n) << 4);
+            ldmatrix_x4(addr, bf[nt]);
+          }
+#pragma unroll
+          for (int p = 0; p < NPROJ; ++p) {
+            uint4 v[2];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+              const int row = rA + 8 * r;
+              uint32_t w0, w1 = 0;
+              if constexpr (BITS == 4) {
+                const unsigned char* rowp = base + p * S::kABox + row * 128;
+                w0 = *reinterpret_cast<const uint32_t*>(rowp + ((j ^ (row & 7)) << 4) + 4 * t);
+              } else {
+                // block j = words 8j .. 8j+7 of the stage: box j/4, chunk 2(j%4) + t/2
+                const unsigned char* rowp = base + (p * S::kABoxes + (j >> 2)) * S::kABox + row * 128;
+                const uint2 ww = *reinterpret_cast<const uint2*>(
+                    rowp + (((2 * (j & 3) + (t >> 1)) ^ (row & 7)) << 4) + 8 * (t & 1));
+                w0 = ww.x;
+                w1 = ww.y;
+              }
+              v[r] = dequant_pairs<BITS>(w0, w1, gc[p][r], all_sub);
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              mma16816(acc[p][nt], v[0].x, v[1].x, v[0].y, v[1].y, bf[nt][0], bf[nt][1]);
+              mma16816(acc[p][nt], v[0].z, v[1].z, v[0].w, v[1].w, bf[nt][2], bf[nt][3]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_empty[slot]);
+    }
+    if (!ok) break;
+
+    // ---- add the two k-halves: warp rg+8 hands its partials to warp rg
+    float* red = sRed + (rg * 32 + lane) * (NPROJ * NT * 4);
+    const uint32_t rph = ti & 1;
+    if (kh == 1) {
+      ok = __all_sync(0xffffffffu, wait_or_abort(&bar_red_empty[rg], rph ^ 1, &s_abort, a.err));
+      if (!ok) break;
+#pragma unroll
+      for (int p = 0; p < NPROJ; ++p)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+          *reinterpret_cast<float4*>(red + (p * NT + nt) * 4) =
+              make_float4(acc[p][nt][0], acc[p][nt][1], acc[p][nt][2], acc[p][nt][3]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_red_full[rg]);
+      continue;
+    }
+    ok = __all_sync(0xffffffffu, wait_or_abort(&bar_red_full[rg], rph, &s_abort, a.err));
+    if (!ok) break;
+#pragma unroll
+    for (int p = 0; p < NPROJ; ++p)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const float4 o = *reinterpret_cast<const float4*>(red + (p * NT + nt) * 4);
+        acc[p][nt][0] += o.x; acc[p][nt][1] += o.y; acc[p][nt][2] += o.z; acc[p][nt][3] += o.w;
+      }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bar_red_empty[rg]);
+
+    // ---- epilogue: lane holds rows (rA, rA+8) x slots (8nt + 2t, +1)
+    bool range_ok = true;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int n = 8 * nt + 2 * t + (i & 1);
+        if (n >= tl.w) continue;
+        const int row = tl.y + rA + 8 * (i >> 1);
+        const size_t o = static_cast<size_t>(tl.z + n) * a.out_stride;
+        if constexpr (NPROJ == 2) {
+          const float gv = round_bf16(acc[0][nt][i]), uv = round_bf16(acc[1][nt][i]);
+          const float h = a.act == 0 ? act_swiglu_mlx(gv, uv) : act_geglu_mlx(gv, uv);
+          range_ok &= fabsf(h) < 65504.0f;
+          a.out[o + kperm32(row)] = __half_as_ushort(__float2half_rn(h));
+        } else {
+          a.out[o + row] = f32_to_bf16_bits(acc[0][nt][i]);
+        }
+      }
+    }
+    if (!range_ok) record_error(a.err, kDevFp16Range);
+  }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ host
+template <int BITS, int NPROJ, int NT>
+static cudaError_t launch_mma_t(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
+                                const TcGemmArgs& a, int tiles_upper, cudaStream_t st) {
+  using S = MmaShape<BITS, NPROJ, NT>;
+  auto kern = qmma_kernel<BITS, NPROJ, NT>;
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), S::kSmem);
+  if (e != cudaSuccess) return e;
+  int sms = 0, dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  int grid = tiles_upper < sms ? tiles_upper : sms;
+  if (grid < 1) grid = 1;
+  if ((tiles_upper + grid - 1) / grid > kMaxTiles) return cudaErrorNotSupported;
+  return launch_pdl(kern, dim3(grid), dim3(kThreads), S::kSmem, st, tA0, tA1, tB, a);
+}
+
+size_t mma_smem_bytes(int bits, int nproj, int nt) {
+#define SENMOE_MMA_SMEM(B, P, N) \
+  if (bits == B && nproj == P && nt == N) return MmaShape<B, P, N>::kSmem;
+  SENMOE_MMA_SMEM(4, 1, 1) SENMOE_MMA_SMEM(4, 1, 2) SENMOE_MMA_SMEM(4, 1, 4)
+  SENMOE_MMA_SMEM(4, 2, 1) SENMOE_MMA_SMEM(4, 2, 2) SENMOE_MMA_SMEM(4, 2, 4)
+  SENMOE_MMA_SMEM(8, 1, 1) SENMOE_MMA_SMEM(8, 1, 2) SENMOE_MMA_SMEM(8, 1, 4)
+  SENMOE_MMA_SMEM(8, 2, 1) SENMOE_MMA_SMEM(8, 2, 2) SENMOE_MMA_SMEM(8, 2, 4)
+#undef SENMOE_MMA_SMEM
+  return 0;
+}
+
+bool mma_supported(int rows, int kdim, int bits) {
+  return (bits == 4 || bits == 8) && rows > 0 && rows % kRows == 0 && kdim > 0 && kdim % kStageCols == 0;
+}
+
+cudaError_t launch_mma_gemm(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
+                            const TcGemmArgs& a, int bits, int nproj, int nt, int tiles_upper, cudaStream_t st) {
+#define SENMOE_MMA_CASE(B, P, N) \
+  if (bits == B && nproj == P && nt == N) return launch_mma_t<B, P, N>(tA0, tA1, tB, a, tiles_upper, st);
+  SENMOE_MMA_CASE(4, 1, 1) SENMOE_MMA_CASE(4, 1, 2) SENMOE_MMA_CASE(4, 1, 4)
+  SENMOE_MMA_CASE(4, 2, 1) SENMOE_MMA_CASE(4, 2, 2) SENMOE_MMA_CASE(4, 2, 4)
+  SENMOE_MMA_CASE(8, 1, 1) SENMOE_MMA_CASE(8, 1, 2) SENMOE_MMA_CASE(8, 1, 4)
+  SENMOE_MMA_CASE(8, 2, 1) SENMOE_MMA_CASE(8, 2, 2) SENMOE_MMA_CASE(8, 2, 4)
+#undef SENMOE_MMA_CASE
+  return cudaErrorNotSupported;
+}
+
+}  // namespace senmoe

@@ -43,7 +43,9 @@
 #include <cuda_fp16.h>
 
 #include "common.cuh"
+#include "dequant.cuh"
 #include "kernels.h"
+#include "tiles.cuh"
 
 namespace senmoe {
 namespace {
@@ -64,14 +66,6 @@ template <int N>
 __device__ __forceinline__ constexpr uint32_t idesc_f16_f32() {
   // D fp32 (bits 4-5 = 1), A and B fp16 (format 0), both K-major, N >> 3, M >> 4.
   return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-      : "memory");
 }
 
 // A from TMEM (row m in lane m, K pairs per 32-bit column), B from shared memory.
@@ -118,23 +112,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Bounded wait that also gives up as soon as another role of the CTA has.
-// Warp-wide callers combine the result with __all_sync so that every lane
-// takes the same branch (they arrive per warp and issue .sync.aligned ops).
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitLimitCycles) {
-      *abort_flag = 1;
-      record_error(err, kDevWaitTimeout);
-      return false;
-    }
-  }
-}
-
 // ------------------------------------------------------- dequantisation
 // Within every aligned block of 8 k-columns both MMA operands are stored in
 // the order (0,4,1,5,2,6,3,7): it is the order in which the 4-bit codes of a
@@ -144,39 +121,6 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 __device__ __forceinline__ int kperm8(int col) {
   const int j = col & 7;
   return (col & ~7) | (j < 4 ? 2 * j : 2 * (j - 4) + 1);
-}
-
-// 8 consecutive 4-bit codes (one u32) -> 8 fp16 w = q * s + b, k-permuted.
-__device__ __forceinline__ uint4 dequant8_u4(uint32_t w, __half2 s2, __half2 b2) {
-  const __half2 k1024 = __floats2half2_rn(1024.0f, 1024.0f);
-  uint32_t v[4];
-  v[0] = (w & 0x000F000Fu) | 0x64006400u;          // codes 0, 4 as fp16 1024 + q
-  v[1] = ((w >> 4) & 0x000F000Fu) | 0x64006400u;   // 1, 5
-  v[2] = ((w >> 8) & 0x000F000Fu) | 0x64006400u;   // 2, 6
-  v[3] = ((w >> 12) & 0x000F000Fu) | 0x64006400u;  // 3, 7
-  uint32_t o[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    __half2 q = __hsub2(*reinterpret_cast<__half2*>(&v[i]), k1024);  // exact
-    __half2 r = __hfma2(q, s2, b2);                                 // one rounding
-    o[i] = *reinterpret_cast<uint32_t*>(&r);
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);  // (0,4),(1,5),(2,6),(3,7)
-}
-
-// Same result through fp16 subnormals: (w << 6, << 2, >> 2, >> 6) & 0x03C003C0
-// puts code k (and k + 4) in mantissa bits 6-9, i.e. the fp16 value q * 2^-18,
-// and fma(q * 2^-18, s * 2^18, b) = q * s + b with one rounding.  s * 2^18 is
-// exact in fp16 for 2^-32 < |s| < 0.2498; callers use dequant8_u4 otherwise.
-__device__ __forceinline__ uint4 dequant8_u4_sub(uint32_t w, __half2 s18, __half2 b2) {
-  const uint32_t m = 0x03C003C0u;
-  const uint32_t v0 = (w << 6) & m, v1 = (w << 2) & m, v2 = (w >> 2) & m, v3 = (w >> 6) & m;
-  __half2 r0 = __hfma2(*reinterpret_cast<const __half2*>(&v0), s18, b2);
-  __half2 r1 = __hfma2(*reinterpret_cast<const __half2*>(&v1), s18, b2);
-  __half2 r2 = __hfma2(*reinterpret_cast<const __half2*>(&v2), s18, b2);
-  __half2 r3 = __hfma2(*reinterpret_cast<const __half2*>(&v3), s18, b2);
-  return make_uint4(*reinterpret_cast<uint32_t*>(&r0), *reinterpret_cast<uint32_t*>(&r1),
-                    *reinterpret_cast<uint32_t*>(&r2), *reinterpret_cast<uint32_t*>(&r3));
 }
 
 // 8 consecutive 8-bit codes (two u32) -> 8 fp16 w = q * s + b, k-permuted.
@@ -322,27 +266,15 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
   pdl_launch_dependents();
 
   // ---- this CTA's tiles: global tile t (m-block fastest within an expert's
-  // slot block) belongs to CTA t % gridDim.x
-  if (tid == 0) {
-    int n = 0, t0 = 0;
-    const int G = gridDim.x, b = blockIdx.x;
-    const int nact = *a.active_count;
-    for (int i = 0; i < nact; ++i) {
-      const int e = a.active[i];
-      const int s0 = a.offsets[e], cnt = a.offsets[e + 1] - s0;
-      const int tiles_e = ((cnt + BN - 1) / BN) * a.m_tiles;
-      for (int t = t0 + ((b - t0 % G) % G + G) % G; t < t0 + tiles_e; t += G) {
-        if (n == kMaxTilesPerCta) {
-          record_error(a.err, kDevTileOverflow);
-          break;
-        }
-        const int local = t - t0, nt = local / a.m_tiles, mt = local % a.m_tiles;
-        s_tiles[n++] = make_int4(e - a.expert_begin, mt * BM, s0 + nt * BN, min(BN, cnt - nt * BN));
-      }
-      t0 += tiles_e;
+  // slot block) belongs to CTA t % gridDim.x.  The packed-code ring is free
+  // until the producer starts: it is the list's scratch.
+  {
+    const int n = list_tiles(a.active, a.active_count, a.offsets, a.expert_begin, a.m_tiles, BM, BN, true, s_tiles,
+                             kMaxTilesPerCta, reinterpret_cast<int*>(sP), a.err);
+    if (tid == 0) {
+      s_ntiles = n;
+      s_abort = 0;
     }
-    s_ntiles = n;
-    s_abort = 0;
   }
   tc_fence_before();
   __syncthreads();
@@ -707,11 +639,46 @@ cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
 // k-permuted within each block of 8 columns like the dequantised weights.
 __global__ void gather_rows_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ perm, int k_div,
                                    uint16_t* __restrict__ out, int hidden, int* err,
-                                   const int32_t* __restrict__ offsets, int eb, int ee) {
+                                   const int32_t* __restrict__ offsets, int eb, int ee, int perm32) {
   pdl_wait();
   pdl_launch_dependents();
   const int s = blockIdx.x;
   if (offsets && (s < offsets[eb] || s >= offsets[ee])) return;  // another rank's slot
+  if (perm32) {
+    // one 32-column block per thread: output chunk p of the block holds
+    // columns p + 8t + 4h at position 8p + 2t + h (kperm32)
+    const int token = perm[s] / k_div;
+    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(token) * hidden);
+    uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(s) * hidden);
+    bool ok = true;
+    for (int b = threadIdx.x; b < hidden / 32; b += blockDim.x) {
+      float f[32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 v = src[4 * b + c];
+        const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          f[8 * c + 2 * k] = bf16_lo(in[k]);
+          f[8 * c + 2 * k + 1] = bf16_hi(in[k]);
+        }
+      }
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        uint32_t o[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float lo = f[8 * t + p], hi = f[8 * t + p + 4];
+          ok &= fabsf(lo) < 65504.0f && fabsf(hi) < 65504.0f;
+          const __half2 h = __floats2half2_rn(lo, hi);
+          o[t] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        dst[4 * b + p] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    if (!ok) record_error(err, kDevFp16Range);
+    return;
+  }
   const int token = perm[s] / k_div;
   const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(token) * hidden);
   uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(s) * hidden);
@@ -739,11 +706,12 @@ __global__ void gather_rows_kernel(const uint16_t* __restrict__ x, const int32_t
 
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
                                int num_slots, int hidden, int* err, cudaStream_t st,
-                               const int32_t* offsets, int eb, int ee) {
+                               const int32_t* offsets, int eb, int ee, bool perm32) {
   if (num_slots <= 0) return cudaSuccess;
-  const int threads = hidden / 8 < 256 ? ((hidden / 8 + 31) / 32) * 32 : 256;
+  const int per = perm32 ? 32 : 8;  // columns per thread
+  const int threads = hidden / per < 256 ? ((hidden / per + 31) / 32) * 32 : 256;
   return launch_pdl(gather_rows_kernel, dim3(num_slots), dim3(threads), 0, st, x, perm, k_div, x_sorted, hidden, err,
-                    offsets, eb, ee);
+                    offsets, eb, ee, perm32 ? 1 : 0);
 }
 
 }  // namespace senmoe

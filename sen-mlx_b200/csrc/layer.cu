@@ -74,8 +74,13 @@ constexpr int kDownRows = 64;
 // 256-token tile of gate and up would fill it with accumulators alone.
 constexpr int kTcTiles[4] = {16, 32, 64, 128};
 constexpr int kTcMaxTile = 3;  // index of the widest tile
-constexpr double kTcMinTokensPerExpert = 3.0;
-enum ExpertPath { kPathAuto = 0, kPathGemv = 1, kPathTensorCore = 2 };
+// Measured on B200 over the 48-layer config-1 stack: the warp-MMA kernel is
+// fastest from 1 to 4 tokens per touched expert (batch 1-64), the tcgen05
+// GEMM from 8 (batch 128+); the CUDA-core GEMV is kept for shapes the tensor
+// paths do not support and as the forced reference path.
+constexpr double kTcMinTokensPerExpert = 6.0;
+constexpr double kMmaMinTokensPerExpert = 0.0;
+enum ExpertPath { kPathAuto = 0, kPathGemv = 1, kPathTensorCore = 2, kPathMma = 3 };
 
 int tc_tile_index(double tokens_per_expert) {
   for (int i = 0; i < kTcMaxTile; ++i)
@@ -115,6 +120,9 @@ struct SenMoeLayer {
   uint16_t* h16 = nullptr;       // fp16 [Tmax*K, I] SwiGLU output (B operand of the down GEMM)
   CUtensorMap tm_gate{}, tm_up{}, tm_down{};  // packed codes, [rows, words]
   CUtensorMap tm_xs[4]{}, tm_h[4]{};          // activation tiles per token-tile width
+  // warp-MMA path
+  bool mma_ok = false;
+  CUtensorMap tm_xs8{}, tm_h8{};              // 8-slot activation tiles
   // expert parallelism (senmoe_layer_connect_peers)
   size_t arena_bytes = 0, o_d = 0, o_flags = 0;
   uint32_t* ep_flags = nullptr;  // ready[8], done[8]: written by peers
@@ -264,26 +272,30 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
   L->arena_bytes = off;
   L->o_d = o_d;
   L->o_flags = o_flags;
-  {  // tensor maps for the tcgen05 path (host-side encoding only)
+  {  // tensor maps for the tensor-core paths (host-side encoding only)
     const int bits = c.bits, El = c.expert_end - c.expert_begin;
     const uint64_t gw = uint64_t(H) * bits / 32, dw = uint64_t(I) * bits / 32;
-    bool ok = tc_supported(int(I), int(H), bits, 2, 128) && tc_supported(int(H), int(I), bits, 1, 128);
     // packed codes: 128-row x 128-byte boxes (32 words), SWIZZLE_128B; a
     // row shorter than a box would need a box wider than the tensor
-    ok = ok && gw >= 32 && dw >= 32;
-    ok = ok && make_tmap_2d(&L->tm_gate, L->w.gate_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, gw, uint64_t(El) * I,
-                            gw * 4, 32, 128, true) == cudaSuccess;
-    ok = ok && make_tmap_2d(&L->tm_up, L->w.up_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, gw, uint64_t(El) * I, gw * 4,
-                            32, 128, true) == cudaSuccess;
-    ok = ok && make_tmap_2d(&L->tm_down, L->w.down_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, dw, uint64_t(El) * H,
-                            dw * 4, 32, 128, true) == cudaSuccess;
-    for (int i = 0; i < 4 && ok; ++i) {
-      ok = make_tmap_2d(&L->tm_xs[i], L->xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, H, P, H * 2, 64, kTcTiles[i], true) ==
-               cudaSuccess &&
-           make_tmap_2d(&L->tm_h[i], L->h16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, I, P, I * 2, 64, kTcTiles[i], true) ==
-               cudaSuccess;
+    bool maps = gw >= 32 && dw >= 32 && I % 128 == 0 && H % 128 == 0;
+    maps = maps && make_tmap_2d(&L->tm_gate, L->w.gate_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, gw,
+                                uint64_t(El) * I, gw * 4, 32, 128, true) == cudaSuccess;
+    maps = maps && make_tmap_2d(&L->tm_up, L->w.up_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, gw, uint64_t(El) * I,
+                                gw * 4, 32, 128, true) == cudaSuccess;
+    maps = maps && make_tmap_2d(&L->tm_down, L->w.down_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, dw,
+                                uint64_t(El) * H, dw * 4, 32, 128, true) == cudaSuccess;
+    for (int i = 0; i < 4 && maps; ++i) {
+      maps = make_tmap_2d(&L->tm_xs[i], L->xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, H, P, H * 2, 64, kTcTiles[i],
+                          true) == cudaSuccess &&
+             make_tmap_2d(&L->tm_h[i], L->h16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, I, P, I * 2, 64, kTcTiles[i],
+                          true) == cudaSuccess;
     }
-    L->tc_ok = ok;
+    L->tc_ok = maps && tc_supported(int(I), int(H), bits, 2, 128) && tc_supported(int(H), int(I), bits, 1, 128);
+    L->mma_ok = maps && mma_supported(int(I), int(H), bits) && mma_supported(int(H), int(I), bits) &&
+                make_tmap_2d(&L->tm_xs8, L->xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, H, P, H * 2, 64, 8, true) ==
+                    cudaSuccess &&
+                make_tmap_2d(&L->tm_h8, L->h16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, I, P, I * 2, 64, 8, true) ==
+                    cudaSuccess;
   }
   e = cudaMemset(L->arena, 0, off);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -314,16 +326,28 @@ int senmoe_layer_destroy(SenMoeLayer* layer) {
   return SENMOE_OK;
 }
 
-// Expert-product kernels one forward of `pairs` (token, slot) pairs takes.
-static bool uses_tensor_cores(const SenMoeLayer* L, int64_t pairs) {
+// Expected tokens per touched local expert for `pairs` (token, slot) pairs.
+static double tokens_per_expert(const SenMoeLayer* L, int64_t pairs) {
   const SenMoeConfig& c = L->cfg;
   const int64_t e_local = c.expert_end - c.expert_begin;
   // expert-parallel ranks see only their experts' share of the pairs
   if (L->ep_world > 0) pairs = pairs * e_local / c.n_routed_experts;
   if (pairs < 1) pairs = 1;
-  const double per_expert = double(pairs) / double(pairs < e_local ? pairs : e_local);
-  const int path = c.reserved[0];
-  return L->tc_ok && (path == kPathTensorCore || (path == kPathAuto && per_expert >= kTcMinTokensPerExpert));
+  return double(pairs) / double(pairs < e_local ? pairs : e_local);
+}
+
+// Expert-product kernels one forward of `pairs` pairs takes (ExpertPath).
+static int expert_path_for(const SenMoeLayer* L, int64_t pairs) {
+  const int forced = L->cfg.reserved[0];
+  if (forced == kPathTensorCore && L->tc_ok) return kPathTensorCore;
+  if (forced == kPathMma && L->mma_ok) return kPathMma;
+  if (forced == kPathGemv) return kPathGemv;
+  if (forced != kPathAuto) return kPathGemv;  // forced path not available for this shape
+  const double pe = tokens_per_expert(L, pairs);
+  if (pe >= kTcMinTokensPerExpert && L->tc_ok) return kPathTensorCore;
+  if (pe >= kMmaMinTokensPerExpert && L->mma_ok) return kPathMma;
+  if (pe >= kMmaMinTokensPerExpert && L->tc_ok) return kPathTensorCore;
+  return kPathGemv;
 }
 
 static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void* y, const SenMoeDebug* debug,
@@ -407,11 +431,48 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   // 3-4. expert products over the touched local experts: h [P, I], d [P, H]
   const int E_local = c.expert_end - c.expert_begin;
   const int max_items = P < E_local ? P : E_local;
-  int64_t P_est = ep ? int64_t(P) * E_local / E : P;  // expected local pairs (as uses_tensor_cores)
-  if (P_est < 1) P_est = 1;
-  const double per_expert = double(P_est) / double(P_est < E_local ? P_est : E_local);
-  const bool use_tc = uses_tensor_cores(L, P);
-  if (use_tc) {
+  const double per_expert = tokens_per_expert(L, P);
+  const int path = expert_path_for(L, P);
+  if (path == kPathMma) {
+    const int nt = per_expert <= 6.0 ? 1 : (per_expert <= 12.0 ? 2 : 4);
+    const CUtensorMap& tb_x = nt == 1 ? L->tm_xs8 : L->tm_xs[nt == 2 ? 0 : 1];
+    const CUtensorMap& tb_h = nt == 1 ? L->tm_h8 : L->tm_h[nt == 2 ? 0 : 1];
+    SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
+                                   ep ? L->offsets : nullptr, c.expert_begin, c.expert_end, true));
+    SENMOE_CUDA(mark(2));
+    TcGemmArgs ga{};
+    ga.s[0] = static_cast<const uint16_t*>(L->w.gate_scales);
+    ga.b[0] = static_cast<const uint16_t*>(L->w.gate_biases);
+    ga.s[1] = static_cast<const uint16_t*>(L->w.up_scales);
+    ga.b[1] = static_cast<const uint16_t*>(L->w.up_biases);
+    ga.rows = I;
+    ga.kdim = H;
+    ga.m_tiles = I / 128;
+    ga.active = L->active;
+    ga.active_count = L->active_count;
+    ga.offsets = L->offsets;
+    ga.expert_begin = c.expert_begin;
+    ga.out = L->h16;
+    ga.out_stride = I;
+    ga.act = c.activation;
+    ga.err = L->err;
+    SENMOE_CUDA(launch_mma_gemm(L->tm_gate, L->tm_up, tb_x, ga, c.bits, 2, nt, (P / (8 * nt) + max_items) * ga.m_tiles,
+                                st));
+    SENMOE_CUDA(mark(3));
+    TcGemmArgs gd = ga;
+    gd.s[0] = static_cast<const uint16_t*>(L->w.down_scales);
+    gd.b[0] = static_cast<const uint16_t*>(L->w.down_biases);
+    gd.s[1] = gd.s[0];
+    gd.b[1] = gd.b[0];
+    gd.rows = H;
+    gd.kdim = I;
+    gd.m_tiles = H / 128;
+    gd.out = L->d;
+    gd.out_stride = H;
+    SENMOE_CUDA(launch_mma_gemm(L->tm_down, L->tm_down, tb_h, gd, c.bits, 1, nt, (P / (8 * nt) + max_items) * gd.m_tiles,
+                                st));
+    SENMOE_CUDA(mark(4));
+  } else if (path == kPathTensorCore) {
     const int ti = tc_tile_index(per_expert), bn = kTcTiles[ti];
     SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
                                    ep ? L->offsets : nullptr, c.expert_begin, c.expert_end));
@@ -582,7 +643,7 @@ int senmoe_layer_expert_path(const SenMoeLayer* L, int64_t num_tokens) {
   g_last_error.clear();
   if (!L) return -fail(SENMOE_ERR_BAD_ARG, "layer is NULL");
   if (num_tokens <= 0) return kPathGemv;
-  return uses_tensor_cores(L, num_tokens * L->cfg.num_experts_per_tok) ? kPathTensorCore : kPathGemv;
+  return expert_path_for(L, num_tokens * L->cfg.num_experts_per_tok);
 }
 
 int senmoe_layer_set_profiling(SenMoeLayer* L, int enable) {

@@ -31,7 +31,9 @@ LIB_PATH = os.path.abspath(os.path.join(_HERE, "..", "lib", "libsenmoe.so"))
 OK, ERR_BAD_ARG, ERR_CUDA, ERR_NCCL, ERR_TIMEOUT, ERR_UNSUPPORTED, ERR_NO_MEMORY, ERR_DEVICE = range(8)
 ROUTER_SOFTMAX_TOPK = 0
 ACT_SWIGLU, ACT_GEGLU = 0, 1
-PATH_AUTO, PATH_GEMV, PATH_TENSOR_CORE = 0, 1, 2  # expert-product kernels (SenMoeConfig.reserved[0])
+# expert-product kernels (SenMoeConfig.reserved[0]): CUDA-core GEMV, tcgen05 GEMM, warp-MMA GEMM
+PATH_AUTO, PATH_GEMV, PATH_TENSOR_CORE, PATH_MMA = 0, 1, 2, 3
+PATH_NAMES = {PATH_GEMV: "gemv", PATH_TENSOR_CORE: "tcgen05", PATH_MMA: "mma"}
 
 
 class SenMoeError(RuntimeError):
@@ -188,7 +190,7 @@ class MoeArgs:
     group_size: int = 64
     activation: int = ACT_SWIGLU
     shared_gate: bool = False  # sigmoid-gated shared expert (no reference counterpart)
-    expert_path: int = PATH_AUTO  # AUTO picks tcgen05 GEMM once experts average >= 3 tokens
+    expert_path: int = PATH_AUTO  # AUTO: GEMV (~1 token per expert), warp MMA (decode), tcgen05 (prefill)
 
 
 @dataclass
@@ -294,7 +296,7 @@ class DeepseekMoe:
         return h
 
     def expert_path(self, num_tokens: int) -> int:
-        """PATH_GEMV or PATH_TENSOR_CORE: the expert kernels a forward of num_tokens runs."""
+        """PATH_GEMV, PATH_MMA or PATH_TENSOR_CORE: the expert kernels a forward of num_tokens runs."""
         r = lib().senmoe_layer_expert_path(self._handle, int(num_tokens))
         if r < 0:
             _check(-r)

@@ -26,7 +26,7 @@ def senmoe():
     return s
 
 
-PATHS = {"gemv": 1, "tc": 2}
+PATHS = {"gemv": 1, "tc": 2, "mma": 3}
 
 
 def run_block(senmoe, cfg, mw, x_bits, max_tokens=None, path=0):
@@ -81,7 +81,7 @@ def config0_layer():
     return cfg, O.make_layer(cfg, seed=0)
 
 
-@pytest.mark.parametrize("path", ["gemv", "tc"])
+@pytest.mark.parametrize("path", ["gemv", "tc", "mma"])
 @pytest.mark.parametrize("T", [1, 8, 16, 64])
 def test_config0_block_vs_oracle(senmoe, config0_layer, T, path):
     cfg, mw = config0_layer
@@ -111,7 +111,20 @@ def test_tensor_core_tiles_vs_oracle(senmoe, bits, T):
     check_against_oracle(cfg, mw, x, got)
 
 
-@pytest.mark.parametrize("path", ["gemv", "tc"])
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("T", [3, 40, 200])
+def test_warp_mma_tiles_vs_oracle(senmoe, bits, T):
+    """Warp-MMA decode kernel at each slot-tile width (8, 16, 32 slots: about 1,
+    10 and 50 tokens per expert, the last in several slot chunks per expert),
+    both code widths, on a small layer (H=256, I=256, E=16, K=4)."""
+    cfg = O.MoeConfig(hidden=256, intermediate=256, num_experts=16, top_k=4, bits=bits)
+    mw = O.make_layer(cfg, seed=40 + bits)
+    x = O.make_tokens(T, cfg.hidden, seed=T + 7 * bits)
+    got = run_block(senmoe, cfg, mw, x, path=PATHS["mma"])
+    check_against_oracle(cfg, mw, x, got)
+
+
+@pytest.mark.parametrize("path", ["gemv", "tc", "mma"])
 def test_block_8bit_shared_gated_large_e(senmoe, path):
     """Config-3-like: E=512, K=10, I=512, sigmoid-gated shared expert (I_s=512)."""
     cfg = O.MoeConfig(hidden=2048, intermediate=512, num_experts=512, top_k=10, bits=4,
@@ -122,7 +135,7 @@ def test_block_8bit_shared_gated_large_e(senmoe, path):
     check_against_oracle(cfg, mw, x, got)
 
 
-@pytest.mark.parametrize("path", ["gemv", "tc"])
+@pytest.mark.parametrize("path", ["gemv", "tc", "mma"])
 def test_block_8bit_skewed(senmoe, path):
     """Config-4-like: 8-bit weights, Zipf-biased router (many tokens on few experts)."""
     cfg = O.MoeConfig(hidden=2048, intermediate=768, num_experts=128, top_k=8, bits=8)
@@ -142,7 +155,7 @@ def test_block_8bit_skewed(senmoe, path):
     check_against_oracle(cfg, mw, x, got)
 
 
-@pytest.mark.parametrize("path", ["gemv", "tc"])
+@pytest.mark.parametrize("path", ["gemv", "tc", "mma"])
 def test_many_tokens_multi_chunk_dispatch(senmoe, path):
     """T*K > 2048 pairs takes the three-kernel dispatch; small H/I keep the oracle fast."""
     cfg = O.MoeConfig(hidden=256, intermediate=256, num_experts=64, top_k=8, bits=4)
