@@ -20,15 +20,16 @@
 //                 tile (fp16 [slots, k], 64-column x 8*NT-row boxes,
 //                 SWIZZLE_128B), into a ring of stages.  No multicast.
 //   warps 0-15    warp w computes rows 16*(w%8) .. +16 for the k-half w/8 of
-//                 every stage (blocks of 32 columns), then the two k-halves
+//                 every stage (half of its 32-column chunks), then the two k-halves
 //                 are added through shared memory and warps 0-7 run the
 //                 epilogue (SwiGLU / GeGLU with MLX's bf16 rounding, or the
 //                 bf16 down output).
-// k order: inside each 32-column block the operands are stored in the order
-// that puts one packed word's code pairs (p, p+4) in the k-pairs of the
-// A fragment (kperm32); B (activations, written by gather_rows_kernel and by
-// the gate/up epilogue) uses the same order, and the contraction does not
-// depend on it.  Operands are fp16 (exact codes, q*s+b rounded once, bf16
+// k order: lane t of k-half kh reads one 32-column chunk (2t + kh) of each
+// 256-column stage, one 16-byte line per row, inside one quantization group;
+// each packed word's code pairs (p, p+4) land in the k-pairs of the A
+// fragment.  B (activations, written by gather_rows_kernel and by the gate/up
+// epilogue) is stored in the matching order (kperm256), and the contraction
+// does not depend on it.  Operands are fp16 (exact codes, q*s+b rounded once, bf16
 // activations exact), accumulation fp32, as on the tcgen05 path.
 // Every mbarrier wait is bounded; a timeout aborts the CTA cleanly.
 
@@ -132,11 +133,14 @@ __device__ __forceinline__ uint4 dequant_pairs(uint32_t w0, uint32_t w1, const G
   }
 }
 
-// Position of feature `col` in the kperm32 order (see the file comment):
-// within each 32-block, column 8t + p + 4h goes to 8p + 2t + h.
-__device__ __forceinline__ int kperm32(int col) {
-  const int c = col & 31, t = c >> 3, r = c & 7, p = r & 3, h = r >> 2;
-  return (col & ~31) | (p << 3) | (t << 1) | h;
+// Position of feature `col` in the kperm256 order of the activation operand:
+// within each 256-column stage, column 32 (2t + kh) + 8b + p + 4h (lane t of
+// k-half kh, block b, code pair p, half h) is stored in 16-byte segment
+// 16 kh + 4 b + p at half 2t + h, so one ldmatrix row per (block, pair)
+// carries the four lanes' pairs in fragment order.
+__device__ __forceinline__ int kperm256(int col) {
+  const int c = col & 255, ch = c >> 5, t = ch >> 1, kh = ch & 1, b = (c >> 3) & 3, r = c & 7;
+  return (col & ~255) | ((16 * kh + 4 * b + (r & 3)) << 3) | (t << 1) | (r >> 2);
 }
 
 template <int BITS, int NPROJ, int NT>
@@ -222,19 +226,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool ok = true;
   const uint32_t sStage_u32 = smem_u32(sStage);
   const int rA = 16 * rg + g;  // tile row of this lane's first fragment row
-  // scales / biases of this lane's two rows for the two groups of its k-half
-  // of a stage: u32 = (group q0, group q0+1), prefetched one stage ahead,
-  // across tile boundaries too
-  uint32_t scur[NPROJ][2], bcur[NPROJ][2], snext[NPROJ][2], bnext[NPROJ][2];
+  // Lane t of k-half kh owns the 32-column chunk c = 2t + kh of every stage
+  // (four 8-column blocks b; one 16-byte line of each row at 4 bits), all
+  // inside quantization group t of the stage.  Its scale / bias for each of
+  // its two rows and each projection are prefetched one stage ahead, across
+  // tile boundaries too.
+  const int cs = 2 * t + kh;
+  uint16_t scur[NPROJ][2], bcur[NPROJ][2], snext[NPROJ][2], bnext[NPROJ][2];
   auto load_sb = [&](int ti, int st) {
     const int4 tn = s_tiles[ti];
-    const size_t row = static_cast<size_t>(tn.x * a.rows + tn.y + rA) * groups + static_cast<size_t>(st) * 4 + kh * 2;
+    const size_t row = static_cast<size_t>(tn.x * a.rows + tn.y + rA) * groups + static_cast<size_t>(st) * 4 + t;
 #pragma unroll
     for (int p = 0; p < NPROJ; ++p) {
-      snext[p][0] = __ldg(reinterpret_cast<const uint32_t*>(a.s[p] + row));
-      snext[p][1] = __ldg(reinterpret_cast<const uint32_t*>(a.s[p] + row + 8 * groups));
-      bnext[p][0] = __ldg(reinterpret_cast<const uint32_t*>(a.b[p] + row));
-      bnext[p][1] = __ldg(reinterpret_cast<const uint32_t*>(a.b[p] + row + 8 * groups));
+      snext[p][0] = __ldg(a.s[p] + row);
+      snext[p][1] = __ldg(a.s[p] + row + 8 * groups);
+      bnext[p][0] = __ldg(a.b[p] + row);
+      bnext[p][1] = __ldg(a.b[p] + row + 8 * groups);
     }
   };
   if (ntiles > 0) load_sb(0, 0);
@@ -260,56 +267,66 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       const unsigned char* base = sStage + slot * S::kStageBytes;
       const uint32_t bbase = sStage_u32 + slot * S::kStageBytes + S::kABytes;
+      GroupConst gc[NPROJ][2];
+      bool all_sub = true;
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {  // the two 64-column groups of this k-half
-        GroupConst gc[NPROJ][2];
-        bool all_sub = true;
+      for (int p = 0; p < NPROJ; ++p)
 #pragma unroll
-        for (int p = 0; p < NPROJ; ++p)
+        for (int r = 0; r < 2; ++r) {
+          gc[p][r] = group_const<BITS>(scur[p][r], bcur[p][r]);
+          all_sub = all_sub && gc[p][r].sub;
+        }
+      all_sub = __all_sync(0xffffffffu, all_sub);
+      // this lane's packed words of the stage, per projection and row:
+      // 4-bit: one 16-byte line (word b for block b); 8-bit: two lines
+      // (words 2b, 2b+1 for block b), chunks 2(c%4), +1 of box c/4
+      uint4 wl[NPROJ][2][BITS / 4];
+#pragma unroll
+      for (int p = 0; p < NPROJ; ++p)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int row = rA + 8 * r;
+          if constexpr (BITS == 4) {
+            wl[p][r][0] = *reinterpret_cast<const uint4*>(base + p * S::kABox + row * 128 + ((cs ^ (row & 7)) << 4));
+          } else {
+            const unsigned char* rowp = base + (p * S::kABoxes + (cs >> 2)) * S::kABox + row * 128;
+            const int c0 = 2 * (cs & 3);
+            wl[p][r][0] = *reinterpret_cast<const uint4*>(rowp + ((c0 ^ (row & 7)) << 4));
+            wl[p][r][1] = *reinterpret_cast<const uint4*>(rowp + (((c0 + 1) ^ (row & 7)) << 4));
+          }
+        }
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        // B fragments (all n-tiles) for the block's two k-steps: segment
+        // 16 kh + 4 b + p of the stage = box 2 kh + b/2, chunk 4 (b%2) + p
+        uint32_t bf[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int n = lane & 7, mi = lane >> 3;
+          const uint32_t addr = bbase + (2 * kh + (b >> 1)) * S::kBBox + (8 * nt + n) * 128 +
+                                ((((b & 1) * 4 + mi) ^ n) << 4);
+          ldmatrix_x4(addr, bf[nt]);
+        }
+#pragma unroll
+        for (int p = 0; p < NPROJ; ++p) {
+          uint4 v[2];
 #pragma unroll
           for (int r = 0; r < 2; ++r) {
-            gc[p][r] = group_const<BITS>(static_cast<uint16_t>(scur[p][r] >> (16 * q)),
-                                         static_cast<uint16_t>(bcur[p][r] >> (16 * q)));
-            all_sub = all_sub && gc[p][r].sub;
+            uint32_t w0, w1 = 0;
+            if constexpr (BITS == 4) {
+              const uint4& L4 = wl[p][r][0];
+              w0 = b == 0 ? L4.x : b == 1 ? L4.y : b == 2 ? L4.z : L4.w;
+            } else {
+              const uint4& L8 = wl[p][r][b >> 1];
+              w0 = (b & 1) ? L8.z : L8.x;
+              w1 = (b & 1) ? L8.w : L8.y;
+            }
+            v[r] = dequant_pairs<BITS>(w0, w1, gc[p][r], all_sub);
           }
-        all_sub = __all_sync(0xffffffffu, all_sub);
-#pragma unroll
-        for (int jj = 0; jj < 2; ++jj) {
-          const int j = kh * 4 + q * 2 + jj;  // 32-column block within the stage
-          // B fragments (all n-tiles) for the block's two k-steps
-          uint32_t bf[NT][4];
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            const int n = lane & 7, mi = lane >> 3;
-            const uint32_t addr = bbase + (j >> 1) * S::kBBox + (8 * nt + n) * 128 +
-                                  ((((j & 1) * 4 + mi) ^ n) << 4);
-            ldmatrix_x4(addr, bf[nt]);
-          }
-#pragma unroll
-          for (int p = 0; p < NPROJ; ++p) {
-            uint4 v[2];
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-              const int row = rA + 8 * r;
-              uint32_t w0, w1 = 0;
-              if constexpr (BITS == 4) {
-                const unsigned char* rowp = base + p * S::kABox + row * 128;
-                w0 = *reinterpret_cast<const uint32_t*>(rowp + ((j ^ (row & 7)) << 4) + 4 * t);
-              } else {
-                // block j = words 8j .. 8j+7 of the stage: box j/4, chunk 2(j%4) + t/2
-                const unsigned char* rowp = base + (p * S::kABoxes + (j >> 2)) * S::kABox + row * 128;
-                const uint2 ww = *reinterpret_cast<const uint2*>(
-                    rowp + (((2 * (j & 3) + (t >> 1)) ^ (row & 7)) << 4) + 8 * (t & 1));
-                w0 = ww.x;
-                w1 = ww.y;
-              }
-              v[r] = dequant_pairs<BITS>(w0, w1, gc[p][r], all_sub);
-            }
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              mma16816(acc[p][nt], v[0].x, v[1].x, v[0].y, v[1].y, bf[nt][0], bf[nt][1]);
-              mma16816(acc[p][nt], v[0].z, v[1].z, v[0].w, v[1].w, bf[nt][2], bf[nt][3]);
-            }
+            mma16816(acc[p][nt], v[0].x, v[1].x, v[0].y, v[1].y, bf[nt][0], bf[nt][1]);
+            mma16816(acc[p][nt], v[0].z, v[1].z, v[0].w, v[1].w, bf[nt][2], bf[nt][3]);
           }
         }
       }
@@ -360,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float gv = round_bf16(acc[0][nt][i]), uv = round_bf16(acc[1][nt][i]);
           const float h = a.act == 0 ? act_swiglu_mlx(gv, uv) : act_geglu_mlx(gv, uv);
           range_ok &= fabsf(h) < 65504.0f;
-          a.out[o + kperm32(row)] = __half_as_ushort(__float2half_rn(h));
+          a.out[o + kperm256(row)] = __half_as_ushort(__float2half_rn(h));
         } else {
           a.out[o + row] = f32_to_bf16_bits(acc[0][nt][i]);
         }

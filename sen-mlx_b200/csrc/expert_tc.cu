@@ -645,36 +645,25 @@ __global__ void gather_rows_kernel(const uint16_t* __restrict__ x, const int32_t
   const int s = blockIdx.x;
   if (offsets && (s < offsets[eb] || s >= offsets[ee])) return;  // another rank's slot
   if (perm32) {
-    // one 32-column block per thread: output chunk p of the block holds
-    // columns p + 8t + 4h at position 8p + 2t + h (kperm32)
+    // kperm256 (warp-MMA operand order): output segment sg (8 halves) of
+    // stage st = sg / 32 holds, at half 2t + h, column
+    // 256 st + 32 (2t + kh) + 8 b + p + 4h with s = sg % 32 = 16 kh + 4 b + p
     const int token = perm[s] / k_div;
-    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(token) * hidden);
+    const uint16_t* src = x + static_cast<size_t>(token) * hidden;
     uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(s) * hidden);
     bool ok = true;
-    for (int b = threadIdx.x; b < hidden / 32; b += blockDim.x) {
-      float f[32];
+    for (int sg = threadIdx.x; sg < hidden / 8; sg += blockDim.x) {
+      const int st = sg >> 5, sp = sg & 31, kh = sp >> 4, b = (sp >> 2) & 3, p = sp & 3;
+      const uint16_t* col0 = src + st * 256 + 32 * kh + 8 * b + p;
+      uint32_t o[4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 v = src[4 * b + c];
-        const uint32_t in[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          f[8 * c + 2 * k] = bf16_lo(in[k]);
-          f[8 * c + 2 * k + 1] = bf16_hi(in[k]);
-        }
+      for (int t = 0; t < 4; ++t) {
+        const float lo = bf16_bits_to_f32(col0[64 * t]), hi = bf16_bits_to_f32(col0[64 * t + 4]);
+        ok &= fabsf(lo) < 65504.0f && fabsf(hi) < 65504.0f;
+        const __half2 h = __floats2half2_rn(lo, hi);
+        o[t] = *reinterpret_cast<const uint32_t*>(&h);
       }
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        uint32_t o[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float lo = f[8 * t + p], hi = f[8 * t + p + 4];
-          ok &= fabsf(lo) < 65504.0f && fabsf(hi) < 65504.0f;
-          const __half2 h = __floats2half2_rn(lo, hi);
-          o[t] = *reinterpret_cast<const uint32_t*>(&h);
-        }
-        dst[4 * b + p] = make_uint4(o[0], o[1], o[2], o[3]);
-      }
+      dst[sg] = make_uint4(o[0], o[1], o[2], o[3]);
     }
     if (!ok) record_error(err, kDevFp16Range);
     return;
@@ -708,8 +697,7 @@ cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div
                                int num_slots, int hidden, int* err, cudaStream_t st,
                                const int32_t* offsets, int eb, int ee, bool perm32) {
   if (num_slots <= 0) return cudaSuccess;
-  const int per = perm32 ? 32 : 8;  // columns per thread
-  const int threads = hidden / per < 256 ? ((hidden / per + 31) / 32) * 32 : 256;
+  const int threads = hidden / 8 < 256 ? ((hidden / 8 + 31) / 32) * 32 : 256;
   return launch_pdl(gather_rows_kernel, dim3(num_slots), dim3(threads), 0, st, x, perm, k_div, x_sorted, hidden, err,
                     offsets, eb, ee, perm32 ? 1 : 0);
 }

@@ -124,17 +124,17 @@ cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
 // `hidden`); a value outside fp16 range records kDevFp16Range in *err.
 // With `offsets` non-null only the slots of experts [eb, ee), i.e. slots
 // offsets[eb] .. offsets[ee], are gathered.  perm32 selects the k order of
-// the warp-MMA kernel (kperm32, 32-column blocks) instead of the tcgen05
-// kernel's (kperm8).
+// the warp-MMA kernel (kperm256, 256-column stages; hidden % 256 == 0)
+// instead of the tcgen05 kernel's (kperm8).
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
                                int num_slots, int hidden, int* err, cudaStream_t st,
                                const int32_t* offsets = nullptr, int eb = 0, int ee = 0, bool perm32 = false);
 
 // ------------------------------------------- warp-MMA expert GEMM (decode)
 // Same arguments as the tcgen05 GEMM (TcGemmArgs; out holds h as fp16 in
-// kperm32 order for the two-projection form, bf16 d for the one-projection
+// kperm256 order for the two-projection form, bf16 d for the one-projection
 // form).  tA*: packed codes [E_local*rows, words] u32, 32-word x 128-row
-// boxes, SWIZZLE_128B; tB: fp16 [slots, kdim] in kperm32 order, 64-column x
+// boxes, SWIZZLE_128B; tB: fp16 [slots, kdim] in kperm256 order, 64-column x
 // 8*nt-row boxes, SWIZZLE_128B.  nt in {1, 2, 4}: 8*nt slots per tile.
 size_t mma_smem_bytes(int bits, int nproj, int nt);
 bool mma_supported(int rows, int kdim, int bits);
