@@ -37,6 +37,8 @@
 
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "dequant.cuh"
 #include "kernels.h"
@@ -48,6 +50,9 @@ namespace {
 constexpr int kRows = 128;           // weight rows per tile
 constexpr int kStageCols = 256;      // k columns per stage
 constexpr int kComputeWarps = 16;    // 8 row groups x 2 k-halves
+// + one producer warp.  (Folding the producer into a compute warp would lift
+// the 96-register cap that a 17th warp imposes, but measured slower: the
+// issuing warp then waits for the slowest warp at every stage.)
 constexpr int kThreads = (kComputeWarps + 1) * 32;
 constexpr int kMaxTiles = 128;       // per CTA
 constexpr int kSmemBudget = 226 * 1024;
@@ -87,19 +92,23 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t (&r)[4]) {
 
 // Per (row, group) dequantisation constants.
 struct GroupConst {
-  __half2 s;    // scale (x 2^18 / 2^22 for the subnormal form)
+  __half2 s;    // scale (x 2^20 at 4 bits / 2^22 at 8 bits for the subnormal form)
   __half2 b;    // bias
   bool sub;     // subnormal form usable
 };
 
+// The subnormal form places each code at fp16 mantissa bits 4-7 (4-bit,
+// value q * 2^-20) or 2-9 (8-bit, q * 2^-22); one fma with s * 2^20 (2^22)
+// then gives q * s + b with a single rounding.  s * 2^20 must stay inside
+// fp16 range: |s| < 0.0624 (4-bit), 0.0156 (8-bit); other groups take the
+// 1024 + q form.
 template <int BITS>
 __device__ __forceinline__ GroupConst group_const(uint16_t sbits, uint16_t bbits) {
   const float sf = bf16_bits_to_f32(sbits);
   GroupConst c;
   c.b = __float2half2_rn(bf16_bits_to_f32(bbits));
-  // 4-bit codes sit at mantissa bits 6-9 (q * 2^-18), 8-bit at bits 2-9 (q * 2^-22)
-  constexpr float kUp = BITS == 4 ? 262144.0f : 4194304.0f;
-  constexpr float kMax = BITS == 4 ? 0.2498f : 0.0156f;
+  constexpr float kUp = BITS == 4 ? 1048576.0f : 4194304.0f;
+  constexpr float kMax = BITS == 4 ? 0.0624f : 0.0156f;
   c.sub = fabsf(sf) < kMax;
   c.s = __float2half2_rn(c.sub ? sf * kUp : sf);
   return c;
@@ -107,19 +116,30 @@ __device__ __forceinline__ GroupConst group_const(uint16_t sbits, uint16_t bbits
 
 // Code pairs (p, p+4), p = 0..3, of the 8 codes a lane holds for one row of a
 // 32-column block, as fp16 q*s+b.  4-bit: one word; 8-bit: two words.
-template <int BITS>
-__device__ __forceinline__ uint4 dequant_pairs(uint32_t w0, uint32_t w1, const GroupConst& c, bool all_sub) {
+// FAST: every group of the warp takes the subnormal form (warp-uniform).
+template <int BITS, bool FAST>
+__device__ __forceinline__ uint4 dequant_pairs(uint32_t w0, uint32_t w1, const GroupConst& c) {
+  uint32_t o[4];
   if constexpr (BITS == 4) {
     (void)w1;
-    return all_sub ? dequant8_u4_sub(w0, c.s, c.b) : (c.sub ? dequant8_u4_sub(w0, c.s, c.b) : dequant8_u4(w0, c.s, c.b));
+    if (FAST || c.sub) {
+      const uint32_t m = 0x00F000F0u;
+      const uint32_t v[4] = {(w0 << 4) & m, w0 & m, (w0 >> 4) & m, (w0 >> 8) & m};
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&v[p]), c.s, c.b);
+        o[p] = *reinterpret_cast<const uint32_t*>(&r);
+      }
+      return make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    return dequant8_u4(w0, c.s, c.b);
   } else {
-    uint32_t o[4];
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
       // bytes: [w0.p, w0.0, w1.p, w0.0]
       const uint32_t t = __byte_perm(w0, w1, static_cast<uint32_t>(p | ((4 + p) << 8)));
       __half2 r;
-      if (all_sub || c.sub) {
+      if (FAST || c.sub) {
         const uint32_t v = (t << 2) & 0x03FC03FCu;  // q * 2^-22 in each half
         r = __hfma2(*reinterpret_cast<const __half2*>(&v), c.s, c.b);
       } else {
@@ -295,41 +315,46 @@ __global__ void __launch_bounds__(kThreads, 1)
             wl[p][r][1] = *reinterpret_cast<const uint4*>(rowp + (((c0 + 1) ^ (row & 7)) << 4));
           }
         }
+      auto run_blocks = [&](auto fast) {
+        constexpr bool F = decltype(fast)::value;
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        // B fragments (all n-tiles) for the block's two k-steps: segment
-        // 16 kh + 4 b + p of the stage = box 2 kh + b/2, chunk 4 (b%2) + p
-        uint32_t bf[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const int n = lane & 7, mi = lane >> 3;
-          const uint32_t addr = bbase + (2 * kh + (b >> 1)) * S::kBBox + (8 * nt + n) * 128 +
-                                ((((b & 1) * 4 + mi) ^ n) << 4);
-          ldmatrix_x4(addr, bf[nt]);
-        }
-#pragma unroll
-        for (int p = 0; p < NPROJ; ++p) {
-          uint4 v[2];
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            uint32_t w0, w1 = 0;
-            if constexpr (BITS == 4) {
-              const uint4& L4 = wl[p][r][0];
-              w0 = b == 0 ? L4.x : b == 1 ? L4.y : b == 2 ? L4.z : L4.w;
-            } else {
-              const uint4& L8 = wl[p][r][b >> 1];
-              w0 = (b & 1) ? L8.z : L8.x;
-              w1 = (b & 1) ? L8.w : L8.y;
-            }
-            v[r] = dequant_pairs<BITS>(w0, w1, gc[p][r], all_sub);
-          }
+        for (int b = 0; b < 4; ++b) {
+          // B fragments (all n-tiles) for the block's two k-steps: segment
+          // 16 kh + 4 b + p of the stage = box 2 kh + b/2, chunk 4 (b%2) + p
+          uint32_t bf[NT][4];
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            mma16816(acc[p][nt], v[0].x, v[1].x, v[0].y, v[1].y, bf[nt][0], bf[nt][1]);
-            mma16816(acc[p][nt], v[0].z, v[1].z, v[0].w, v[1].w, bf[nt][2], bf[nt][3]);
+            const int n = lane & 7, mi = lane >> 3;
+            const uint32_t addr = bbase + (2 * kh + (b >> 1)) * S::kBBox + (8 * nt + n) * 128 +
+                                  ((((b & 1) * 4 + mi) ^ n) << 4);
+            ldmatrix_x4(addr, bf[nt]);
+          }
+#pragma unroll
+          for (int p = 0; p < NPROJ; ++p) {
+            uint4 v[2];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+              uint32_t w0, w1 = 0;
+              if constexpr (BITS == 4) {
+                const uint4& L4 = wl[p][r][0];
+                w0 = b == 0 ? L4.x : b == 1 ? L4.y : b == 2 ? L4.z : L4.w;
+              } else {
+                const uint4& L8 = wl[p][r][b >> 1];
+                w0 = (b & 1) ? L8.z : L8.x;
+                w1 = (b & 1) ? L8.w : L8.y;
+              }
+              v[r] = dequant_pairs<BITS, F>(w0, w1, gc[p][r]);
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              mma16816(acc[p][nt], v[0].x, v[1].x, v[0].y, v[1].y, bf[nt][0], bf[nt][1]);
+              mma16816(acc[p][nt], v[0].z, v[1].z, v[0].w, v[1].w, bf[nt][2], bf[nt][3]);
+            }
           }
         }
-      }
+      };
+      if (all_sub) run_blocks(std::true_type{});
+      else run_blocks(std::false_type{});
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_empty[slot]);
     }

@@ -75,10 +75,10 @@ constexpr int kDownRows = 64;
 constexpr int kTcTiles[4] = {16, 32, 64, 128};
 constexpr int kTcMaxTile = 3;  // index of the widest tile
 // Measured on B200 over the 48-layer config-1 stack: the warp-MMA kernel is
-// fastest up to ~8 tokens per touched expert (batch 1-128), the tcgen05 GEMM
-// from 16 (batch 256+); the CUDA-core GEMV is kept for shapes the tensor
-// paths do not support and as the forced reference path.
-constexpr double kTcMinTokensPerExpert = 10.0;
+// fastest up to at least 16 tokens per touched expert (batch 1-256), the
+// tcgen05 GEMM for prefill-size groups; the CUDA-core GEMV is kept for shapes
+// the tensor paths do not support and as the forced reference path.
+constexpr double kTcMinTokensPerExpert = 24.0;
 constexpr double kMmaMinTokensPerExpert = 0.0;
 enum ExpertPath { kPathAuto = 0, kPathGemv = 1, kPathTensorCore = 2, kPathMma = 3 };
 
@@ -434,7 +434,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   const double per_expert = tokens_per_expert(L, P);
   const int path = expert_path_for(L, P);
   if (path == kPathMma) {
-    const int nt = per_expert <= 8.0 ? 1 : (per_expert <= 16.0 ? 2 : 4);
+    const int nt = per_expert <= 8.0 ? 1 : (per_expert <= 16.0 ? 2 : 4);  // slots per tile: 8 * nt
     const CUtensorMap& tb_x = nt == 1 ? L->tm_xs8 : L->tm_xs[nt == 2 ? 0 : 1];
     const CUtensorMap& tb_h = nt == 1 ? L->tm_h8 : L->tm_h[nt == 2 ? 0 : 1];
     SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
