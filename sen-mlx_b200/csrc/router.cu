@@ -83,20 +83,18 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_logits_kernel(Router
 
 // One warp per token: softmax over E (fp32), scores rounded to bf16, K rounds
 // of warp arg-max (score desc, id asc), then renorm / scaling in fp32.
+// Softmax, top-k and renormalisation of token t's logits, by one warp.
+// Logits are read with ld.global.cg (the fused router reads rows that other
+// CTAs of its grid wrote).
 template <int EPL>  // experts per lane = ceil(E / 32)
-__global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(RouterArgs a) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int t = blockIdx.x * kTopkWarps + warp;
-  pdl_wait();
-  pdl_launch_dependents();
-  if (t >= a.num_tokens) return;
+__device__ __forceinline__ void topk_token(const RouterArgs& a, int t, int lane) {
   const float* lg = a.logits + static_cast<size_t>(t) * a.num_experts;
   float p[EPL];
   float m = -INFINITY;
 #pragma unroll
   for (int j = 0; j < EPL; ++j) {
     const int e = lane + 32 * j;
-    p[j] = e < a.num_experts ? lg[e] : -INFINITY;
+    p[j] = e < a.num_experts ? __ldcg(lg + e) : -INFINITY;
     m = fmaxf(m, p[j]);
   }
 #pragma unroll
@@ -155,6 +153,16 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(RouterArgs
       a.topk_weights[static_cast<size_t>(t) * a.top_k + k] = sel_w[k];
     }
   }
+}
+
+template <int EPL>
+__global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(RouterArgs a) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.x * kTopkWarps + warp;
+  pdl_wait();
+  pdl_launch_dependents();
+  if (t >= a.num_tokens) return;
+  topk_token<EPL>(a, t, lane);
 }
 
 __global__ void sigmoid_inplace_kernel(float* v, int n) {
