@@ -59,6 +59,18 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def measured_traffic():
+    """DRAM bytes (read + write) of one gate/up launch at batch 64 from the
+    committed ncu summary, or None."""
+    import re
+    try:
+        with open(os.path.join(ROOT, "profiles", "qmma_decode_b64.md")) as f:
+            m = re.search(r"traffic_bytes_per_launch_gate_up:\s*(\d+)", f.read())
+        return int(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
 def tensor_peak():
     """Dense 16-bit tensor peak (TFLOP/s): the burst figure, as the expert GEMMs
     are timed as individual launches."""
@@ -84,7 +96,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
+                                          "-i", str(self.gpu), "-lms", "20"], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
@@ -220,10 +232,20 @@ def run_reference(args):
                                        "CPU restatement of the reference block (the reference is Rust+MLX/Metal, "
                                        "not runnable on this box)"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ------------------------------------------------------------ GPU arm
+_JSON_OUT = None
+
+
+def emit(line: dict) -> None:
+    """Writes the result line to the process's original stdout."""
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -240,6 +262,12 @@ def main():
                     help="profiling mode: plain (non-graph) forwards of the workload, W warm-up + K steps, no "
                          "timing or JSON; every step launches 6 kernels per layer in order")
     args = ap.parse_args()
+    # stdout carries only the JSON line: anything else written to fd 1 (NCCL's
+    # version banner, library prints) goes to stderr
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         run_reference(args)
@@ -253,7 +281,6 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")  # stdout carries only the JSON line
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -439,8 +466,12 @@ def main():
                    "experts_per_gpu": E // world,
                    "l2": "weights 16.3 GB per step >> 126 MB L2 (no flush needed)", "cuda_graph": True},
         "sweep": {str(t): r for t, r in results.items()},
-        "roofline": {"bound": "hbm", "kernel": "expert gate/up (+SwiGLU)", "achieved": achieved, "peak": hbm_peak,
-                     "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": None,
+        "roofline": {"bound": "hbm", "kernel": f"expert gate/up (+SwiGLU), {head['expert_kernels']} path",
+                     "achieved": achieved, "peak": hbm_peak,
+                     "unit": "GB/s", "frac": achieved / hbm_peak,
+                     "traffic": (measured_traffic() if args.batch == 64 and world == 1
+                                 and head["expert_kernels"] == "mma" else None),
+                     "traffic_source": "profiles/qmma_decode_b64.md (ncu dram__bytes_read+write, one launch)",
                      "peak_source": hbm_kind,
                      "algorithmic_bytes_per_launch": gate_up_bytes, "avg_launch_ms": gate_up_s * 1e3,
                      "step_hbm_gbs": head["hbm_gbs"], "step_frac": head["hbm_gbs"] / hbm_peak},
@@ -456,7 +487,7 @@ def main():
         line["cpu_baseline"] = cpu_baseline(T=args.batch)
     stack.release()
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -82,8 +82,8 @@ typedef struct SenMoeConfig {
   int32_t max_tokens;              /* T_max: scratch is sized for this at create time */
   int32_t expert_begin;            /* first expert held by this rank (0 on one GPU) */
   int32_t expert_end;              /* one past the last local expert (E on one GPU) */
-  int32_t reserved[3];             /* [0]: expert kernels, 0 auto, 1 CUDA-core GEMV, 2 tcgen05 GEMM;
-                                      [1], [2]: zero */
+  int32_t reserved[3];             /* [0]: expert kernels, 0 auto, 1 CUDA-core GEMV, 2 tcgen05 GEMM,
+                                      3 warp-MMA GEMM; [1], [2]: zero */
 } SenMoeConfig;
 
 /* Device pointers, caller-owned, valid for the layer's lifetime.  Expert
@@ -145,8 +145,8 @@ int senmoe_layer_forward_residual(SenMoeLayer* layer, const void* x, int64_t num
 
 /* Per-stage timing (the build's counterpart of the reference's tracing of
  * prefill/decode rates, src/engine/mlx_native.rs:916-936).  When enabled,
- * forward records CUDA events between its stages on the stream (also inside
- * a CUDA-graph capture).  senmoe_layer_stage_times waits for the last
+ * forward records CUDA events between its stages on the stream (outside a
+ * CUDA-graph capture; inside one the events are skipped).  senmoe_layer_stage_times waits for the last
  * forward's final event and writes that forward's per-stage milliseconds to
  * ms[0 .. n): router, dispatch, gate/up, down, shared expert, combine.
  * Returns the number of stages written (or a negative status). */
@@ -156,8 +156,9 @@ int senmoe_layer_set_profiling(SenMoeLayer* layer, int enable);
 int senmoe_layer_stage_times(SenMoeLayer* layer, float* ms, int n);
 
 /* Which expert-product kernels a forward of num_tokens tokens runs: 1 = the
- * CUDA-core dequant-GEMV (decode-size batches), 2 = the tcgen05 grouped GEMM
- * (prefill-size batches); SenMoeConfig.reserved[0] can force either. */
+ * CUDA-core dequant-GEMV, 2 = the tcgen05 grouped GEMM (prefill-size groups of
+ * tokens per expert), 3 = the warp-MMA grouped GEMM (decode-size groups);
+ * SenMoeConfig.reserved[0] can force one (0 = choose by tokens per expert). */
 int senmoe_layer_expert_path(const SenMoeLayer* layer, int64_t num_tokens);
 
 /* Synchronises `stream` and reports any error a kernel recorded on the
