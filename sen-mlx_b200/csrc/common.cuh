@@ -70,13 +70,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps until it completes (or about kWaitSleepNs passes) instead of
+// returning at once, so waiting warps do not spin through issue slots that
+// working warps need.
+constexpr uint32_t kWaitSleepNs = 20000;
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kWaitSleepNs)
+      : "memory");
+  return ok != 0;
+}
 // Waits for the phase with the given parity to complete, for at most
 // kWaitLimitCycles.  On timeout records kDevWaitTimeout and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
     if (clock64() - t0 > kWaitLimitCycles) {
       record_error(err, kDevWaitTimeout);
       return false;
@@ -153,7 +169,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > kWaitLimitCycles) {
       *abort_flag = 1;

@@ -398,13 +398,27 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
     int pi = 0, ai = 0;
     // scales / biases of the next packed stage, prefetched one stage ahead,
     // across tile boundaries too
-    uint32_t sv[KP / 2], bv[KP / 2], sn[KP / 2], bn[KP / 2];
+    // (sv, bv) this packed stage, (sn, bn) the next, (snn, bnn) the one after:
+    // prefetched two packed stages ahead, across tile boundaries too
+    uint32_t sv[KP / 2], bv[KP / 2], sn[KP / 2], bn[KP / 2], snn[KP / 2], bnn[KP / 2];
     auto group_ptr = [&](int ti, const uint16_t* base_ptr) {
       const int4 t = s_tiles[ti];
       return base_ptr + static_cast<size_t>(t.x * a.rows + t.y + row) * groups;
     };
-    load_group_params<KP>(group_ptr(0, a.s[proj]), sn);
-    load_group_params<KP>(group_ptr(0, a.b[proj]), bn);
+    // loads the parameters of the packed stage `ahead` stages after (ti, kt)
+    auto prefetch = [&](int ti, int kt, int ahead, uint32_t (&sd)[KP / 2], uint32_t (&bd)[KP / 2]) {
+      kt += ahead * KP;
+      while (kt >= ktiles && ti < ntiles) {
+        kt -= ktiles;
+        ++ti;
+      }
+      if (ti < ntiles) {
+        load_group_params<KP>(group_ptr(ti, a.s[proj]) + kt, sd);
+        load_group_params<KP>(group_ptr(ti, a.b[proj]) + kt, bd);
+      }
+    };
+    prefetch(0, 0, 0, sn, bn);
+    prefetch(0, 0, 1, snn, bnn);
     for (int ti = 0; ti < ntiles && ok; ++ti) {
       int ps = 0;
       for (int st = 0; st < nsteps; ++st, ++ai) {
@@ -418,14 +432,10 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
           for (int i = 0; i < KP / 2; ++i) {
             sv[i] = sn[i];
             bv[i] = bn[i];
+            sn[i] = snn[i];
+            bn[i] = bnn[i];
           }
-          if (kt0 + KP < ktiles) {
-            load_group_params<KP>(group_ptr(ti, a.s[proj]) + kt0 + KP, sn);
-            load_group_params<KP>(group_ptr(ti, a.b[proj]) + kt0 + KP, bn);
-          } else if (ti + 1 < ntiles) {
-            load_group_params<KP>(group_ptr(ti + 1, a.s[proj]), sn);
-            load_group_params<KP>(group_ptr(ti + 1, a.b[proj]), bn);
-          }
+          prefetch(ti, kt0, 2, snn, bnn);
         }
         const int as = ai % SA, aph = (ai / SA) & 1;
         ok = __all_sync(0xffffffffu, wait_or_abort(&bar_aempty[as], aph ^ 1, &s_abort, a.err));
@@ -456,7 +466,15 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
           if constexpr (BITS == 4) {  // one word (8 codes) -> four columns
             const float sf = bf16_bits_to_f32(sb);
             const __half2 b2 = __float2half2_rn(bf16_bits_to_f32(bb));
-            if (fabsf(sf) < 0.2498f) {
+            // warp-uniform choice of the dequant form (no divergent branch)
+            if (__all_sync(0xffffffffu, fabsf(sf) < 0.0624f)) {
+              const __half2 s20 = __float2half2_rn(sf * 1048576.0f);
+#pragma unroll
+              for (int i = 0; i < WPT; ++i) {
+                const uint4 v = dequant8_u4_sub20(wd[i], s20, b2);
+                out[4 * i] = v.x; out[4 * i + 1] = v.y; out[4 * i + 2] = v.z; out[4 * i + 3] = v.w;
+              }
+            } else if (fabsf(sf) < 0.2498f) {
               const __half2 s18 = __float2half2_rn(sf * 262144.0f);
 #pragma unroll
               for (int i = 0; i < WPT; ++i) {

@@ -29,8 +29,16 @@ struct RouterArgs {
   int norm_topk_prob;
   float routed_scaling_factor;
   int round_logits;         // 1: logits rounded to bf16 (nn::Linear output dtype)
+  int* err;                 // device error word (bounded waits of the tiled router), may be null
 };
 cudaError_t launch_router_logits(const RouterArgs& a, cudaStream_t st);
+// Prefill router: logits (bf16 tensor-core MMA, fp32 accumulation, bf16
+// rounded) and softmax / top-k in one launch, 32 tokens per CTA; logits are
+// not written to global memory.  tX: x bf16 [T, H], tW: Wg bf16 [E, H], both
+// 64-column boxes with SWIZZLE_128B (32 and 128 rows).  H % 64 == 0, E <= 512.
+bool router_tc_supported(int hidden, int num_experts, int top_k);
+size_t router_tc_smem_bytes(int num_experts);
+cudaError_t launch_router_tc(const CUtensorMap& tX, const CUtensorMap& tW, const RouterArgs& a, cudaStream_t st);
 cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st);
 bool router_supported(int hidden, int num_experts, int top_k);
 

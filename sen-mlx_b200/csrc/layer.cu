@@ -81,6 +81,9 @@ constexpr int kTcMaxTile = 3;  // index of the widest tile
 constexpr double kTcMinTokensPerExpert = 24.0;
 constexpr double kMmaMinTokensPerExpert = 0.0;
 enum ExpertPath { kPathAuto = 0, kPathGemv = 1, kPathTensorCore = 2, kPathMma = 3 };
+// From this many tokens the router runs as one tensor-core launch (logits
+// and top-k, 32 tokens per CTA) instead of the CUDA-core logits + top-k pair.
+constexpr int kRouterTcMinTokens = 128;
 
 int tc_tile_index(double tokens_per_expert) {
   for (int i = 0; i < kTcMaxTile; ++i)
@@ -120,6 +123,9 @@ struct SenMoeLayer {
   uint16_t* h16 = nullptr;       // fp16 [Tmax*K, I] SwiGLU output (B operand of the down GEMM)
   CUtensorMap tm_gate{}, tm_up{}, tm_down{};  // packed codes, [rows, words]
   CUtensorMap tm_xs[4]{}, tm_h[4]{};          // activation tiles per token-tile width
+  // tensor-core prefill router (Wg tensor map; x's is encoded per call)
+  bool rtc_ok = false;
+  CUtensorMap tm_router{};
   // warp-MMA path
   bool mma_ok = false;
   CUtensorMap tm_xs8{}, tm_h8{};              // 8-slot activation tiles
@@ -297,6 +303,9 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                 make_tmap_2d(&L->tm_h8, L->h16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, I, P, I * 2, 64, 8, true) ==
                     cudaSuccess;
   }
+  L->rtc_ok = router_tc_supported(int(H), int(E), int(K)) && E >= 128 &&
+              make_tmap_2d(&L->tm_router, L->w.router_weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, E, H * 2, 64, 128,
+                           true) == cudaSuccess;
   e = cudaMemset(L->arena, 0, off);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   cudaSetDevice(cur);
@@ -389,8 +398,16 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   ra.norm_topk_prob = c.norm_topk_prob;
   ra.routed_scaling_factor = c.routed_scaling_factor;
   ra.round_logits = 1;
-  SENMOE_CUDA(launch_router_logits(ra, st));
-  SENMOE_CUDA(launch_router_topk(ra, st));
+  ra.err = L->err;
+  if (L->rtc_ok && T >= kRouterTcMinTokens) {
+    // prefill sizes: logits on the tensor cores and top-k in one launch
+    CUtensorMap tm_x;
+    SENMOE_CUDA(make_tmap_2d(&tm_x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, T, uint64_t(H) * 2, 64, 32, true));
+    SENMOE_CUDA(launch_router_tc(tm_x, L->tm_router, ra, st));
+  } else {
+    SENMOE_CUDA(launch_router_logits(ra, st));
+    SENMOE_CUDA(launch_router_topk(ra, st));
+  }
   SENMOE_CUDA(mark(1));
 
   // 2. dispatch

@@ -83,18 +83,15 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_logits_kernel(Router
 
 // One warp per token: softmax over E (fp32), scores rounded to bf16, K rounds
 // of warp arg-max (score desc, id asc), then renorm / scaling in fp32.
-// Softmax, top-k and renormalisation of token t's logits, by one warp.
-// Logits are read with ld.global.cg (the fused router reads rows that other
-// CTAs of its grid wrote).
-template <int EPL>  // experts per lane = ceil(E / 32)
-__device__ __forceinline__ void topk_token(const RouterArgs& a, int t, int lane) {
-  const float* lg = a.logits + static_cast<size_t>(t) * a.num_experts;
+// lg is token t's logits row, in global memory (kShared false) or shared.
+template <int EPL, bool kShared>  // experts per lane = ceil(E / 32)
+__device__ __forceinline__ void topk_row(const RouterArgs& a, const float* lg, int t, int lane) {
   float p[EPL];
   float m = -INFINITY;
 #pragma unroll
   for (int j = 0; j < EPL; ++j) {
     const int e = lane + 32 * j;
-    p[j] = e < a.num_experts ? __ldcg(lg + e) : -INFINITY;
+    p[j] = e < a.num_experts ? (kShared ? lg[e] : __ldcg(lg + e)) : -INFINITY;
     m = fmaxf(m, p[j]);
   }
 #pragma unroll
@@ -162,7 +159,143 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(RouterArgs
   pdl_wait();
   pdl_launch_dependents();
   if (t >= a.num_tokens) return;
-  topk_token<EPL>(a, t, lane);
+  topk_row<EPL, false>(a, a.logits + static_cast<size_t>(t) * a.num_experts, t, lane);
+}
+
+// ------------------------------------------- prefill router (tensor cores)
+// For prefill-size batches: CTA = 32 tokens x all experts.  x and Wg stream
+// through a ring of 64-column stages by TMA (2-D tensor maps, SWIZZLE_128B,
+// no multicast), warps take bf16 m16n8k16 MMA fragments from the stages with
+// ldmatrix (products exact in fp32, fp32 accumulation), the bf16-rounded
+// logits stay in shared memory, and the same CTA runs softmax / top-k for its
+// tokens.  Experts come in chunks of 128 (E <= 512).
+namespace {
+constexpr int kRtTok = 32, kRtExp = 128, kRtStages = 4;
+constexpr int kRtCompute = 8;                     // 2 token halves x 4 expert quarters
+constexpr int kRtThreads = (kRtCompute + 1) * 32; // + one TMA warp
+constexpr uint32_t kRtXBytes = kRtTok * 128, kRtWBytes = kRtExp * 128;
+constexpr uint32_t kRtStageBytes = kRtXBytes + kRtWBytes;  // 20 KB
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+}  // namespace
+
+size_t router_tc_smem_bytes(int num_experts) {
+  return 1024 + size_t(kRtStages) * kRtStageBytes + size_t(kRtTok) * num_experts * 4;
+}
+
+template <int EPL>
+__global__ void __launch_bounds__(kRtThreads, 1)
+    router_tc_kernel(const __grid_constant__ CUtensorMap tX, const __grid_constant__ CUtensorMap tW, RouterArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* s_logits = reinterpret_cast<float*>(smem + kRtStages * kRtStageBytes);  // [kRtTok][E]
+  __shared__ __align__(8) uint64_t bar_full[kRtStages], bar_empty[kRtStages];
+  __shared__ int s_abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.x * kRtTok;
+  const int nk = a.hidden / 64, nchunk = (a.num_experts + kRtExp - 1) / kRtExp;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kRtStages; ++i) {
+      mbar_init(&bar_full[i], 1);
+      mbar_init(&bar_empty[i], kRtCompute);
+    }
+    fence_mbar_init();
+    s_abort = 0;
+  }
+  __syncthreads();
+  pdl_wait();  // x comes from the previous kernel
+  pdl_launch_dependents();
+
+  if (warp == kRtCompute) {
+    // ---------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int c = 0; c < nchunk && ok; ++c)
+        for (int k = 0; k < nk; ++k, ++it) {
+          const int slot = it % kRtStages, ph = (it / kRtStages) & 1;
+          if (!(ok = wait_or_abort(&bar_empty[slot], ph ^ 1, &s_abort, a.err))) break;
+          unsigned char* st = smem + slot * kRtStageBytes;
+          mbar_arrive_expect_tx(&bar_full[slot], kRtStageBytes);
+          tma_load_2d(st, &tX, k * 64, t0, &bar_full[slot]);
+          tma_load_2d(st + kRtXBytes, &tW, k * 64, c * kRtExp, &bar_full[slot]);
+        }
+      int never = 0;  // the last stages must land before the CTA exits
+      for (int k = (it > kRtStages ? it - kRtStages : 0); k < it; ++k)
+        wait_or_abort(&bar_full[k % kRtStages], (k / kRtStages) & 1, &never, nullptr);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------ compute warps
+  const int mi = warp & 1, nq = warp >> 1;  // tokens 16 mi .. +16, experts 32 nq .. +32 of a chunk
+  const uint32_t base = smem_u32(smem);
+  int it = 0;
+  bool ok = true;
+  for (int c = 0; c < nchunk && ok; ++c) {
+    float acc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[j][i] = 0.f;
+    for (int k = 0; k < nk; ++k, ++it) {
+      const int slot = it % kRtStages, ph = (it / kRtStages) & 1;
+      ok = __all_sync(0xffffffffu, wait_or_abort(&bar_full[slot], ph, &s_abort, a.err));
+      if (!ok) break;
+      const uint32_t xs = base + slot * kRtStageBytes, ws = xs + kRtXBytes;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {  // four k16 steps of the 64-column stage
+        // A: rows 16 mi + (l & 7) + 8 ((l >> 3) & 1), 16-byte chunk 2 ks + (l >> 4)
+        uint32_t af[4];
+        {
+          const int row = 16 * mi + (lane & 7) + 8 * ((lane >> 3) & 1), ch = 2 * ks + (lane >> 4);
+          ldsm_x4(xs + row * 128 + ((ch ^ (row & 7)) << 4), af);
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // two ldmatrix.x4 = four n-tiles of 8 experts
+          // matrix j = lane >> 3: n-tile 2h + (j >> 1), k half j & 1
+          const int j = lane >> 3;
+          const int row = 32 * nq + 8 * (2 * h + (j >> 1)) + (lane & 7), ch = 2 * ks + (j & 1);
+          uint32_t bfr[4];
+          ldsm_x4(ws + row * 128 + ((ch ^ (row & 7)) << 4), bfr);
+          mma_bf16(acc[2 * h], af, bfr[0], bfr[1]);
+          mma_bf16(acc[2 * h + 1], af, bfr[2], bfr[3]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_empty[slot]);
+    }
+    if (!ok) break;
+    // bf16-rounded logits of this chunk -> shared [token][expert]
+    const int g = lane >> 2, tq = lane & 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int tok = 16 * mi + g + 8 * (i >> 1), e = c * kRtExp + 32 * nq + 8 * j + 2 * tq + (i & 1);
+        if (e < a.num_experts) s_logits[tok * a.num_experts + e] = a.round_logits ? round_bf16(acc[j][i]) : acc[j][i];
+      }
+  }
+  ok = __all_sync(0xffffffffu, ok);
+  // all compute warps' logits are in place (named barrier: the TMA warp has left)
+  asm volatile("bar.sync 1, %0;" ::"r"(kRtCompute * 32) : "memory");
+  if (!ok) return;
+  for (int tl = warp; tl < kRtTok; tl += kRtCompute) {
+    const int tok = t0 + tl;
+    if (tok < a.num_tokens) topk_row<EPL, true>(a, s_logits + tl * a.num_experts, tok, lane);
+  }
 }
 
 __global__ void sigmoid_inplace_kernel(float* v, int n) {
@@ -208,6 +341,27 @@ cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st) {
 cudaError_t launch_sigmoid_inplace(float* v, int n, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
   return launch_pdl(sigmoid_inplace_kernel, dim3((n + 255) / 256), dim3(256), 0, st, v, n);
+}
+
+bool router_tc_supported(int hidden, int num_experts, int top_k) {
+  return router_supported(hidden, num_experts, top_k) && hidden % 64 == 0 && num_experts <= 512;
+}
+
+cudaError_t launch_router_tc(const CUtensorMap& tX, const CUtensorMap& tW, const RouterArgs& a, cudaStream_t st) {
+  if (a.num_tokens == 0) return cudaSuccess;
+  if (!router_tc_supported(a.hidden, a.num_experts, a.top_k)) return cudaErrorNotSupported;
+  const int epl = (a.num_experts + 31) / 32;
+  const size_t smem = router_tc_smem_bytes(a.num_experts);
+  const dim3 grid((a.num_tokens + kRtTok - 1) / kRtTok);
+#define SENMOE_RT_CASE(V)                                                                              \
+  if (epl <= V) {                                                                                    \
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(router_tc_kernel<V>), smem);     \
+    if (e != cudaSuccess) return e;                                                                  \
+    return launch_pdl(router_tc_kernel<V>, grid, dim3(kRtThreads), smem, st, tX, tW, a);             \
+  }
+  SENMOE_RT_CASE(1) SENMOE_RT_CASE(2) SENMOE_RT_CASE(4) SENMOE_RT_CASE(8) SENMOE_RT_CASE(16)
+#undef SENMOE_RT_CASE
+  return cudaErrorNotSupported;
 }
 
 }  // namespace senmoe

@@ -135,6 +135,17 @@ def test_block_8bit_shared_gated_large_e(senmoe, path):
     check_against_oracle(cfg, mw, x, got)
 
 
+def test_prefill_router_large_e(senmoe):
+    """Prefill-size batch at E=512 (config 3 shape, gated shared expert): the
+    tensor-core router runs its four 128-expert chunks, then the tcgen05 path."""
+    cfg = O.MoeConfig(hidden=2048, intermediate=512, num_experts=512, top_k=10, bits=4,
+                      shared_intermediate=512, shared_gate=True)
+    mw = O.make_layer(cfg, seed=13, router_std=1.0 / np.sqrt(2048))
+    x = O.make_tokens(160, cfg.hidden, seed=14)
+    got = run_block(senmoe, cfg, mw, x)
+    check_against_oracle(cfg, mw, x, got)
+
+
 @pytest.mark.parametrize("path", ["gemv", "tc", "mma"])
 def test_block_8bit_skewed(senmoe, path):
     """Config-4-like: 8-bit weights, Zipf-biased router (many tokens on few experts)."""
