@@ -79,7 +79,8 @@ __device__ __forceinline__ int owner_of(const EpArgs& a, int e) {
 // y[t, :] = bf16( sum_j f32(d_owner(j)[inv[t*K + j], :]) * w[t, j]  (+ gate_t * shared[t, :]) (+ residual) )
 // with the one-GPU combine's arithmetic and slot order.  Grid: x covers the
 // hidden columns (8 per thread), y strides over tokens.
-__global__ void __launch_bounds__(256) ep_combine_kernel(EpArgs a, CombineArgs c, int num_tokens) {
+template <int KMAX>  // compile-time bound on top_k sizing the per-thread arrays
+__global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) ep_combine_kernel(EpArgs a, CombineArgs c, int num_tokens) {
   pdl_wait();  // d, ids, inverse and weights of this call are complete
   pdl_launch_dependents();
   const uint32_t epoch = *a.epoch;
@@ -93,7 +94,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(EpArgs a, CombineArgs c
   __syncthreads();
 
   const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
-  constexpr int kMaxK = 16;
+  constexpr int kMaxK = KMAX;
   if (col < c.hidden) {
     for (int t = blockIdx.y; t < num_tokens; t += gridDim.y) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -176,7 +177,8 @@ cudaError_t launch_ep_combine(const EpArgs& a, const CombineArgs& c, int num_tok
   // enough CTAs to cover the tokens of a decode batch in one wave; larger
   // batches loop (each CTA announces and waits once)
   const int gy = num_tokens < 1024 ? num_tokens : 1024;
-  return launch_pdl(ep_combine_kernel, dim3(gx, gy), dim3(threads), 0, st, a, c, num_tokens);
+  if (c.top_k <= 8) return launch_pdl(ep_combine_kernel<8>, dim3(gx, gy), dim3(threads), 0, st, a, c, num_tokens);
+  return launch_pdl(ep_combine_kernel<16>, dim3(gx, gy), dim3(threads), 0, st, a, c, num_tokens);
 }
 
 }  // namespace senmoe

@@ -219,7 +219,10 @@ __global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(QGemvArgs a) {
 
 // y[t, :] = bf16( sum_j f32(d[inv[t*K + j], :]) * w[t, j]  (+ gate_t * shared[t, :]) )
 // in slot order j = 0..K-1 with fp32 accumulation (deepseek_v2.rs:546-552).
-__global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
+// KMAX: compile-time bound on top_k (8 or 16) sizing the per-thread slot and
+// row arrays, so that the register budget allows several CTAs per SM.
+template <int KMAX>
+__global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) combine_kernel(CombineArgs a) {
   pdl_wait();
   pdl_launch_dependents();
   const int t = blockIdx.y;
@@ -228,7 +231,7 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   // all slot indices and weights first, then all rows, so the loads overlap;
   // the sum still runs in slot order j = 0..K-1
-  constexpr int kMaxK = 16;
+  constexpr int kMaxK = KMAX;
   int slot[kMaxK];
   float wj[kMaxK];
 #pragma unroll
@@ -331,7 +334,8 @@ cudaError_t launch_combine(const CombineArgs& a, int num_tokens, cudaStream_t st
   if (num_tokens == 0) return cudaSuccess;
   const int threads = 256;
   dim3 grid((a.hidden / 8 + threads - 1) / threads, num_tokens);
-  return launch_pdl(combine_kernel, grid, dim3(threads), 0, st, a);
+  if (a.top_k <= 8) return launch_pdl(combine_kernel<8>, grid, dim3(threads), 0, st, a);
+  return launch_pdl(combine_kernel<16>, grid, dim3(threads), 0, st, a);
 }
 
 }  // namespace senmoe

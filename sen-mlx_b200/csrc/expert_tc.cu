@@ -654,61 +654,90 @@ cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
 }
 
 // Slot-ordered fp16 copy of the token rows (bf16 -> fp16 is exact in range),
-// k-permuted within each block of 8 columns like the dequantised weights.
-__global__ void gather_rows_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ perm, int k_div,
-                                   uint16_t* __restrict__ out, int hidden, int* err,
-                                   const int32_t* __restrict__ offsets, int eb, int ee, int perm32) {
+// k-permuted within each block of 8 columns like the dequantised weights
+// (kperm8), or in the warp-MMA kernel's kperm256 order.  Each CTA copies
+// kGatherSlots slots, issuing all of its row loads before converting.
+constexpr int kGatherSlots = 4;
+
+__global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __restrict__ x,
+                                                          const int32_t* __restrict__ perm, int k_div,
+                                                          uint16_t* __restrict__ out, int num_slots, int hidden,
+                                                          int* err, const int32_t* __restrict__ offsets, int eb,
+                                                          int ee, int perm32) {
   pdl_wait();
   pdl_launch_dependents();
-  const int s = blockIdx.x;
-  if (offsets && (s < offsets[eb] || s >= offsets[ee])) return;  // another rank's slot
+  const int s0 = blockIdx.x * kGatherSlots;
+  int lo_slot = 0, hi_slot = num_slots;
+  if (offsets) {  // expert parallelism: only this rank's slots
+    lo_slot = offsets[eb];
+    hi_slot = offsets[ee];
+  }
+  const uint16_t* src[kGatherSlots];
+  bool live[kGatherSlots];
+#pragma unroll
+  for (int j = 0; j < kGatherSlots; ++j) {
+    const int s = s0 + j;
+    live[j] = s < num_slots && s >= lo_slot && s < hi_slot;
+    src[j] = x + static_cast<size_t>(live[j] ? perm[s] / k_div : 0) * hidden;
+  }
+  bool ok = true;
   if (perm32) {
     // kperm256 (warp-MMA operand order): output segment sg (8 halves) of
     // stage st = sg / 32 holds, at half 2t + h, column
-    // 256 st + 32 (2t + kh) + 8 b + p + 4h with s = sg % 32 = 16 kh + 4 b + p
-    const int token = perm[s] / k_div;
-    const uint16_t* src = x + static_cast<size_t>(token) * hidden;
-    uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(s) * hidden);
-    bool ok = true;
+    // 256 st + 32 (2t + kh) + 8 b + p + 4h with sg % 32 = 16 kh + 4 b + p
     for (int sg = threadIdx.x; sg < hidden / 8; sg += blockDim.x) {
       const int st = sg >> 5, sp = sg & 31, kh = sp >> 4, b = (sp >> 2) & 3, p = sp & 3;
-      const uint16_t* col0 = src + st * 256 + 32 * kh + 8 * b + p;
-      uint32_t o[4];
+      const int c0 = st * 256 + 32 * kh + 8 * b + p;
+      uint16_t v[kGatherSlots][8];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float lo = bf16_bits_to_f32(col0[64 * t]), hi = bf16_bits_to_f32(col0[64 * t + 4]);
-        ok &= fabsf(lo) < 65504.0f && fabsf(hi) < 65504.0f;
-        const __half2 h = __floats2half2_rn(lo, hi);
-        o[t] = *reinterpret_cast<const uint32_t*>(&h);
+      for (int j = 0; j < kGatherSlots; ++j)
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          v[j][2 * t] = live[j] ? src[j][c0 + 64 * t] : 0;
+          v[j][2 * t + 1] = live[j] ? src[j][c0 + 64 * t + 4] : 0;
+        }
+#pragma unroll
+      for (int j = 0; j < kGatherSlots; ++j) {
+        if (!live[j]) continue;
+        uint32_t o[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float lo = bf16_bits_to_f32(v[j][2 * t]), hi = bf16_bits_to_f32(v[j][2 * t + 1]);
+          ok &= fabsf(lo) < 65504.0f && fabsf(hi) < 65504.0f;
+          const __half2 h = __floats2half2_rn(lo, hi);
+          o[t] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        reinterpret_cast<uint4*>(out + static_cast<size_t>(s0 + j) * hidden)[sg] = make_uint4(o[0], o[1], o[2], o[3]);
       }
-      dst[sg] = make_uint4(o[0], o[1], o[2], o[3]);
     }
-    if (!ok) record_error(err, kDevFp16Range);
-    return;
-  }
-  const int token = perm[s] / k_div;
-  const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(token) * hidden);
-  uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(s) * hidden);
-  bool range_ok = true;
-  for (int i = threadIdx.x; i < hidden / 8; i += blockDim.x) {
-    const uint4 v = src[i];
-    const uint32_t in[4] = {v.x, v.y, v.z, v.w};
-    float f[8];
+  } else {
+    for (int i = threadIdx.x; i < hidden / 8; i += blockDim.x) {
+      uint4 v[kGatherSlots];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      f[2 * k] = bf16_lo(in[k]);
-      f[2 * k + 1] = bf16_hi(in[k]);
-    }
-    uint32_t o[4];
+      for (int j = 0; j < kGatherSlots; ++j)
+        v[j] = live[j] ? reinterpret_cast<const uint4*>(src[j])[i] : make_uint4(0, 0, 0, 0);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {  // k-permuted pairs (k, k + 4), see kperm8
-      range_ok &= fabsf(f[k]) < 65504.0f && fabsf(f[k + 4]) < 65504.0f;
-      const __half2 h = __floats2half2_rn(f[k], f[k + 4]);
-      o[k] = *reinterpret_cast<const uint32_t*>(&h);
+      for (int j = 0; j < kGatherSlots; ++j) {
+        if (!live[j]) continue;
+        const uint32_t in[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+        float f[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          f[2 * k] = bf16_lo(in[k]);
+          f[2 * k + 1] = bf16_hi(in[k]);
+        }
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {  // k-permuted pairs (k, k + 4), see kperm8
+          ok &= fabsf(f[k]) < 65504.0f && fabsf(f[k + 4]) < 65504.0f;
+          const __half2 h = __floats2half2_rn(f[k], f[k + 4]);
+          o[k] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        reinterpret_cast<uint4*>(out + static_cast<size_t>(s0 + j) * hidden)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
     }
-    dst[i] = make_uint4(o[0], o[1], o[2], o[3]);
   }
-  if (!range_ok) record_error(err, kDevFp16Range);
+  if (!ok) record_error(err, kDevFp16Range);
 }
 
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
@@ -716,8 +745,9 @@ cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div
                                const int32_t* offsets, int eb, int ee, bool perm32) {
   if (num_slots <= 0) return cudaSuccess;
   const int threads = hidden / 8 < 256 ? ((hidden / 8 + 31) / 32) * 32 : 256;
-  return launch_pdl(gather_rows_kernel, dim3(num_slots), dim3(threads), 0, st, x, perm, k_div, x_sorted, hidden, err,
-                    offsets, eb, ee, perm32 ? 1 : 0);
+  const int grid = (num_slots + kGatherSlots - 1) / kGatherSlots;
+  return launch_pdl(gather_rows_kernel, dim3(grid), dim3(threads), 0, st, x, perm, k_div, x_sorted, num_slots,
+                    hidden, err, offsets, eb, ee, perm32 ? 1 : 0);
 }
 
 }  // namespace senmoe
