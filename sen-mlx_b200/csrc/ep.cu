@@ -172,7 +172,7 @@ cudaError_t launch_ep_fence(const EpArgs& a, cudaStream_t st) {
 }
 
 cudaError_t launch_ep_combine(const EpArgs& a, const CombineArgs& c, int num_tokens, cudaStream_t st) {
-  const int threads = 256;
+  const int threads = num_tokens < 256 ? 64 : 256;  // narrow CTAs for small batches (>= 8 ranks' flag threads)
   const int gx = (c.hidden / 8 + threads - 1) / threads;
   // enough CTAs to cover the tokens of a decode batch in one wave; larger
   // batches loop (each CTA announces and waits once)

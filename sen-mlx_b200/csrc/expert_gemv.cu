@@ -332,7 +332,8 @@ bool qgemv_supported(int kdim, int bits) {
 
 cudaError_t launch_combine(const CombineArgs& a, int num_tokens, cudaStream_t st) {
   if (num_tokens == 0) return cudaSuccess;
-  const int threads = 256;
+  // small batches: narrow CTAs, so a token's row spreads over several SMs
+  const int threads = num_tokens < 256 ? 64 : 256;
   dim3 grid((a.hidden / 8 + threads - 1) / threads, num_tokens);
   if (a.top_k <= 8) return launch_pdl(combine_kernel<8>, grid, dim3(threads), 0, st, a);
   return launch_pdl(combine_kernel<16>, grid, dim3(threads), 0, st, a);

@@ -82,8 +82,9 @@ constexpr double kTcMinTokensPerExpert = 24.0;
 constexpr double kMmaMinTokensPerExpert = 0.0;
 enum ExpertPath { kPathAuto = 0, kPathGemv = 1, kPathTensorCore = 2, kPathMma = 3 };
 // From this many tokens the router runs as one tensor-core launch (logits
-// and top-k, 32 tokens per CTA) instead of the CUDA-core logits + top-k pair.
-constexpr int kRouterTcMinTokens = 128;
+// and top-k, 32 tokens per CTA, so at least 16 CTAs) instead of the CUDA-core
+// logits + top-k pair.
+constexpr int kRouterTcMinTokens = 512;
 
 int tc_tile_index(double tokens_per_expert) {
   for (int i = 0; i < kTcMaxTile; ++i)

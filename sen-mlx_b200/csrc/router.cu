@@ -19,7 +19,8 @@ namespace senmoe {
 
 namespace {
 constexpr int kRouterWarps = 4;        // experts per CTA (one per warp)
-constexpr int kRouterTokTile = 16;     // tokens per CTA (x tile in shared memory)
+constexpr int kRouterTokTile = 4;      // tokens per CTA (x tile in shared memory): short serial
+                                       // work per warp and 8x E/4 CTAs per 32 tokens
 constexpr int kTopkWarps = 4;          // tokens per CTA in the top-k kernel
 constexpr int kMaxTopK = 16;
 }  // namespace

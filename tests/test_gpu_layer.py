@@ -141,7 +141,7 @@ def test_prefill_router_large_e(senmoe):
     cfg = O.MoeConfig(hidden=2048, intermediate=512, num_experts=512, top_k=10, bits=4,
                       shared_intermediate=512, shared_gate=True)
     mw = O.make_layer(cfg, seed=13, router_std=1.0 / np.sqrt(2048))
-    x = O.make_tokens(160, cfg.hidden, seed=14)
+    x = O.make_tokens(512, cfg.hidden, seed=14)
     got = run_block(senmoe, cfg, mw, x)
     check_against_oracle(cfg, mw, x, got)
 
