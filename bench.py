@@ -177,11 +177,14 @@ def make_stack(torch, senmoe, device, layers, max_tokens, seed=0, rank=0, world=
 
 
 def launches_per_forward(T, tensor_cores, world):
-    """Kernels one forward launches: router logits + top-k, dispatch (one
-    kernel up to 2048 pairs, else three), the expert-parallel fence, the
-    gathered-activation copy (tensor-core paths), gate/up, down, combine."""
+    """Kernels one forward launches: the router (one kernel from 128 tokens,
+    where top-k runs in the logits kernel's last CTAs or the tensor-core
+    router; logits + top-k below), dispatch (one kernel up to 2048 pairs,
+    else three), the expert-parallel fence, the gathered-activation copy
+    (tensor-core paths), gate/up, down, combine."""
+    router = 1 if T >= 128 else 2
     disp = 1 if (T * K + 1023) // 1024 <= 2 else 3
-    return 2 + disp + (1 if world > 1 else 0) + (1 if tensor_cores else 0) + 3
+    return router + disp + (1 if world > 1 else 0) + (1 if tensor_cores else 0) + 3
 
 
 # --------------------------------------------------------- CPU baseline

@@ -18,30 +18,6 @@ enum DeviceError : int {
   kDevPeerTimeout = 5,  // a bounded wait on another rank's flag ran out
 };
 
-// ---------------------------------------------------------------- router
-struct RouterArgs {
-  const uint16_t* x;        // bf16 [T, H]
-  const uint16_t* weight;   // bf16 [E, H]
-  float* logits;            // fp32 [T, E] (bf16-rounded values unless raw)
-  int32_t* topk_ids;        // [T, K]
-  float* topk_weights;      // [T, K]
-  int num_tokens, hidden, num_experts, top_k;
-  int norm_topk_prob;
-  float routed_scaling_factor;
-  int round_logits;         // 1: logits rounded to bf16 (nn::Linear output dtype)
-  int* err;                 // device error word (bounded waits of the tiled router), may be null
-};
-cudaError_t launch_router_logits(const RouterArgs& a, cudaStream_t st);
-// Prefill router: logits (bf16 tensor-core MMA, fp32 accumulation, bf16
-// rounded) and softmax / top-k in one launch, 32 tokens per CTA; logits are
-// not written to global memory.  tX: x bf16 [T, H], tW: Wg bf16 [E, H], both
-// 64-column boxes with SWIZZLE_128B (32 and 128 rows).  H % 64 == 0, E <= 512.
-bool router_tc_supported(int hidden, int num_experts, int top_k);
-size_t router_tc_smem_bytes(int num_experts);
-cudaError_t launch_router_tc(const CUtensorMap& tX, const CUtensorMap& tW, const RouterArgs& a, cudaStream_t st);
-cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st);
-bool router_supported(int hidden, int num_experts, int top_k);
-
 // -------------------------------------------------------------- dispatch
 struct DispatchArgs {
   const int32_t* topk_ids;  // [P] = [T*K]
@@ -56,6 +32,34 @@ struct DispatchArgs {
   int* err;
   int keep_remote_slots;    // 1: inverse keeps the slot of non-local experts too
 };
+// ---------------------------------------------------------------- router
+struct RouterArgs {
+  const uint16_t* x;        // bf16 [T, H]
+  const uint16_t* weight;   // bf16 [E, H]
+  float* logits;            // fp32 [T, E] (bf16-rounded values unless raw)
+  int32_t* topk_ids;        // [T, K]
+  float* topk_weights;      // [T, K]
+  int num_tokens, hidden, num_experts, top_k;
+  int norm_topk_prob;
+  float routed_scaling_factor;
+  int round_logits;         // 1: logits rounded to bf16 (nn::Linear output dtype)
+  int* err;                 // device error word (bounded waits of the tiled router), may be null
+  // Fusion (router_logits_kernel only): with tile_cnt set, the last CTA of
+  // each 4-token tile runs top-k for its tokens (tile_cnt: one zeroed int per
+  // tile, left zero), so no top-k launch follows.
+  int* tile_cnt;
+};
+cudaError_t launch_router_logits(const RouterArgs& a, cudaStream_t st);
+// Prefill router: logits (bf16 tensor-core MMA, fp32 accumulation, bf16
+// rounded) and softmax / top-k in one launch, 32 tokens per CTA; logits are
+// not written to global memory.  tX: x bf16 [T, H], tW: Wg bf16 [E, H], both
+// 64-column boxes with SWIZZLE_128B (32 and 128 rows).  H % 64 == 0, E <= 512.
+bool router_tc_supported(int hidden, int num_experts, int top_k);
+size_t router_tc_smem_bytes(int num_experts);
+cudaError_t launch_router_tc(const CUtensorMap& tX, const CUtensorMap& tW, const RouterArgs& a, cudaStream_t st);
+cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st);
+bool router_supported(int hidden, int num_experts, int top_k);
+
 constexpr int kDispatchChunk = 1024;
 cudaError_t launch_dispatch(const DispatchArgs& a, cudaStream_t st);
 size_t dispatch_smem_bytes(int num_experts);

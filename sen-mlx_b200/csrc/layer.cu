@@ -85,6 +85,9 @@ enum ExpertPath { kPathAuto = 0, kPathGemv = 1, kPathTensorCore = 2, kPathMma = 
 // and top-k, 32 tokens per CTA, so at least 16 CTAs) instead of the CUDA-core
 // logits + top-k pair.
 constexpr int kRouterTcMinTokens = 512;
+// From this many tokens the CUDA-core router runs top-k in its own last CTAs
+// (measured: a separate top-k launch is as fast below that).
+constexpr int kFusedTopkMinTokens = 128;
 
 int tc_tile_index(double tokens_per_expert) {
   for (int i = 0; i < kTcMaxTile; ++i)
@@ -124,6 +127,7 @@ struct SenMoeLayer {
   uint16_t* h16 = nullptr;       // fp16 [Tmax*K, I] SwiGLU output (B operand of the down GEMM)
   CUtensorMap tm_gate{}, tm_up{}, tm_down{};  // packed codes, [rows, words]
   CUtensorMap tm_xs[4]{}, tm_h[4]{};          // activation tiles per token-tile width
+  int* route_cnt = nullptr;      // fused top-k tile counters [ceil(Tmax/4)] (null: separate top-k)
   // tensor-core prefill router (Wg tensor map; x's is encoded per call)
   bool rtc_ok = false;
   CUtensorMap tm_router{};
@@ -246,7 +250,8 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                o_err = take(4), o_hist = take(size_t(L->nchunks_max) * E * 4), o_h = take(P * I * 2),
                o_d = take(P * H * 2), o_shh = take(Is ? T * Is * 2 : 0), o_sho = take(Is ? T * H * 2 : 0),
                o_shg = take(Is ? T * 4 : 0), o_zero = take(Is ? T * 4 : 0), o_xs = take(P * H * 2),
-               o_h16 = take(P * I * 2), o_flags = take(kEpFlagBytes), o_local = take(8);
+               o_h16 = take(P * I * 2), o_flags = take(kEpFlagBytes), o_local = take(8),
+               o_route = take((T + 3) / 4 * 4);
   cudaError_t e = cudaMalloc(&L->arena, off);
   if (e != cudaSuccess) {
     delete L;
@@ -274,6 +279,7 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
   }
   L->xs = reinterpret_cast<uint16_t*>(base + o_xs);
   L->h16 = reinterpret_cast<uint16_t*>(base + o_h16);
+  L->route_cnt = reinterpret_cast<int*>(base + o_route);
   L->ep_flags = reinterpret_cast<uint32_t*>(base + o_flags);
   L->ep_local = reinterpret_cast<uint32_t*>(base + o_local);
   L->arena_bytes = off;
@@ -400,16 +406,6 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   ra.routed_scaling_factor = c.routed_scaling_factor;
   ra.round_logits = 1;
   ra.err = L->err;
-  if (L->rtc_ok && T >= kRouterTcMinTokens) {
-    // prefill sizes: logits on the tensor cores and top-k in one launch
-    CUtensorMap tm_x;
-    SENMOE_CUDA(make_tmap_2d(&tm_x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, T, uint64_t(H) * 2, 64, 32, true));
-    SENMOE_CUDA(launch_router_tc(tm_x, L->tm_router, ra, st));
-  } else {
-    SENMOE_CUDA(launch_router_logits(ra, st));
-    SENMOE_CUDA(launch_router_topk(ra, st));
-  }
-  SENMOE_CUDA(mark(1));
 
   // 2. dispatch
   DispatchArgs da{};
@@ -427,7 +423,26 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   da.err = L->err;
   const bool ep = L->ep_world > 0;
   da.keep_remote_slots = ep ? 1 : 0;  // the combine reads remote slots from their owners
-  SENMOE_CUDA(launch_dispatch(da, st));
+  if (L->rtc_ok && T >= kRouterTcMinTokens) {
+    // prefill sizes: logits on the tensor cores and top-k in one launch
+    CUtensorMap tm_x;
+    SENMOE_CUDA(make_tmap_2d(&tm_x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, T, uint64_t(H) * 2, 64, 32, true));
+    SENMOE_CUDA(launch_router_tc(tm_x, L->tm_router, ra, st));
+    SENMOE_CUDA(mark(1));
+    SENMOE_CUDA(launch_dispatch(da, st));
+  } else if (L->route_cnt && T >= kFusedTopkMinTokens) {
+    // one launch: logits, then top-k by the last CTA of each 4-token tile
+    RouterArgs rf = ra;
+    rf.tile_cnt = L->route_cnt;
+    SENMOE_CUDA(launch_router_logits(rf, st));
+    SENMOE_CUDA(mark(1));
+    SENMOE_CUDA(launch_dispatch(da, st));
+  } else {
+    SENMOE_CUDA(launch_router_logits(ra, st));
+    SENMOE_CUDA(launch_router_topk(ra, st));
+    SENMOE_CUDA(mark(1));
+    SENMOE_CUDA(launch_dispatch(da, st));
+  }
   EpArgs ea{};
   if (ep) {
     ea.rank = L->ep_rank;
@@ -609,6 +624,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
       gr.logits = L->sh_gate;
       gr.num_experts = 1;
       gr.round_logits = 0;
+      gr.tile_cnt = nullptr;  // a plain dot product: no top-k
       SENMOE_CUDA(launch_router_logits(gr, st));
       SENMOE_CUDA(launch_sigmoid_inplace(L->sh_gate, T, st));
     }

@@ -20,67 +20,11 @@ namespace senmoe {
 namespace {
 constexpr int kRouterWarps = 4;        // experts per CTA (one per warp)
 constexpr int kRouterTokTile = 4;      // tokens per CTA (x tile in shared memory): short serial
-                                       // work per warp and 8x E/4 CTAs per 32 tokens
+                                       // work per warp, E/4 x T/4 CTAs
+static_assert(kRouterTokTile <= kRouterWarps, "fused top-k runs one warp per token of a tile");
 constexpr int kTopkWarps = 4;          // tokens per CTA in the top-k kernel
 constexpr int kMaxTopK = 16;
 }  // namespace
-
-// Each warp owns one expert row (held in registers as packed bf16; lane l
-// holds columns 256 i + 8 l .. +8), each CTA a tile of tokens staged in shared
-// memory; one fp32 dot per (token, expert), reduced by warp shuffles.
-template <int VPL>  // 16-byte vectors per lane = ceil(H / 256)
-__global__ void __launch_bounds__(kRouterWarps * 32) router_logits_kernel(RouterArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ __align__(8) uint64_t bar;
-  uint4* xs = reinterpret_cast<uint4*>(smem);  // [tile][H/8]
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int e = blockIdx.x * kRouterWarps + warp;
-  const int t0 = blockIdx.y * kRouterTokTile;
-  const int nt = min(kRouterTokTile, a.num_tokens - t0);
-  const int vec_per_row = a.hidden / 8;
-
-  // The router weights do not depend on the previous kernel: load them before
-  // waiting for it (programmatic dependent launch).
-  float wv[VPL][8];
-  const uint4* wrow = reinterpret_cast<const uint4*>(a.weight + static_cast<size_t>(e < a.num_experts ? e : 0) *
-                                                                    a.hidden);
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const uint4 v = (32 * i + lane < vec_per_row) ? wrow[32 * i + lane] : make_uint4(0, 0, 0, 0);
-    wv[i][0] = bf16_lo(v.x); wv[i][1] = bf16_hi(v.x); wv[i][2] = bf16_lo(v.y); wv[i][3] = bf16_hi(v.y);
-    wv[i][4] = bf16_lo(v.z); wv[i][5] = bf16_hi(v.z); wv[i][6] = bf16_lo(v.w); wv[i][7] = bf16_hi(v.w);
-  }
-  if (threadIdx.x == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  pdl_wait();
-  pdl_launch_dependents();
-  // the token tile is one contiguous range of x: a single bulk copy
-  if (threadIdx.x == 0) {
-    const uint32_t bytes = static_cast<uint32_t>(nt) * a.hidden * 2;
-    mbar_arrive_expect_tx(&bar, bytes);
-    bulk_g2s(xs, a.x + static_cast<size_t>(t0) * a.hidden, bytes, &bar, policy_evict_last());
-  }
-  if (!mbar_wait(&bar, 0, nullptr)) return;
-  if (e >= a.num_experts) return;
-  for (int t = 0; t < nt; ++t) {
-    float acc = 0.f;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      if (32 * i + lane >= vec_per_row) break;
-      const uint4 v = xs[t * vec_per_row + 32 * i + lane];
-      acc = fmaf(bf16_lo(v.x), wv[i][0], acc); acc = fmaf(bf16_hi(v.x), wv[i][1], acc);
-      acc = fmaf(bf16_lo(v.y), wv[i][2], acc); acc = fmaf(bf16_hi(v.y), wv[i][3], acc);
-      acc = fmaf(bf16_lo(v.z), wv[i][4], acc); acc = fmaf(bf16_hi(v.z), wv[i][5], acc);
-      acc = fmaf(bf16_lo(v.w), wv[i][6], acc); acc = fmaf(bf16_hi(v.w), wv[i][7], acc);
-    }
-    acc = warp_sum(acc);
-    if (lane == 0)
-      a.logits[static_cast<size_t>(t0 + t) * a.num_experts + e] = a.round_logits ? round_bf16(acc) : acc;
-  }
-}
 
 // One warp per token: softmax over E (fp32), scores rounded to bf16, K rounds
 // of warp arg-max (score desc, id asc), then renorm / scaling in fp32.
@@ -151,6 +95,89 @@ __device__ __forceinline__ void topk_row(const RouterArgs& a, const float* lg, i
       a.topk_weights[static_cast<size_t>(t) * a.top_k + k] = sel_w[k];
     }
   }
+}
+
+// top-k of token t for any E <= 512 (logits row in global memory).
+__device__ __forceinline__ void topk_any(const RouterArgs& a, int t, int lane) {
+  const float* lg = a.logits + static_cast<size_t>(t) * a.num_experts;
+  const int epl = (a.num_experts + 31) / 32;
+  if (epl <= 1) topk_row<1, false>(a, lg, t, lane);
+  else if (epl <= 2) topk_row<2, false>(a, lg, t, lane);
+  else if (epl <= 4) topk_row<4, false>(a, lg, t, lane);
+  else if (epl <= 8) topk_row<8, false>(a, lg, t, lane);
+  else topk_row<16, false>(a, lg, t, lane);
+}
+
+// Each warp owns one expert row (held in registers as packed bf16; lane l
+// holds columns 256 i + 8 l .. +8), each CTA a tile of tokens staged in shared
+// memory; one fp32 dot per (token, expert), reduced by warp shuffles.
+template <int VPL>  // 16-byte vectors per lane = ceil(H / 256)
+__global__ void __launch_bounds__(kRouterWarps * 32) router_logits_kernel(RouterArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ __align__(8) uint64_t bar;
+  uint4* xs = reinterpret_cast<uint4*>(smem);  // [tile][H/8]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int e = blockIdx.x * kRouterWarps + warp;
+  const int t0 = blockIdx.y * kRouterTokTile;
+  const int nt = min(kRouterTokTile, a.num_tokens - t0);
+  const int vec_per_row = a.hidden / 8;
+
+  // The router weights do not depend on the previous kernel: load them before
+  // waiting for it (programmatic dependent launch).
+  float wv[VPL][8];
+  const uint4* wrow = reinterpret_cast<const uint4*>(a.weight + static_cast<size_t>(e < a.num_experts ? e : 0) *
+                                                                    a.hidden);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const uint4 v = (32 * i + lane < vec_per_row) ? wrow[32 * i + lane] : make_uint4(0, 0, 0, 0);
+    wv[i][0] = bf16_lo(v.x); wv[i][1] = bf16_hi(v.x); wv[i][2] = bf16_lo(v.y); wv[i][3] = bf16_hi(v.y);
+    wv[i][4] = bf16_lo(v.z); wv[i][5] = bf16_hi(v.z); wv[i][6] = bf16_lo(v.w); wv[i][7] = bf16_hi(v.w);
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_launch_dependents();
+  // the token tile is one contiguous range of x: a single bulk copy
+  if (threadIdx.x == 0) {
+    const uint32_t bytes = static_cast<uint32_t>(nt) * a.hidden * 2;
+    mbar_arrive_expect_tx(&bar, bytes);
+    bulk_g2s(xs, a.x + static_cast<size_t>(t0) * a.hidden, bytes, &bar, policy_evict_last());
+  }
+  const bool ok = mbar_wait(&bar, 0, a.err);
+  if (ok && e < a.num_experts) {
+    for (int t = 0; t < nt; ++t) {
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      if (32 * i + lane >= vec_per_row) break;
+      const uint4 v = xs[t * vec_per_row + 32 * i + lane];
+      acc = fmaf(bf16_lo(v.x), wv[i][0], acc); acc = fmaf(bf16_hi(v.x), wv[i][1], acc);
+      acc = fmaf(bf16_lo(v.y), wv[i][2], acc); acc = fmaf(bf16_hi(v.y), wv[i][3], acc);
+      acc = fmaf(bf16_lo(v.z), wv[i][4], acc); acc = fmaf(bf16_hi(v.z), wv[i][5], acc);
+      acc = fmaf(bf16_lo(v.w), wv[i][6], acc); acc = fmaf(bf16_hi(v.w), wv[i][7], acc);
+    }
+      acc = warp_sum(acc);
+      if (lane == 0)
+        a.logits[static_cast<size_t>(t0 + t) * a.num_experts + e] = a.round_logits ? round_bf16(acc) : acc;
+    }
+  }
+  if (!a.tile_cnt) return;
+
+  // ---- fused top-k: the last CTA to finish this token tile (one warp per token)
+  __shared__ int s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s_last = atomicAdd(&a.tile_cnt[blockIdx.y], 1) == static_cast<int>(gridDim.x) - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  if (threadIdx.x == 0) a.tile_cnt[blockIdx.y] = 0;  // ready for the next call
+  __threadfence();
+  if (warp < nt) topk_any(a, t0 + warp, lane);
 }
 
 template <int EPL>
