@@ -57,7 +57,7 @@ constexpr int kThreads = (kComputeWarps + 1) * 32;
 constexpr int kMaxTiles = 128;       // per CTA
 constexpr int kSmemBudget = 226 * 1024;
 
-template <int BITS, int NPROJ, int NT>
+template <int BITS, int NPROJ, int NT, bool G4>
 struct MmaShape {
   static constexpr int kABoxes = BITS / 4;                   // 128-byte boxes per row per stage
   static constexpr int kABox = kRows * 128;                  // 16 KB
@@ -65,7 +65,11 @@ struct MmaShape {
   static constexpr int kBRows = 8 * NT;
   static constexpr int kBBox = kBRows * 128;                 // 64 fp16 columns x kBRows
   static constexpr int kBBytes = 4 * kBBox;
-  static constexpr int kStageBytes = kABytes + kBBytes;      // multiple of 1024
+  static constexpr int kTmaBytes = kABytes + kBBytes;        // bytes the TMA copies per stage
+  // group-scaled form: the stage's scales and biases, [proj][s, b][row][4 groups] bf16
+  static constexpr int kSBOff = kTmaBytes;
+  static constexpr int kSBBytes = G4 ? NPROJ * 2 * kRows * 8 : 0;
+  static constexpr int kStageBytes = kTmaBytes + kSBBytes;   // multiple of 1024
   static constexpr int kRedBytes = 8 * 32 * NPROJ * NT * 4 * 4;
   static constexpr int kMisc = 4096;                         // barriers + tile list
   static constexpr int kFit = (kSmemBudget - kRedBytes - kMisc - 1024) / kStageBytes;
@@ -89,6 +93,56 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t (&r)[4]) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
 }
+
+// MMAs of the group-scaled form: no memory operands, so the compiler may
+// schedule them freely; the _z form starts from a zero accumulator.
+__device__ __forceinline__ void mma_acc(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                      uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%10, %10, %10, %10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
+// ---------------------------------------------------------------------------
+// Group-scaled 4-bit form.  Instead of dequantising every weight to fp16, the
+// MMA multiplies the raw codes and each 64-column quantization group is
+// scaled afterwards in fp32, the way MLX's own quantized GEMV accumulates
+//   y = sum_G ( s_G * sum_{k in G} q_k x_k  +  b_G * sum_{k in G} x_k ).
+// A code goes into the A fragment as an fp16 subnormal with one AND: bits
+// 0-3 of a half hold q * 2^-24, bits 4-7 hold q * 2^-20 (mma.sync multiplies
+// subnormal fp16 operands exactly).  Each MMA k-step takes codes of one
+// position kind only -- even k-steps the nibbles at bits 0-3 (and, from the
+// word shifted right by 8, bits 8-11), odd k-steps those at bits 4-7 (12-15)
+// -- and the activations of odd k-steps are stored divided by 16, so every
+// product lands in units of 2^-24 and one accumulator serves the group.  The
+// group sums of x come from four more MMAs per group whose A is the constant
+// 2^-24 (even k-steps) or 2^-20 (odd), on the otherwise idle tensor pipe.
+//
+// k order inside each 64-column group (the same for every group): physical
+// column u = 8 w + i (packed word w = 0..7 of the group, nibble i) is MMA
+// k-step s = 2 (w / 4) + (i & 1), fragment index kappa = 2 (w % 4) + (i >> 2)
+// + 8 ((i >> 1) & 1), and is stored at position 16 s + kappa; columns with
+// odd u hold x / 16.  Lane t then needs words t and 4 + t of the group for
+// each of its rows: one ldmatrix.x4 of the packed codes.
+__device__ __forceinline__ int kperm_g4(int col) {
+  const int u = col & 63, w = u >> 3, i = u & 7;
+  const int s = 2 * (w >> 2) + (i & 1);
+  const int kappa = 2 * (w & 3) + (i >> 2) + 8 * ((i >> 1) & 1);
+  return (col & ~63) | (16 * s + kappa);
+}
+constexpr uint32_t kCodeLo = 0x000F000Fu;   // codes at bits 0-3 of each half: q * 2^-24
+constexpr uint32_t kCodeHi = 0x00F000F0u;   // codes at bits 4-7: q * 2^-20
+constexpr uint32_t kOne24 = 0x00010001u;    // fp16 2^-24 in both halves
+constexpr uint32_t kOne20 = 0x00100010u;    // fp16 2^-20
+constexpr float kG4Scale = 16777216.0f;     // 2^24: accumulator units back to 1
 
 // Per (row, group) dequantisation constants.
 struct GroupConst {
@@ -163,11 +217,14 @@ __device__ __forceinline__ int kperm256(int col) {
   return (col & ~255) | ((16 * kh + 4 * b + (r & 3)) << 3) | (t << 1) | (r >> 2);
 }
 
-template <int BITS, int NPROJ, int NT>
+// G4: the group-scaled 4-bit form (kperm_g4 activations); otherwise every
+// weight is dequantised to fp16 (kperm256 activations).
+template <int BITS, int NPROJ, int NT, bool G4>
 __global__ void __launch_bounds__(kThreads, 1)
     qmma_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ CUtensorMap tA1,
                 const __grid_constant__ CUtensorMap tB, TcGemmArgs a) {
-  using S = MmaShape<BITS, NPROJ, NT>;
+  using S = MmaShape<BITS, NPROJ, NT, G4>;
+  static_assert(!G4 || BITS == 4, "group-scaled form is 4-bit");
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -184,7 +241,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < S::kStages; ++i) {
-      mbar_init(&bar_full[i], 1);
+      // group-scaled form: + one cp.async arrival per producer lane
+      mbar_init(&bar_full[i], G4 ? 33 : 1);
       mbar_init(&bar_empty[i], kComputeWarps);
     }
     for (int i = 0; i < 8; ++i) {
@@ -204,35 +262,58 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ntiles = s_ntiles;
   const int nst = a.kdim / kStageCols;
 
+  const int groups = a.kdim / 64;
   if (warp == kComputeWarps) {
     // ===================================================== TMA producer
-    if (lane == 0) {
-      int it = 0;
+    // Lane 0 issues the stage's TMA boxes (packed codes, activations).  In
+    // the group-scaled form every lane also copies 8 * NPROJ of the stage's
+    // 256 * NPROJ scale / bias runs (8 bytes = 4 groups of one row each) with
+    // cp.async, whose completion the stage's full barrier counts as one
+    // arrival per lane.
+    if (G4 || lane == 0) {
+      int slot = 0;
+      uint32_t ph = 0;
+      int issued = 0;
       bool ok = true;
       for (int ti = 0; ti < ntiles && ok; ++ti) {
         const int4 tl = s_tiles[ti];
         const int arow = tl.x * a.rows + tl.y;
-        for (int st = 0; st < nst; ++st, ++it) {
-          const int slot = it % S::kStages, ph = (it / S::kStages) & 1;
-          if (!(ok = wait_or_abort(&bar_empty[slot], ph ^ 1, &s_abort, a.err))) break;
+        const size_t sb_row0 = static_cast<size_t>(arow + lane) * groups;  // (row lane, group 0)
+        for (int st = 0; st < nst; ++st, ++issued) {
+          bool w = wait_or_abort(&bar_empty[slot], ph ^ 1, &s_abort, a.err);
+          if constexpr (G4) w = __all_sync(0xffffffffu, w);
+          if (!(ok = w)) break;
           unsigned char* base = sStage + slot * S::kStageBytes;
-          mbar_arrive_expect_tx(&bar_full[slot], S::kStageBytes);
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&bar_full[slot], S::kTmaBytes);
 #pragma unroll
-          for (int p = 0; p < NPROJ; ++p)
+            for (int p = 0; p < NPROJ; ++p)
 #pragma unroll
-            for (int bx = 0; bx < S::kABoxes; ++bx)
-              tma_load_2d(base + (p * S::kABoxes + bx) * S::kABox, p ? &tA1 : &tA0, (st * S::kABoxes + bx) * 32,
-                          arow, &bar_full[slot]);
+              for (int bx = 0; bx < S::kABoxes; ++bx)
+                tma_load_2d(base + (p * S::kABoxes + bx) * S::kABox, p ? &tA1 : &tA0, (st * S::kABoxes + bx) * 32,
+                            arow, &bar_full[slot]);
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            tma_load_2d(base + S::kABytes + j * S::kBBox, &tB, st * kStageCols + j * 64, tl.z, &bar_full[slot]);
+            for (int j = 0; j < 4; ++j)
+              tma_load_2d(base + S::kABytes + j * S::kBBox, &tB, st * kStageCols + j * 64, tl.z, &bar_full[slot]);
+          }
+          if constexpr (G4) {
+            const uint32_t dst = smem_u32(base + S::kSBOff) + lane * 8;
+#pragma unroll
+            for (int i = 0; i < 8 * NPROJ; ++i) {  // run (array pa = i / 4, row lane + 32 (i % 4))
+              const int pa = i >> 2, r = 32 * (i & 3);
+              const uint16_t* src = ((pa & 1) ? a.b[pa >> 1] : a.s[pa >> 1]) + sb_row0 +
+                                    static_cast<size_t>(r) * groups + 4 * st;
+              cp_async_8(dst + (pa * kRows + r) * 8, src);
+            }
+            cp_async_arrive_noinc(&bar_full[slot]);
+          }
+          if (++slot == S::kStages) { slot = 0; ph ^= 1; }
         }
       }
       // drain: the copies of the last stages must land before the CTA may
       // exit, consumed or not (bounded; each slot's latest use only)
-      const int last = it;
       int never = 0;
-      for (int k = (last > S::kStages ? last - S::kStages : 0); k < last; ++k)
+      for (int k = (issued > S::kStages ? issued - S::kStages : 0); k < issued; ++k)
         wait_or_abort(&bar_full[k % S::kStages], (k / S::kStages) & 1, &never, nullptr);
     }
     return;
@@ -241,16 +322,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ======================================================= compute warps
   const int rg = warp & 7, kh = warp >> 3;
   const int g = lane >> 2, t = lane & 3;
-  const int groups = a.kdim / 64;
-  int it = 0;
+  int slot = 0;
+  uint32_t ph = 0;
   bool ok = true;
   const uint32_t sStage_u32 = smem_u32(sStage);
   const int rA = 16 * rg + g;  // tile row of this lane's first fragment row
-  // Lane t of k-half kh owns the 32-column chunk c = 2t + kh of every stage
-  // (four 8-column blocks b; one 16-byte line of each row at 4 bits), all
-  // inside quantization group t of the stage.  Its scale / bias for each of
-  // its two rows and each projection are prefetched one stage ahead, across
-  // tile boundaries too.
+  // Dequantising form: lane t of k-half kh owns the 32-column chunk
+  // c = 2t + kh of every stage (four 8-column blocks b; one 16-byte line of
+  // each row at 4 bits), all inside quantization group t of the stage; its
+  // scale / bias for each of its two rows and each projection are prefetched
+  // into registers one stage ahead, across tile boundaries too.
+  // Group-scaled form: warps of k-half kh take groups 2kh and 2kh + 1 of
+  // every stage whole; the scales / biases arrive with the stage (producer).
   const int cs = 2 * t + kh;
   uint16_t scur[NPROJ][2], bcur[NPROJ][2], snext[NPROJ][2], bnext[NPROJ][2];
   auto load_sb = [&](int ti, int st) {
@@ -264,7 +347,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       bnext[p][1] = __ldg(a.b[p] + row + 8 * groups);
     }
   };
-  if (ntiles > 0) load_sb(0, 0);
+  // Group-scaled form, per-lane shared-memory offsets inside a stage.
+  // ldmatrix: lane supplies row (lane & 7) of matrix (lane >> 3).  Codes of
+  // group j (chunks 2j, 2j+1 of each row): matrix m = rows 8 (m & 1) ..,
+  // chunk 2j + m / 2.  Activations of group j (box j): x4 load hw covers
+  // k-steps 2hw (chunks 4hw, +1) and 2hw + 1 (chunks 4hw + 2, +3).
+  const int lm = lane >> 3, lr = lane & 7;
+  uint32_t offA[2] = {0, 0}, offB[2][2] = {{0, 0}, {0, 0}}, offSB = 0;
+  if constexpr (G4) {
+    const uint32_t a_row = static_cast<uint32_t>(16 * rg + lr + 8 * (lm & 1)) * 128u;
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi) {
+      const int j = 2 * kh + gi;
+      offA[gi] = a_row + ((static_cast<uint32_t>(2 * j + (lm >> 1)) ^ lr) << 4);
+#pragma unroll
+      for (int hw = 0; hw < 2; ++hw)
+        offB[gi][hw] = S::kABytes + j * S::kBBox + lr * 128 + ((static_cast<uint32_t>(4 * hw + lm) ^ lr) << 4);
+    }
+    offSB = S::kSBOff + rA * 8 + kh * 4;  // bf16 pair (groups 2kh, 2kh + 1) of row rA
+  } else {
+    if (ntiles > 0) load_sb(0, 0);
+  }
   for (int ti = 0; ti < ntiles && ok; ++ti) {
     const int4 tl = s_tiles[ti];
     float acc[NPROJ][NT][4];
@@ -274,19 +377,82 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[p][nt][i] = 0.f;
-    for (int st = 0; st < nst; ++st, ++it) {
+    for (int st = 0; st < nst; ++st) {
+      if constexpr (!G4) {
 #pragma unroll
-      for (int p = 0; p < NPROJ; ++p) {
-        scur[p][0] = snext[p][0]; scur[p][1] = snext[p][1];
-        bcur[p][0] = bnext[p][0]; bcur[p][1] = bnext[p][1];
+        for (int p = 0; p < NPROJ; ++p) {
+          scur[p][0] = snext[p][0]; scur[p][1] = snext[p][1];
+          bcur[p][0] = bnext[p][0]; bcur[p][1] = bnext[p][1];
+        }
+        if (st + 1 < nst) load_sb(ti, st + 1);
+        else if (ti + 1 < ntiles) load_sb(ti + 1, 0);
       }
-      if (st + 1 < nst) load_sb(ti, st + 1);
-      else if (ti + 1 < ntiles) load_sb(ti + 1, 0);
-      const int slot = it % S::kStages, ph = (it / S::kStages) & 1;
       ok = __all_sync(0xffffffffu, wait_or_abort(&bar_full[slot], ph, &s_abort, a.err));
       if (!ok) break;
       const unsigned char* base = sStage + slot * S::kStageBytes;
-      const uint32_t bbase = sStage_u32 + slot * S::kStageBytes + S::kABytes;
+      const uint32_t sbase = sStage_u32 + slot * S::kStageBytes;
+      const uint32_t bbase = sbase + S::kABytes;
+      if constexpr (G4) {
+        // scales / biases of rows rA, rA + 8: bf16 pairs, group 2kh low, 2kh + 1 high
+        uint32_t sv[NPROJ][2], bv[NPROJ][2];
+#pragma unroll
+        for (int p = 0; p < NPROJ; ++p)
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            sv[p][r] = *reinterpret_cast<const uint32_t*>(base + offSB + (2 * p) * kRows * 8 + r * 64);
+            bv[p][r] = *reinterpret_cast<const uint32_t*>(base + offSB + (2 * p + 1) * kRows * 8 + r * 64);
+          }
+#pragma unroll
+        for (int gi = 0; gi < 2; ++gi) {
+          uint32_t bf[NT][2][4];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            ldmatrix_x4(sbase + offB[gi][0] + nt * 1024, bf[nt][0]);
+            ldmatrix_x4(sbase + offB[gi][1] + nt * 1024, bf[nt][1]);
+          }
+          // group sums of the activations, in units of 2^-24 (all rows alike)
+          float xs[NT][4];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            mma_z(xs[nt], kOne24, kOne24, kOne24, kOne24, bf[nt][0][0], bf[nt][0][1]);
+            mma_acc(xs[nt], kOne20, kOne20, kOne20, kOne20, bf[nt][0][2], bf[nt][0][3]);
+            mma_acc(xs[nt], kOne24, kOne24, kOne24, kOne24, bf[nt][1][0], bf[nt][1][1]);
+            mma_acc(xs[nt], kOne20, kOne20, kOne20, kOne20, bf[nt][1][2], bf[nt][1][3]);
+          }
+#pragma unroll
+          for (int p = 0; p < NPROJ; ++p) {
+            // words t (regs 0, 1: rows g, g+8) and 4 + t (regs 2, 3) of the group
+            uint32_t w[4];
+            ldmatrix_x4(sbase + offA[gi] + p * S::kABox, w);
+            float grp[NT][4];
+#pragma unroll
+            for (int hw = 0; hw < 2; ++hw) {
+              const uint32_t x0 = w[2 * hw], x1 = w[2 * hw + 1], y0 = x0 >> 8, y1 = x1 >> 8;
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) {
+                if (hw == 0)
+                  mma_z(grp[nt], x0 & kCodeLo, x1 & kCodeLo, y0 & kCodeLo, y1 & kCodeLo, bf[nt][0][0], bf[nt][0][1]);
+                else
+                  mma_acc(grp[nt], x0 & kCodeLo, x1 & kCodeLo, y0 & kCodeLo, y1 & kCodeLo, bf[nt][1][0],
+                          bf[nt][1][1]);
+                mma_acc(grp[nt], x0 & kCodeHi, x1 & kCodeHi, y0 & kCodeHi, y1 & kCodeHi, bf[nt][hw][2],
+                        bf[nt][hw][3]);
+              }
+            }
+            const float s0 = gi ? bf16_hi(sv[p][0]) : bf16_lo(sv[p][0]);
+            const float s1 = gi ? bf16_hi(sv[p][1]) : bf16_lo(sv[p][1]);
+            const float b0 = gi ? bf16_hi(bv[p][0]) : bf16_lo(bv[p][0]);
+            const float b1 = gi ? bf16_hi(bv[p][1]) : bf16_lo(bv[p][1]);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              acc[p][nt][0] = fmaf(s0, grp[nt][0], fmaf(b0, xs[nt][0], acc[p][nt][0]));
+              acc[p][nt][1] = fmaf(s0, grp[nt][1], fmaf(b0, xs[nt][1], acc[p][nt][1]));
+              acc[p][nt][2] = fmaf(s1, grp[nt][2], fmaf(b1, xs[nt][2], acc[p][nt][2]));
+              acc[p][nt][3] = fmaf(s1, grp[nt][3], fmaf(b1, xs[nt][3], acc[p][nt][3]));
+            }
+          }
+        }
+      } else {
       GroupConst gc[NPROJ][2];
       bool all_sub = true;
 #pragma unroll
@@ -355,8 +521,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       if (all_sub) run_blocks(std::true_type{});
       else run_blocks(std::false_type{});
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_empty[slot]);
+      if (++slot == S::kStages) { slot = 0; ph ^= 1; }
     }
     if (!ok) break;
 
@@ -398,13 +566,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (n >= tl.w) continue;
         const int row = tl.y + rA + 8 * (i >> 1);
         const size_t o = static_cast<size_t>(tl.z + n) * a.out_stride;
+        constexpr float kUnit = G4 ? kG4Scale : 1.0f;  // accumulator units (exact power of two)
         if constexpr (NPROJ == 2) {
-          const float gv = round_bf16(acc[0][nt][i]), uv = round_bf16(acc[1][nt][i]);
+          const float gv = round_bf16(acc[0][nt][i] * kUnit), uv = round_bf16(acc[1][nt][i] * kUnit);
           const float h = a.act == 0 ? act_swiglu_mlx(gv, uv) : act_geglu_mlx(gv, uv);
           range_ok &= fabsf(h) < 65504.0f;
-          a.out[o + kperm256(row)] = __half_as_ushort(__float2half_rn(h));
+          if constexpr (G4)
+            a.out[o + kperm_g4(row)] = __half_as_ushort(__float2half_rn((row & 1) ? h * 0.0625f : h));
+          else
+            a.out[o + kperm256(row)] = __half_as_ushort(__float2half_rn(h));
         } else {
-          a.out[o + row] = f32_to_bf16_bits(acc[0][nt][i]);
+          a.out[o + row] = f32_to_bf16_bits(acc[0][nt][i] * kUnit);
         }
       }
     }
@@ -415,11 +587,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace
 
 // ------------------------------------------------------------------ host
-template <int BITS, int NPROJ, int NT>
+template <int BITS, int NPROJ, int NT, bool G4>
 static cudaError_t launch_mma_t(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
                                 const TcGemmArgs& a, int tiles_upper, cudaStream_t st) {
-  using S = MmaShape<BITS, NPROJ, NT>;
-  auto kern = qmma_kernel<BITS, NPROJ, NT>;
+  using S = MmaShape<BITS, NPROJ, NT, G4>;
+  auto kern = qmma_kernel<BITS, NPROJ, NT, G4>;
   cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), S::kSmem);
   if (e != cudaSuccess) return e;
   int sms = 0, dev = 0;
@@ -431,9 +603,12 @@ static cudaError_t launch_mma_t(const CUtensorMap& tA0, const CUtensorMap& tA1, 
   return launch_pdl(kern, dim3(grid), dim3(kThreads), S::kSmem, st, tA0, tA1, tB, a);
 }
 
-size_t mma_smem_bytes(int bits, int nproj, int nt) {
+size_t mma_smem_bytes(int bits, int nproj, int nt, bool g4) {
+  if (g4 && bits == 4 && nt == 1) return nproj == 2 ? MmaShape<4, 2, 1, true>::kSmem : MmaShape<4, 1, 1, true>::kSmem;
+  if (g4 && bits == 4 && nt == 2) return nproj == 2 ? MmaShape<4, 2, 2, true>::kSmem : MmaShape<4, 1, 2, true>::kSmem;
+  if (g4) return 0;
 #define SENMOE_MMA_SMEM(B, P, N) \
-  if (bits == B && nproj == P && nt == N) return MmaShape<B, P, N>::kSmem;
+  if (bits == B && nproj == P && nt == N) return MmaShape<B, P, N, false>::kSmem;
   SENMOE_MMA_SMEM(4, 1, 1) SENMOE_MMA_SMEM(4, 1, 2) SENMOE_MMA_SMEM(4, 1, 4)
   SENMOE_MMA_SMEM(4, 2, 1) SENMOE_MMA_SMEM(4, 2, 2) SENMOE_MMA_SMEM(4, 2, 4)
   SENMOE_MMA_SMEM(8, 1, 1) SENMOE_MMA_SMEM(8, 1, 2) SENMOE_MMA_SMEM(8, 1, 4)
@@ -446,10 +621,26 @@ bool mma_supported(int rows, int kdim, int bits) {
   return (bits == 4 || bits == 8) && rows > 0 && rows % kRows == 0 && kdim > 0 && kdim % kStageCols == 0;
 }
 
+bool mma_g4_supported(int bits, int nt, const TcGemmArgs& a) {
+  auto aligned4 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; };
+  bool ok = bits == 4 && (nt == 1 || nt == 2);
+  for (int p = 0; p < 2; ++p) ok = ok && aligned4(a.s[p]) && aligned4(a.b[p]);
+  return ok;
+}
+
 cudaError_t launch_mma_gemm(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
-                            const TcGemmArgs& a, int bits, int nproj, int nt, int tiles_upper, cudaStream_t st) {
+                            const TcGemmArgs& a, int bits, int nproj, int nt, bool g4, int tiles_upper,
+                            cudaStream_t st) {
+  if (g4) {
+    if (!mma_g4_supported(bits, nt, a)) return cudaErrorInvalidValue;
+    if (nproj == 2) return nt == 1 ? launch_mma_t<4, 2, 1, true>(tA0, tA1, tB, a, tiles_upper, st)
+                                   : launch_mma_t<4, 2, 2, true>(tA0, tA1, tB, a, tiles_upper, st);
+    if (nproj == 1) return nt == 1 ? launch_mma_t<4, 1, 1, true>(tA0, tA1, tB, a, tiles_upper, st)
+                                   : launch_mma_t<4, 1, 2, true>(tA0, tA1, tB, a, tiles_upper, st);
+    return cudaErrorNotSupported;
+  }
 #define SENMOE_MMA_CASE(B, P, N) \
-  if (bits == B && nproj == P && nt == N) return launch_mma_t<B, P, N>(tA0, tA1, tB, a, tiles_upper, st);
+  if (bits == B && nproj == P && nt == N) return launch_mma_t<B, P, N, false>(tA0, tA1, tB, a, tiles_upper, st);
   SENMOE_MMA_CASE(4, 1, 1) SENMOE_MMA_CASE(4, 1, 2) SENMOE_MMA_CASE(4, 1, 4)
   SENMOE_MMA_CASE(4, 2, 1) SENMOE_MMA_CASE(4, 2, 2) SENMOE_MMA_CASE(4, 2, 4)
   SENMOE_MMA_CASE(8, 1, 1) SENMOE_MMA_CASE(8, 1, 2) SENMOE_MMA_CASE(8, 1, 4)

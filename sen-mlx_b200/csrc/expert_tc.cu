@@ -655,15 +655,15 @@ cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
 
 // Slot-ordered fp16 copy of the token rows (bf16 -> fp16 is exact in range),
 // k-permuted within each block of 8 columns like the dequantised weights
-// (kperm8), or in the warp-MMA kernel's kperm256 order.  Each CTA copies
-// kGatherSlots slots, issuing all of its row loads before converting.
+// (kperm8), or in one of the warp-MMA kernel's orders (kperm256; kperm_g4,
+// odd columns divided by 16).  Each CTA copies kGatherSlots slots.
 constexpr int kGatherSlots = 4;
 
 __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __restrict__ x,
                                                           const int32_t* __restrict__ perm, int k_div,
                                                           uint16_t* __restrict__ out, int num_slots, int hidden,
                                                           int* err, const int32_t* __restrict__ offsets, int eb,
-                                                          int ee, int perm32) {
+                                                          int ee, int order) {
   pdl_wait();
   pdl_launch_dependents();
   const int s0 = blockIdx.x * kGatherSlots;
@@ -681,7 +681,40 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
     src[j] = x + static_cast<size_t>(live[j] ? perm[s] / k_div : 0) * hidden;
   }
   bool ok = true;
-  if (perm32) {
+  if (order == kOrderMmaG4) {
+    // kperm_g4, one thread per (slot, 64-column group): output position
+    // 16 s + kappa (kappa = 8 a2 + 2 t + h) holds column
+    // 8 (t + 4 (s / 2)) + (s & 1) + 2 a2 + 4 h, divided by 16 for odd s
+    const int groups = hidden / 64;
+    for (int it = threadIdx.x; it < kGatherSlots * groups; it += blockDim.x) {
+      const int j = it / groups, G = it - j * groups, s = s0 + j;
+      if (!(s < num_slots && s >= lo_slot && s < hi_slot)) continue;
+      const uint4* in = reinterpret_cast<const uint4*>(x + static_cast<size_t>(perm[s] / k_div) * hidden + 64 * G);
+      uint32_t w[32];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const uint4 v = __ldg(in + q);
+        w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+      }
+      uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(s) * hidden + 64 * G);
+#pragma unroll
+      for (int sg = 0; sg < 8; ++sg) {  // 16-byte segment: k-step sg / 2, kappa half sg % 2
+        const int ks = sg >> 1, a2 = sg & 1;
+        const float sc = (ks & 1) ? 0.0625f : 1.0f;
+        uint32_t o[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int u0 = 8 * (t + 4 * (ks >> 1)) + (ks & 1) + 2 * a2, u1 = u0 + 4;
+          const float f0 = (u0 & 1) ? bf16_hi(w[u0 >> 1]) : bf16_lo(w[u0 >> 1]);
+          const float f1 = (u1 & 1) ? bf16_hi(w[u1 >> 1]) : bf16_lo(w[u1 >> 1]);
+          ok &= fabsf(f0) < 65504.0f && fabsf(f1) < 65504.0f;
+          const __half2 hv = __floats2half2_rn(f0 * sc, f1 * sc);
+          o[t] = *reinterpret_cast<const uint32_t*>(&hv);
+        }
+        dst[sg] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  } else if (order == kOrderMma) {
     // kperm256 (warp-MMA operand order): output segment sg (8 halves) of
     // stage st = sg / 32 holds, at half 2t + h, column
     // 256 st + 32 (2t + kh) + 8 b + p + 4h with sg % 32 = 16 kh + 4 b + p
@@ -742,12 +775,12 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
 
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
                                int num_slots, int hidden, int* err, cudaStream_t st,
-                               const int32_t* offsets, int eb, int ee, bool perm32) {
+                               const int32_t* offsets, int eb, int ee, int order) {
   if (num_slots <= 0) return cudaSuccess;
   const int threads = hidden / 8 < 256 ? ((hidden / 8 + 31) / 32) * 32 : 256;
   const int grid = (num_slots + kGatherSlots - 1) / kGatherSlots;
   return launch_pdl(gather_rows_kernel, dim3(grid), dim3(threads), 0, st, x, perm, k_div, x_sorted, num_slots,
-                    hidden, err, offsets, eb, ee, perm32 ? 1 : 0);
+                    hidden, err, offsets, eb, ee, order);
 }
 
 }  // namespace senmoe

@@ -135,23 +135,31 @@ cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
 // x_sorted[s, :] = fp16(x[perm[s] / k_div, :]) for s < num_slots (x bf16, rows of
 // `hidden`); a value outside fp16 range records kDevFp16Range in *err.
 // With `offsets` non-null only the slots of experts [eb, ee), i.e. slots
-// offsets[eb] .. offsets[ee], are gathered.  perm32 selects the k order of
-// the warp-MMA kernel (kperm256, 256-column stages; hidden % 256 == 0)
-// instead of the tcgen05 kernel's (kperm8).
+// offsets[eb] .. offsets[ee], are gathered.  `order` selects the k order of
+// the consuming kernel: kOrderTc (tcgen05, kperm8), kOrderMma (warp-MMA
+// dequantising form, kperm256, 256-column stages; hidden % 256 == 0) or
+// kOrderMmaG4 (warp-MMA group-scaled form, kperm_g4 with odd columns / 16;
+// hidden % 64 == 0).
+enum ActivationOrder { kOrderTc = 0, kOrderMma = 1, kOrderMmaG4 = 2 };
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
                                int num_slots, int hidden, int* err, cudaStream_t st,
-                               const int32_t* offsets = nullptr, int eb = 0, int ee = 0, bool perm32 = false);
+                               const int32_t* offsets = nullptr, int eb = 0, int ee = 0, int order = kOrderTc);
 
 // ------------------------------------------- warp-MMA expert GEMM (decode)
 // Same arguments as the tcgen05 GEMM (TcGemmArgs; out holds h as fp16 in
-// kperm256 order for the two-projection form, bf16 d for the one-projection
-// form).  tA*: packed codes [E_local*rows, words] u32, 32-word x 128-row
-// boxes, SWIZZLE_128B; tB: fp16 [slots, kdim] in kperm256 order, 64-column x
-// 8*nt-row boxes, SWIZZLE_128B.  nt in {1, 2, 4}: 8*nt slots per tile.
-size_t mma_smem_bytes(int bits, int nproj, int nt);
+// the activation order of the form for the two-projection form, bf16 d for
+// the one-projection form).  tA*: packed codes [E_local*rows, words] u32,
+// 32-word x 128-row boxes, SWIZZLE_128B; tB: fp16 [slots, kdim] in the
+// form's activation order, 64-column x 8*nt-row boxes, SWIZZLE_128B.
+// nt in {1, 2, 4}: 8*nt slots per tile.  g4 selects the group-scaled form
+// (kOrderMmaG4 activations; 4-bit, nt <= 2, scale / bias arrays 4-byte
+// aligned: mma_g4_supported), else the dequantising form (kOrderMma).
+size_t mma_smem_bytes(int bits, int nproj, int nt, bool g4);
 bool mma_supported(int rows, int kdim, int bits);
+bool mma_g4_supported(int bits, int nt, const TcGemmArgs& a);
 cudaError_t launch_mma_gemm(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
-                            const TcGemmArgs& a, int bits, int nproj, int nt, int tiles_upper, cudaStream_t st);
+                            const TcGemmArgs& a, int bits, int nproj, int nt, bool g4, int tiles_upper,
+                            cudaStream_t st);
 
 // ------------------------------------------------- expert parallelism
 constexpr int kEpMaxRanks = 8;

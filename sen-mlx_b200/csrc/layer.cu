@@ -81,6 +81,9 @@ constexpr int kTcMaxTile = 3;  // index of the widest tile
 constexpr double kTcMinTokensPerExpert = 24.0;
 constexpr double kMmaMinTokensPerExpert = 0.0;
 enum ExpertPath { kPathAuto = 0, kPathGemv = 1, kPathTensorCore = 2, kPathMma = 3 };
+// SenMoeConfig.reserved[1]: warp-MMA form, 0 = group-scaled where supported
+// (4-bit, up to 16 slots per tile), 1 = always dequantise to fp16
+enum MmaForm { kMmaFormAuto = 0, kMmaFormDequant = 1 };
 // From this many tokens the router runs as one tensor-core launch (logits
 // and top-k, 32 tokens per CTA, so at least 16 CTAs) instead of the CUDA-core
 // logits + top-k pair.
@@ -470,9 +473,6 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     const int nt = per_expert <= 8.0 ? 1 : (per_expert <= 16.0 ? 2 : 4);  // slots per tile: 8 * nt
     const CUtensorMap& tb_x = nt == 1 ? L->tm_xs8 : L->tm_xs[nt == 2 ? 0 : 1];
     const CUtensorMap& tb_h = nt == 1 ? L->tm_h8 : L->tm_h[nt == 2 ? 0 : 1];
-    SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
-                                   ep ? L->offsets : nullptr, c.expert_begin, c.expert_end, true));
-    SENMOE_CUDA(mark(2));
     TcGemmArgs ga{};
     ga.s[0] = static_cast<const uint16_t*>(L->w.gate_scales);
     ga.b[0] = static_cast<const uint16_t*>(L->w.gate_biases);
@@ -489,8 +489,15 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     ga.out_stride = I;
     ga.act = c.activation;
     ga.err = L->err;
-    SENMOE_CUDA(launch_mma_gemm(L->tm_gate, L->tm_up, tb_x, ga, c.bits, 2, nt, (P / (8 * nt) + max_items) * ga.m_tiles,
-                                st));
+    // group-scaled form (4-bit, up to 16 slots per tile) unless the
+    // dequantising form is forced
+    const bool g4 = c.reserved[1] != kMmaFormDequant && mma_g4_supported(c.bits, nt, ga);
+    SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
+                                   ep ? L->offsets : nullptr, c.expert_begin, c.expert_end,
+                                   g4 ? kOrderMmaG4 : kOrderMma));
+    SENMOE_CUDA(mark(2));
+    SENMOE_CUDA(launch_mma_gemm(L->tm_gate, L->tm_up, tb_x, ga, c.bits, 2, nt, g4,
+                                (P / (8 * nt) + max_items) * ga.m_tiles, st));
     SENMOE_CUDA(mark(3));
     TcGemmArgs gd = ga;
     gd.s[0] = static_cast<const uint16_t*>(L->w.down_scales);
@@ -502,8 +509,8 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     gd.m_tiles = H / 128;
     gd.out = L->d;
     gd.out_stride = H;
-    SENMOE_CUDA(launch_mma_gemm(L->tm_down, L->tm_down, tb_h, gd, c.bits, 1, nt, (P / (8 * nt) + max_items) * gd.m_tiles,
-                                st));
+    SENMOE_CUDA(launch_mma_gemm(L->tm_down, L->tm_down, tb_h, gd, c.bits, 1, nt, g4,
+                                (P / (8 * nt) + max_items) * gd.m_tiles, st));
     SENMOE_CUDA(mark(4));
   } else if (path == kPathTensorCore) {
     const int ti = tc_tile_index(per_expert), bn = kTcTiles[ti];

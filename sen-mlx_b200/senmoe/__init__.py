@@ -191,6 +191,7 @@ class MoeArgs:
     activation: int = ACT_SWIGLU
     shared_gate: bool = False  # sigmoid-gated shared expert (no reference counterpart)
     expert_path: int = PATH_AUTO  # AUTO: GEMV (~1 token per expert), warp MMA (decode), tcgen05 (prefill)
+    mma_dequant: bool = False  # warp MMA: dequantise every weight instead of the group-scaled 4-bit form
 
 
 @dataclass
@@ -245,6 +246,7 @@ class DeepseekMoe:
         cfg.max_tokens = int(max_tokens)
         cfg.expert_begin, cfg.expert_end = eb, ee
         cfg.reserved[0] = int(args.expert_path)
+        cfg.reserved[1] = int(args.mma_dequant)
         self._cfg = cfg
         wt = SenMoeWeights()
         wt.router_weight = _ptr(weights.router_weight)

@@ -29,10 +29,12 @@ def senmoe():
 PATHS = {"gemv": 1, "tc": 2, "mma": 3}
 
 
-def run_block(senmoe, cfg, mw, x_bits, max_tokens=None, path=0):
+def run_block(senmoe, cfg, mw, x_bits, max_tokens=None, path=0, mma_dequant=False):
     import torch
     T = x_bits.shape[0]
-    blk = senmoe.DeepseekMoe(moe_args(cfg, path), device_weights(mw), max_tokens=max_tokens or max(T, 1))
+    args = moe_args(cfg, path)
+    args.mma_dequant = mma_dequant
+    blk = senmoe.DeepseekMoe(args, device_weights(mw), max_tokens=max_tokens or max(T, 1))
     if path:
         assert blk.expert_path(T) == path, "the forced expert path is not the one that runs"
     dbg = dict(topk_ids=torch.empty((T, cfg.top_k), dtype=torch.int32, device="cuda"),
@@ -113,15 +115,41 @@ def test_tensor_core_tiles_vs_oracle(senmoe, bits, T):
 
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("T", [3, 40, 200])
-def test_warp_mma_tiles_vs_oracle(senmoe, bits, T):
+@pytest.mark.parametrize("dequant", [False, True])
+def test_warp_mma_tiles_vs_oracle(senmoe, bits, T, dequant):
     """Warp-MMA decode kernel at each slot-tile width (8, 16, 32 slots: about 1,
     10 and 50 tokens per expert, the last in several slot chunks per expert),
-    both code widths, on a small layer (H=256, I=256, E=16, K=4)."""
+    both code widths, on a small layer (H=256, I=256, E=16, K=4); 4-bit at 8
+    and 16 slots takes the group-scaled form unless the dequantising form is
+    forced."""
     cfg = O.MoeConfig(hidden=256, intermediate=256, num_experts=16, top_k=4, bits=bits)
     mw = O.make_layer(cfg, seed=40 + bits)
     x = O.make_tokens(T, cfg.hidden, seed=T + 7 * bits)
-    got = run_block(senmoe, cfg, mw, x, path=PATHS["mma"])
+    got = run_block(senmoe, cfg, mw, x, path=PATHS["mma"], mma_dequant=dequant)
     check_against_oracle(cfg, mw, x, got)
+
+
+@pytest.mark.parametrize("T", [5, 60])
+def test_warp_mma_group_scaled_wide_scales(senmoe, T):
+    """Group-scaled 4-bit form with scales beyond the dequantising form's fp16
+    fast range (|s| > 0.0624 for ~6 % of the groups) and activations up to
+    ~16 (h up to ~7e3): the fp32 post-scale has no such limit."""
+    cfg = O.MoeConfig(hidden=512, intermediate=256, num_experts=16, top_k=4, bits=4)
+    mw = O.make_layer(cfg, seed=77)
+    rng = np.random.default_rng(5)
+    for name in ("gate_s", "up_s", "down_s"):
+        s = O.bf16_to_f32(getattr(mw, name))
+        setattr(mw, name, O.f32_to_bf16((s * rng.uniform(3.0, 10.0, s.shape)).astype(np.float32)))
+    x = O.bf16_to_f32(O.make_tokens(T, cfg.hidden, seed=T))
+    x = x * rng.choice([1.0, 4.0], size=x.shape).astype(np.float32)
+    x_bits = O.f32_to_bf16(x.astype(np.float32))
+    got = run_block(senmoe, cfg, mw, x_bits, path=PATHS["mma"])
+    ref = O.moe_forward(cfg, mw, x_bits, mode=0)
+    same = (got["topk_ids"] == ref["ids"]).all(axis=1)
+    y, yr = got["y"][same], ref["y_f32"][same]
+    scale = max(1.0, float(np.abs(yr).max()))
+    assert np.abs(y - yr).max() <= MAX_ABS_TOL * scale
+    assert rel_l2(y, yr) <= REL_L2_TOL
 
 
 @pytest.mark.parametrize("path", ["gemv", "tc", "mma"])
