@@ -84,7 +84,8 @@ typedef struct SenMoeConfig {
   int32_t expert_end;              /* one past the last local expert (E on one GPU) */
   int32_t reserved[3];             /* [0]: expert kernels, 0 auto, 1 CUDA-core GEMV, 2 tcgen05 GEMM,
                                       3 warp-MMA GEMM; [1]: warp-MMA form, 0 group-scaled where
-                                      supported (4-bit), 1 dequantise every weight; [2]: zero */
+                                      supported (4-bit), 1 dequantise every weight, 2 group-scaled
+                                      with one CTA per SM; [2]: zero */
 } SenMoeConfig;
 
 /* Device pointers, caller-owned, valid for the layer's lifetime.  Expert

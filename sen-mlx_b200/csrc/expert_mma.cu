@@ -54,6 +54,12 @@ constexpr int kComputeWarps = 16;    // 8 row groups x 2 k-halves
 // the 96-register cap that a 17th warp imposes, but measured slower: the
 // issuing warp then waits for the slowest warp at every stage.)
 constexpr int kThreads = (kComputeWarps + 1) * 32;
+// The group-scaled form has four loader warps (16-19, one per scheduler):
+// lane 0 of warp 16 issues the TMA copies, and each of the 128 loader lanes
+// copies one weight row's scales / biases per stage, so the copy work does
+// not pile onto one scheduler.  Twenty warps still leave 96 registers each.
+constexpr int kLoaderWarps = 4;
+constexpr int kThreadsG4 = (kComputeWarps + kLoaderWarps) * 32;
 constexpr int kMaxTiles = 128;       // per CTA
 constexpr int kSmemBudget = 226 * 1024;
 
@@ -220,7 +226,7 @@ __device__ __forceinline__ int kperm256(int col) {
 // G4: the group-scaled 4-bit form (kperm_g4 activations); otherwise every
 // weight is dequantised to fp16 (kperm256 activations).
 template <int BITS, int NPROJ, int NT, bool G4>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(G4 ? kThreadsG4 : kThreads, 1)
     qmma_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ CUtensorMap tA1,
                 const __grid_constant__ CUtensorMap tB, TcGemmArgs a) {
   using S = MmaShape<BITS, NPROJ, NT, G4>;
@@ -241,8 +247,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < S::kStages; ++i) {
-      // group-scaled form: + one cp.async arrival per producer lane
-      mbar_init(&bar_full[i], G4 ? 33 : 1);
+      // group-scaled form: + one cp.async arrival per loader lane
+      mbar_init(&bar_full[i], G4 ? 1 + 32 * kLoaderWarps : 1);
       mbar_init(&bar_empty[i], kComputeWarps);
     }
     for (int i = 0; i < 8; ++i) {
@@ -263,14 +269,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nst = a.kdim / kStageCols;
 
   const int groups = a.kdim / 64;
-  if (warp == kComputeWarps) {
+  if (warp >= kComputeWarps) {
     // ===================================================== TMA producer
-    // Lane 0 issues the stage's TMA boxes (packed codes, activations).  In
-    // the group-scaled form every lane also copies 8 * NPROJ of the stage's
-    // 256 * NPROJ scale / bias runs (8 bytes = 4 groups of one row each) with
-    // cp.async, whose completion the stage's full barrier counts as one
-    // arrival per lane.
-    if (G4 || lane == 0) {
+    // Lane 0 of warp 16 issues the stage's TMA boxes (packed codes,
+    // activations).  In the group-scaled form the loader lane l = 0..127 of
+    // warps 16-19 also copies weight row l's scale / bias runs (8 bytes = 4
+    // groups) of every projection with cp.async, whose completion the
+    // stage's full barrier counts as one arrival per loader lane.
+    const int ll = (warp - kComputeWarps) * 32 + lane;  // loader lane
+    if (G4 || ll == 0) {
       int slot = 0;
       uint32_t ph = 0;
       int issued = 0;
@@ -278,13 +285,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ti = 0; ti < ntiles && ok; ++ti) {
         const int4 tl = s_tiles[ti];
         const int arow = tl.x * a.rows + tl.y;
-        const size_t sb_row0 = static_cast<size_t>(arow + lane) * groups;  // (row lane, group 0)
+        const size_t sb_row0 = static_cast<size_t>(arow + ll) * groups;  // (row ll, group 0)
         for (int st = 0; st < nst; ++st, ++issued) {
           bool w = wait_or_abort(&bar_empty[slot], ph ^ 1, &s_abort, a.err);
           if constexpr (G4) w = __all_sync(0xffffffffu, w);
           if (!(ok = w)) break;
           unsigned char* base = sStage + slot * S::kStageBytes;
-          if (lane == 0) {
+          if (ll == 0) {
             mbar_arrive_expect_tx(&bar_full[slot], S::kTmaBytes);
 #pragma unroll
             for (int p = 0; p < NPROJ; ++p)
@@ -297,14 +304,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d(base + S::kABytes + j * S::kBBox, &tB, st * kStageCols + j * 64, tl.z, &bar_full[slot]);
           }
           if constexpr (G4) {
-            const uint32_t dst = smem_u32(base + S::kSBOff) + lane * 8;
+            static_assert(32 * kLoaderWarps == kRows, "one loader lane per weight row");
+            const uint32_t dst = smem_u32(base + S::kSBOff) + ll * 8;
 #pragma unroll
-            for (int i = 0; i < 8 * NPROJ; ++i) {  // run (array pa = i / 4, row lane + 32 (i % 4))
-              const int pa = i >> 2, r = 32 * (i & 3);
-              const uint16_t* src = ((pa & 1) ? a.b[pa >> 1] : a.s[pa >> 1]) + sb_row0 +
-                                    static_cast<size_t>(r) * groups + 4 * st;
-              cp_async_8(dst + (pa * kRows + r) * 8, src);
-            }
+            for (int pa = 0; pa < 2 * NPROJ; ++pa)  // array pa: scales (even) / biases (odd) of proj pa / 2
+              cp_async_8(dst + pa * kRows * 8, ((pa & 1) ? a.b[pa >> 1] : a.s[pa >> 1]) + sb_row0 + 4 * st);
             cp_async_arrive_noinc(&bar_full[slot]);
           }
           if (++slot == S::kStages) { slot = 0; ph ^= 1; }
@@ -325,6 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   int slot = 0;
   uint32_t ph = 0;
   bool ok = true;
+  bool next_ready = false;  // group-scaled form: early test of the next stage's barrier
   const uint32_t sStage_u32 = smem_u32(sStage);
   const int rA = 16 * rg + g;  // tile row of this lane's first fragment row
   // Dequantising form: lane t of k-half kh owns the 32-column chunk
@@ -387,12 +392,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (st + 1 < nst) load_sb(ti, st + 1);
         else if (ti + 1 < ntiles) load_sb(ti + 1, 0);
       }
-      ok = __all_sync(0xffffffffu, wait_or_abort(&bar_full[slot], ph, &s_abort, a.err));
+      ok = __all_sync(0xffffffffu, next_ready || wait_or_abort(&bar_full[slot], ph, &s_abort, a.err));
       if (!ok) break;
       const unsigned char* base = sStage + slot * S::kStageBytes;
       const uint32_t sbase = sStage_u32 + slot * S::kStageBytes;
       const uint32_t bbase = sbase + S::kABytes;
       if constexpr (G4) {
+        // ask now whether the next stage has landed: the barrier round trip
+        // then overlaps this stage's work
+        const int ns = slot + 1 == S::kStages ? 0 : slot + 1;
+        next_ready = mbar_test_wait(&bar_full[ns], ns == 0 ? ph ^ 1 : ph);
         // scales / biases of rows rA, rA + 8: bf16 pairs, group 2kh low, 2kh + 1 high
         uint32_t sv[NPROJ][2], bv[NPROJ][2];
 #pragma unroll
@@ -584,6 +593,236 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Group-scaled form, two CTAs per SM (qmma_q4_kernel, 8-slot tiles).  The
+// kernel above runs 16 compute warps per SM, four per scheduler, each at the
+// 96-register cap, and at decode sizes it is bound by how much MMA and
+// shared-memory latency those warps hide, not by HBM (the same kernel with
+// its weights resident in L2 is only ~10 % faster).  This form halves the
+// tile (64 weight rows) and the per-warp state (one quantization group per
+// stage) so that two CTAs fit on an SM: eight compute warps per scheduler.
+//   warps 0-15   warp w: rows 16 (w % 4) .. +16 of the tile, quantization
+//                group w / 4 (k-quarter kq) of every 256-column stage
+//   warp 16      producer: TMA of the codes (64-row boxes) and activations,
+//                cp.async of the stage's scales / biases
+// The k-quarters are added in a fixed order (kq = 1, 2, 3 into kq = 0)
+// through shared memory; warps kq = 0 run the epilogue.
+constexpr int kQRows = 64;
+template <int NPROJ>
+struct QShape {
+  static constexpr int kABox = kQRows * 128;                 // 8 KB: 64 rows x 128 B
+  static constexpr int kABytes = NPROJ * kABox;
+  static constexpr int kBBox = 8 * 128;                      // 64 fp16 columns x 8 slots
+  static constexpr int kBBytes = 4 * kBBox;
+  static constexpr int kTmaBytes = kABytes + kBBytes;
+  static constexpr int kSBOff = kTmaBytes;                   // [proj][s, b][row][4 groups] bf16
+  static constexpr int kSBBytes = NPROJ * 2 * kQRows * 8;
+  static constexpr int kStageBytes = kTmaBytes + kSBBytes;   // 13 or 22 KB
+  static constexpr int kRedSlice = 4 * 32 * NPROJ * 4;       // floats of one k-quarter's partials
+  static constexpr int kRedBytes = 3 * kRedSlice * 4;
+  static constexpr int kMisc = 4096;                         // barriers + tile list
+  static constexpr int kBudget = 112 * 1024;                 // two CTAs per SM
+  static constexpr int kFit = (kBudget - kRedBytes - kMisc - 1024) / kStageBytes;
+  static constexpr int kStages = kFit > 8 ? 8 : kFit;
+  static constexpr int kSmem = 1024 + kStages * kStageBytes + kRedBytes + kMisc;
+  static_assert(kStages >= 3, "pipeline depth");
+  static_assert(kStageBytes % 1024 == 0, "stage alignment");
+};
+
+template <int NPROJ>
+__global__ void __launch_bounds__(kThreads, 2)
+    qmma_q4_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ CUtensorMap tA1,
+                   const __grid_constant__ CUtensorMap tB, TcGemmArgs a) {
+  using S = QShape<NPROJ>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sStage = smem;
+  float* sRed = reinterpret_cast<float*>(smem + S::kStages * S::kStageBytes);
+  uint64_t* bar_full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes + S::kRedBytes);
+  uint64_t* bar_empty = bar_full + S::kStages;
+  uint64_t* bar_red_full = bar_empty + S::kStages;   // [4] k-quarters 1-3 of row group rg written
+  uint64_t* bar_red_empty = bar_red_full + 4;        // [4] consumed
+  int4* s_tiles = reinterpret_cast<int4*>(bar_red_empty + 4);
+  __shared__ int s_ntiles;
+  __shared__ int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S::kStages; ++i) {
+      mbar_init(&bar_full[i], 33);  // the TMA thread + one cp.async arrival per producer lane
+      mbar_init(&bar_empty[i], kComputeWarps);
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&bar_red_full[i], 3);
+      mbar_init(&bar_red_empty[i], 1);
+    }
+    fence_mbar_init();
+    s_abort = 0;
+  }
+  pdl_wait();  // active list / offsets (dispatch) and the activation rows (gather or gate/up)
+  pdl_launch_dependents();
+  const int nlisted = list_tiles(a.active, a.active_count, a.offsets, a.expert_begin, a.m_tiles, kQRows, 8, false,
+                                 s_tiles, kMaxTiles, reinterpret_cast<int*>(sStage), a.err);
+  if (threadIdx.x == 0) s_ntiles = nlisted;
+  __syncthreads();
+  const int ntiles = s_ntiles;
+  const int nst = a.kdim / kStageCols;
+  const int groups = a.kdim / 64;
+
+  if (warp == kComputeWarps) {
+    // ===================================================== producer
+    int slot = 0;
+    uint32_t ph = 0;
+    int issued = 0;
+    bool ok = true;
+    for (int ti = 0; ti < ntiles && ok; ++ti) {
+      const int4 tl = s_tiles[ti];
+      const int arow = tl.x * a.rows + tl.y;
+      const size_t sb_row0 = static_cast<size_t>(arow + lane) * groups;  // (row lane, group 0)
+      for (int st = 0; st < nst; ++st, ++issued) {
+        if (!(ok = __all_sync(0xffffffffu, wait_or_abort(&bar_empty[slot], ph ^ 1, &s_abort, a.err)))) break;
+        unsigned char* base = sStage + slot * S::kStageBytes;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bar_full[slot], S::kTmaBytes);
+#pragma unroll
+          for (int p = 0; p < NPROJ; ++p)
+            tma_load_2d(base + p * S::kABox, p ? &tA1 : &tA0, st * 32, arow, &bar_full[slot]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tma_load_2d(base + S::kABytes + j * S::kBBox, &tB, st * kStageCols + j * 64, tl.z, &bar_full[slot]);
+        }
+        // scale / bias runs: 8 bytes (4 groups of one row) each, NPROJ * 2 * 64 per stage
+        const uint32_t dst = smem_u32(base + S::kSBOff) + lane * 8;
+#pragma unroll
+        for (int i = 0; i < 4 * NPROJ; ++i) {  // run (array pa = i / 2, row lane + 32 (i % 2))
+          const int pa = i >> 1, r = 32 * (i & 1);
+          const uint16_t* src = ((pa & 1) ? a.b[pa >> 1] : a.s[pa >> 1]) + sb_row0 +
+                                static_cast<size_t>(r) * groups + 4 * st;
+          cp_async_8(dst + (pa * kQRows + r) * 8, src);
+        }
+        cp_async_arrive_noinc(&bar_full[slot]);
+        if (++slot == S::kStages) { slot = 0; ph ^= 1; }
+      }
+    }
+    // drain: the copies of the last stages must land before the CTA may exit
+    int never = 0;
+    for (int k = (issued > S::kStages ? issued - S::kStages : 0); k < issued; ++k)
+      wait_or_abort(&bar_full[k % S::kStages], (k / S::kStages) & 1, &never, nullptr);
+    return;
+  }
+
+  // ======================================================= compute warps
+  const int rg = warp & 3, kq = warp >> 2;
+  const int g = lane >> 2, t = lane & 3, lm = lane >> 3, lr = lane & 7;
+  const int rA = 16 * rg + g;
+  const uint32_t sStage_u32 = smem_u32(sStage);
+  // ldmatrix offsets inside a stage (see the k order of the group-scaled form)
+  const uint32_t offA = static_cast<uint32_t>(16 * rg + lr + 8 * (lm & 1)) * 128u +
+                        ((static_cast<uint32_t>(2 * kq + (lm >> 1)) ^ lr) << 4);
+  const uint32_t offB0 = S::kABytes + kq * S::kBBox + lr * 128 + ((static_cast<uint32_t>(lm) ^ lr) << 4);
+  const uint32_t offB1 = S::kABytes + kq * S::kBBox + lr * 128 + ((static_cast<uint32_t>(4 + lm) ^ lr) << 4);
+  const int offSB = S::kSBOff + rA * 8 + kq * 2;  // bf16 of group kq, row rA
+  int slot = 0;
+  uint32_t ph = 0;
+  bool ok = true;
+  for (int ti = 0; ti < ntiles && ok; ++ti) {
+    const int4 tl = s_tiles[ti];
+    float acc[NPROJ][4];
+#pragma unroll
+    for (int p = 0; p < NPROJ; ++p)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[p][i] = 0.f;
+    for (int st = 0; st < nst; ++st) {
+      ok = __all_sync(0xffffffffu, wait_or_abort(&bar_full[slot], ph, &s_abort, a.err));
+      if (!ok) break;
+      const unsigned char* base = sStage + slot * S::kStageBytes;
+      const uint32_t sbase = sStage_u32 + slot * S::kStageBytes;
+      uint32_t bf[2][4];
+      ldmatrix_x4(sbase + offB0, bf[0]);
+      ldmatrix_x4(sbase + offB1, bf[1]);
+      float xs[4];  // group sums of the activations, units of 2^-24
+      mma_z(xs, kOne24, kOne24, kOne24, kOne24, bf[0][0], bf[0][1]);
+      mma_acc(xs, kOne20, kOne20, kOne20, kOne20, bf[0][2], bf[0][3]);
+      mma_acc(xs, kOne24, kOne24, kOne24, kOne24, bf[1][0], bf[1][1]);
+      mma_acc(xs, kOne20, kOne20, kOne20, kOne20, bf[1][2], bf[1][3]);
+#pragma unroll
+      for (int p = 0; p < NPROJ; ++p) {
+        uint32_t w[4];
+        ldmatrix_x4(sbase + offA + p * S::kABox, w);
+        float grp[4];
+#pragma unroll
+        for (int hw = 0; hw < 2; ++hw) {
+          const uint32_t x0 = w[2 * hw], x1 = w[2 * hw + 1], y0 = x0 >> 8, y1 = x1 >> 8;
+          if (hw == 0)
+            mma_z(grp, x0 & kCodeLo, x1 & kCodeLo, y0 & kCodeLo, y1 & kCodeLo, bf[0][0], bf[0][1]);
+          else
+            mma_acc(grp, x0 & kCodeLo, x1 & kCodeLo, y0 & kCodeLo, y1 & kCodeLo, bf[1][0], bf[1][1]);
+          mma_acc(grp, x0 & kCodeHi, x1 & kCodeHi, y0 & kCodeHi, y1 & kCodeHi, bf[hw][2], bf[hw][3]);
+        }
+        const unsigned char* sbp = base + offSB + 2 * p * kQRows * 8;
+        const float s0 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(sbp));
+        const float s1 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(sbp + 64));
+        const float b0 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(sbp + kQRows * 8));
+        const float b1 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(sbp + kQRows * 8 + 64));
+        acc[p][0] = fmaf(s0, grp[0], fmaf(b0, xs[0], acc[p][0]));
+        acc[p][1] = fmaf(s0, grp[1], fmaf(b0, xs[1], acc[p][1]));
+        acc[p][2] = fmaf(s1, grp[2], fmaf(b1, xs[2], acc[p][2]));
+        acc[p][3] = fmaf(s1, grp[3], fmaf(b1, xs[3], acc[p][3]));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_empty[slot]);
+      if (++slot == S::kStages) { slot = 0; ph ^= 1; }
+    }
+    if (!ok) break;
+
+    // ---- add the k-quarters: warps kq = 1..3 hand their partials to kq = 0
+    float* red = sRed + (rg * 32 + lane) * (NPROJ * 4);
+    const uint32_t rph = ti & 1;
+    if (kq != 0) {
+      ok = __all_sync(0xffffffffu, wait_or_abort(&bar_red_empty[rg], rph ^ 1, &s_abort, a.err));
+      if (!ok) break;
+#pragma unroll
+      for (int p = 0; p < NPROJ; ++p)
+        *reinterpret_cast<float4*>(red + (kq - 1) * S::kRedSlice + p * 4) =
+            make_float4(acc[p][0], acc[p][1], acc[p][2], acc[p][3]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_red_full[rg]);
+      continue;
+    }
+    ok = __all_sync(0xffffffffu, wait_or_abort(&bar_red_full[rg], rph, &s_abort, a.err));
+    if (!ok) break;
+#pragma unroll
+    for (int q = 0; q < 3; ++q)
+#pragma unroll
+      for (int p = 0; p < NPROJ; ++p) {
+        const float4 o = *reinterpret_cast<const float4*>(red + q * S::kRedSlice + p * 4);
+        acc[p][0] += o.x; acc[p][1] += o.y; acc[p][2] += o.z; acc[p][3] += o.w;
+      }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bar_red_empty[rg]);
+
+    // ---- epilogue: lane holds rows (rA, rA + 8) x slots (2t, 2t + 1)
+    bool range_ok = true;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int n = 2 * t + (i & 1);
+      if (n >= tl.w) continue;
+      const int row = tl.y + rA + 8 * (i >> 1);
+      const size_t o = static_cast<size_t>(tl.z + n) * a.out_stride;
+      if constexpr (NPROJ == 2) {
+        const float gv = round_bf16(acc[0][i] * kG4Scale), uv = round_bf16(acc[1][i] * kG4Scale);
+        const float h = a.act == 0 ? act_swiglu_mlx(gv, uv) : act_geglu_mlx(gv, uv);
+        range_ok &= fabsf(h) < 65504.0f;
+        a.out[o + kperm_g4(row)] = __half_as_ushort(__float2half_rn((row & 1) ? h * 0.0625f : h));
+      } else {
+        a.out[o + row] = f32_to_bf16_bits(acc[0][i] * kG4Scale);
+      }
+    }
+    if (!range_ok) record_error(a.err, kDevFp16Range);
+  }
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------ host
@@ -592,6 +831,7 @@ static cudaError_t launch_mma_t(const CUtensorMap& tA0, const CUtensorMap& tA1, 
                                 const TcGemmArgs& a, int tiles_upper, cudaStream_t st) {
   using S = MmaShape<BITS, NPROJ, NT, G4>;
   auto kern = qmma_kernel<BITS, NPROJ, NT, G4>;
+  constexpr int threads = G4 ? kThreadsG4 : kThreads;
   cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), S::kSmem);
   if (e != cudaSuccess) return e;
   int sms = 0, dev = 0;
@@ -600,7 +840,31 @@ static cudaError_t launch_mma_t(const CUtensorMap& tA0, const CUtensorMap& tA1, 
   int grid = tiles_upper < sms ? tiles_upper : sms;
   if (grid < 1) grid = 1;
   if ((tiles_upper + grid - 1) / grid > kMaxTiles) return cudaErrorNotSupported;
+  return launch_pdl(kern, dim3(grid), dim3(threads), S::kSmem, st, tA0, tA1, tB, a);
+}
+
+template <int NPROJ>
+static cudaError_t launch_q4_t(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
+                               const TcGemmArgs& a, int tiles_upper, cudaStream_t st) {
+  using S = QShape<NPROJ>;
+  auto kern = qmma_q4_kernel<NPROJ>;
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), S::kSmem);
+  if (e != cudaSuccess) return e;
+  int sms = 0, dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  int grid = tiles_upper < 2 * sms ? tiles_upper : 2 * sms;  // two CTAs per SM
+  if (grid < 1) grid = 1;
+  if ((tiles_upper + grid - 1) / grid > kMaxTiles) return cudaErrorNotSupported;
   return launch_pdl(kern, dim3(grid), dim3(kThreads), S::kSmem, st, tA0, tA1, tB, a);
+}
+
+cudaError_t launch_mma_q4(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
+                          const TcGemmArgs& a, int bits, int nproj, int tiles_upper, cudaStream_t st) {
+  if (!mma_g4_supported(bits, 1, a)) return cudaErrorInvalidValue;
+  if (nproj == 2) return launch_q4_t<2>(tA0, tA1, tB, a, tiles_upper, st);
+  if (nproj == 1) return launch_q4_t<1>(tA0, tA1, tB, a, tiles_upper, st);
+  return cudaErrorNotSupported;
 }
 
 size_t mma_smem_bytes(int bits, int nproj, int nt, bool g4) {

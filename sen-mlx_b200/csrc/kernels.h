@@ -160,6 +160,10 @@ bool mma_g4_supported(int bits, int nt, const TcGemmArgs& a);
 cudaError_t launch_mma_gemm(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
                             const TcGemmArgs& a, int bits, int nproj, int nt, bool g4, int tiles_upper,
                             cudaStream_t st);
+// Group-scaled form at two CTAs per SM: 64-row tiles (a.m_tiles = rows / 64;
+// tA* with 64-row boxes), 8 slots per tile, 4-bit.
+cudaError_t launch_mma_q4(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
+                          const TcGemmArgs& a, int bits, int nproj, int tiles_upper, cudaStream_t st);
 
 // ------------------------------------------------- expert parallelism
 constexpr int kEpMaxRanks = 8;

@@ -82,8 +82,9 @@ constexpr double kTcMinTokensPerExpert = 24.0;
 constexpr double kMmaMinTokensPerExpert = 0.0;
 enum ExpertPath { kPathAuto = 0, kPathGemv = 1, kPathTensorCore = 2, kPathMma = 3 };
 // SenMoeConfig.reserved[1]: warp-MMA form, 0 = group-scaled where supported
-// (4-bit, up to 16 slots per tile), 1 = always dequantise to fp16
-enum MmaForm { kMmaFormAuto = 0, kMmaFormDequant = 1 };
+// (4-bit, up to 16 slots per tile; two CTAs per SM at 8 slots), 1 = always
+// dequantise to fp16, 2 = group-scaled, one CTA per SM at every tile width
+enum MmaForm { kMmaFormAuto = 0, kMmaFormDequant = 1, kMmaFormG4Single = 2 };
 // From this many tokens the router runs as one tensor-core launch (logits
 // and top-k, 32 tokens per CTA, so at least 16 CTAs) instead of the CUDA-core
 // logits + top-k pair.
@@ -129,6 +130,9 @@ struct SenMoeLayer {
   uint16_t* xs = nullptr;        // fp16 [Tmax*K, H] activations gathered into slot order
   uint16_t* h16 = nullptr;       // fp16 [Tmax*K, I] SwiGLU output (B operand of the down GEMM)
   CUtensorMap tm_gate{}, tm_up{}, tm_down{};  // packed codes, [rows, words]
+  CUtensorMap tm_gate64{}, tm_up64{}, tm_down64{};  // the same with 64-row boxes (two-CTA form)
+  bool q4_ok = false;
+  int sms = 148;  // SMs of the layer's device
   CUtensorMap tm_xs[4]{}, tm_h[4]{};          // activation tiles per token-tile width
   int* route_cnt = nullptr;      // fused top-k tile counters [ceil(Tmax/4)] (null: separate top-k)
   // tensor-core prefill router (Wg tensor map; x's is encoded per call)
@@ -313,6 +317,17 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                 make_tmap_2d(&L->tm_h8, L->h16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, I, P, I * 2, 64, 8, true) ==
                     cudaSuccess;
   }
+  cudaDeviceGetAttribute(&L->sms, cudaDevAttrMultiProcessorCount, device);
+  if (L->mma_ok && c.bits == 4) {
+    const int El = c.expert_end - c.expert_begin;
+    const uint64_t gw = uint64_t(H) / 8, dw = uint64_t(I) / 8;
+    L->q4_ok = make_tmap_2d(&L->tm_gate64, L->w.gate_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, gw, uint64_t(El) * I,
+                            gw * 4, 32, 64, true) == cudaSuccess &&
+               make_tmap_2d(&L->tm_up64, L->w.up_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, gw, uint64_t(El) * I,
+                            gw * 4, 32, 64, true) == cudaSuccess &&
+               make_tmap_2d(&L->tm_down64, L->w.down_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, dw, uint64_t(El) * H,
+                            dw * 4, 32, 64, true) == cudaSuccess;
+  }
   L->rtc_ok = router_tc_supported(int(H), int(E), int(K)) && E >= 128 &&
               make_tmap_2d(&L->tm_router, L->w.router_weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, E, H * 2, 64, 128,
                            true) == cudaSuccess;
@@ -491,13 +506,25 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     ga.err = L->err;
     // group-scaled form (4-bit, up to 16 slots per tile) unless the
     // dequantising form is forced
-    const bool g4 = c.reserved[1] != kMmaFormDequant && mma_g4_supported(c.bits, nt, ga);
+    // Form (measured on the 48-layer decode stack): the group-scaled form
+    // wins at 8-slot tiles, the dequantising form from 16 slots on (the
+    // group-scaled post-scale grows with the slot count, dequantisation
+    // does not); the two-CTA kernel only while the 128-row gate/up tiles
+    // cannot fill the SMs (about one token per expert).
+    const bool g4 = mma_g4_supported(c.bits, nt, ga) &&
+                    (c.reserved[1] == kMmaFormG4Single || (c.reserved[1] == kMmaFormAuto && nt == 1));
+    const bool q4 = g4 && nt == 1 && L->q4_ok && c.reserved[1] == kMmaFormAuto && max_items * (I / 128) < L->sms;
     SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
                                    ep ? L->offsets : nullptr, c.expert_begin, c.expert_end,
                                    g4 ? kOrderMmaG4 : kOrderMma));
     SENMOE_CUDA(mark(2));
-    SENMOE_CUDA(launch_mma_gemm(L->tm_gate, L->tm_up, tb_x, ga, c.bits, 2, nt, g4,
-                                (P / (8 * nt) + max_items) * ga.m_tiles, st));
+    if (q4) {
+      ga.m_tiles = I / 64;
+      SENMOE_CUDA(launch_mma_q4(L->tm_gate64, L->tm_up64, tb_x, ga, c.bits, 2, (P / 8 + max_items) * ga.m_tiles, st));
+    } else {
+      SENMOE_CUDA(launch_mma_gemm(L->tm_gate, L->tm_up, tb_x, ga, c.bits, 2, nt, g4,
+                                  (P / (8 * nt) + max_items) * ga.m_tiles, st));
+    }
     SENMOE_CUDA(mark(3));
     TcGemmArgs gd = ga;
     gd.s[0] = static_cast<const uint16_t*>(L->w.down_scales);
@@ -509,8 +536,14 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     gd.m_tiles = H / 128;
     gd.out = L->d;
     gd.out_stride = H;
-    SENMOE_CUDA(launch_mma_gemm(L->tm_down, L->tm_down, tb_h, gd, c.bits, 1, nt, g4,
-                                (P / (8 * nt) + max_items) * gd.m_tiles, st));
+    if (q4) {
+      gd.m_tiles = H / 64;
+      SENMOE_CUDA(launch_mma_q4(L->tm_down64, L->tm_down64, tb_h, gd, c.bits, 1, (P / 8 + max_items) * gd.m_tiles,
+                                st));
+    } else {
+      SENMOE_CUDA(launch_mma_gemm(L->tm_down, L->tm_down, tb_h, gd, c.bits, 1, nt, g4,
+                                  (P / (8 * nt) + max_items) * gd.m_tiles, st));
+    }
     SENMOE_CUDA(mark(4));
   } else if (path == kPathTensorCore) {
     const int ti = tc_tile_index(per_expert), bn = kTcTiles[ti];

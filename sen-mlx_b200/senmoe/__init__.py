@@ -191,7 +191,9 @@ class MoeArgs:
     activation: int = ACT_SWIGLU
     shared_gate: bool = False  # sigmoid-gated shared expert (no reference counterpart)
     expert_path: int = PATH_AUTO  # AUTO: GEMV (~1 token per expert), warp MMA (decode), tcgen05 (prefill)
-    mma_dequant: bool = False  # warp MMA: dequantise every weight instead of the group-scaled 4-bit form
+    # warp-MMA form: 0 group-scaled 4-bit where supported (two CTAs per SM at 8-slot tiles),
+    # 1 dequantise every weight to fp16, 2 group-scaled with one CTA per SM at every tile width
+    mma_form: int = 0
 
 
 @dataclass
@@ -246,7 +248,7 @@ class DeepseekMoe:
         cfg.max_tokens = int(max_tokens)
         cfg.expert_begin, cfg.expert_end = eb, ee
         cfg.reserved[0] = int(args.expert_path)
-        cfg.reserved[1] = int(args.mma_dequant)
+        cfg.reserved[1] = int(args.mma_form)
         self._cfg = cfg
         wt = SenMoeWeights()
         wt.router_weight = _ptr(weights.router_weight)

@@ -29,11 +29,11 @@ def senmoe():
 PATHS = {"gemv": 1, "tc": 2, "mma": 3}
 
 
-def run_block(senmoe, cfg, mw, x_bits, max_tokens=None, path=0, mma_dequant=False):
+def run_block(senmoe, cfg, mw, x_bits, max_tokens=None, path=0, mma_form=0):
     import torch
     T = x_bits.shape[0]
     args = moe_args(cfg, path)
-    args.mma_dequant = mma_dequant
+    args.mma_form = mma_form
     blk = senmoe.DeepseekMoe(args, device_weights(mw), max_tokens=max_tokens or max(T, 1))
     if path:
         assert blk.expert_path(T) == path, "the forced expert path is not the one that runs"
@@ -115,22 +115,23 @@ def test_tensor_core_tiles_vs_oracle(senmoe, bits, T):
 
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("T", [3, 40, 200])
-@pytest.mark.parametrize("dequant", [False, True])
-def test_warp_mma_tiles_vs_oracle(senmoe, bits, T, dequant):
+@pytest.mark.parametrize("form", [0, 1, 2])
+def test_warp_mma_tiles_vs_oracle(senmoe, bits, T, form):
     """Warp-MMA decode kernel at each slot-tile width (8, 16, 32 slots: about 1,
     10 and 50 tokens per expert, the last in several slot chunks per expert),
     both code widths, on a small layer (H=256, I=256, E=16, K=4); 4-bit at 8
-    and 16 slots takes the group-scaled form unless the dequantising form is
-    forced."""
+    and 16 slots takes the group-scaled form (at 8 slots the two-CTA kernel)
+    unless form 1 (dequantise) or 2 (one CTA per SM) is forced."""
     cfg = O.MoeConfig(hidden=256, intermediate=256, num_experts=16, top_k=4, bits=bits)
     mw = O.make_layer(cfg, seed=40 + bits)
     x = O.make_tokens(T, cfg.hidden, seed=T + 7 * bits)
-    got = run_block(senmoe, cfg, mw, x, path=PATHS["mma"], mma_dequant=dequant)
+    got = run_block(senmoe, cfg, mw, x, path=PATHS["mma"], mma_form=form)
     check_against_oracle(cfg, mw, x, got)
 
 
 @pytest.mark.parametrize("T", [5, 60])
-def test_warp_mma_group_scaled_wide_scales(senmoe, T):
+@pytest.mark.parametrize("form", [0, 2])
+def test_warp_mma_group_scaled_wide_scales(senmoe, T, form):
     """Group-scaled 4-bit form with scales beyond the dequantising form's fp16
     fast range (|s| > 0.0624 for ~6 % of the groups) and activations up to
     ~16 (h up to ~7e3): the fp32 post-scale has no such limit."""
@@ -143,7 +144,7 @@ def test_warp_mma_group_scaled_wide_scales(senmoe, T):
     x = O.bf16_to_f32(O.make_tokens(T, cfg.hidden, seed=T))
     x = x * rng.choice([1.0, 4.0], size=x.shape).astype(np.float32)
     x_bits = O.f32_to_bf16(x.astype(np.float32))
-    got = run_block(senmoe, cfg, mw, x_bits, path=PATHS["mma"])
+    got = run_block(senmoe, cfg, mw, x_bits, path=PATHS["mma"], mma_form=form)
     ref = O.moe_forward(cfg, mw, x_bits, mode=0)
     same = (got["topk_ids"] == ref["ids"]).all(axis=1)
     y, yr = got["y"][same], ref["y_f32"][same]
