@@ -14,6 +14,12 @@
  *   senmoe_layer_forward    <- DeepseekMoe::forward(&mut self, x: &Array) -> Result<Array>
  *                              src/engine/mlx_lm/models/deepseek_v2.rs:520-553
  *   senmoe_router           <- the router half of DeepseekMoe::forward, :526-543
+ *   senmoe_gemma_router     <- gemma4::Router::forward(&mut self, x) -> (indices, weights)
+ *                              src/engine/mlx_lm/models/gemma4.rs:716-736
+ *   senmoe_layer_experts_forward
+ *                           <- gemma4::Experts::forward(&self, x, indices, weights)
+ *                              src/engine/mlx_lm/models/gemma4.rs:842-848 (also the expert
+ *                              half of DeepseekMoe::forward, deepseek_v2.rs:544-552)
  *   senmoe_dispatch         <- (no counterpart: the reference gathers per (token, slot)
  *                              with sorted_indices=false, deepseek_v2.rs:441; this is the
  *                              build's expert-contiguous permutation)
@@ -56,7 +62,9 @@ typedef enum SenMoeStatus {
 } SenMoeStatus;
 
 typedef enum SenMoeRouter {
-  SENMOE_ROUTER_SOFTMAX_TOPK = 0 /* DeepSeek/Qwen: softmax over E, top-k, optional renorm */
+  SENMOE_ROUTER_SOFTMAX_TOPK = 0, /* DeepSeek/Qwen: softmax over E, top-k, optional renorm */
+  SENMOE_ROUTER_TOPK_SOFTMAX = 1  /* Gemma-4: rms_norm, quantized proj, top-k, softmax over k,
+                                     x per-expert scale (senmoe_gemma_router) */
 } SenMoeRouter;
 
 typedef enum SenMoeActivation {
@@ -91,7 +99,8 @@ typedef struct SenMoeConfig {
 /* Device pointers, caller-owned, valid for the layer's lifetime.  Expert
  * tensors hold experts [expert_begin, expert_end) only. */
 typedef struct SenMoeWeights {
-  const void* router_weight;      /* bf16 [E, H]  (mlp.gate.weight, unquantized) */
+  const void* router_weight;      /* bf16 [E, H]  (mlp.gate.weight, unquantized); NULL: the
+                                     layer serves senmoe_layer_experts_forward only */
   const uint32_t* gate_weight;    /* u32 [E_local, I, H*bits/32] (switch_mlp.gate_proj) */
   const void* gate_scales;        /* bf16 [E_local, I, H/group] */
   const void* gate_biases;
@@ -209,6 +218,40 @@ int senmoe_router(const void* x, int64_t num_tokens, const void* router_weight, 
                   int32_t num_experts, int32_t top_k, int32_t norm_topk_prob, float routed_scaling_factor,
                   float* logits_scratch /* [T, E] fp32 device */, int32_t* topk_ids, float* topk_weights,
                   senmoe_stream_t stream);
+
+/* Gemma-4 router (Router::forward, gemma4.rs:716-736), field names after
+ * its parameters (gemma4.rs:683-700):
+ *   normed = rms_norm(x, f32(scale) * hidden_size^-1/2, rms_norm_eps)   fp32
+ *   scores = proj(normed)        affine-quantized [E, H] linear (MLX layout,
+ *                                8-bit in the checkpoint), fp32
+ *   ids    = top-k of scores     (score desc, id asc: MLX leaves the order open)
+ *   w      = softmax(scores[ids]) * f32(per_expert_scale[ids])
+ * x bf16 [T, H]; proj_weight u32 [E, H*bits/32], proj_scales/biases bf16
+ * [E, H/group_size]; scale bf16 [H]; per_expert_scale bf16 [E]; topk_ids
+ * int32 [T, K], topk_weights fp32 [T, K] (device memory). */
+typedef struct SenMoeGemmaRouter {
+  int32_t hidden_size;
+  int32_t num_experts;
+  int32_t top_k;             /* <= 16 */
+  int32_t bits;              /* 4 or 8 */
+  int32_t group_size;        /* 64 */
+  float rms_norm_eps;
+  const uint32_t* proj_weight;
+  const void* proj_scales;
+  const void* proj_biases;
+  const void* scale;
+  const void* per_expert_scale;
+} SenMoeGemmaRouter;
+int senmoe_gemma_router(const SenMoeGemmaRouter* router, const void* x, int64_t num_tokens, int32_t* topk_ids,
+                        float* topk_weights, senmoe_stream_t stream);
+
+/* Experts::forward (gemma4.rs:842-848): the layer's experts over routing the
+ * caller computed, y[t] = bf16( sum_j f32(expert_ids[t,j](x[t])) * w[t,j] )
+ * (+ the layer's shared experts; fused residual: no).  topk_ids int32 [T, K]
+ * in [0, n_routed_experts), topk_weights fp32 [T, K], device memory.  A layer
+ * used only this way may be created with router_weight = NULL. */
+int senmoe_layer_experts_forward(SenMoeLayer* layer, const void* x, int64_t num_tokens, const int32_t* topk_ids,
+                                 const float* topk_weights, void* y, senmoe_stream_t stream);
 
 /* Dispatch alone: stable counting sort of the T*K pairs by expert.
  * perm [T*K], inverse [T*K] (slot of each pair), offsets [E + 1]; scratch is

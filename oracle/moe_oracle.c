@@ -17,6 +17,8 @@
  *
  * Reference graph followed (paths inside the reference project):
  *   router           src/engine/mlx_lm/models/deepseek_v2.rs:526-548
+ *   Gemma router     src/engine/mlx_lm/models/gemma4.rs:716-736 (orc_gemma_router)
+ *   Gemma experts    src/engine/mlx_lm/models/gemma4.rs:809-848 (GeGLU, weighted sum)
  *   SwitchGlu        src/engine/mlx_lm/models/deepseek_v2.rs:466-478
  *   SwitchLinear     src/engine/mlx_lm/models/deepseek_v2.rs:431-443
  *   gather_qmm       src/engine/mlx_lm/utils/moe.rs:20-77
@@ -260,7 +262,7 @@ typedef struct {
   int32_t shared_intermediate; /* moe_intermediate_size * n_shared_experts; 0 = none */
   int32_t shared_gate;         /* 1: y += sigmoid(x . w_sg) * shared(x) (no reference counterpart) */
   int32_t mode;                /* 0 = MLX bf16 rounding points, 1 = fp32 */
-  int32_t reserved;
+  int32_t activation;          /* 0 SwiGLU (deepseek_v2.rs:472-474), 1 GeGLU (gemma4.rs:817-819) */
 } OrcConfig;
 
 typedef struct {
@@ -274,6 +276,10 @@ typedef struct {
 
 static inline float maybe_rbf(float v, int mode) { return mode == 0 ? rbf(v) : v; }
 static inline float sigmoidf_(float v) { return 1.0f / (1.0f + expf(-v)); }
+/* nn::gelu_approximate, the tanh form 0.5 g (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3))). */
+static inline float gelu_tanh_(float g) {
+  return 0.5f * g * (1.0f + tanhf(0.7978845608028654f * (g + 0.044715f * g * g * g)));
+}
 
 /* Router: deepseek_v2.rs:528-543.  ids[t*K+j] / weights[t*K+j] in canonical
  * slot order (score desc, expert id asc).  scores_out (optional) [T, E]. */
@@ -362,10 +368,10 @@ int orc_dispatch(const int32_t* ids, int64_t T, int32_t K, int32_t E, int32_t* p
   return ORC_OK;
 }
 
-/* SwiGLU expert MLP over the slots of one expert (deepseek_v2.rs:466-478 and
- * the dense twin :389-392).  xs: n rows of in=H floats (already bf16 values);
+/* Gated expert MLP (SwiGLU: deepseek_v2.rs:466-478 and the dense twin
+ * :389-392; GeGLU: gemma4.rs:809-823) over the slots of one expert.  xs: n rows of in=H floats (already bf16 values);
  * out: n rows of H floats, rounded per mode.  Weights are one expert's slice. */
-static void swiglu_expert(const OrcConfig* cfg, int64_t H, int64_t I, const uint32_t* gw, const uint16_t* gs,
+static void glu_expert(const OrcConfig* cfg, int64_t H, int64_t I, const uint32_t* gw, const uint16_t* gs,
                           const uint16_t* gb, const uint32_t* uw, const uint16_t* us, const uint16_t* ub,
                           const uint32_t* dw, const uint16_t* ds, const uint16_t* db, const float* xs, int64_t n,
                           float* hbuf, float* rowg, float* rowu, float* out) {
@@ -389,7 +395,11 @@ static void swiglu_expert(const OrcConfig* cfg, int64_t H, int64_t I, const uint
         }
       }
       const float g = maybe_rbf((float)ag, mode), u = maybe_rbf((float)au, mode);
-      const float a = maybe_rbf(g * maybe_rbf(sigmoidf_(g), mode), mode);
+      /* SwiGLU: nn::silu(g) = g * sigmoid(g), one bf16 rounding per op;
+       * GeGLU: nn::gelu_approximate(g) rounded once to bf16 (assumed: one
+       * fused activation op, as MLX compiles its elementwise chains) */
+      const float a = cfg->activation == 1 ? maybe_rbf(gelu_tanh_(g), mode)
+                                           : maybe_rbf(g * maybe_rbf(sigmoidf_(g), mode), mode);
       hbuf[r * I + i] = maybe_rbf(a * u, mode);
     }
   }
@@ -409,12 +419,12 @@ static void swiglu_expert(const OrcConfig* cfg, int64_t H, int64_t I, const uint
   }
 }
 
-/* Full block: DeepseekMoe::forward (deepseek_v2.rs:520-553).
- * Outputs: y_f32 [T, H] (the reference's f32 result), y_bf16 (optional),
- * ids/weights [T, K] in canonical slot order, perm [T*K], offsets [E+1]
- * (optional).  Weights are for all E experts. */
-int orc_moe_forward(const OrcConfig* cfg, const OrcWeights* wt, const uint16_t* x, int64_t T, float* y_f32,
-                    uint16_t* y_bf16, int32_t* ids_out, float* w_out, int32_t* perm_out, int32_t* offsets_out) {
+/* Block body: the router's (or the caller's) routing, then the experts and the
+ * weighted combine.  ext_ids / ext_w: [T, K] routing from the caller, or NULL
+ * to run orc_router. */
+static int moe_forward_impl(const OrcConfig* cfg, const OrcWeights* wt, const uint16_t* x, int64_t T,
+                            const int32_t* ext_ids, const float* ext_w, float* y_f32, uint16_t* y_bf16,
+                            int32_t* ids_out, float* w_out, int32_t* perm_out, int32_t* offsets_out) {
   const int64_t H = cfg->hidden, I = cfg->intermediate, E = cfg->num_experts, K = cfg->top_k;
   const int32_t G = cfg->group_size, B = cfg->bits;
   if (T < 0 || H <= 0 || I <= 0 || H % G || I % G || !(B == 4 || B == 8)) return ORC_BAD_ARG;
@@ -433,7 +443,12 @@ int orc_moe_forward(const OrcConfig* cfg, const OrcWeights* wt, const uint16_t* 
     goto done;
   }
   for (int64_t i = 0; i < T * H; ++i) xf[i] = bf2f(x[i]);
-  if ((err = orc_router(cfg, wt, x, T, ids, wts, NULL))) goto done;
+  if (ext_ids) {  /* routing given by the caller (Experts::forward, gemma4.rs:842-848) */
+    memcpy(ids, ext_ids, sizeof(int32_t) * (size_t)P);
+    memcpy(wts, ext_w, sizeof(float) * (size_t)P);
+  } else if ((err = orc_router(cfg, wt, x, T, ids, wts, NULL))) {
+    goto done;
+  }
   if ((err = orc_dispatch(ids, T, (int32_t)K, (int32_t)E, perm, offs, inv))) goto done;
 
   const int64_t wsg = I * (H * B / 32), ssg = I * (H / G); /* gate/up strides per expert */
@@ -456,7 +471,7 @@ int orc_moe_forward(const OrcConfig* cfg, const OrcWeights* wt, const uint16_t* 
         const int64_t s0 = offs[e], n = offs[e + 1] - offs[e];
         if (n == 0) continue;
         for (int64_t r = 0; r < n; ++r) memcpy(xs + r * H, xf + (perm[s0 + r] / K) * H, sizeof(float) * (size_t)H);
-        swiglu_expert(cfg, H, I, wt->gate_w + e * wsg, wt->gate_s + e * ssg, wt->gate_b + e * ssg,
+        glu_expert(cfg, H, I, wt->gate_w + e * wsg, wt->gate_s + e * ssg, wt->gate_b + e * ssg,
                       wt->up_w + e * wsg, wt->up_s + e * ssg, wt->up_b + e * ssg, wt->down_w + e * wsd,
                       wt->down_s + e * ssd, wt->down_b + e * ssd, xs, n, hb, rg, ru, ob);
         memcpy(d + s0 * H, ob, sizeof(float) * (size_t)(n * H));
@@ -494,7 +509,7 @@ int orc_moe_forward(const OrcConfig* cfg, const OrcWeights* wt, const uint16_t* 
       } else {
 #pragma omp for schedule(dynamic, 1)
         for (int64_t t = 0; t < T; ++t) {
-          swiglu_expert(cfg, H, Is, wt->sh_gate_w, wt->sh_gate_s, wt->sh_gate_b, wt->sh_up_w, wt->sh_up_s,
+          glu_expert(cfg, H, Is, wt->sh_gate_w, wt->sh_gate_s, wt->sh_gate_b, wt->sh_up_w, wt->sh_up_s,
                         wt->sh_up_b, wt->sh_down_w, wt->sh_down_s, wt->sh_down_b, xf + t * H, 1, hb, rg, ru, ob);
           float gate = 1.0f;
           if (cfg->shared_gate) {
@@ -526,5 +541,100 @@ done:
   free(offs);
   free(xf);
   free(d);
+  return err;
+}
+
+/* Full block: DeepseekMoe::forward (deepseek_v2.rs:520-553).
+ * Outputs: y_f32 [T, H] (the reference's f32 result), y_bf16 (optional),
+ * ids/weights [T, K] in canonical slot order, perm [T*K], offsets [E+1]
+ * (optional).  Weights are for all E experts. */
+int orc_moe_forward(const OrcConfig* cfg, const OrcWeights* wt, const uint16_t* x, int64_t T, float* y_f32,
+                    uint16_t* y_bf16, int32_t* ids_out, float* w_out, int32_t* perm_out, int32_t* offsets_out) {
+  return moe_forward_impl(cfg, wt, x, T, NULL, NULL, y_f32, y_bf16, ids_out, w_out, perm_out, offsets_out);
+}
+
+/* Experts::forward (gemma4.rs:842-848; the DeepSeek block's expert half,
+ * deepseek_v2.rs:544-552): the experts of the given routing ids / weights
+ * [T, K] and their weighted sum in f32 (+ the shared experts of cfg).  The
+ * router weights of wt are not used. */
+int orc_experts_forward(const OrcConfig* cfg, const OrcWeights* wt, const uint16_t* x, int64_t T,
+                        const int32_t* ids, const float* weights, float* y_f32, uint16_t* y_bf16) {
+  if (!ids || !weights) return ORC_BAD_ARG;
+  return moe_forward_impl(cfg, wt, x, T, ids, weights, y_f32, y_bf16, NULL, NULL, NULL, NULL);
+}
+
+/* ---------------------------------------------------------- Gemma router */
+typedef struct {
+  int32_t hidden;       /* H */
+  int32_t num_experts;  /* E */
+  int32_t top_k;        /* K */
+  int32_t group_size;   /* of the quantized projection (64) */
+  int32_t bits;         /* 8 in the shipped checkpoint (gemma4.rs:691-694) */
+  float eps;            /* rms_norm_eps */
+} OrcGemmaRouterConfig;
+
+typedef struct {
+  const uint32_t* proj_w;             /* [E, H*bits/32] */
+  const uint16_t *proj_s, *proj_b;    /* [E, H/group] bf16 */
+  const uint16_t* scale;              /* [H] bf16, the bare learned norm weight */
+  const uint16_t* per_expert_scale;   /* [E] bf16 */
+} OrcGemmaRouterWeights;
+
+/* Router::forward (gemma4.rs:716-736):
+ *   w      = f32(scale) * H^-1/2          (bf16 array x array!(f32): f32)
+ *   normed = fast::rms_norm(x, w, eps)    x bf16, w f32 -> f32 out:
+ *            x * 1/sqrt(mean(x^2) + eps) (fp32), then * w
+ *   scores = proj(normed)                 quantized linear, f32 in -> f32
+ *   top-k of scores (order: score desc, id asc; MLX leaves it unspecified)
+ *   w_k    = softmax_fp32(scores[top-k]) * f32(per_expert_scale[top-k])
+ * ids / weights [T, K]; scores_out [T, E] optional. */
+int orc_gemma_router(const OrcGemmaRouterConfig* rc, const OrcGemmaRouterWeights* rw, const uint16_t* x, int64_t T,
+                     int32_t* ids, float* weights, float* scores_out) {
+  const int64_t H = rc->hidden, E = rc->num_experts, K = rc->top_k;
+  const int32_t G = rc->group_size, B = rc->bits;
+  if (K <= 0 || K > E || H <= 0 || G <= 0 || H % G || !(B == 4 || B == 8)) return ORC_BAD_ARG;
+  const float root = powf((float)H, -0.5f);
+  int err = ORC_OK;
+#pragma omp parallel
+  {
+    float* xn = (float*)malloc(sizeof(float) * (size_t)H);
+    float* sc = (float*)malloc(sizeof(float) * (size_t)E);
+    unsigned char* taken = (unsigned char*)malloc((size_t)E);
+    if (!xn || !sc || !taken) {
+#pragma omp atomic write
+      err = ORC_NO_MEM;
+    } else {
+#pragma omp for schedule(static)
+      for (int64_t t = 0; t < T; ++t) {
+        const uint16_t* xr = x + t * H;
+        float ss = 0.0f;
+        for (int64_t h = 0; h < H; ++h) ss += bf2f(xr[h]) * bf2f(xr[h]);
+        const float inv = 1.0f / sqrtf(ss / (float)H + rc->eps);
+        for (int64_t h = 0; h < H; ++h) xn[h] = (bf2f(xr[h]) * inv) * (bf2f(rw->scale[h]) * root);
+        for (int64_t e = 0; e < E; ++e) sc[e] = (float)qdot_row(rw->proj_w, rw->proj_s, rw->proj_b, e, H, G, B, xn);
+        if (scores_out)
+          for (int64_t e = 0; e < E; ++e) scores_out[t * E + e] = sc[e];
+        memset(taken, 0, (size_t)E);
+        for (int64_t j = 0; j < K; ++j) { /* select max, lowest id on ties */
+          int64_t best = -1;
+          for (int64_t e = 0; e < E; ++e)
+            if (!taken[e] && (best < 0 || sc[e] > sc[best])) best = e;
+          taken[best] = 1;
+          ids[t * K + j] = (int32_t)best;
+        }
+        const float mx = sc[ids[t * K]];  /* the first pick is the maximum */
+        float sum = 0.0f;
+        for (int64_t j = 0; j < K; ++j) {
+          weights[t * K + j] = expf(sc[ids[t * K + j]] - mx);
+          sum += weights[t * K + j];
+        }
+        for (int64_t j = 0; j < K; ++j)
+          weights[t * K + j] = (weights[t * K + j] / sum) * bf2f(rw->per_expert_scale[ids[t * K + j]]);
+      }
+    }
+    free(xn);
+    free(sc);
+    free(taken);
+  }
   return err;
 }

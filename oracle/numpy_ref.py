@@ -2,9 +2,10 @@
 MoE block as moe_oracle.c, written separately so the two can check each other
 (small sizes only; it is vectorised but not fast).
 
-Follows src/engine/mlx_lm/models/deepseek_v2.rs:466-553 and
-src/engine/mlx_lm/utils/moe.rs:20-77 with the MLX rounding points listed in
-moe_oracle.c.  bf16 values are carried as uint16 bit patterns.
+Follows src/engine/mlx_lm/models/deepseek_v2.rs:466-553,
+src/engine/mlx_lm/models/gemma4.rs:716-736 (router) and :809-848 (GeGLU
+experts) and src/engine/mlx_lm/utils/moe.rs:20-77 with the MLX rounding points
+listed in moe_oracle.c.  bf16 values are carried as uint16 bit patterns.
 """
 from __future__ import annotations
 
@@ -98,14 +99,21 @@ def route(cfg, w, x, mode: int = 0):
     return ids, wts
 
 
-def expert_mlp(xr, gd, ud, dd, mode: int = 0) -> np.ndarray:
-    """One SwitchGlu expert on one token (deepseek_v2.rs:443-462): x row fp64,
-    dequantised gate/up/down fp64; returns the down output (bf16 values, fp32)."""
+def expert_mlp(xr, gd, ud, dd, mode: int = 0, activation: int = 0) -> np.ndarray:
+    """One SwitchGlu expert on one token (deepseek_v2.rs:443-462; GeGLU:
+    gemma4.rs:811-823): x row fp64, dequantised gate/up/down fp64; returns the
+    down output (bf16 values, fp32)."""
     R = rounding(mode)
     g = R((gd @ xr).astype(np.float32))
     u = R((ud @ xr).astype(np.float32))
-    sg = R((1.0 / (1.0 + np.exp(-g.astype(np.float32)))).astype(np.float32))
-    h = R(R(g * sg) * u)
+    if activation == 1:  # gelu_approximate, tanh form, rounded once
+        g32 = g.astype(np.float32)
+        a = R((np.float32(0.5) * g32 * (np.float32(1.0) + np.tanh(
+            np.float32(0.7978845608028654) * (g32 + np.float32(0.044715) * g32 * g32 * g32)))).astype(np.float32))
+    else:
+        sg = R((1.0 / (1.0 + np.exp(-g.astype(np.float32)))).astype(np.float32))
+        a = R(g * sg)
+    h = R(a * u)
     return R((dd @ h.astype(np.float64)).astype(np.float32))
 
 
@@ -124,12 +132,15 @@ def shared_out(cfg, w, x, mode: int = 0) -> np.ndarray:
     return out
 
 
-def moe_forward(cfg, w, x_bits, mode: int = 0):
-    """cfg/w: oracle.MoeConfig / oracle.MoeWeights.  Same outputs as the C oracle."""
+def moe_forward(cfg, w, x_bits, mode: int = 0, ids=None, wts=None):
+    """cfg/w: oracle.MoeConfig / oracle.MoeWeights.  Same outputs as the C
+    oracle; ids / wts [T, K] given: Experts::forward (gemma4.rs:842-848)."""
     H, K = cfg.hidden, cfg.top_k
     x = bf16_val(x_bits).reshape(-1, H)
     T = x.shape[0]
-    ids, wts = route(cfg, w, x, mode)
+    if ids is None:
+        ids, wts = route(cfg, w, x, mode)
+    act = getattr(cfg, "activation", 0)
     g_d = dequantize(w.gate_w, w.gate_s, w.gate_b, cfg.group_size, cfg.bits).astype(np.float64)
     u_d = dequantize(w.up_w, w.up_s, w.up_b, cfg.group_size, cfg.bits).astype(np.float64)
     d_d = dequantize(w.down_w, w.down_s, w.down_b, cfg.group_size, cfg.bits).astype(np.float64)
@@ -138,9 +149,30 @@ def moe_forward(cfg, w, x_bits, mode: int = 0):
         acc = np.zeros(H, dtype=np.float32)
         for j in range(K):
             e = ids[t, j]
-            acc = (acc + expert_mlp(x[t].astype(np.float64), g_d[e], u_d[e], d_d[e], mode) * wts[t, j]).astype(
-                np.float32)
+            acc = (acc + expert_mlp(x[t].astype(np.float64), g_d[e], u_d[e], d_d[e], mode, act) *
+                   wts[t, j]).astype(np.float32)
         y[t] = acc
     if cfg.shared_intermediate:
         y = (y + shared_out(cfg, w, x, mode)).astype(np.float32)
     return dict(y_f32=y, y_bf16=bf16_bits(y), ids=ids, weights=wts)
+
+
+def gemma_route(rc, rw, x_bits):
+    """Router::forward of gemma4.rs:716-736 (rc / rw: oracle.GemmaRouterConfig /
+    GemmaRouterWeights): rms_norm in f32 with weight f32(scale) * H^-1/2,
+    quantized projection in f32, top-k (score desc, id asc), softmax over
+    the k, * per_expert_scale.  Returns (ids [T, K], weights [T, K], scores)."""
+    H, E, K = rc.hidden, rc.num_experts, rc.top_k
+    x = bf16_val(x_bits).reshape(-1, H).astype(np.float32)
+    ms = (x.astype(np.float64) ** 2).mean(-1, keepdims=True)
+    inv = (1.0 / np.sqrt(ms + rc.eps)).astype(np.float32)
+    weff = (bf16_val(rw.scale) * np.float32(H ** -0.5)).astype(np.float32)
+    xn = ((x * inv).astype(np.float32) * weff).astype(np.float32)
+    pd = dequantize(rw.proj_w, rw.proj_s, rw.proj_b, rc.group_size, rc.bits).astype(np.float64)
+    scores = (xn.astype(np.float64) @ pd.T).astype(np.float32)
+    order = np.lexsort((np.broadcast_to(np.arange(E), scores.shape), -scores), axis=-1)
+    ids = order[:, :K].astype(np.int32)
+    picked = np.take_along_axis(scores, ids, -1).astype(np.float32)
+    ex = np.exp((picked - picked.max(-1, keepdims=True)).astype(np.float32)).astype(np.float32)
+    wts = (ex / ex.sum(-1, keepdims=True)).astype(np.float32) * bf16_val(rw.per_expert_scale)[ids]
+    return ids, wts.astype(np.float32), scores

@@ -39,11 +39,21 @@ class OrcConfig(C.Structure):
         ("top_k", C.c_int32), ("bits", C.c_int32), ("group_size", C.c_int32),
         ("norm_topk_prob", C.c_int32), ("routed_scaling_factor", C.c_float),
         ("shared_intermediate", C.c_int32), ("shared_gate", C.c_int32),
-        ("mode", C.c_int32), ("reserved", C.c_int32),
+        ("mode", C.c_int32), ("activation", C.c_int32),
     ]
 
 
 _P = C.c_void_p
+
+
+class OrcGemmaRouterConfig(C.Structure):
+    _fields_ = [("hidden", C.c_int32), ("num_experts", C.c_int32), ("top_k", C.c_int32),
+                ("group_size", C.c_int32), ("bits", C.c_int32), ("eps", C.c_float)]
+
+
+class OrcGemmaRouterWeights(C.Structure):
+    _fields_ = [("proj_w", C.c_void_p), ("proj_s", C.c_void_p), ("proj_b", C.c_void_p),
+                ("scale", C.c_void_p), ("per_expert_scale", C.c_void_p)]
 
 
 class OrcWeights(C.Structure):
@@ -69,6 +79,9 @@ def lib():
         L.orc_dispatch.argtypes = [_P, i64, i32, i32, _P, _P, _P]
         L.orc_moe_forward.argtypes = [C.POINTER(OrcConfig), C.POINTER(OrcWeights), _P, i64,
                                       _P, _P, _P, _P, _P, _P]
+        L.orc_experts_forward.argtypes = [C.POINTER(OrcConfig), C.POINTER(OrcWeights), _P, i64, _P, _P, _P, _P]
+        L.orc_gemma_router.argtypes = [C.POINTER(OrcGemmaRouterConfig), C.POINTER(OrcGemmaRouterWeights), _P, i64,
+                                       _P, _P, _P]
         L.orc_f32_to_bf16.argtypes = [_P, _P, i64]
         L.orc_bf16_to_f32.argtypes = [_P, _P, i64]
         L.orc_fill_normal.argtypes = [C.c_uint64, _P, i64, C.c_float]
@@ -199,11 +212,12 @@ class MoeConfig:
     routed_scaling_factor: float = 1.0
     shared_intermediate: int = 0
     shared_gate: bool = False
+    activation: int = 0  # 0 SwiGLU (DeepSeek), 1 GeGLU (Gemma)
 
     def to_c(self, mode: int = 0) -> OrcConfig:
         return OrcConfig(self.hidden, self.intermediate, self.num_experts, self.top_k, self.bits,
                          self.group_size, int(self.norm_topk_prob), float(self.routed_scaling_factor),
-                         self.shared_intermediate, int(self.shared_gate), int(mode), 0)
+                         self.shared_intermediate, int(self.shared_gate), int(mode), int(self.activation))
 
 
 def router(cfg: MoeConfig, w: MoeWeights, x_bf16: np.ndarray, mode: int = 0):
@@ -259,3 +273,75 @@ def make_layer(cfg: MoeConfig, seed: int = 0, router_std: float = 0.02, expert_s
 def make_tokens(T: int, hidden: int, seed: int = 1) -> np.ndarray:
     """x ~ N(0, 1) as bf16 bits, [T, hidden]."""
     return f32_to_bf16(normal(seed * 64 + 63, (T, hidden), 1.0))
+
+
+def experts_forward(cfg: MoeConfig, w: MoeWeights, x_bf16: np.ndarray, ids: np.ndarray, weights: np.ndarray,
+                    mode: int = 0):
+    """Experts::forward (gemma4.rs:842-848): the experts of the given routing
+    ids / weights [T, K] and their f32 weighted sum (+ shared experts).
+    Returns (y_f32 [T, H], y_bf16 bits [T, H])."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16).reshape(-1, cfg.hidden)
+    T, H = x.shape[0], cfg.hidden
+    ids = np.ascontiguousarray(ids, dtype=np.int32).reshape(T, cfg.top_k)
+    weights = np.ascontiguousarray(weights, dtype=np.float32).reshape(T, cfg.top_k)
+    y = np.zeros((T, H), dtype=np.float32)
+    yb = np.zeros((T, H), dtype=np.uint16)
+    c, cw = cfg.to_c(mode), w.to_c()
+    _check(lib().orc_experts_forward(C.byref(c), C.byref(cw), _ptr(x), T, _ptr(ids), _ptr(weights), _ptr(y),
+                                     _ptr(yb)), "experts_forward")
+    return y, yb
+
+
+@dataclass
+class GemmaRouterConfig:
+    hidden: int
+    num_experts: int
+    top_k: int
+    group_size: int = 64
+    bits: int = 8
+    eps: float = 1e-6
+
+    def to_c(self) -> OrcGemmaRouterConfig:
+        return OrcGemmaRouterConfig(self.hidden, self.num_experts, self.top_k, self.group_size, self.bits,
+                                    float(self.eps))
+
+
+@dataclass
+class GemmaRouterWeights:
+    """Gemma Router parameters (gemma4.rs:683-700), numpy; bf16 as uint16 bits."""
+    proj_w: np.ndarray   # [E, H*bits/32] u32
+    proj_s: np.ndarray   # [E, H/group] bf16
+    proj_b: np.ndarray
+    scale: np.ndarray    # [H] bf16
+    per_expert_scale: np.ndarray  # [E] bf16
+
+    def to_c(self) -> OrcGemmaRouterWeights:
+        self._keep = [np.ascontiguousarray(v) for v in (self.proj_w, self.proj_s, self.proj_b, self.scale,
+                                                         self.per_expert_scale)]
+        return OrcGemmaRouterWeights(*[_ptr(v) for v in self._keep])
+
+
+def make_gemma_router(rc: GemmaRouterConfig, seed: int = 0) -> GemmaRouterWeights:
+    """Seeded synthetic router: projection N(0, 1) quantized at rc.bits (the norm
+    weight folds in H^-1/2, so logits come out ~N(0, 1)),
+    norm scale around 1, per-expert scales in (0.5, 1.5)."""
+    E, H = rc.num_experts, rc.hidden
+    sub = lambda k: seed * 64 + 40 + k
+    pw, ps, pb = quantize(normal(sub(0), (E, H), 1.0), rc.group_size, rc.bits)  # logits ~ N(0, 1)
+    scale = f32_to_bf16(1.0 + normal(sub(1), (H,), 0.2))
+    pes = f32_to_bf16(1.0 + 0.5 * np.tanh(normal(sub(2), (E,), 1.0)))
+    return GemmaRouterWeights(pw, ps, pb, scale, pes)
+
+
+def gemma_router(rc: GemmaRouterConfig, rw: GemmaRouterWeights, x_bf16: np.ndarray):
+    """Router::forward (gemma4.rs:716-736).  Returns (ids [T,K] int32,
+    weights [T,K] f32, scores [T,E] f32)."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16).reshape(-1, rc.hidden)
+    T = x.shape[0]
+    ids = np.empty((T, rc.top_k), dtype=np.int32)
+    wts = np.empty((T, rc.top_k), dtype=np.float32)
+    scores = np.empty((T, rc.num_experts), dtype=np.float32)
+    c, cw = rc.to_c(), rw.to_c()
+    _check(lib().orc_gemma_router(C.byref(c), C.byref(cw), _ptr(x), T, _ptr(ids), _ptr(wts), _ptr(scores)),
+           "gemma_router")
+    return ids, wts, scores

@@ -60,6 +60,24 @@ cudaError_t launch_router_tc(const CUtensorMap& tX, const CUtensorMap& tW, const
 cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st);
 bool router_supported(int hidden, int num_experts, int top_k);
 
+// Gemma-4 router (router_gemma.cu, gemma4.rs:716-736): rms_norm with weight
+// f32(scale) * root (root = H^-1/2), the affine-quantized projection, top-k,
+// softmax over the k, * per_expert_scale.  One CTA per token.
+struct GemmaRouterArgs {
+  const uint16_t* x;                 // bf16 [T, H]
+  const uint32_t* proj_w;            // [E, H * bits / 32]
+  const uint16_t* proj_s;            // bf16 [E, H / group]
+  const uint16_t* proj_b;
+  const uint16_t* scale;             // bf16 [H]
+  const uint16_t* per_expert_scale;  // bf16 [E]
+  int32_t* topk_ids;                 // [T, K]
+  float* topk_weights;               // [T, K]
+  int num_tokens, hidden, num_experts, top_k, bits, group_size;
+  float eps, root;
+};
+bool gemma_router_supported(int hidden, int num_experts, int top_k, int bits, int group_size);
+cudaError_t launch_gemma_router(const GemmaRouterArgs& a, cudaStream_t st);
+
 constexpr int kDispatchChunk = 1024;
 cudaError_t launch_dispatch(const DispatchArgs& a, cudaStream_t st);
 size_t dispatch_smem_bytes(int num_experts);
@@ -135,7 +153,9 @@ cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
 // x_sorted[s, :] = fp16(x[perm[s] / k_div, :]) for s < num_slots (x bf16, rows of
 // `hidden`); a value outside fp16 range records kDevFp16Range in *err.
 // With `offsets` non-null only the slots of experts [eb, ee), i.e. slots
-// offsets[eb] .. offsets[ee], are gathered.  `order` selects the k order of
+// offsets[eb] .. offsets[ee], are gathered (the layer always passes them:
+// slots past offsets[E] hold no placed pair when the dispatch rejected an
+// out-of-range expert id).  `order` selects the k order of
 // the consuming kernel: kOrderTc (tcgen05, kperm8), kOrderMma (warp-MMA
 // dequantising form, kperm256, 256-column stages; hidden % 256 == 0) or
 // kOrderMmaG4 (warp-MMA group-scaled form, kperm_g4 with odd columns / 16;

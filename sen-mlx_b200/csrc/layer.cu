@@ -187,8 +187,11 @@ static int validate_config(const SenMoeConfig* c) {
 
 static int validate_weights(const SenMoeConfig* c, const SenMoeWeights* w) {
   if (!w) return fail(SENMOE_ERR_BAD_ARG, "weights is NULL");
-  const void* req[] = {w->router_weight, w->gate_weight, w->gate_scales, w->gate_biases, w->up_weight,
-                       w->up_scales,     w->up_biases,   w->down_weight, w->down_scales, w->down_biases};
+  // router_weight may be NULL (a layer used only through senmoe_layer_experts_forward)
+  if (w->router_weight && !aligned16(w->router_weight))
+    return fail(SENMOE_ERR_BAD_ARG, "router_weight %p is not 16-byte aligned", w->router_weight);
+  const void* req[] = {w->gate_weight, w->gate_scales, w->gate_biases, w->up_weight, w->up_scales,
+                       w->up_biases,   w->down_weight, w->down_scales, w->down_biases};
   for (const void* p : req) {
     if (!p) return fail(SENMOE_ERR_BAD_ARG, "a required weight pointer is NULL");
     if (!aligned16(p)) return fail(SENMOE_ERR_BAD_ARG, "weight pointer %p is not 16-byte aligned", p);
@@ -328,7 +331,7 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                make_tmap_2d(&L->tm_down64, L->w.down_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, dw, uint64_t(El) * H,
                             dw * 4, 32, 64, true) == cudaSuccess;
   }
-  L->rtc_ok = router_tc_supported(int(H), int(E), int(K)) && E >= 128 &&
+  L->rtc_ok = L->w.router_weight && router_tc_supported(int(H), int(E), int(K)) && E >= 128 &&
               make_tmap_2d(&L->tm_router, L->w.router_weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, E, H * 2, 64, 128,
                            true) == cudaSuccess;
   e = cudaMemset(L->arena, 0, off);
@@ -384,8 +387,11 @@ static int expert_path_for(const SenMoeLayer* L, int64_t pairs) {
   return kPathGemv;
 }
 
+// ext_ids / ext_w: routing [T, K] from the caller (Experts::forward), or
+// null to run the layer's router.
 static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void* y, const SenMoeDebug* debug,
-                         bool residual, senmoe_stream_t stream) {
+                         bool residual, senmoe_stream_t stream, const int32_t* ext_ids = nullptr,
+                         const float* ext_w = nullptr) {
   g_last_error.clear();
   if (!L) return fail(SENMOE_ERR_BAD_ARG, "layer is NULL");
   const SenMoeConfig& c = L->cfg;
@@ -394,7 +400,11 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   if (num_tokens == 0) return SENMOE_OK;
   if (!x || !y) return fail(SENMOE_ERR_BAD_ARG, "x or y is NULL");
   if (!aligned16(x) || !aligned16(y)) return fail(SENMOE_ERR_BAD_ARG, "x and y must be 16-byte aligned");
+  if (!ext_ids && !L->w.router_weight)
+    return fail(SENMOE_ERR_BAD_ARG, "the layer has no router weight: use senmoe_layer_experts_forward");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int32_t* const ids = ext_ids ? const_cast<int32_t*>(ext_ids) : L->ids;   // read-only when given
+  float* const wts = ext_w ? const_cast<float*>(ext_w) : L->wts;
   const int T = static_cast<int>(num_tokens), K = c.num_experts_per_tok, E = c.n_routed_experts;
   const int H = c.hidden_size, I = c.moe_intermediate_size, Is = c.shared_intermediate;
   const int P = T * K;
@@ -427,7 +437,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
 
   // 2. dispatch
   DispatchArgs da{};
-  da.topk_ids = L->ids;
+  da.topk_ids = ids;
   da.num_pairs = P;
   da.num_experts = E;
   da.expert_begin = c.expert_begin;
@@ -441,7 +451,10 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   da.err = L->err;
   const bool ep = L->ep_world > 0;
   da.keep_remote_slots = ep ? 1 : 0;  // the combine reads remote slots from their owners
-  if (L->rtc_ok && T >= kRouterTcMinTokens) {
+  if (ext_ids) {
+    SENMOE_CUDA(mark(1));  // routing given by the caller
+    SENMOE_CUDA(launch_dispatch(da, st));
+  } else if (L->rtc_ok && T >= kRouterTcMinTokens) {
     // prefill sizes: logits on the tensor cores and top-k in one launch
     CUtensorMap tm_x;
     SENMOE_CUDA(make_tmap_2d(&tm_x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, T, uint64_t(H) * 2, 64, 32, true));
@@ -473,7 +486,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     ea.flags = L->ep_flags;
     ea.epoch = L->ep_local;
     ea.finished = L->ep_local + 1;
-    ea.topk_ids = L->ids;
+    ea.topk_ids = ids;
     ea.err = L->err;
     // d is about to be overwritten: wait until the peers have read the last call's rows
     SENMOE_CUDA(launch_ep_fence(ea, st));
@@ -515,7 +528,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
                     (c.reserved[1] == kMmaFormG4Single || (c.reserved[1] == kMmaFormAuto && nt == 1));
     const bool q4 = g4 && nt == 1 && L->q4_ok && c.reserved[1] == kMmaFormAuto && max_items * (I / 128) < L->sms;
     SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
-                                   ep ? L->offsets : nullptr, c.expert_begin, c.expert_end,
+                                   L->offsets, c.expert_begin, c.expert_end,
                                    g4 ? kOrderMmaG4 : kOrderMma));
     SENMOE_CUDA(mark(2));
     if (q4) {
@@ -548,7 +561,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   } else if (path == kPathTensorCore) {
     const int ti = tc_tile_index(per_expert), bn = kTcTiles[ti];
     SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
-                                   ep ? L->offsets : nullptr, c.expert_begin, c.expert_end));
+                                   L->offsets, c.expert_begin, c.expert_end));
     SENMOE_CUDA(mark(2));
     TcGemmArgs ga{};
     ga.s[0] = static_cast<const uint16_t*>(L->w.gate_scales);
@@ -676,7 +689,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   CombineArgs ca{};
   ca.d = L->d;
   ca.inverse = L->inv;
-  ca.weights = L->wts;
+  ca.weights = wts;
   ca.shared_out = Is > 0 ? L->sh_out : nullptr;
   ca.shared_gate = (Is > 0 && c.shared_gate) ? L->sh_gate : nullptr;
   ca.y = static_cast<uint16_t*>(y);
@@ -693,9 +706,9 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
 
   if (debug) {
     if (debug->topk_ids)
-      SENMOE_CUDA(cudaMemcpyAsync(debug->topk_ids, L->ids, size_t(P) * 4, cudaMemcpyDeviceToDevice, st));
+      SENMOE_CUDA(cudaMemcpyAsync(debug->topk_ids, ids, size_t(P) * 4, cudaMemcpyDeviceToDevice, st));
     if (debug->topk_weights)
-      SENMOE_CUDA(cudaMemcpyAsync(debug->topk_weights, L->wts, size_t(P) * 4, cudaMemcpyDeviceToDevice, st));
+      SENMOE_CUDA(cudaMemcpyAsync(debug->topk_weights, wts, size_t(P) * 4, cudaMemcpyDeviceToDevice, st));
     if (debug->perm) SENMOE_CUDA(cudaMemcpyAsync(debug->perm, L->perm, size_t(P) * 4, cudaMemcpyDeviceToDevice, st));
     if (debug->offsets)
       SENMOE_CUDA(cudaMemcpyAsync(debug->offsets, L->offsets, size_t(E + 1) * 4, cudaMemcpyDeviceToDevice, st));
@@ -876,6 +889,47 @@ int senmoe_router(const void* x, int64_t num_tokens, const void* router_weight, 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   SENMOE_CUDA(launch_router_logits(ra, st));
   SENMOE_CUDA(launch_router_topk(ra, st));
+  return SENMOE_OK;
+}
+
+int senmoe_layer_experts_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, const int32_t* topk_ids,
+                                 const float* topk_weights, void* y, senmoe_stream_t stream) {
+  g_last_error.clear();
+  if (num_tokens > 0 && (!topk_ids || !topk_weights)) return fail(SENMOE_ERR_BAD_ARG, "topk_ids / topk_weights NULL");
+  return layer_forward(L, x, num_tokens, y, nullptr, false, stream, topk_ids, topk_weights);
+}
+
+int senmoe_gemma_router(const SenMoeGemmaRouter* r, const void* x, int64_t num_tokens, int32_t* topk_ids,
+                        float* topk_weights, senmoe_stream_t stream) {
+  g_last_error.clear();
+  if (!r) return fail(SENMOE_ERR_BAD_ARG, "router is NULL");
+  if (num_tokens < 0 || num_tokens > (1ll << 28)) return fail(SENMOE_ERR_BAD_ARG, "num_tokens=%lld", (long long)num_tokens);
+  if (!gemma_router_supported(r->hidden_size, r->num_experts, r->top_k, r->bits, r->group_size))
+    return fail(SENMOE_ERR_UNSUPPORTED, "gemma router: H=%d E=%d K=%d bits=%d group=%d unsupported", r->hidden_size,
+                r->num_experts, r->top_k, r->bits, r->group_size);
+  if (!(r->rms_norm_eps >= 0.0f)) return fail(SENMOE_ERR_BAD_ARG, "rms_norm_eps must be >= 0");
+  if (num_tokens == 0) return SENMOE_OK;
+  if (!x || !r->proj_weight || !r->proj_scales || !r->proj_biases || !r->scale || !r->per_expert_scale ||
+      !topk_ids || !topk_weights)
+    return fail(SENMOE_ERR_BAD_ARG, "NULL pointer");
+  GemmaRouterArgs a{};
+  a.x = static_cast<const uint16_t*>(x);
+  a.proj_w = r->proj_weight;
+  a.proj_s = static_cast<const uint16_t*>(r->proj_scales);
+  a.proj_b = static_cast<const uint16_t*>(r->proj_biases);
+  a.scale = static_cast<const uint16_t*>(r->scale);
+  a.per_expert_scale = static_cast<const uint16_t*>(r->per_expert_scale);
+  a.topk_ids = topk_ids;
+  a.topk_weights = topk_weights;
+  a.num_tokens = static_cast<int>(num_tokens);
+  a.hidden = r->hidden_size;
+  a.num_experts = r->num_experts;
+  a.top_k = r->top_k;
+  a.bits = r->bits;
+  a.group_size = r->group_size;
+  a.eps = r->rms_norm_eps;
+  a.root = powf(static_cast<float>(r->hidden_size), -0.5f);  // (hidden_size as f32).powf(-0.5), gemma4.rs:705
+  SENMOE_CUDA(launch_gemma_router(a, reinterpret_cast<cudaStream_t>(stream)));
   return SENMOE_OK;
 }
 

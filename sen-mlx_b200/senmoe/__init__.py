@@ -66,6 +66,13 @@ class SenMoeWeights(C.Structure):
     _fields_ = [(n, _P) for n in WEIGHT_FIELDS]
 
 
+class SenMoeGemmaRouter(C.Structure):
+    _fields_ = [("hidden_size", C.c_int32), ("num_experts", C.c_int32), ("top_k", C.c_int32),
+                ("bits", C.c_int32), ("group_size", C.c_int32), ("rms_norm_eps", C.c_float),
+                ("proj_weight", C.c_void_p), ("proj_scales", C.c_void_p), ("proj_biases", C.c_void_p),
+                ("scale", C.c_void_p), ("per_expert_scale", C.c_void_p)]
+
+
 class SenMoeDebug(C.Structure):
     _fields_ = [("topk_ids", _P), ("topk_weights", _P), ("perm", _P), ("offsets", _P)]
 
@@ -99,6 +106,8 @@ SIGNATURES = {
     "senmoe_gather_qmm": (C.c_int, [_P, _i64, _P, _P, _P, _P, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _P,
                                     _P]),
     "senmoe_moe_forward_noalloc": (C.c_int, [C.POINTER(SenMoeConfig), C.POINTER(SenMoeWeights), _P, _i64, _P, _P]),
+    "senmoe_gemma_router": (C.c_int, [C.c_void_p, _P, _i64, _P, _P, _P]),
+    "senmoe_layer_experts_forward": (C.c_int, [_P, _P, _i64, _P, _P, _P, _P]),
 }
 
 _lib = None
@@ -206,7 +215,7 @@ class SwitchLinear:
 
 @dataclass
 class MoeWeights:
-    router_weight: torch.Tensor  # bf16 [E, H]
+    router_weight: torch.Tensor | None  # bf16 [E, H]; None: experts_forward only
     gate_proj: SwitchLinear
     up_proj: SwitchLinear
     down_proj: SwitchLinear
@@ -289,6 +298,26 @@ class DeepseekMoe:
 
     __call__ = forward
 
+    def experts_forward(self, x: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor, stream=None,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+        """Experts::forward(x, indices, weights) (gemma4.rs:842-848): the layer's
+        experts over routing from the caller (e.g. GemmaRouter.forward), their
+        weighted sum in fp32, bf16 out.  x [..., H] bf16, indices int32 /
+        weights fp32 [..., K] on the device."""
+        H, K = self.args.hidden_size, self.args.num_experts_per_tok
+        if x.dtype != torch.bfloat16 or not x.is_cuda or x.shape[-1] != H:
+            raise TypeError("x must be a CUDA bfloat16 tensor [..., hidden_size]")
+        xc = x.contiguous()
+        T = xc.numel() // H
+        ids = indices.to(torch.int32).contiguous()
+        w = weights.to(torch.float32).contiguous()
+        if ids.numel() != T * K or w.numel() != T * K:
+            raise SenMoeError(ERR_BAD_ARG, f"indices / weights must hold {T} x {K} entries")
+        y = torch.empty_like(xc) if out is None else out
+        _check(lib().senmoe_layer_experts_forward(self._handle, _ptr(xc), T, _ptr(ids), _ptr(w), _ptr(y),
+                                                  _stream(stream)))
+        return y
+
     def forward_residual(self, x: torch.Tensor, stream=None, out: torch.Tensor | None = None) -> torch.Tensor:
         """h = x + forward(x): DecoderLayer::forward's residual add (deepseek_v2.rs:619) fused in."""
         if x.dtype != torch.bfloat16 or not x.is_cuda or x.shape[-1] != self.args.hidden_size:
@@ -367,6 +396,47 @@ def router(x: torch.Tensor, router_weight: torch.Tensor, top_k: int, norm_topk_p
     _check(lib().senmoe_router(_ptr(xc), T, _ptr(router_weight.contiguous()), H, E, top_k, int(norm_topk_prob),
                                float(routed_scaling_factor), _ptr(logits), _ptr(ids), _ptr(wts), _stream(stream)))
     return ids, wts
+
+
+@dataclass
+class GemmaRouterWeights:
+    """gemma4::Router parameters (gemma4.rs:683-700): the quantized ``proj``
+    ([E, H*bits/32] u32, bf16 scales / biases [E, H/group]), the norm
+    ``scale`` [H] and ``per_expert_scale`` [E], both bf16."""
+    proj: SwitchLinear
+    scale: torch.Tensor
+    per_expert_scale: torch.Tensor
+
+
+class GemmaRouter:
+    """gemma4::Router::forward (gemma4.rs:716-736) on the GPU: rms_norm with
+    weight scale * H^-1/2, quantized projection, top-k, softmax over the k,
+    * per_expert_scale.  Borrows the weight tensors."""
+
+    def __init__(self, hidden_size: int, num_experts: int, top_k: int, weights: GemmaRouterWeights,
+                 rms_norm_eps: float = 1e-6, bits: int = 8, group_size: int = 64):
+        self.top_k, self.weights = top_k, weights
+        r = SenMoeGemmaRouter()
+        r.hidden_size, r.num_experts, r.top_k, r.bits, r.group_size = hidden_size, num_experts, top_k, bits, group_size
+        r.rms_norm_eps = float(rms_norm_eps)
+        self._w32 = _u32(weights.proj.weight)
+        r.proj_weight, r.proj_scales, r.proj_biases = _ptr(self._w32), _ptr(weights.proj.scales), _ptr(weights.proj.biases)
+        r.scale, r.per_expert_scale = _ptr(weights.scale), _ptr(weights.per_expert_scale)
+        self._r = r
+
+    def forward(self, x: torch.Tensor, stream=None):
+        """x [..., H] bf16 -> (indices int32 [..., K], weights fp32 [..., K])."""
+        H = self._r.hidden_size
+        if x.dtype != torch.bfloat16 or not x.is_cuda or x.shape[-1] != H:
+            raise TypeError("x must be a CUDA bfloat16 tensor [..., hidden_size]")
+        xc = x.contiguous()
+        T = xc.numel() // H
+        ids = torch.empty((*x.shape[:-1], self.top_k), dtype=torch.int32, device=x.device)
+        w = torch.empty((*x.shape[:-1], self.top_k), dtype=torch.float32, device=x.device)
+        _check(lib().senmoe_gemma_router(C.byref(self._r), _ptr(xc), T, _ptr(ids), _ptr(w), _stream(stream)))
+        return ids, w
+
+    __call__ = forward
 
 
 def dispatch(topk_ids: torch.Tensor, num_experts: int, stream=None):

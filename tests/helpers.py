@@ -41,7 +41,7 @@ def device_weights(mw, device="cuda"):
     import senmoe
     sl = lambda w, s, b: senmoe.SwitchLinear(t_u32(w, device), t_bf16(s, device), t_bf16(b, device))
     out = senmoe.MoeWeights(
-        router_weight=t_bf16(mw.router_w, device),
+        router_weight=None if mw.router_w is None else t_bf16(mw.router_w, device),
         gate_proj=sl(mw.gate_w, mw.gate_s, mw.gate_b),
         up_proj=sl(mw.up_w, mw.up_s, mw.up_b),
         down_proj=sl(mw.down_w, mw.down_s, mw.down_b),
@@ -62,7 +62,8 @@ def moe_args(cfg, expert_path=0):
                           n_routed_experts=cfg.num_experts, num_experts_per_tok=cfg.top_k,
                           n_shared_experts=(cfg.shared_intermediate // cfg.intermediate) if cfg.shared_intermediate else 0,
                           norm_topk_prob=cfg.norm_topk_prob, routed_scaling_factor=cfg.routed_scaling_factor,
-                          bits=cfg.bits, group_size=cfg.group_size, shared_gate=cfg.shared_gate)
+                          bits=cfg.bits, group_size=cfg.group_size, shared_gate=cfg.shared_gate,
+                          activation=getattr(cfg, "activation", 0))
 
 
 def topk_match_except_ties(ids_gpu, ids_ref, scores_ref, ulp_rel=2.0 ** -7):
