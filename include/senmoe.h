@@ -9,6 +9,8 @@
  * Reference interfaces replaced (paths inside the sen-mlx project):
  *   senmoe_gather_qmm       <- gather_qmm / mlx_sys::mlx_gather_qmm
  *                              src/engine/mlx_lm/utils/moe.rs:33-77
+ *   senmoe_quantized_linear <- nn::QuantizedLinear::forward (the quantized projections
+ *                              next to the block, deepseek_v2.rs:190-205, 367-394)
  *   senmoe_layer_create     <- DeepseekMoe::new + SwitchGlu/SwitchLinear weight slots
  *                              src/engine/mlx_lm/models/deepseek_v2.rs:400-428, 485-518
  *   senmoe_layer_forward    <- DeepseekMoe::forward(&mut self, x: &Array) -> Result<Array>
@@ -274,6 +276,17 @@ int senmoe_gather_qmm(const void* x, int64_t x_rows, const uint32_t* w, const vo
                       const uint32_t* rhs_indices, int64_t n_indices, int64_t in_features, int64_t out_features,
                       int32_t num_experts, int32_t transpose, int32_t group_size, int32_t bits,
                       int32_t sorted_indices, void* out, senmoe_stream_t stream);
+
+/* The dense quantized Linear next to the block (nn::QuantizedLinear without
+ * bias, as DeepSeek builds its projections: deepseek_v2.rs:213, :382; the
+ * step either side of the MoE block in decode):
+ *   y[t, :] = bf16( x[t, :] @ dequant(w)^T )
+ * x bf16 [T, in_features]; w u32 [out_features, in*bits/32]; scales/biases
+ * bf16 [out_features, in/group]; y bf16 [T, out_features].  Same arithmetic
+ * as senmoe_gather_qmm (one expert). */
+int senmoe_quantized_linear(const void* x, int64_t num_tokens, const uint32_t* w, const void* scales,
+                            const void* biases, int64_t in_features, int64_t out_features, int32_t group_size,
+                            int32_t bits, void* y, senmoe_stream_t stream);
 
 /* Allocation-free forward (no counterpart in the reference; this build adds
  * it for callers that cannot allocate device memory at call time: code inside

@@ -145,8 +145,8 @@ __global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(QGemvArgs a) {
     s_begin = a.offsets[expert];
     s_end = a.offsets[expert + 1];
     expert -= a.expert_begin;
-  } else {  // kItemsGather: one index per CTA row
-    const uint32_t e = a.gather_idx[blockIdx.x];
+  } else {  // kItemsGather: one index per CTA row (no index list: expert 0, a dense linear)
+    const uint32_t e = a.gather_idx ? a.gather_idx[blockIdx.x] : 0u;
     if (e >= static_cast<uint32_t>(a.num_experts)) {
       if (threadIdx.x == 0) record_error(a.err, kDevBadExpert);
       return;

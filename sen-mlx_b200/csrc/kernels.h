@@ -100,6 +100,7 @@ struct QGemvArgs {
   int x_by_slot;            // 1: x row of slot s is s itself (the down projection)
   int expert_begin;
   // gather items: CTA x-index i serves index i, token i / rep, expert gather_idx[i]
+  // (gather_idx null: expert 0 for every index)
   const uint32_t* gather_idx;
   long long rep;
   int num_experts;

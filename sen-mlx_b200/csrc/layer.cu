@@ -957,36 +957,35 @@ int senmoe_dispatch(const int32_t* topk_ids, int64_t num_tokens, int32_t top_k, 
   return SENMOE_OK;
 }
 
-int senmoe_gather_qmm(const void* x, int64_t x_rows, const uint32_t* w, const void* scales, const void* biases,
-                      const uint32_t* rhs_indices, int64_t n_indices, int64_t in_features, int64_t out_features,
-                      int32_t num_experts, int32_t transpose, int32_t group_size, int32_t bits,
-                      int32_t sorted_indices, void* out, senmoe_stream_t stream) {
-  (void)sorted_indices;
-  g_last_error.clear();
-  if (!transpose)
-    return fail(SENMOE_ERR_UNSUPPORTED, "gather_qmm: transpose=false is not supported (the reference only uses "
-                                        "transpose=true)");
-  if (bits != 4 && bits != 8) return fail(SENMOE_ERR_UNSUPPORTED, "gather_qmm: bits=%d", bits);
-  if (group_size != 64) return fail(SENMOE_ERR_UNSUPPORTED, "gather_qmm: group_size=%d", group_size);
+// The quantized product behind gather_qmm and the dense quantized Linear:
+// out[i, :] = bf16( x[i / (n_indices / x_rows), :] @ dequant(w[idx[i]])^T ),
+// idx null = expert 0 for every row (the dense form, num_experts == 1);
+// need_idx: the caller's form requires an index list.
+static int quantized_product(const char* who, const void* x, int64_t x_rows, const uint32_t* w, const void* scales,
+                             const void* biases, const uint32_t* idx, bool need_idx, int64_t n_indices,
+                             int64_t in_features, int64_t out_features, int32_t num_experts, int32_t group_size,
+                             int32_t bits, void* out, senmoe_stream_t stream) {
+  if (bits != 4 && bits != 8) return fail(SENMOE_ERR_UNSUPPORTED, "%s: bits=%d", who, bits);
+  if (group_size != 64) return fail(SENMOE_ERR_UNSUPPORTED, "%s: group_size=%d", who, group_size);
   if (x_rows <= 0 || n_indices < 0 || n_indices % x_rows || num_experts <= 0 || out_features <= 0 ||
       n_indices > (1ll << 31) - 1)
-    return fail(SENMOE_ERR_BAD_ARG, "gather_qmm: x_rows=%lld n_indices=%lld (must be a multiple)", (long long)x_rows,
+    return fail(SENMOE_ERR_BAD_ARG, "%s: x_rows=%lld n_indices=%lld (must be a multiple)", who, (long long)x_rows,
                 (long long)n_indices);
   if (in_features <= 0 || in_features > (1 << 20) || !qgemv_supported(static_cast<int>(in_features), bits))
-    return fail(SENMOE_ERR_UNSUPPORTED, "gather_qmm: in_features=%lld unsupported at %d bits",
+    return fail(SENMOE_ERR_UNSUPPORTED, "%s: in_features=%lld unsupported at %d bits", who,
                 (long long)in_features, bits);
   if (n_indices == 0) return SENMOE_OK;
-  if (!x || !w || !scales || !biases || !rhs_indices || !out) return fail(SENMOE_ERR_BAD_ARG, "NULL pointer");
+  if (!x || !w || !scales || !biases || !out || (need_idx && !idx)) return fail(SENMOE_ERR_BAD_ARG, "NULL pointer");
   if (!aligned16(x) || !aligned16(w) || !aligned16(scales) || !aligned16(biases))
-    return fail(SENMOE_ERR_BAD_ARG, "gather_qmm: x / w / scales / biases must be 16-byte aligned");
+    return fail(SENMOE_ERR_BAD_ARG, "%s: x / w / scales / biases must be 16-byte aligned", who);
   // Bulk copies move [rows_per_cta, groups] scale blocks: every block start
   // and size must be a 16-byte multiple.
   const int groups = static_cast<int>(in_features / 64);
   int rows_per_cta = 16;
   while ((rows_per_cta * groups * 2) % 16) rows_per_cta *= 2;
   if ((out_features * groups * 2) % 16 || ((out_features % rows_per_cta) * groups * 2) % 16)
-    return fail(SENMOE_ERR_UNSUPPORTED, "gather_qmm: out_features=%lld with in_features=%lld leaves scale rows "
-                "that are not 16-byte multiples", (long long)out_features, (long long)in_features);
+    return fail(SENMOE_ERR_UNSUPPORTED, "%s: out_features=%lld with in_features=%lld leaves scale rows that are "
+                "not 16-byte multiples", who, (long long)out_features, (long long)in_features);
   QGemvArgs g{};
   g.x = static_cast<const uint16_t*>(x);
   g.w[0] = w;
@@ -996,7 +995,7 @@ int senmoe_gather_qmm(const void* x, int64_t x_rows, const uint32_t* w, const vo
   g.rows = static_cast<int>(out_features);
   g.rows_per_cta = rows_per_cta;
   g.mode = kItemsGather;
-  g.gather_idx = rhs_indices;
+  g.gather_idx = idx;
   g.rep = n_indices / x_rows;
   g.num_experts = num_experts;
   g.out = static_cast<uint16_t*>(out);
@@ -1005,6 +1004,29 @@ int senmoe_gather_qmm(const void* x, int64_t x_rows, const uint32_t* w, const vo
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   SENMOE_CUDA(launch_qgemv(g, 1, bits, static_cast<int>(n_indices), st));
   return SENMOE_OK;
+}
+
+int senmoe_gather_qmm(const void* x, int64_t x_rows, const uint32_t* w, const void* scales, const void* biases,
+                      const uint32_t* rhs_indices, int64_t n_indices, int64_t in_features, int64_t out_features,
+                      int32_t num_experts, int32_t transpose, int32_t group_size, int32_t bits,
+                      int32_t sorted_indices, void* out, senmoe_stream_t stream) {
+  (void)sorted_indices;
+  g_last_error.clear();
+  if (!transpose)
+    return fail(SENMOE_ERR_UNSUPPORTED, "gather_qmm: transpose=false is not supported (the reference only uses "
+                                        "transpose=true)");
+  return quantized_product("gather_qmm", x, x_rows, w, scales, biases, rhs_indices, true, n_indices, in_features,
+                           out_features, num_experts, group_size, bits, out, stream);
+}
+
+int senmoe_quantized_linear(const void* x, int64_t num_tokens, const uint32_t* w, const void* scales,
+                            const void* biases, int64_t in_features, int64_t out_features, int32_t group_size,
+                            int32_t bits, void* y, senmoe_stream_t stream) {
+  g_last_error.clear();
+  if (num_tokens < 0) return fail(SENMOE_ERR_BAD_ARG, "quantized_linear: num_tokens=%lld", (long long)num_tokens);
+  if (num_tokens == 0) return SENMOE_OK;
+  return quantized_product("quantized_linear", x, num_tokens, w, scales, biases, nullptr, false, num_tokens,
+                           in_features, out_features, 1, group_size, bits, y, stream);
 }
 
 }  // extern "C"

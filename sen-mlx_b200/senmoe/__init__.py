@@ -107,6 +107,7 @@ SIGNATURES = {
                                     _P]),
     "senmoe_moe_forward_noalloc": (C.c_int, [C.POINTER(SenMoeConfig), C.POINTER(SenMoeWeights), _P, _i64, _P, _P]),
     "senmoe_gemma_router": (C.c_int, [C.c_void_p, _P, _i64, _P, _P, _P]),
+    "senmoe_quantized_linear": (C.c_int, [_P, _i64, _P, _P, _P, _i64, _i64, C.c_int32, C.c_int32, _P, _P]),
     "senmoe_layer_experts_forward": (C.c_int, [_P, _P, _i64, _P, _P, _P, _P]),
 }
 
@@ -396,6 +397,22 @@ def router(x: torch.Tensor, router_weight: torch.Tensor, top_k: int, norm_topk_p
     _check(lib().senmoe_router(_ptr(xc), T, _ptr(router_weight.contiguous()), H, E, top_k, int(norm_topk_prob),
                                float(routed_scaling_factor), _ptr(logits), _ptr(ids), _ptr(wts), _stream(stream)))
     return ids, wts
+
+
+def quantized_linear(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                     group_size: int = 64, bits: int = 4, stream=None) -> torch.Tensor:
+    """nn::QuantizedLinear::forward without bias: x [..., in] bf16 @
+    dequant(w [out, in*bits/32])^T -> [..., out] bf16."""
+    if x.dtype != torch.bfloat16 or not x.is_cuda:
+        raise TypeError("x must be a CUDA bfloat16 tensor")
+    out_f, in_f = w.shape[0], x.shape[-1]
+    xc = x.contiguous()
+    T = xc.numel() // in_f
+    y = torch.empty((*x.shape[:-1], out_f), dtype=torch.bfloat16, device=x.device)
+    _check(lib().senmoe_quantized_linear(_ptr(xc), T, _ptr(_u32(w)), _ptr(scales.contiguous()),
+                                         _ptr(biases.contiguous()), in_f, out_f, group_size, bits, _ptr(y),
+                                         _stream(stream)))
+    return y
 
 
 @dataclass

@@ -147,3 +147,17 @@ def test_gather_qmm_skips_bad_index_without_fault(senmoe, torch_cuda):
     y = senmoe.gather_qmm(x, t_u32(wq), t_bf16(s), t_bf16(b), idx)  # expert 5 of 2: skipped, no fault
     torch.cuda.synchronize()
     assert y.shape == (1, 2, 1, 32)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("T,in_f,out_f", [(1, 2048, 3072), (16, 2048, 512), (5, 768, 2048)])
+def test_quantized_linear_vs_oracle(senmoe, torch_cuda, bits, T, in_f, out_f):
+    """nn::QuantizedLinear without bias (the projections beside the block,
+    deepseek_v2.rs:213, :382): the oracle's gather_qmm with one expert."""
+    wq, s, b = O.quantize(O.normal(in_f + out_f + bits, (1, out_f, in_f), 0.02), 64, bits)
+    x = O.make_tokens(T, in_f, seed=T + bits)
+    ref = bf16_np_to_f32(O.gather_qmm(x, wq, s, b, np.zeros((T, 1), np.int32), 64, bits)).reshape(T, out_f)
+    y = senmoe.quantized_linear(t_bf16(x), t_u32(wq[0]), t_bf16(s[0]), t_bf16(b[0]), 64, bits)
+    assert y.shape == (T, out_f)
+    got = bf16_np_to_f32(to_numpy_bf16(y))
+    assert np.all(np.abs(got - ref) <= 2.0 ** -7 * np.abs(ref) + 1e-5)
