@@ -13,9 +13,12 @@ L2, so every step streams them from HBM (no L2 flush needed).
 
 On N GPUs (torchrun, one rank per GPU) the same 48-layer stack runs expert
 parallel: rank r holds experts [r*128/N, (r+1)*128/N) of every layer, every
-rank takes the same batch, and each layer's combine reads the other ranks'
-expert rows over NVLink (senmoe.ep).  Total work per step is fixed as N grows
-(strong scaling); `value` is the batch's tokens/s.
+rank takes the whole batch and routes it, runs its experts' pairs, combines
+the batch's r-th block of tokens reading the other ranks' expert rows over
+NVLink, and sends the combined rows to every peer (senmoe.ep).  By default
+the batch is 64 tokens per GPU, 64*N in all (weak scaling: each GPU's share
+of the expert pairs and of the combine stays fixed as N grows); `value` is
+the whole batch's tokens/s.  `--scaling strong` keeps the batch at 64 in all.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl senmoe|reference]
 
@@ -180,11 +183,11 @@ def launches_per_forward(T, tensor_cores, world):
     """Kernels one forward launches: the router (one kernel from 128 tokens,
     where top-k runs in the logits kernel's last CTAs or the tensor-core
     router; logits + top-k below), dispatch (one kernel up to 2048 pairs,
-    else three), the expert-parallel fence, the gathered-activation copy
-    (tensor-core paths), gate/up, down, combine."""
+    else three), the expert-parallel fence and row gather, the
+    gathered-activation copy (tensor-core paths), gate/up, down, combine."""
     router = 1 if T >= 128 else 2
     disp = 1 if (T * K + 1023) // 1024 <= 2 else 3
-    return router + disp + (1 if world > 1 else 0) + (1 if tensor_cores else 0) + 3
+    return router + disp + (2 if world > 1 else 0) + (1 if tensor_cores else 0) + 3
 
 
 # --------------------------------------------------------- CPU baseline
@@ -215,6 +218,8 @@ def run_reference(args):
         return
     from oracle import oracle as O
     O.build()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    args.batch *= world if args.scaling == "weak" else 1  # the GPU arm's whole batch
     cfg = O.MoeConfig(hidden=H, intermediate=I, num_experts=E, top_k=K, bits=BITS, group_size=G)
     mw = O.make_layer(cfg, seed=0, router_std=1.0 / math.sqrt(H))
     x = O.make_tokens(args.batch, H, seed=1)
@@ -226,7 +231,8 @@ def run_reference(args):
     dt = (time.perf_counter() - t0) / args.steps  # one layer per step
     value = args.batch / (dt * LAYERS)
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": dt * LAYERS * 1e3, "higher_is_better": True, "scaling": "strong",
+            "warmup": args.warmup, "ms_per_step": dt * LAYERS * 1e3, "higher_is_better": True,
+            "scaling": args.scaling,
             "vs_baseline": None, "dtype": "u4/bf16 (fp32 accumulate)", "data": "synthetic",
             "impl": "reference",
             "config": {"workload": WORKLOAD, "global_batch": args.batch, "layers": LAYERS},
@@ -255,7 +261,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="senmoe", choices=["senmoe", "reference"])
-    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--batch", type=int, default=64, help="decode batch per GPU (weak) or in all (strong)")
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="N > 1: batch per GPU fixed (weak) or total batch fixed (strong)")
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -312,7 +320,10 @@ def main():
         torch.cuda.synchronize()
         return
 
-    batches = [args.batch] if args.no_sweep else sorted({1, 8, 32, args.batch})
+    scale = world if args.scaling == "weak" else 1
+    per_gpu = args.batch
+    args.batch = per_gpu * scale  # the whole batch of a step
+    batches = [args.batch] if args.no_sweep else sorted({b * scale for b in (1, 8, 32, per_gpu)})
     tmax = max(batches)
     layers, _keep = make_stack(torch, senmoe, local, args.layers, tmax, rank=rank, world=world)
     stack = senmoe.MoeStack(layers, tmax, use_graph=True)
@@ -461,10 +472,12 @@ def main():
     head = results[args.batch]
     line = {
         "metric": METRIC, "value": head["tokens_per_s"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+        "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "u4 weights / bf16 activations (fp32 accumulate)",
         "data": "synthetic (random-init 4-bit MLX-layout weights, x ~ N(0,1))",
-        "config": {"workload": WORKLOAD, "global_batch": args.batch, "layers": args.layers,
+        "config": {"workload": WORKLOAD if world == 1 else
+                   f"{WORKLOAD} per GPU ({args.batch} tokens in all)" if args.scaling == "weak" else WORKLOAD,
+                   "global_batch": args.batch, "batch_per_gpu": args.batch / world, "layers": args.layers,
                    "parallelism": f"ep{world}" if world > 1 else "single",
                    "experts_per_gpu": E // world,
                    "l2": "weights 16.3 GB per step >> 126 MB L2 (no flush needed)", "cuda_graph": True},

@@ -6,22 +6,31 @@
 // the full dispatch itself (both are deterministic, so every rank computes
 // the same global slot order), and runs the expert products of its own
 // experts only, writing their rows at their global slots of its `d` buffer.
-// The weighted combine then reads each (token, slot) pair's row from the
-// rank that owns the pair's expert, through CUDA IPC mappings of the peers'
-// buffers, and sums the slots in order exactly as the one-GPU combine does,
-// so every rank ends with the same y.
+// The tokens are split in contiguous blocks too (ep_token_begin): rank r's
+// weighted combine takes its own tokens, reads each (token, slot) pair's row
+// from the rank that owns the pair's expert, through CUDA IPC mappings of the
+// peers' buffers, and sums the slots in order exactly as the one-GPU combine
+// does.  It stores each combined row to its own y and into every peer's row
+// exchange (peer stores over NVLink); ep_gather_rows_kernel then copies the
+// other ranks' tokens from the exchange into y, so every rank ends with the
+// same y.  Per layer a rank reads K rows for T / world tokens and sends
+// T / world rows to each peer, instead of reading K rows for all T tokens.
 //
-// Two rank flags per layer order the exchange, both in the flag block of
-// each rank's arena and both holding a call epoch:
+// Three rank flags per layer order the exchange, all in the flag block of
+// each rank's arena and all holding a call epoch:
 //   ready[r]  rank r's expert rows of epoch e are complete (written by r's
-//             combine kernel into every peer's block before it reads);
+//             combine kernel into every peer's block before it reads), and
+//             r has finished reading its exchange of epoch e - 1;
 //   done[r]   rank r has finished reading its peers' rows of epoch e (written
-//             by the last CTA of r's combine).
+//             by the last CTA of r's combine);
+//   rows[r]   rank r's combined rows of epoch e are in this rank's exchange
+//             (written by the last CTA of r's combine).
 // A rank waits for done[*] >= e - 1 before its expert kernels overwrite d
-// (ep_fence_kernel) and for ready[*] >= e before reading (ep_combine_kernel).
-// Every wait is bounded: on timeout the kernel records kDevPeerTimeout and
-// continues, so a missing peer turns into a status the host reads, never a
-// hung GPU.
+// (ep_fence_kernel), for ready[*] >= e before reading rows or writing into a
+// peer's exchange (ep_combine_kernel) and for rows[*] >= e before reading its
+// exchange (ep_gather_rows_kernel).  Every wait is bounded: on timeout the
+// kernel records kDevPeerTimeout and continues, so a missing peer turns into
+// a status the host reads, never a hung GPU.
 
 #include "common.cuh"
 #include "kernels.h"
@@ -77,8 +86,9 @@ __device__ __forceinline__ int owner_of(const EpArgs& a, int e) {
 }
 
 // y[t, :] = bf16( sum_j f32(d_owner(j)[inv[t*K + j], :]) * w[t, j]  (+ gate_t * shared[t, :]) (+ residual) )
-// with the one-GPU combine's arithmetic and slot order.  Grid: x covers the
-// hidden columns (8 per thread), y strides over tokens.
+// for this rank's tokens, with the one-GPU combine's arithmetic and slot
+// order.  Grid: x covers the hidden columns (8 per thread), y strides over
+// the rank's tokens.
 template <int KMAX>  // compile-time bound on top_k sizing the per-thread arrays
 __global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) ep_combine_kernel(EpArgs a, CombineArgs c, int num_tokens) {
   pdl_wait();  // d, ids, inverse and weights of this call are complete
@@ -94,9 +104,11 @@ __global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) ep_combine_kernel(EpAr
   __syncthreads();
 
   const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  const int t_begin = ep_token_begin(num_tokens, a.world, a.rank);
+  const int t_end = ep_token_begin(num_tokens, a.world, a.rank + 1);
   constexpr int kMaxK = KMAX;
   if (col < c.hidden) {
-    for (int t = blockIdx.y; t < num_tokens; t += gridDim.y) {
+    for (int t = t_begin + blockIdx.y; t < t_end; t += gridDim.y) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       const uint16_t* src[kMaxK];
       float wj[kMaxK];
@@ -146,22 +158,56 @@ __global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) ep_combine_kernel(EpAr
       o.y = uint32_t(f32_to_bf16_bits(acc[2])) | (uint32_t(f32_to_bf16_bits(acc[3])) << 16);
       o.z = uint32_t(f32_to_bf16_bits(acc[4])) | (uint32_t(f32_to_bf16_bits(acc[5])) << 16);
       o.w = uint32_t(f32_to_bf16_bits(acc[6])) | (uint32_t(f32_to_bf16_bits(acc[7])) << 16);
-      *reinterpret_cast<uint4*>(c.y + static_cast<size_t>(t) * c.hidden + col) = o;
+      const size_t off = static_cast<size_t>(t) * c.hidden + col;
+      *reinterpret_cast<uint4*>(c.y + off) = o;
+      for (int q = 0; q < a.world; ++q)
+        if (q != a.rank) *reinterpret_cast<uint4*>(a.peer_y[q] + off) = o;
     }
   }
 
-  // The last CTA to finish tells every peer that this rank is done reading.
+  // The last CTA to finish tells every peer that this rank is done reading
+  // and that its combined rows are in the peer's exchange.  Every thread
+  // fences its own peer stores before the CTA counts itself finished.
   __shared__ bool s_last;
+  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
     const uint32_t total = gridDim.x * gridDim.y;
     s_last = atomicAdd(a.finished, 1u) == total - 1u;
+    __threadfence_system();
   }
   __syncthreads();
   if (s_last) {
     if (threadIdx.x == 0) *a.finished = 0u;
-    if (r < a.world) st_release_sys(a.peer_flags[r] + kEpDoneOffset + a.rank, epoch);
+    if (r < a.world) {
+      st_release_sys(a.peer_flags[r] + kEpDoneOffset + a.rank, epoch);
+      if (r != a.rank) st_release_sys(a.peer_flags[r] + kEpRowsOffset + a.rank, epoch);
+    }
+  }
+}
+
+// y[t, :] = exchange[t, :] for the tokens other ranks own.  Grid: x covers
+// the hidden columns (8 per thread), y strides over those tokens.
+__global__ void __launch_bounds__(256) ep_gather_rows_kernel(EpArgs a, uint16_t* y, int hidden, int num_tokens) {
+  pdl_wait();  // y's previous readers have finished; this call's epoch is set
+  pdl_launch_dependents();
+  const int t_begin = ep_token_begin(num_tokens, a.world, a.rank);
+  const int t_end = ep_token_begin(num_tokens, a.world, a.rank + 1);
+  const int others = num_tokens - (t_end - t_begin);
+  if (others == 0) return;
+  const uint32_t epoch = *a.epoch;
+  const int r = threadIdx.x;
+  if (r < a.world && r != a.rank) {
+    if (!wait_flag(a.flags + kEpRowsOffset + r, epoch, a.err)) record_error(a.err, kDevPeerTimeout);
+  }
+  __syncthreads();
+  const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (col >= hidden) return;
+  const uint16_t* ex = a.peer_y[a.rank];
+  for (int u = blockIdx.y; u < others; u += gridDim.y) {
+    const int t = u < t_begin ? u : u + (t_end - t_begin);
+    const size_t off = static_cast<size_t>(t) * hidden + col;
+    *reinterpret_cast<uint4*>(y + off) = __ldcg(reinterpret_cast<const uint4*>(ex + off));
   }
 }
 
@@ -172,13 +218,24 @@ cudaError_t launch_ep_fence(const EpArgs& a, cudaStream_t st) {
 }
 
 cudaError_t launch_ep_combine(const EpArgs& a, const CombineArgs& c, int num_tokens, cudaStream_t st) {
-  const int threads = num_tokens < 256 ? 64 : 256;  // narrow CTAs for small batches (>= 8 ranks' flag threads)
+  const int own = ep_token_begin(num_tokens, a.world, a.rank + 1) - ep_token_begin(num_tokens, a.world, a.rank);
+  const int threads = own < 256 ? 64 : 256;  // narrow CTAs for small batches (>= 8 ranks' flag threads)
   const int gx = (c.hidden / 8 + threads - 1) / threads;
-  // enough CTAs to cover the tokens of a decode batch in one wave; larger
-  // batches loop (each CTA announces and waits once)
-  const int gy = num_tokens < 1024 ? num_tokens : 1024;
+  // enough CTAs to cover the rank's tokens of a decode batch in one wave;
+  // larger batches loop (each CTA announces and waits once).  A rank that
+  // owns no token still launches one row of CTAs for the flag hand-over.
+  const int gy = own < 1 ? 1 : (own < 1024 ? own : 1024);
   if (c.top_k <= 8) return launch_pdl(ep_combine_kernel<8>, dim3(gx, gy), dim3(threads), 0, st, a, c, num_tokens);
   return launch_pdl(ep_combine_kernel<16>, dim3(gx, gy), dim3(threads), 0, st, a, c, num_tokens);
+}
+
+cudaError_t launch_ep_gather_rows(const EpArgs& a, uint16_t* y, int hidden, int num_tokens, cudaStream_t st) {
+  const int own = ep_token_begin(num_tokens, a.world, a.rank + 1) - ep_token_begin(num_tokens, a.world, a.rank);
+  const int others = num_tokens - own;
+  const int threads = others < 256 ? 64 : 256;
+  const int gx = (hidden / 8 + threads - 1) / threads;
+  const int gy = others < 1 ? 1 : (others < 1024 ? others : 1024);
+  return launch_pdl(ep_gather_rows_kernel, dim3(gx, gy), dim3(threads), 0, st, a, y, hidden, num_tokens);
 }
 
 }  // namespace senmoe

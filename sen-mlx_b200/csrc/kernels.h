@@ -190,11 +190,18 @@ cudaError_t launch_mma_q4(const CUtensorMap& tA0, const CUtensorMap& tA1, const 
 constexpr int kEpMaxRanks = 8;
 constexpr int kEpReadyOffset = 0;   // u32 index of ready[0] in a rank's flag block
 constexpr int kEpDoneOffset = 8;    // u32 index of done[0]
-constexpr size_t kEpFlagBytes = 64; // ready[8], done[8]
+constexpr int kEpRowsOffset = 16;   // u32 index of rows[0]: rank r's combined rows are in this rank's exchange
+constexpr size_t kEpFlagBytes = 128; // ready[8], done[8], rows[8]
+// Token ownership of the expert-parallel combine: rank r combines tokens
+// [ep_token_begin(T, world, r), ep_token_begin(T, world, r + 1)).
+__host__ __device__ inline int ep_token_begin(int num_tokens, int world, int r) {
+  return static_cast<int>(static_cast<long long>(num_tokens) * r / world);
+}
 struct EpArgs {
   int rank, world;
   int bounds[kEpMaxRanks + 1];         // rank r owns experts [bounds[r], bounds[r+1])
   const uint16_t* peer_d[kEpMaxRanks]; // expert rows [P, H] of each rank, mapped here (own included)
+  uint16_t* peer_y[kEpMaxRanks];       // combined-row exchange [Tmax, H] of each rank, mapped here (own included)
   uint32_t* peer_flags[kEpMaxRanks];   // flag block of each rank, mapped here (own included)
   uint32_t* flags;                     // this rank's flag block
   uint32_t* epoch;                     // this rank's call counter
@@ -206,8 +213,13 @@ struct EpArgs {
 // the previous call; advances the call epoch.  Launch before the expert kernels.
 cudaError_t launch_ep_fence(const EpArgs& a, cudaStream_t st);
 // Announces this rank's rows, waits (bounded) for every peer's, and runs the
-// weighted combine reading each pair's row from its owner (CombineArgs.d unused).
+// weighted combine of this rank's tokens, reading each pair's row from its
+// owner (CombineArgs.d unused); every combined row goes to c.y and to each
+// peer's exchange, and the last CTA raises rows[rank] in every peer's flags.
 cudaError_t launch_ep_combine(const EpArgs& a, const CombineArgs& c, int num_tokens, cudaStream_t st);
+// Waits (bounded) for every peer's combined rows and copies the tokens this
+// rank does not own from its exchange into y [T, H].  Launch after the combine.
+cudaError_t launch_ep_gather_rows(const EpArgs& a, uint16_t* y, int hidden, int num_tokens, cudaStream_t st);
 
 // Launch with programmatic dependent launch enabled: the kernel may start
 // while its predecessor in the stream is still running; it must call

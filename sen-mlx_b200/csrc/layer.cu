@@ -142,12 +142,13 @@ struct SenMoeLayer {
   bool mma_ok = false;
   CUtensorMap tm_xs8{}, tm_h8{};              // 8-slot activation tiles
   // expert parallelism (senmoe_layer_connect_peers)
-  size_t arena_bytes = 0, o_d = 0, o_flags = 0;
-  uint32_t* ep_flags = nullptr;  // ready[8], done[8]: written by peers
+  size_t arena_bytes = 0, o_d = 0, o_flags = 0, o_yx = 0;
+  uint32_t* ep_flags = nullptr;  // ready[8], done[8], rows[8]: written by peers
   uint32_t* ep_local = nullptr;  // [0] call epoch, [1] combine CTA counter
   int ep_world = 0, ep_rank = 0; // ep_world 0: not connected
   int ep_bounds[kEpMaxRanks + 1] = {};
   const uint16_t* ep_peer_d[kEpMaxRanks] = {};
+  uint16_t* ep_peer_y[kEpMaxRanks] = {};     // combined-row exchanges [Tmax, H]
   uint32_t* ep_peer_flags[kEpMaxRanks] = {};
   void* ep_opened[kEpMaxRanks] = {};  // IPC mappings to close
   // per-stage timing
@@ -261,7 +262,7 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                o_d = take(P * H * 2), o_shh = take(Is ? T * Is * 2 : 0), o_sho = take(Is ? T * H * 2 : 0),
                o_shg = take(Is ? T * 4 : 0), o_zero = take(Is ? T * 4 : 0), o_xs = take(P * H * 2),
                o_h16 = take(P * I * 2), o_flags = take(kEpFlagBytes), o_local = take(8),
-               o_route = take((T + 3) / 4 * 4);
+               o_route = take((T + 3) / 4 * 4), o_yx = take(T * H * 2);
   cudaError_t e = cudaMalloc(&L->arena, off);
   if (e != cudaSuccess) {
     delete L;
@@ -295,6 +296,7 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
   L->arena_bytes = off;
   L->o_d = o_d;
   L->o_flags = o_flags;
+  L->o_yx = o_yx;
   {  // tensor maps for the tensor-core paths (host-side encoding only)
     const int bits = c.bits, El = c.expert_end - c.expert_begin;
     const uint64_t gw = uint64_t(H) * bits / 32, dw = uint64_t(I) * bits / 32;
@@ -481,6 +483,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     for (int r = 0; r <= L->ep_world; ++r) ea.bounds[r] = L->ep_bounds[r];
     for (int r = 0; r < L->ep_world; ++r) {
       ea.peer_d[r] = L->ep_peer_d[r];
+      ea.peer_y[r] = L->ep_peer_y[r];
       ea.peer_flags[r] = L->ep_peer_flags[r];
     }
     ea.flags = L->ep_flags;
@@ -697,9 +700,10 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   ca.y_f32 = nullptr;
   ca.hidden = H;
   ca.top_k = K;
-  if (ep)
+  if (ep) {
     SENMOE_CUDA(launch_ep_combine(ea, ca, T, st));
-  else
+    SENMOE_CUDA(launch_ep_gather_rows(ea, ca.y, H, T, st));
+  } else
     SENMOE_CUDA(launch_combine(ca, T, st));
   SENMOE_CUDA(mark(6));
   if (profile) L->profiled_once = true;
@@ -852,6 +856,7 @@ int senmoe_layer_connect_peers(SenMoeLayer* L, int32_t rank, int32_t world_size,
   cudaSetDevice(cur);
   for (int r = 0; r < world_size; ++r) {
     L->ep_peer_d[r] = reinterpret_cast<const uint16_t*>(bases[r] + L->o_d);
+    L->ep_peer_y[r] = reinterpret_cast<uint16_t*>(bases[r] + L->o_yx);
     L->ep_peer_flags[r] = reinterpret_cast<uint32_t*>(bases[r] + L->o_flags);
     L->ep_opened[r] = r == rank ? nullptr : bases[r];
     L->ep_bounds[r] = peers[r].expert_begin;

@@ -96,8 +96,9 @@ def exchange(rank, world, n_layers, extra_on_rank=-1):
 def decomposition(rank, world, bits):
     """The expert-parallel data flow on the CPU: every rank routes all tokens,
     computes the rows of its own experts at their global slots, the rows are
-    all-gathered, and each rank combines every pair's row from its owner in
-    slot order.  Returns this rank's y (fp32)."""
+    all-gathered, each rank combines its own block of tokens (every pair's
+    row from its owner, in slot order) and the combined rows are
+    all-gathered into y.  Returns this rank's y (fp32)."""
     import torch
     import torch.distributed as dist
 
@@ -127,16 +128,21 @@ def decomposition(rank, world, bits):
             rows[slot[p]] = N.expert_mlp(x[p // K].astype(np.float64), gd[e - eb], ud[e - eb], dd[e - eb])
     gathered = [torch.zeros(P, H) for _ in range(world)]
     dist.all_gather(gathered, torch.from_numpy(rows))
-    y = np.zeros((T, H), dtype=np.float32)
-    for t in range(T):
+    tb = [T * r // world for r in range(world + 1)]  # token blocks, as ep_token_begin
+    mine = np.zeros((T, H), dtype=np.float32)
+    sh = N.shared_out(cfg, w, x) if cfg.shared_intermediate else None
+    for t in range(tb[rank], tb[rank + 1]):
         acc = np.zeros(H, dtype=np.float32)
         for j in range(K):
             p = t * K + j
             owner = bisect.bisect_right(b, int(ids[t, j])) - 1
             acc = (acc + gathered[owner][slot[p]].numpy() * wts[t, j]).astype(np.float32)
-        y[t] = acc
-    if cfg.shared_intermediate:
-        y = (y + N.shared_out(cfg, w, x)).astype(np.float32)
+        mine[t] = acc if sh is None else (acc + sh[t]).astype(np.float32)
+    blocks = [torch.zeros(T, H) for _ in range(world)]
+    dist.all_gather(blocks, torch.from_numpy(mine))
+    y = np.zeros((T, H), dtype=np.float32)
+    for r in range(world):
+        y[tb[r]:tb[r + 1]] = blocks[r].numpy()[tb[r]:tb[r + 1]]
     return y
 
 
