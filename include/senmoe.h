@@ -186,9 +186,10 @@ int senmoe_layer_check(SenMoeLayer* layer, senmoe_stream_t stream);
  * the host exchanges them (e.g. torch.distributed all_gather), and every rank
  * connects with the full table.  After that, forward on every rank takes the
  * SAME tokens x (replicated), and every rank returns the same y: each rank
- * computes only its experts' rows and the combine reads every row from its
- * owner over NVLink (CUDA IPC mappings), in slot order, with the one-GPU
- * combine's arithmetic.  All ranks must run the same sequence of forwards
+ * computes only its experts' rows, combines its own contiguous block of the
+ * tokens reading every row from its owner over NVLink (CUDA IPC mappings), in
+ * slot order, with the one-GPU combine's arithmetic, and sends the combined
+ * rows to every peer.  All ranks must run the same sequence of forwards
  * (same num_tokens); a rank that does not shows up as SENMOE_ERR_TIMEOUT from
  * senmoe_layer_check on the others (every cross-GPU wait is bounded). */
 #define SENMOE_MAX_RANKS 8
