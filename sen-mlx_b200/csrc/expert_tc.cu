@@ -527,22 +527,41 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
         tmem_ld16(lane_addr + c0, g);
         tmem_ld16(lane_addr + BN + c0, u);
         tmem_ld_wait();
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          if (c0 + jj >= tl.w) break;
-          uint16_t bits;
-          if constexpr (NPROJ == 2) {  // h = act(bf16(g), bf16(u)) (a bf16 value), stored as fp16
+        // h feeds the down GEMM as its k dimension: store it k-permuted like x
+        const int col = NPROJ == 2 ? kperm8(r) : r;
+        uint16_t* orow = a.out + static_cast<size_t>(tl.z + c0) * a.out_stride + col;
+        // h = act(bf16(g), bf16(u)) (a bf16 value, stored as fp16), or the
+        // down projection's two partial sums added and rounded to bf16; bad
+        // flags an h outside fp16 range
+        auto value = [&](int jj, bool& bad) -> uint16_t {
+          if constexpr (NPROJ == 2) {
             const float gg = round_bf16(__uint_as_float(g[jj])), uu = round_bf16(__uint_as_float(u[jj]));
             const float v = a.act == 0 ? act_swiglu_mlx(gg, uu) : act_geglu_mlx(gg, uu);
-            if (!(fabsf(v) < 65504.0f)) record_error(a.err, kDevFp16Range);
-            bits = __half_as_ushort(__float2half_rn(v));
+            bad = bad || !(fabsf(v) < 65504.0f);
+            return __half_as_ushort(__float2half_rn(v));
           } else {
-            bits = f32_to_bf16_bits(__uint_as_float(g[jj]) + __uint_as_float(u[jj]));
+            return f32_to_bf16_bits(__uint_as_float(g[jj]) + __uint_as_float(u[jj]));
           }
-          // h feeds the down GEMM as its k dimension: store it k-permuted like x
-          const int col = NPROJ == 2 ? kperm8(r) : r;
-          a.out[static_cast<size_t>(tl.z + c0 + jj) * a.out_stride + col] = bits;
+        };
+        bool bad = false;
+        if (c0 + 16 <= tl.w) {
+          // a full chunk (warp-uniform): 16 independent chains that interleave,
+          // where a per-column exit would run them one after another
+          uint16_t bits[16];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) bits[jj] = value(jj, bad);
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) orow[static_cast<size_t>(jj) * a.out_stride] = bits[jj];
+        } else {
+          // the tile's last valid slots only: columns past them hold other
+          // experts' activations (or none) and are never evaluated.  Fully
+          // unrolled, so g and u stay in registers (a runtime index would
+          // put them in local memory).
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj)
+            if (c0 + jj < tl.w) orow[static_cast<size_t>(jj) * a.out_stride] = value(jj, bad);
         }
+        if (bad) record_error(a.err, kDevFp16Range);
       }
       tc_fence_before();
       __syncwarp();
