@@ -170,10 +170,18 @@ template <int BITS, int NPROJ, int BN> struct TcShape {
   static constexpr int kBFit = int(65536u / kBBytes);
   static constexpr int kB = kBFit < 2 ? 2 : (kBFit > 8 ? 8 : kBFit);
   static constexpr uint32_t kPBytes = 128 * 128;                // one projection's packed stage
+  // With a single accumulator (gate/up at BN = 128) the epilogue first copies
+  // it into a shared-memory staging row per thread (bf16 gate/up pairs; rows
+  // padded by 16 bytes so 16-byte accesses spread over the banks), releases
+  // it, and evaluates the activation from there while the next tile's MMAs
+  // run.  A tile's activation math takes about as long as its main loop.
+  static constexpr bool kStage = NPROJ == 2 && kAcc == 1;
+  static constexpr uint32_t kEStride = BN * 4 + 16;
+  static constexpr uint32_t kEBytes = kStage ? 128u * kEStride : 0u;
   // packed stages fill the rest of shared memory (at most 8)
-  static constexpr int kPFit = int((200u * 1024u - kB * kBBytes) / (NPROJ * kPBytes));
+  static constexpr int kPFit = int((200u * 1024u - kB * kBBytes - kEBytes) / (NPROJ * kPBytes));
   static constexpr int kP = kPFit > 8 ? 8 : kPFit;
-  static constexpr size_t kSmem = 1024 + size_t(kB) * kBBytes + size_t(kP) * NPROJ * kPBytes;
+  static constexpr size_t kSmem = 1024 + size_t(kB) * kBBytes + size_t(kP) * NPROJ * kPBytes + kEBytes;
 };
 
 constexpr int kMaxTilesPerCta = 64;
@@ -245,6 +253,7 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
   unsigned char* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   unsigned char* sB = base;                       // [SB][KA][BN*128]
   unsigned char* sP = sB + SB * kBBytes;          // [SP][NPROJ][16 KB]
+  unsigned char* sE = sP + SP * NPROJ * kPBytes;  // [128 rows][kEStride] epilogue staging (kStage)
 
   // ---- barriers and TMEM first: they do not depend on the previous kernel
   if (warp == 0 && lane == 0) {
@@ -521,12 +530,9 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
       const int4 tl = s_tiles[ti];
       const int r = tl.y + q * 32 + lane;  // output row of this thread
       const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ab * S::kAccCols;
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        if (c0 >= tl.w) break;  // uniform across the warp
-        uint32_t g[16], u[16];  // gate / up, or the two partial sums of down
-        tmem_ld16(lane_addr + c0, g);
-        tmem_ld16(lane_addr + BN + c0, u);
-        tmem_ld_wait();
+      // One 16-column chunk from fp32 bit patterns: g / u are gate / up, or
+      // the two partial sums of down.
+      auto emit_chunk = [&](int c0, const uint32_t (&g)[16], const uint32_t (&u)[16]) {
         // h feeds the down GEMM as its k dimension: store it k-permuted like x
         const int col = NPROJ == 2 ? kperm8(r) : r;
         uint16_t* orow = a.out + static_cast<size_t>(tl.z + c0) * a.out_stride + col;
@@ -562,10 +568,59 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
             if (c0 + jj < tl.w) orow[static_cast<size_t>(jj) * a.out_stride] = value(jj, bad);
         }
         if (bad) record_error(a.err, kDevFp16Range);
+      };
+      if constexpr (S::kStage) {
+        // accumulator -> this thread's staging row as (bf16 gate, bf16 up)
+        // pairs, the rounding the activation applies first; then release the
+        // accumulator and evaluate from the staging row
+        unsigned char* erow = sE + static_cast<uint32_t>(q * 32 + lane) * S::kEStride;
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          if (c0 >= tl.w) break;  // uniform across the warp
+          uint32_t g[16], u[16];
+          tmem_ld16(lane_addr + c0, g);
+          tmem_ld16(lane_addr + BN + c0, u);
+          tmem_ld_wait();
+          uint32_t pk[16];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj)
+            pk[jj] = uint32_t(f32_to_bf16_bits(__uint_as_float(g[jj]))) |
+                     (uint32_t(f32_to_bf16_bits(__uint_as_float(u[jj]))) << 16);
+          uint4* dst = reinterpret_cast<uint4*>(erow + c0 * 4);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_accempty[ab]);
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          if (c0 >= tl.w) break;
+          const uint4* src = reinterpret_cast<const uint4*>(erow + c0 * 4);
+          uint32_t g[16], u[16];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 v = src[i];
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              g[4 * i + k] = w[k] << 16;
+              u[4 * i + k] = w[k] & 0xffff0000u;
+            }
+          }
+          emit_chunk(c0, g, u);
+        }
+      } else {
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          if (c0 >= tl.w) break;  // uniform across the warp
+          uint32_t g[16], u[16];
+          tmem_ld16(lane_addr + c0, g);
+          tmem_ld16(lane_addr + BN + c0, u);
+          tmem_ld_wait();
+          emit_chunk(c0, g, u);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_accempty[ab]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_accempty[ab]);
     }
   }
 
