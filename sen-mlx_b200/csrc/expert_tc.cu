@@ -154,10 +154,16 @@ template <int BITS, int NPROJ, int BN> struct TcShape {
   // few hundred cycles even when its phase has already completed.
   static constexpr int KA = NPROJ == 2 ? 2 : (KP < 4 ? KP : 4);
   static constexpr int kACols = NPROJ * KA * 32;                // TMEM columns of one A stage
-  // TMEM (512 columns): ACC accumulator sets of 2*BN columns (gate and up, or
-  // the down projection's two partial sums, one per MMA issuer), then kA A
-  // stages (128 rows x 64 k per k-block, two fp16 per column).
-  static constexpr int kAccCols = 2 * BN;
+  // MMA issuers: gate/up has one per projection.  The down projection has
+  // two at small BN, where one thread's issue latency bounds the rate, each
+  // taking alternate K steps into its own partial sum; at BN = 128 an MMA
+  // takes longer than its issue, so one issuer keeps up and its single
+  // accumulator leaves TMEM room for two accumulator sets.
+  static constexpr int kIss = (NPROJ == 1 && BN >= 128) ? 1 : 2;
+  // TMEM (512 columns): ACC accumulator sets of kIss*BN columns (gate and up,
+  // or the down projection's partial sums), then kA A stages (128 rows x 64 k
+  // per k-block, two fp16 per column).
+  static constexpr int kAccCols = kIss * BN;
   static constexpr int kAcc = 2 * kAccCols + 2 * kACols <= 512 ? 2 : 1;
   static constexpr int kAFit = (512 - kAcc * kAccCols) / kACols;
   static constexpr int kA = kAFit > 4 ? 4 : kAFit;              // TMEM A stages
@@ -197,7 +203,6 @@ constexpr int kMaxTilesPerCta = 64;
 constexpr int kEpiWarp0 = 2 + kDqWarps;
 constexpr int kBWarp = kEpiWarp0 + 4;
 constexpr int kMma1Warp = kBWarp + 1;
-constexpr int kIssuers = 2;
 constexpr int kTcThreadsP = (kMma1Warp + 1) * 32;
 
 // Scale/bias of k-block j (0 <= j < KP) from KP bf16 values held as packed u32s.
@@ -239,7 +244,7 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
 
   extern __shared__ unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t bar_pfull[SP], bar_pempty[SP], bar_afull[SA], bar_aempty[SA], bar_bfull[SB],
-      bar_bempty[SB], bar_accfull[ACC], bar_accempty[ACC], bar_drain[kIssuers];
+      bar_bempty[SB], bar_accfull[ACC], bar_accempty[ACC], bar_drain[S::kIss];
   __shared__ uint32_t s_tmem;
   __shared__ int4 s_tiles[kMaxTilesPerCta];  // local expert, first weight row, first slot, valid slots
   __shared__ int s_ntiles;
@@ -259,10 +264,10 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
   if (warp == 0 && lane == 0) {
     // consumer-side barriers count warps: each warp fences, syncs, and arrives once
     for (int i = 0; i < SP; ++i) { mbar_init(&bar_pfull[i], 1); mbar_init(&bar_pempty[i], kDqWarps); }
-    for (int i = 0; i < SA; ++i) { mbar_init(&bar_afull[i], kDqWarps); mbar_init(&bar_aempty[i], kIssuers); }
-    for (int i = 0; i < SB; ++i) { mbar_init(&bar_bfull[i], 1); mbar_init(&bar_bempty[i], kIssuers); }
-    for (int i = 0; i < ACC; ++i) { mbar_init(&bar_accfull[i], kIssuers); mbar_init(&bar_accempty[i], 4); }
-    for (int i = 0; i < kIssuers; ++i) mbar_init(&bar_drain[i], 1);
+    for (int i = 0; i < SA; ++i) { mbar_init(&bar_afull[i], kDqWarps); mbar_init(&bar_aempty[i], S::kIss); }
+    for (int i = 0; i < SB; ++i) { mbar_init(&bar_bfull[i], 1); mbar_init(&bar_bempty[i], S::kIss); }
+    for (int i = 0; i < ACC; ++i) { mbar_init(&bar_accfull[i], S::kIss); mbar_init(&bar_accempty[i], 4); }
+    for (int i = 0; i < S::kIss; ++i) mbar_init(&bar_drain[i], 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -346,7 +351,9 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
     }
   } else if (warp == 1 || warp == kMma1Warp) {
     // ================================================= MMA issuers
-    if (lane == 0) {
+    // (a single-issuer shape leaves the second issuer warp without work; it
+    // goes straight to the teardown barrier)
+    if (lane == 0 && (warp == 1 || S::kIss == 2)) {
       const int iss = warp == 1 ? 0 : 1;
       bool ok = true;
       int ai = 0;  // pipeline steps issued (A and B stages advance together)
@@ -371,11 +378,11 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
               for (int k = 0; k < BK / 16; ++k)  // K = 16 per MMA: 8 TMEM columns of A, 32 bytes of B
                 umma_f16_ts(d, a_stage + (iss * KA + kk) * 32 + k * 8, b_desc0 + ((kk * kBTile + k * 32) >> 4),
                             kIdesc, (st | kk | k) != 0);
-          } else {  // K steps of parity iss into this issuer's partial sum
+          } else {  // K steps iss, iss + kIss, ... into this issuer's partial sum
 #pragma unroll
             for (int kk = 0; kk < KA; ++kk)
 #pragma unroll
-              for (int k = iss; k < BK / 16; k += 2)
+              for (int k = iss; k < BK / 16; k += S::kIss)
                 umma_f16_ts(d, a_stage + kk * 32 + k * 8, b_desc0 + ((kk * kBTile + k * 32) >> 4), kIdesc,
                             (st | kk | (k - iss)) != 0);
           }
@@ -545,6 +552,8 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
             const float v = a.act == 0 ? act_swiglu_mlx(gg, uu) : act_geglu_mlx(gg, uu);
             bad = bad || !(fabsf(v) < 65504.0f);
             return __half_as_ushort(__float2half_rn(v));
+          } else if constexpr (S::kIss == 1) {  // one accumulator: the whole sum
+            return f32_to_bf16_bits(__uint_as_float(g[jj]));
           } else {
             return f32_to_bf16_bits(__uint_as_float(g[jj]) + __uint_as_float(u[jj]));
           }
@@ -613,7 +622,7 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
           if (c0 >= tl.w) break;  // uniform across the warp
           uint32_t g[16], u[16];
           tmem_ld16(lane_addr + c0, g);
-          tmem_ld16(lane_addr + BN + c0, u);
+          if constexpr (S::kIss == 2) tmem_ld16(lane_addr + BN + c0, u);
           tmem_ld_wait();
           emit_chunk(c0, g, u);
         }

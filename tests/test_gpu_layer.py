@@ -92,9 +92,11 @@ def test_config0_block_vs_oracle(senmoe, config0_layer, T, path):
     check_against_oracle(cfg, mw, x, got)
 
 
-@pytest.mark.parametrize("T", [256, 1024])
+@pytest.mark.parametrize("T", [256, 1024, 2048])
 def test_config0_prefill_tensor_core_vs_oracle(senmoe, config0_layer, T):
-    """Prefill-size batches (32..64+ tokens per expert) on the tcgen05 path."""
+    """Prefill-size batches on the tcgen05 path: 16, 64 and 128 tokens per
+    expert, i.e. the 16-, 64- and 128-slot tiles (the last with the staged
+    gate/up epilogue and the single-issuer down kernel)."""
     cfg, mw = config0_layer
     x = O.make_tokens(T, cfg.hidden, seed=100 + T)
     got = run_block(senmoe, cfg, mw, x, path=PATHS["tc"])
