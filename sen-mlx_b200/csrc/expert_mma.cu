@@ -75,7 +75,10 @@ struct MmaShape {
   // group-scaled form: the stage's scales and biases, [proj][s, b][row][4 groups] bf16
   static constexpr int kSBOff = kTmaBytes;
   static constexpr int kSBBytes = G4 ? NPROJ * 2 * kRows * 8 : 0;
-  static constexpr int kStageBytes = kTmaBytes + kSBBytes;   // multiple of 1024
+  // group-scaled gate/up: the stage's activation group sums, [slot][4 groups] fp32
+  static constexpr int kXOff = kSBOff + kSBBytes;
+  static constexpr int kXBytes = (G4 && NPROJ == 2) ? 8 * NT * 16 : 0;
+  static constexpr int kStageBytes = (kTmaBytes + kSBBytes + kXBytes + 1023) / 1024 * 1024;
   static constexpr int kRedBytes = 8 * 32 * NPROJ * NT * 4 * 4;
   static constexpr int kMisc = 4096;                         // barriers + tile list
   static constexpr int kFit = (kSmemBudget - kRedBytes - kMisc - 1024) / kStageBytes;
@@ -309,6 +312,16 @@ __global__ void __launch_bounds__(G4 ? kThreadsG4 : kThreads, 1)
 #pragma unroll
             for (int pa = 0; pa < 2 * NPROJ; ++pa)  // array pa: scales (even) / biases (odd) of proj pa / 2
               cp_async_8(dst + pa * kRows * 8, ((pa & 1) ? a.b[pa >> 1] : a.s[pa >> 1]) + sb_row0 + 4 * st);
+            if constexpr (NPROJ == 2) {
+              // the group sums of the stage's 4 groups: 16 bytes per slot,
+              // two 8-byte halves per loader lane (rows past the valid slots
+              // exist: the buffer has 16 spare rows)
+              if (ll < 16 * NT) {
+                const int sl = ll >> 1, half = ll & 1;
+                cp_async_8(smem_u32(base + S::kXOff) + sl * 16 + half * 8,
+                           a.xsum + static_cast<size_t>(tl.z + sl) * groups + 4 * st + 2 * half);
+              }
+            }
             cp_async_arrive_noinc(&bar_full[slot]);
           }
           if (++slot == S::kStages) { slot = 0; ph ^= 1; }
@@ -411,6 +424,18 @@ __global__ void __launch_bounds__(G4 ? kThreadsG4 : kThreads, 1)
             sv[p][r] = *reinterpret_cast<const uint32_t*>(base + offSB + (2 * p) * kRows * 8 + r * 64);
             bv[p][r] = *reinterpret_cast<const uint32_t*>(base + offSB + (2 * p + 1) * kRows * 8 + r * 64);
           }
+        // gate/up: group sums of slots 2t (c0, c2) and 2t + 1 (c1, c3) for
+        // this k-half's groups 2kh, 2kh + 1
+        float xlo[NT][2], xhi[NT][2];
+        if constexpr (NPROJ == 2) {
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const float2 v0 = *reinterpret_cast<const float2*>(base + S::kXOff + (8 * nt + 2 * t) * 16 + kh * 8);
+            const float2 v1 = *reinterpret_cast<const float2*>(base + S::kXOff + (8 * nt + 2 * t + 1) * 16 + kh * 8);
+            xlo[nt][0] = v0.x; xlo[nt][1] = v0.y;
+            xhi[nt][0] = v1.x; xhi[nt][1] = v1.y;
+          }
+        }
 #pragma unroll
         for (int gi = 0; gi < 2; ++gi) {
           uint32_t bf[NT][2][4];
@@ -419,14 +444,21 @@ __global__ void __launch_bounds__(G4 ? kThreadsG4 : kThreads, 1)
             ldmatrix_x4(sbase + offB[gi][0] + nt * 1024, bf[nt][0]);
             ldmatrix_x4(sbase + offB[gi][1] + nt * 1024, bf[nt][1]);
           }
-          // group sums of the activations, in units of 2^-24 (all rows alike)
+          // group sums of the activations, in units of 2^-24 (all rows alike):
+          // gate/up reads them (gather_rows computed them), down forms them
+          // with four more MMAs whose A is the constant 2^-24 / 2^-20
           float xs[NT][4];
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            mma_z(xs[nt], kOne24, kOne24, kOne24, kOne24, bf[nt][0][0], bf[nt][0][1]);
-            mma_acc(xs[nt], kOne20, kOne20, kOne20, kOne20, bf[nt][0][2], bf[nt][0][3]);
-            mma_acc(xs[nt], kOne24, kOne24, kOne24, kOne24, bf[nt][1][0], bf[nt][1][1]);
-            mma_acc(xs[nt], kOne20, kOne20, kOne20, kOne20, bf[nt][1][2], bf[nt][1][3]);
+            if constexpr (NPROJ == 2) {
+              xs[nt][0] = xs[nt][2] = xlo[nt][gi];
+              xs[nt][1] = xs[nt][3] = xhi[nt][gi];
+            } else {
+              mma_z(xs[nt], kOne24, kOne24, kOne24, kOne24, bf[nt][0][0], bf[nt][0][1]);
+              mma_acc(xs[nt], kOne20, kOne20, kOne20, kOne20, bf[nt][0][2], bf[nt][0][3]);
+              mma_acc(xs[nt], kOne24, kOne24, kOne24, kOne24, bf[nt][1][0], bf[nt][1][1]);
+              mma_acc(xs[nt], kOne20, kOne20, kOne20, kOne20, bf[nt][1][2], bf[nt][1][3]);
+            }
           }
 #pragma unroll
           for (int p = 0; p < NPROJ; ++p) {
@@ -897,6 +929,7 @@ cudaError_t launch_mma_gemm(const CUtensorMap& tA0, const CUtensorMap& tA1, cons
                             cudaStream_t st) {
   if (g4) {
     if (!mma_g4_supported(bits, nt, a)) return cudaErrorInvalidValue;
+    if (nproj == 2 && !a.xsum) return cudaErrorInvalidValue;  // gate/up reads gather_rows' group sums
     if (nproj == 2) return nt == 1 ? launch_mma_t<4, 2, 1, true>(tA0, tA1, tB, a, tiles_upper, st)
                                    : launch_mma_t<4, 2, 2, true>(tA0, tA1, tB, a, tiles_upper, st);
     if (nproj == 1) return nt == 1 ? launch_mma_t<4, 1, 1, true>(tA0, tA1, tB, a, tiles_upper, st)

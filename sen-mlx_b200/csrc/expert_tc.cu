@@ -746,7 +746,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
                                                           const int32_t* __restrict__ perm, int k_div,
                                                           uint16_t* __restrict__ out, int num_slots, int hidden,
                                                           int* err, const int32_t* __restrict__ offsets, int eb,
-                                                          int ee, int order) {
+                                                          int ee, int order, float* __restrict__ group_sums) {
   pdl_wait();
   pdl_launch_dependents();
   const int s0 = blockIdx.x * kGatherSlots;
@@ -778,6 +778,12 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
       for (int q = 0; q < 8; ++q) {
         const uint4 v = __ldg(in + q);
         w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+      }
+      if (group_sums) {  // the group's sum of x (column order), in the MMA's 2^-24 units
+        float sum = 0.f;
+#pragma unroll
+        for (int q = 0; q < 32; ++q) sum += bf16_lo(w[q]) + bf16_hi(w[q]);
+        group_sums[static_cast<size_t>(s) * groups + G] = sum * 5.9604644775390625e-8f;  // 2^-24
       }
       uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(s) * hidden + 64 * G);
 #pragma unroll
@@ -858,12 +864,12 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
 
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
                                int num_slots, int hidden, int* err, cudaStream_t st,
-                               const int32_t* offsets, int eb, int ee, int order) {
+                               const int32_t* offsets, int eb, int ee, int order, float* group_sums) {
   if (num_slots <= 0) return cudaSuccess;
   const int threads = hidden / 8 < 256 ? ((hidden / 8 + 31) / 32) * 32 : 256;
   const int grid = (num_slots + kGatherSlots - 1) / kGatherSlots;
   return launch_pdl(gather_rows_kernel, dim3(grid), dim3(threads), 0, st, x, perm, k_div, x_sorted, num_slots,
-                    hidden, err, offsets, eb, ee, order);
+                    hidden, err, offsets, eb, ee, order, order == kOrderMmaG4 ? group_sums : nullptr);
 }
 
 }  // namespace senmoe

@@ -141,6 +141,10 @@ struct TcGemmArgs {
   long long out_stride;
   int act;                  // 0 SwiGLU, 1 GeGLU (two-projection form)
   int* err;
+  // Group-scaled two-projection form: per slot row the B operand's 64-column
+  // group sums x 2^-24 ([slots + 16, kdim/64] fp32, from gather_rows); the
+  // one-projection form computes its own.
+  const float* xsum;
 };
 size_t tc_smem_bytes(int bits, int nproj, int bn, int kdim);
 bool tc_supported(int rows, int kdim, int bits, int nproj, int bn);
@@ -162,9 +166,14 @@ cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
 // kOrderMmaG4 (warp-MMA group-scaled form, kperm_g4 with odd columns / 16;
 // hidden % 64 == 0).
 enum ActivationOrder { kOrderTc = 0, kOrderMma = 1, kOrderMmaG4 = 2 };
+// With kOrderMmaG4 and `group_sums` non-null, group_sums[s * hidden/64 + G]
+// also receives 2^-24 * (the fp32 sum of x[perm[s]/k_div, 64 G .. 64 G + 63])
+// for every gathered slot: the group sums the group-scaled gate/up kernel
+// post-scales with.
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
                                int num_slots, int hidden, int* err, cudaStream_t st,
-                               const int32_t* offsets = nullptr, int eb = 0, int ee = 0, int order = kOrderTc);
+                               const int32_t* offsets = nullptr, int eb = 0, int ee = 0, int order = kOrderTc,
+                               float* group_sums = nullptr);
 
 // ------------------------------------------- warp-MMA expert GEMM (decode)
 // Same arguments as the tcgen05 GEMM (TcGemmArgs; out holds h as fp16 in

@@ -129,6 +129,7 @@ struct SenMoeLayer {
   bool tc_ok = false;
   uint16_t* xs = nullptr;        // fp16 [Tmax*K, H] activations gathered into slot order
   uint16_t* h16 = nullptr;       // fp16 [Tmax*K, I] SwiGLU output (B operand of the down GEMM)
+  float* xsum = nullptr;         // [Tmax*K + 16, H/64] group sums of xs (group-scaled gate/up)
   CUtensorMap tm_gate{}, tm_up{}, tm_down{};  // packed codes, [rows, words]
   CUtensorMap tm_gate64{}, tm_up64{}, tm_down64{};  // the same with 64-row boxes (two-CTA form)
   bool q4_ok = false;
@@ -262,7 +263,8 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                o_d = take(P * H * 2), o_shh = take(Is ? T * Is * 2 : 0), o_sho = take(Is ? T * H * 2 : 0),
                o_shg = take(Is ? T * 4 : 0), o_zero = take(Is ? T * 4 : 0), o_xs = take(P * H * 2),
                o_h16 = take(P * I * 2), o_flags = take(kEpFlagBytes), o_local = take(8),
-               o_route = take((T + 3) / 4 * 4), o_yx = take(T * H * 2);
+               o_route = take((T + 3) / 4 * 4), o_yx = take(T * H * 2),
+               o_xsum = take((P + 16) * (H / 64) * 4);
   cudaError_t e = cudaMalloc(&L->arena, off);
   if (e != cudaSuccess) {
     delete L;
@@ -291,6 +293,7 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
   L->xs = reinterpret_cast<uint16_t*>(base + o_xs);
   L->h16 = reinterpret_cast<uint16_t*>(base + o_h16);
   L->route_cnt = reinterpret_cast<int*>(base + o_route);
+  L->xsum = reinterpret_cast<float*>(base + o_xsum);
   L->ep_flags = reinterpret_cast<uint32_t*>(base + o_flags);
   L->ep_local = reinterpret_cast<uint32_t*>(base + o_local);
   L->arena_bytes = off;
@@ -532,7 +535,8 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     const bool q4 = g4 && nt == 1 && L->q4_ok && c.reserved[1] == kMmaFormAuto && max_items * (I / 128) < L->sms;
     SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
                                    L->offsets, c.expert_begin, c.expert_end,
-                                   g4 ? kOrderMmaG4 : kOrderMma));
+                                   g4 ? kOrderMmaG4 : kOrderMma, g4 ? L->xsum : nullptr));
+    ga.xsum = L->xsum;
     SENMOE_CUDA(mark(2));
     if (q4) {
       ga.m_tiles = I / 64;
