@@ -36,6 +36,7 @@ from __future__ import annotations
 import json
 import os
 import struct
+import warnings
 from dataclasses import dataclass
 
 import numpy as np
@@ -115,13 +116,21 @@ def _bf16_bits(ckpt: SafetensorsCheckpoint, name: str) -> np.ndarray:
 
 
 def _to_device(a: np.ndarray, device, bf16: bool = False) -> torch.Tensor:
-    # memory-mapped shards are read-only: a host tensor gets its own copy
-    a = np.array(a, copy=True) if torch.device(device).type == "cpu" else np.ascontiguousarray(a)
-    if bf16:
-        return torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).to(device)
+    # memory-mapped shards are read-only: a host tensor gets its own copy; a
+    # device tensor is copied out of the mapping (the read-only host view
+    # only feeds that copy, so torch's non-writable-array warning is moot)
+    host = torch.device(device).type == "cpu"
+    a = np.array(a, copy=True) if host else np.ascontiguousarray(a)
     if a.dtype == np.uint32:
-        return torch.from_numpy(a.view(np.int32)).to(device)
-    return torch.from_numpy(a).to(device)
+        a = a.view(np.int32)
+    elif bf16:
+        a = a.view(np.int16)
+    with warnings.catch_warnings():
+        warnings.filterwarnings("ignore", message="The given NumPy array is not writable")
+        t = torch.from_numpy(a)
+    if bf16:
+        t = t.view(torch.bfloat16)
+    return t.to(device)
 
 
 def _switch_linear(ckpt, prefix: str, device) -> SwitchLinear:
