@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(RouterArgs
 // logits stay in shared memory, and the same CTA runs softmax / top-k for its
 // tokens.  Experts come in chunks of 128 (E <= 512).
 namespace {
-constexpr int kRtTok = 32, kRtExp = 128, kRtStages = 4;
+constexpr int kRtTok = 32, kRtExp = 128, kRtStages = 8;
 constexpr int kRtCompute = 8;                     // 2 token halves x 4 expert quarters
 constexpr int kRtThreads = (kRtCompute + 1) * 32; // + one TMA warp
 constexpr uint32_t kRtXBytes = kRtTok * 128, kRtWBytes = kRtExp * 128;
