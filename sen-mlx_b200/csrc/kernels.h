@@ -58,6 +58,14 @@ bool router_tc_supported(int hidden, int num_experts, int top_k);
 size_t router_tc_smem_bytes(int num_experts);
 cudaError_t launch_router_tc(const CUtensorMap& tX, const CUtensorMap& tW, const RouterArgs& a, cudaStream_t st);
 cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st);
+// Top-k of every token plus the single-chunk dispatch in one CTA, for small
+// batches (<= kTopkDispatchMaxTokens tokens, <= 2048 pairs); d.topk_ids must
+// be a.topk_ids.  Measured on the 48-layer decode stack: one launch fewer
+// wins at 1-8 tokens (about 1 %); at 32-64 tokens the one CTA's top-k of
+// every token costs more than the launch (+2 %, +5 %).
+constexpr int kTopkDispatchMaxTokens = 8;
+bool router_topk_dispatch_supported(int num_tokens, int num_pairs, int num_experts);
+cudaError_t launch_router_topk_dispatch(const RouterArgs& a, const DispatchArgs& d, cudaStream_t st);
 bool router_supported(int hidden, int num_experts, int top_k);
 
 // Gemma-4 router (router_gemma.cu, gemma4.rs:716-736): rms_norm with weight

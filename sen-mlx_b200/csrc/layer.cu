@@ -473,6 +473,11 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     SENMOE_CUDA(launch_router_logits(rf, st));
     SENMOE_CUDA(mark(1));
     SENMOE_CUDA(launch_dispatch(da, st));
+  } else if (router_topk_dispatch_supported(static_cast<int>(T), P, E)) {
+    // 1-8 tokens: logits, then top-k and the dispatch in one CTA
+    SENMOE_CUDA(launch_router_logits(ra, st));
+    SENMOE_CUDA(launch_router_topk_dispatch(ra, da, st));
+    SENMOE_CUDA(mark(1));
   } else {
     SENMOE_CUDA(launch_router_logits(ra, st));
     SENMOE_CUDA(launch_router_topk(ra, st));

@@ -14,6 +14,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "dispatch_body.cuh"
 
 namespace senmoe {
 
@@ -352,6 +353,42 @@ cudaError_t launch_router_logits(const RouterArgs& a, cudaStream_t st) {
   }
   SENMOE_RL_CASE(1) SENMOE_RL_CASE(2) SENMOE_RL_CASE(4) SENMOE_RL_CASE(8) SENMOE_RL_CASE(12) SENMOE_RL_CASE(16)
 #undef SENMOE_RL_CASE
+  return cudaErrorNotSupported;
+}
+
+// Small batches: the top-k of every token and the whole single-chunk dispatch
+// in one CTA (one launch instead of two).  Warp w takes tokens w, w + 32, ...;
+// after the block barrier the dispatch reads the ids with ld.global.cg, which
+// sees this CTA's writes.
+template <int EPL>
+__global__ void __launch_bounds__(dispatch_detail::kThreads) router_topk_dispatch_kernel(RouterArgs a, DispatchArgs d) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ int sm_disp[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int t = warp; t < a.num_tokens; t += dispatch_detail::kWarps)
+    topk_row<EPL, false>(a, a.logits + static_cast<size_t>(t) * a.num_experts, t, lane);
+  __syncthreads();
+  dispatch_detail::dispatch_single_body(d, sm_disp);
+}
+
+bool router_topk_dispatch_supported(int num_tokens, int num_pairs, int num_experts) {
+  return num_tokens > 0 && num_tokens <= kTopkDispatchMaxTokens && num_pairs <= dispatch_detail::kThreads * 2 &&
+         num_experts <= 512;
+}
+
+cudaError_t launch_router_topk_dispatch(const RouterArgs& a, const DispatchArgs& d, cudaStream_t st) {
+  if (!router_topk_dispatch_supported(a.num_tokens, d.num_pairs, a.num_experts)) return cudaErrorNotSupported;
+  const size_t smem = dispatch_smem_bytes(d.num_experts);
+  const int epl = (a.num_experts + 31) / 32;
+#define SENMOE_TD_CASE(V)                                                                                   \
+  if (epl <= V) {                                                                                         \
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(router_topk_dispatch_kernel<V>), smem); \
+    if (e != cudaSuccess) return e;                                                                       \
+    return launch_pdl(router_topk_dispatch_kernel<V>, dim3(1), dim3(dispatch_detail::kThreads), smem, st, a, d); \
+  }
+  SENMOE_TD_CASE(1) SENMOE_TD_CASE(2) SENMOE_TD_CASE(4) SENMOE_TD_CASE(8) SENMOE_TD_CASE(16)
+#undef SENMOE_TD_CASE
   return cudaErrorNotSupported;
 }
 
