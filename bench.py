@@ -183,8 +183,9 @@ def launches_per_forward(T, tensor_cores, world):
     """Kernels one forward launches: the router (one kernel from 128 tokens,
     where top-k runs in the logits kernel's last CTAs or the tensor-core
     router; logits + top-k below), dispatch (one kernel up to 2048 pairs,
-    else three; up to 8 tokens top-k and dispatch share one launch), the expert-parallel fence and row gather, the
-    gathered-activation copy (tensor-core paths), gate/up, down, combine."""
+    else three; up to 8 tokens top-k and dispatch share one launch), the
+    expert-parallel fence and row gather, the gathered-activation copy
+    (tensor-core paths), gate/up, down, combine."""
     router = 1 if T >= 128 else 2
     disp = 1 if (T * K + 1023) // 1024 <= 2 else 3
     if T <= 8 and T * K <= 2048:
