@@ -87,16 +87,49 @@ def tensor_peak():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """SM clock and clock-event reasons during the timed region, read-only:
+    NVML polled from a background thread every 5 ms (a sample from the first
+    millisecond on), or `nvidia-smi -lms 20` where NVML is unavailable (its
+    start-up takes ~100 ms, so short regions get few samples)."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    NVML_BITS = ("nvmlClocksEventReasonHwSlowdown", "nvmlClocksEventReasonHwThermalSlowdown",
+                 "nvmlClocksEventReasonSwThermalSlowdown", "nvmlClocksEventReasonSwPowerCap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, gpu_index: int, pci_bus_id: str | None = None, period_s: float = 0.005):
+        self.gpu, self.pci, self.period = gpu_index, pci_bus_id, period_s
         self.proc = None
+        self.nv = None
+        self.samples = []   # NVML: (sm_mhz, reason bits)
+        self.lines = []     # nvidia-smi: csv lines
 
     def __enter__(self):
+        try:
+            import threading
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByPciBusId(self.pci) if self.pci else nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.nv, self.stop = nv, threading.Event()
+
+            def poll():
+                while True:
+                    try:
+                        self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), reasons(h)))
+                    except Exception:
+                        pass
+                    if self.stop.wait(self.period):
+                        return
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.nv = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                           "-i", str(self.gpu), "-lms", "20"], stdout=subprocess.PIPE,
@@ -106,7 +139,13 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
+        if self.nv is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            try:
+                self.nv.nvmlShutdown()
+            except Exception:
+                pass
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -118,21 +157,39 @@ class ClockSampler:
 
     def summary(self):
         sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
+        if self.nv is not None:
+            bits = [getattr(self.nv, b, 0) for b in self.NVML_BITS]
+            for mhz, r in self.samples:
+                sm.append(float(mhz))
+                for n, b in zip(self.NAMES, bits):
+                    if b and (r & b):
+                        reasons.add(n)
+            smax, source = float(self.smax), "nvml"
+        else:
+            source = "nvidia-smi"
+            for ln in self.lines:
+                f = [x.strip() for x in ln.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm.append(float(f[1]))
+                    smax = float(f[2])
+                except ValueError:
+                    continue
+                for n, v in zip(self.NAMES, f[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": source}
+
+
+def pci_bus_id(torch, device: int) -> str | None:
+    """The device's PCI bus id in NVML's form, or None."""
+    try:
+        p = torch.cuda.get_device_properties(device)
+        return f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+    except Exception:
+        return None
 
 
 # --------------------------------------------------------------- weights
@@ -390,7 +447,7 @@ def main():
     for T in batches:
         touched = touched_per_layer(layers, T)
         if T == args.batch:
-            with ClockSampler(local) as cs:
+            with ClockSampler(local, pci_bus_id(torch, local)) as cs:
                 secs = timed_steps(stack, T, args.steps, args.warmup)
             clocks = cs.summary()
         else:

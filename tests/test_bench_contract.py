@@ -53,3 +53,64 @@ def test_launch_count(T, world, expect):
     sys.path.insert(0, ROOT)
     import bench
     assert bench.launches_per_forward(T, True, world) == expect
+
+
+class _FakeNvml:
+    """Stands in for pynvml: a device whose SM clock and clock-event reasons
+    follow a script, so the bench's sampler is tested without a GPU (read-only
+    queries only; nothing here changes a setting)."""
+    NVML_CLOCK_SM = 1
+    nvmlClocksEventReasonSwPowerCap = 0x4
+    nvmlClocksEventReasonHwSlowdown = 0x8
+    nvmlClocksEventReasonSwThermalSlowdown = 0x20
+    nvmlClocksEventReasonHwThermalSlowdown = 0x40
+
+    def __init__(self, script):
+        self.script, self.i, self.calls = script, 0, []
+
+    def nvmlInit(self):
+        self.calls.append("init")
+
+    def nvmlShutdown(self):
+        self.calls.append("shutdown")
+
+    def nvmlDeviceGetHandleByPciBusId(self, bus):
+        self.calls.append(("pci", bus))
+        return "h"
+
+    def nvmlDeviceGetHandleByIndex(self, i):
+        self.calls.append(("index", i))
+        return "h"
+
+    def nvmlDeviceGetMaxClockInfo(self, h, which):
+        return 1965
+
+    def nvmlDeviceGetClockInfo(self, h, which):
+        return self.script[min(self.i, len(self.script) - 1)][0]
+
+    def nvmlDeviceGetCurrentClocksEventReasons(self, h):
+        r = self.script[min(self.i, len(self.script) - 1)][1]
+        self.i += 1
+        return r
+
+
+def test_clock_sampler_reads_nvml(monkeypatch):
+    import time
+    sys.path.insert(0, ROOT)
+    import bench
+    fake = _FakeNvml([(1965, 0), (1965, 0x4), (1890, 0x4)])
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    with bench.ClockSampler(0, "00000000:1b:00.0", period_s=0.002) as cs:
+        time.sleep(0.05)
+    s = cs.summary()
+    assert s["source"] == "nvml" and s["samples"] >= 3 and s["sm_max_mhz"] == 1965.0
+    assert s["reasons"] == ["sw_power_cap"]  # power cap seen; no slowdown reason
+    assert fake.calls[0] == "init" and ("pci", "00000000:1b:00.0") in fake.calls and fake.calls[-1] == "shutdown"
+
+    fake = _FakeNvml([(1000, 0x8 | 0x40)])
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    with bench.ClockSampler(2) as cs:
+        time.sleep(0.02)
+    s = cs.summary()
+    assert s["sm_mhz"] == 1000.0 and s["reasons"] == ["hw_slowdown", "hw_thermal_slowdown"]
+    assert ("index", 2) in fake.calls
