@@ -64,12 +64,15 @@ def test_peer_table_exchange_rejects_layer_count_mismatch():
         spawn_ranks("exchange", 2, 2, 1)
 
 
+@pytest.mark.parametrize("world", [2, 3])
 @pytest.mark.parametrize("bits", [4, 8])
-def test_expert_parallel_decomposition_is_exact(bits):
+def test_expert_parallel_decomposition_is_exact(bits, world):
+    """At 3 ranks the fixture's 8 experts split 2/3/3 and its 5 tokens 1/2/2:
+    uneven expert blocks and uneven token-owned combine blocks."""
     d = np.load(os.path.join(GOLD, f"moe_block_small_{bits}bit.npz"))
     cfg, w = fixture_layer(d)
     ref = N.moe_forward(cfg, w, d["x"])["y_f32"]
-    ys = spawn_ranks("decomposition", 2, bits)
+    ys = spawn_ranks("decomposition", world, bits)
     for y in ys:
         np.testing.assert_array_equal(y, ref)  # same rows, same slot order, same fp32 sums
     np.testing.assert_allclose(ys[0], d["y_f32"], rtol=0, atol=1e-4)
