@@ -293,14 +293,28 @@ int senmoe_quantized_linear(const void* x, int64_t num_tokens, const uint32_t* w
  * it for callers that cannot allocate device memory at call time: code inside
  * an open CUDA stream capture, serving loops whose HBM another allocator has
  * fully reserved, plugin hosts that forbid device allocation on the hot path).
- * Same result as senmoe_layer_forward for the same config, weights and x,
- * without a layer handle: all scratch lives in one fixed 4 MiB device array
- * inside the library (held by every GPU that loads it until exit), so
- * num_tokens is limited to what fits (config 0, H=2048 E=128 K=8 I=768: up to
- * 64 tokens); larger calls return SENMOE_ERR_BAD_ARG.  The first call on a
- * device resolves the array's address and should come before any stream
- * capture.  All calls share the array: calls that overlap on the GPU race, so
- * serialise them.  config->max_tokens bounds num_tokens as for a layer. */
+ * DeepseekMoe::forward without a layer handle: all scratch lives in one fixed
+ * 4 MiB device array inside the library (held by every GPU that loads it until
+ * exit).  It always runs the CUDA-core dequant-GEMV expert kernels and the
+ * router's logits and top-k as separate launches (the tensor-core paths need
+ * tensor maps that a layer encodes over its own scratch at create time), so
+ * its output agrees with senmoe_layer_forward within the block tolerance
+ * (max abs 2e-2, relative L2 5e-3), not bit for bit, and at decode batches
+ * it is slower (about 8x in gate/up at 64 tokens of config 0).
+ * Size limit: the scratch of one call is the sum of these pieces, each
+ * rounded up to 256 bytes, and must not exceed 4 MiB (P = num_tokens * K):
+ *   T*E*4, four of P*4, (E+1)*4, E*4, 4, 4, ceil(P/1024)*E*4, P*I*2, P*H*2,
+ *   and with a shared expert T*Is*2, T*H*2, T*4, T*4.
+ * That is 91 tokens at config 0 (H=2048 E=128 K=8 I=768) and 71 at H=2048
+ * E=512 K=10 I=512 with a 512-wide shared expert; larger calls return
+ * SENMOE_ERR_BAD_ARG.  config->max_tokens bounds num_tokens as for a layer.
+ * The first call on a device resolves the array's address (once per device,
+ * kept for the life of the process) and should come before any stream
+ * capture; after cudaDeviceReset that address is stale, so do not call this
+ * entry point again in that process.  All calls share the array, which keeps
+ * the last call's contents: calls that overlap on the GPU race, so serialise
+ * them.  Device-side errors (an expert id out of range) are not reported on
+ * this path: each call clears the array's error word and nothing reads it. */
 int senmoe_moe_forward_noalloc(const SenMoeConfig* config, const SenMoeWeights* weights, const void* x,
                                int64_t num_tokens, void* y, senmoe_stream_t stream);
 

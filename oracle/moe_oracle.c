@@ -171,16 +171,30 @@ static inline uint32_t code_at(const uint32_t* row, int64_t c, int32_t bits) {
   return (row[c / per_word] >> ((c % per_word) * bits)) & ((1u << bits) - 1u);
 }
 
-/* w[r][c] = q * scale + bias, evaluated in fp32 (utils/moe.rs:28-31). */
+/* w[r][c] = q * scale + bias, evaluated in fp32 (utils/moe.rs:28-31).
+ * Unpacks word by word (lower columns in lower bits); the same arithmetic
+ * as (float)code_at(row, c, bits) * sc + bi per element. */
 static void dequant_row(const uint32_t* wq, const uint16_t* s, const uint16_t* b, int64_t r, int64_t cols,
                         int32_t group, int32_t bits, float* out) {
   const int64_t ngroups = cols / group;
+  const int per_word = 32 / bits, words_per_group = group / per_word;
+  const uint32_t mask = (1u << bits) - 1u;
   const uint32_t* row = wq + r * (cols * bits / 32);
   for (int64_t g = 0; g < ngroups; ++g) {
     const float sc = bf2f(s[r * ngroups + g]), bi = bf2f(b[r * ngroups + g]);
-    for (int64_t i = 0; i < group; ++i) {
-      const int64_t c = g * group + i;
-      out[c] = (float)code_at(row, c, bits) * sc + bi;
+    const uint32_t* wp = row + g * words_per_group;
+    float* o = out + g * group;
+    if (bits == 4) { /* constant trip counts, so the compiler can vectorise */
+      for (int w = 0; w < words_per_group; ++w)
+        for (int j = 0; j < 8; ++j) o[w * 8 + j] = (float)((wp[w] >> (j * 4)) & 15u) * sc + bi;
+    } else if (bits == 8) {
+      for (int w = 0; w < words_per_group; ++w)
+        for (int j = 0; j < 4; ++j) o[w * 4 + j] = (float)((wp[w] >> (j * 8)) & 255u) * sc + bi;
+    } else {
+      for (int w = 0; w < words_per_group; ++w) {
+        const uint32_t word = wp[w];
+        for (int j = 0; j < per_word; ++j) o[w * per_word + j] = (float)((word >> (j * bits)) & mask) * sc + bi;
+      }
     }
   }
 }
@@ -369,52 +383,69 @@ int orc_dispatch(const int32_t* ids, int64_t T, int32_t K, int32_t E, int32_t* p
 }
 
 /* Gated expert MLP (SwiGLU: deepseek_v2.rs:466-478 and the dense twin
- * :389-392; GeGLU: gemma4.rs:809-823) over the slots of one expert.  xs: n rows of in=H floats (already bf16 values);
- * out: n rows of H floats, rounded per mode.  Weights are one expert's slice. */
+ * :389-392; GeGLU: gemma4.rs:809-823) over the slots of one expert.  xs: n rows of in=H floats (already bf16 values),
+ * padded with zero rows to a multiple of ORC_TB; hbuf: ceil(n/ORC_TB)*ORC_TB rows of I; out: n rows of H floats,
+ * rounded per mode.  Weights are one expert's slice.
+ * Each dot product sums fp32 products per 64-column group (8 partial sums
+ * in column order) and the groups in double; ORC_TB tokens share one pass
+ * over a dequantized weight row, each token keeping exactly that order. */
+#define ORC_TB 4
+/* AVX2 clone where the host CPU has it (same arithmetic: no contraction, no
+ * reassociation), the baseline x86-64 build otherwise */
+__attribute__((target_clones("avx2", "default")))
 static void glu_expert(const OrcConfig* cfg, int64_t H, int64_t I, const uint32_t* gw, const uint16_t* gs,
                           const uint16_t* gb, const uint32_t* uw, const uint16_t* us, const uint16_t* ub,
                           const uint32_t* dw, const uint16_t* ds, const uint16_t* db, const float* xs, int64_t n,
                           float* hbuf, float* rowg, float* rowu, float* out) {
   const int32_t G = cfg->group_size, B = cfg->bits, mode = cfg->mode;
+  const int64_t nb = (n + ORC_TB - 1) / ORC_TB * ORC_TB;
   for (int64_t i = 0; i < I; ++i) {
     dequant_row(gw, gs, gb, i, H, G, B, rowg);
     dequant_row(uw, us, ub, i, H, G, B, rowu);
-    for (int64_t r = 0; r < n; ++r) {
-      const float* xr = xs + r * H;
-      double ag = 0.0, au = 0.0;
+    for (int64_t r0 = 0; r0 < nb; r0 += ORC_TB) {
+      double ag[ORC_TB] = {0}, au[ORC_TB] = {0};
       for (int64_t c0 = 0; c0 < H; c0 += G) { /* fp32 within a group, double across groups */
-        float pg[8] = {0}, pu[8] = {0};
+        float pg[ORC_TB][8] = {{0}}, pu[ORC_TB][8] = {{0}};
         for (int64_t c = c0; c < c0 + G; c += 8)
-          for (int k = 0; k < 8; ++k) {
-            pg[k] += rowg[c + k] * xr[c + k];
-            pu[k] += rowu[c + k] * xr[c + k];
+          for (int t = 0; t < ORC_TB; ++t) {
+            const float* xr = xs + (r0 + t) * H + c;
+            for (int k = 0; k < 8; ++k) {
+              pg[t][k] += rowg[c + k] * xr[k];
+              pu[t][k] += rowu[c + k] * xr[k];
+            }
           }
-        for (int k = 0; k < 8; ++k) {
-          ag += pg[k];
-          au += pu[k];
-        }
+        for (int t = 0; t < ORC_TB; ++t)
+          for (int k = 0; k < 8; ++k) {
+            ag[t] += pg[t][k];
+            au[t] += pu[t][k];
+          }
       }
-      const float g = maybe_rbf((float)ag, mode), u = maybe_rbf((float)au, mode);
-      /* SwiGLU: nn::silu(g) = g * sigmoid(g), one bf16 rounding per op;
-       * GeGLU: nn::gelu_approximate(g) rounded once to bf16 (assumed: one
-       * fused activation op, as MLX compiles its elementwise chains) */
-      const float a = cfg->activation == 1 ? maybe_rbf(gelu_tanh_(g), mode)
-                                           : maybe_rbf(g * maybe_rbf(sigmoidf_(g), mode), mode);
-      hbuf[r * I + i] = maybe_rbf(a * u, mode);
+      for (int t = 0; t < ORC_TB; ++t) {
+        const float g = maybe_rbf((float)ag[t], mode), u = maybe_rbf((float)au[t], mode);
+        /* SwiGLU: nn::silu(g) = g * sigmoid(g), one bf16 rounding per op;
+         * GeGLU: nn::gelu_approximate(g) rounded once to bf16 (assumed: one
+         * fused activation op, as MLX compiles its elementwise chains) */
+        const float a = cfg->activation == 1 ? maybe_rbf(gelu_tanh_(g), mode)
+                                             : maybe_rbf(g * maybe_rbf(sigmoidf_(g), mode), mode);
+        hbuf[(r0 + t) * I + i] = maybe_rbf(a * u, mode);
+      }
     }
   }
   for (int64_t o = 0; o < H; ++o) {
     dequant_row(dw, ds, db, o, I, G, B, rowg);
-    for (int64_t r = 0; r < n; ++r) {
-      const float* hr = hbuf + r * I;
-      double acc = 0.0;
+    for (int64_t r0 = 0; r0 < nb; r0 += ORC_TB) {
+      double acc[ORC_TB] = {0};
       for (int64_t c0 = 0; c0 < I; c0 += G) {
-        float p[8] = {0};
+        float p[ORC_TB][8] = {{0}};
         for (int64_t c = c0; c < c0 + G; c += 8)
-          for (int k = 0; k < 8; ++k) p[k] += rowg[c + k] * hr[c + k];
-        for (int k = 0; k < 8; ++k) acc += p[k];
+          for (int t = 0; t < ORC_TB; ++t) {
+            const float* hr = hbuf + (r0 + t) * I + c;
+            for (int k = 0; k < 8; ++k) p[t][k] += rowg[c + k] * hr[k];
+          }
+        for (int t = 0; t < ORC_TB; ++t)
+          for (int k = 0; k < 8; ++k) acc[t] += p[t][k];
       }
-      out[r * H + o] = maybe_rbf((float)acc, mode);
+      for (int t = 0; t < ORC_TB && r0 + t < n; ++t) out[(r0 + t) * H + o] = maybe_rbf((float)acc[t], mode);
     }
   }
 }
@@ -457,7 +488,8 @@ static int moe_forward_impl(const OrcConfig* cfg, const OrcWeights* wt, const ui
   {
     int64_t maxn = 0;
     for (int64_t e = 0; e < E; ++e) maxn = offs[e + 1] - offs[e] > maxn ? offs[e + 1] - offs[e] : maxn;
-    float* xs = (float*)malloc(sizeof(float) * (size_t)(maxn * H + 1));
+    maxn = (maxn + ORC_TB - 1) / ORC_TB * ORC_TB; /* glu_expert reads whole blocks of ORC_TB rows */
+    float* xs = (float*)calloc((size_t)(maxn * H + 1), sizeof(float));
     float* hb = (float*)malloc(sizeof(float) * (size_t)(maxn * I + 1));
     float* rg = (float*)malloc(sizeof(float) * (size_t)(H > I ? H : I));
     float* ru = (float*)malloc(sizeof(float) * (size_t)H);
@@ -471,6 +503,7 @@ static int moe_forward_impl(const OrcConfig* cfg, const OrcWeights* wt, const ui
         const int64_t s0 = offs[e], n = offs[e + 1] - offs[e];
         if (n == 0) continue;
         for (int64_t r = 0; r < n; ++r) memcpy(xs + r * H, xf + (perm[s0 + r] / K) * H, sizeof(float) * (size_t)H);
+        for (int64_t r = n; r % ORC_TB; ++r) memset(xs + r * H, 0, sizeof(float) * (size_t)H);
         glu_expert(cfg, H, I, wt->gate_w + e * wsg, wt->gate_s + e * ssg, wt->gate_b + e * ssg,
                       wt->up_w + e * wsg, wt->up_s + e * ssg, wt->up_b + e * ssg, wt->down_w + e * wsd,
                       wt->down_s + e * ssd, wt->down_b + e * ssd, xs, n, hb, rg, ru, ob);
@@ -499,27 +532,34 @@ static int moe_forward_impl(const OrcConfig* cfg, const OrcWeights* wt, const ui
     const int64_t Is = cfg->shared_intermediate;
 #pragma omp parallel
     {
-      float* hb = (float*)malloc(sizeof(float) * (size_t)Is);
+      float* xs = (float*)calloc((size_t)(ORC_TB * H), sizeof(float));
+      float* hb = (float*)malloc(sizeof(float) * (size_t)(ORC_TB * Is));
       float* rg = (float*)malloc(sizeof(float) * (size_t)(H > Is ? H : Is));
       float* ru = (float*)malloc(sizeof(float) * (size_t)H);
-      float* ob = (float*)malloc(sizeof(float) * (size_t)H);
-      if (!hb || !rg || !ru || !ob) {
+      float* ob = (float*)malloc(sizeof(float) * (size_t)(ORC_TB * H));
+      if (!xs || !hb || !rg || !ru || !ob) {
 #pragma omp atomic write
         err = ORC_NO_MEM;
       } else {
 #pragma omp for schedule(dynamic, 1)
-        for (int64_t t = 0; t < T; ++t) {
+        for (int64_t t0 = 0; t0 < T; t0 += ORC_TB) { /* ORC_TB tokens per pass over the shared weights */
+          const int64_t n = T - t0 < ORC_TB ? T - t0 : ORC_TB;
+          memcpy(xs, xf + t0 * H, sizeof(float) * (size_t)(n * H));
+          memset(xs + n * H, 0, sizeof(float) * (size_t)((ORC_TB - n) * H));
           glu_expert(cfg, H, Is, wt->sh_gate_w, wt->sh_gate_s, wt->sh_gate_b, wt->sh_up_w, wt->sh_up_s,
-                        wt->sh_up_b, wt->sh_down_w, wt->sh_down_s, wt->sh_down_b, xf + t * H, 1, hb, rg, ru, ob);
-          float gate = 1.0f;
-          if (cfg->shared_gate) {
-            double a = 0.0;
-            for (int64_t h = 0; h < H; ++h) a += (double)xf[t * H + h] * (double)bf2f(wt->sh_gate_vec[h]);
-            gate = sigmoidf_((float)a);
+                        wt->sh_up_b, wt->sh_down_w, wt->sh_down_s, wt->sh_down_b, xs, n, hb, rg, ru, ob);
+          for (int64_t t = t0; t < t0 + n; ++t) {
+            float gate = 1.0f;
+            if (cfg->shared_gate) {
+              double a = 0.0;
+              for (int64_t h = 0; h < H; ++h) a += (double)xf[t * H + h] * (double)bf2f(wt->sh_gate_vec[h]);
+              gate = sigmoidf_((float)a);
+            }
+            for (int64_t h = 0; h < H; ++h) y_f32[t * H + h] += gate * ob[(t - t0) * H + h];
           }
-          for (int64_t h = 0; h < H; ++h) y_f32[t * H + h] += gate * ob[h];
         }
       }
+      free(xs);
       free(hb);
       free(rg);
       free(ru);

@@ -26,8 +26,8 @@
 //              activation tile (2-D tensor map, SWIZZLE_128B), and once per
 //              tile the rows' scales and biases (1-D bulk copies).  No
 //              multicast anywhere.
-//   warp 1     TMEM owner; one lane issues tcgen05.mma (kind::f16, bf16 x
-//              bf16 -> fp32, M=128, N=BN, K=16) and tcgen05.commit.
+//   warp 1     TMEM owner; one lane issues tcgen05.mma (kind::f16, fp16 x
+//              fp16 -> fp32, M=128, N=BN, K=16) and tcgen05.commit.
 //   warps 2-17 dequantise each 64-column k-block of codes to fp16
 //              (w = q * scale + bias, one rounding) straight into TMEM with
 //              tcgen05.st: the MMA reads its A operand from TMEM, so the

@@ -102,7 +102,9 @@ class SafetensorsCheckpoint:
         count = int(np.prod(shape)) if shape else 1
         if (end - start) != count * np.dtype(dt).itemsize:
             raise ValueError(f"{name}: data size {end - start} does not match shape {shape} x {meta['dtype']}")
-        return np.memmap(path, dtype=dt, mode="r", offset=base + start, shape=shape)
+        # a scalar tensor (shape []) is mapped as one element and reshaped
+        m = np.memmap(path, dtype=dt, mode="r", offset=base + start, shape=shape if shape else (1,))
+        return m if shape else m.reshape(())
 
 
 def _bf16_bits(ckpt: SafetensorsCheckpoint, name: str) -> np.ndarray:
@@ -112,7 +114,13 @@ def _bf16_bits(ckpt: SafetensorsCheckpoint, name: str) -> np.ndarray:
         return np.asarray(a)
     f = np.ascontiguousarray(a, dtype=np.float32)
     u = f.view(np.uint32).astype(np.uint64)
-    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)  # round to nearest even
+    out = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)  # round to nearest even
+    # NaN stays a NaN of the same sign (rounding its payload could carry into
+    # the exponent and give Inf or flip the sign); quiet NaN 0x7FC0 / 0xFFC0
+    nan = np.isnan(f)
+    if nan.any():
+        out[nan] = np.where(np.signbit(f[nan]), 0xFFC0, 0x7FC0).astype(np.uint16)
+    return out.reshape(np.shape(a))  # ascontiguousarray makes a 0-d input 1-d
 
 
 def _to_device(a: np.ndarray, device, bf16: bool = False) -> torch.Tensor:

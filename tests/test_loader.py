@@ -168,3 +168,23 @@ def test_bad_tensor_size_is_rejected(tmp_path):
     ck = loader.SafetensorsCheckpoint(str(tmp_path))
     with pytest.raises(ValueError):
         ck.get("a")
+
+
+def test_float_to_bf16_keeps_nan_and_scalar_tensors(tmp_path):
+    """fp32 -> bf16 conversion rounds to nearest even and keeps every NaN a
+    NaN of the same sign (a payload in the low mantissa bits must not round
+    to Inf); a 0-d tensor reads back as a 0-d array."""
+    from senmoe import loader
+    bits = np.array([0x7F800001, 0xFF800001, 0x7FFFFFFF, 0xFFFFFFFF, 0x7FC00000, 0x3F808000, 0x3F818000,
+                     0x7F7FFFFF, 0x00000001], np.uint32)
+    f = bits.view(np.float32)
+    write_safetensors(os.path.join(tmp_path, "model.safetensors"),
+                      {"v": ("F32", f), "s": ("F32", np.array(2.5, np.float32))})
+    ck = loader.SafetensorsCheckpoint(str(tmp_path))
+    got = loader._bf16_bits(ck, "v")
+    np.testing.assert_array_equal(got[:5], [0x7FC0, 0xFFC0, 0x7FC0, 0xFFC0, 0x7FC0])
+    # 1.00390625 is a tie (rounds to even 1.0); 1.01171875 is a tie that rounds up
+    np.testing.assert_array_equal(got[5:], [0x3F80, 0x3F82, 0x7F80, 0x0000])
+    s = ck.get("s")
+    assert s.shape == () and float(s) == 2.5
+    assert loader._bf16_bits(ck, "s").shape == ()
