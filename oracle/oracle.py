@@ -345,3 +345,27 @@ def gemma_router(rc: GemmaRouterConfig, rw: GemmaRouterWeights, x_bf16: np.ndarr
     _check(lib().orc_gemma_router(C.byref(c), C.byref(cw), _ptr(x), T, _ptr(ids), _ptr(wts), _ptr(scores)),
            "gemma_router")
     return ids, wts, scores
+
+
+def moe_residual(cfg: MoeConfig, w: MoeWeights, x_bf16: np.ndarray, mode: int = 0):
+    """One decoder step of the MoE stack, h = x + DeepseekMoe::forward(x)
+    (DecoderLayer::forward's residual add, deepseek_v2.rs:613-620), with the
+    block's f32 sum and x added in f32 and rounded to bf16 once, as the GPU
+    block's fused residual does.  Returns (h bf16 bits [T, H], the forward's
+    dict)."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16).reshape(-1, cfg.hidden)
+    out = moe_forward(cfg, w, x, mode=mode)
+    return f32_to_bf16(bf16_to_f32(x) + out["y_f32"]), out
+
+
+def weights_from_synth(mw: dict) -> MoeWeights:
+    """oracle MoeWeights from numpy tensors named as senmoe.synth.layer_numpy returns them."""
+    u16 = lambda a: None if a is None else np.ascontiguousarray(a, dtype=np.uint16)
+    u32 = lambda a: None if a is None else np.ascontiguousarray(a).view(np.uint32)
+    w = MoeWeights(u16(mw["router_w"]), u32(mw["gate_w"]), u16(mw["gate_s"]), u16(mw["gate_b"]), u32(mw["up_w"]),
+                   u16(mw["up_s"]), u16(mw["up_b"]), u32(mw["down_w"]), u16(mw["down_s"]), u16(mw["down_b"]))
+    for k in ("sh_gate_w", "sh_up_w", "sh_down_w"):
+        setattr(w, k, u32(mw.get(k)))
+    for k in ("sh_gate_s", "sh_gate_b", "sh_up_s", "sh_up_b", "sh_down_s", "sh_down_b", "sh_gate_vec"):
+        setattr(w, k, u16(mw.get(k)))
+    return w

@@ -101,3 +101,31 @@ def fixture_layer(d):
                   "sh_down_s", "sh_down_b", "sh_gate_vec"):
             setattr(w, k, d[k])
     return cfg, w
+
+
+def routing_mismatches(ids_gpu, ids_ref, scores_ref, ulp_rel=2.0 ** -7):
+    """Tokens whose ordered top-k ids differ between the GPU and the oracle,
+    and whether every one of them is explained by a router tie: a differing
+    expert of the top-k SET within one bf16 ulp of the k-th reference score,
+    or (same set, other order) slot pairs whose reference scores lie within
+    one bf16 ulp of each other.  Returns (mismatched token indices, all_ties)."""
+    ids_gpu = np.asarray(ids_gpu)
+    ids_ref = np.asarray(ids_ref)
+    bad = np.nonzero((ids_gpu != ids_ref).any(axis=1))[0]
+    for t in bad:
+        a, b = ids_gpu[t].tolist(), ids_ref[t].tolist()
+        if set(a) != set(b):
+            kth = scores_ref[t, b[-1]]
+            if not all(abs(scores_ref[t, e] - kth) <= ulp_rel * abs(kth) for e in set(a) ^ set(b)):
+                return bad, False
+        else:
+            for ea, eb in zip(a, b):
+                if ea != eb and abs(scores_ref[t, ea] - scores_ref[t, eb]) > ulp_rel * max(abs(scores_ref[t, eb]),
+                                                                                           1e-30):
+                    return bad, False
+    return bad, True
+
+
+def max_dropped(num_tokens: int) -> int:
+    """Tokens a parity check may leave out for router ties: 1 % of T, at least one."""
+    return max(1, num_tokens // 100)

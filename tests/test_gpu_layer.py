@@ -9,8 +9,8 @@ import os
 import numpy as np
 import pytest
 
-from helpers import (MAX_ABS_TOL, REL_L2_TOL, bf16_np_to_f32, device_weights, fixture_layer, moe_args, rel_l2,
-                     t_bf16, to_numpy_bf16, topk_match_except_ties)
+from helpers import (MAX_ABS_TOL, REL_L2_TOL, bf16_np_to_f32, device_weights, fixture_layer, max_dropped, moe_args,
+                     rel_l2, routing_mismatches, t_bf16, to_numpy_bf16, topk_match_except_ties)
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -49,12 +49,19 @@ def run_block(senmoe, cfg, mw, x_bits, max_tokens=None, path=0, mma_form=0):
 
 
 def check_against_oracle(cfg, mw, x, got):
+    """Top-k ids equal except router ties (each mismatching token must be a
+    tie, and at most 1 % of the tokens may mismatch), dispatch bit-exact
+    when nothing mismatches, block outputs of the other tokens within the
+    tolerance."""
     ref = O.moe_forward(cfg, mw, x, mode=0)
     _, _, scores = O.router(cfg, mw, x)
     ok, ties = topk_match_except_ties(got["topk_ids"], ref["ids"], scores)
     assert ok, "top-k ids differ beyond router ties"
+    bad, all_ties = routing_mismatches(got["topk_ids"], ref["ids"], scores)
+    assert all_ties, f"top-k order differs beyond router ties (tokens {bad.tolist()[:8]})"
+    assert bad.size <= max_dropped(x.shape[0]), f"{bad.size} of {x.shape[0]} tokens differ in routing"
     same = (got["topk_ids"] == ref["ids"]).all(axis=1)
-    if ties == 0:
+    if bad.size == 0:
         # dispatch is a pure function of the ids: bit-exact
         np.testing.assert_array_equal(got["perm"], ref["perm"])
         np.testing.assert_array_equal(got["offsets"], ref["offsets"])
