@@ -19,8 +19,9 @@
 // Three rank flags per layer order the exchange, all in the flag block of
 // each rank's arena and all holding a call epoch:
 //   ready[r]  rank r's expert rows of epoch e are complete (written by r's
-//             combine kernel into every peer's block before it reads), and
-//             r has finished reading its exchange of epoch e - 1;
+//             announce kernel, right after its expert kernels, into every
+//             rank's block), and r has finished reading its exchange of
+//             epoch e - 1;
 //   done[r]   rank r has finished reading its peers' rows of epoch e (written
 //             by the last CTA of r's combine);
 //   rows[r]   rank r's combined rows of epoch e are in this rank's exchange
@@ -77,6 +78,21 @@ __global__ void ep_fence_kernel(EpArgs a) {
   pdl_wait();  // the expert kernels after this one wait on it, and through it on dispatch
 }
 
+// ready[rank] := epoch in every rank's flag block (its own included): this
+// rank's expert rows of the call are complete.  One warp, launched right
+// after the down projection: griddepcontrol.wait returns once the expert
+// kernels have finished and their writes are visible, one system-scope fence
+// orders them before the flag stores, and each peer gets one release store.
+__global__ void ep_announce_kernel(EpArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const uint32_t epoch = *a.epoch;
+  if (threadIdx.x == 0) __threadfence_system();
+  __syncwarp();
+  const int r = threadIdx.x;
+  if (r < a.world) st_release_sys(a.peer_flags[r] + kEpReadyOffset + a.rank, epoch);
+}
+
 // Expert-rows owner of expert e: the rank r with bounds[r] <= e < bounds[r+1].
 __device__ __forceinline__ int owner_of(const EpArgs& a, int e) {
   int r = 0;
@@ -91,14 +107,13 @@ __device__ __forceinline__ int owner_of(const EpArgs& a, int e) {
 // the rank's tokens.
 template <int KMAX>  // compile-time bound on top_k sizing the per-thread arrays
 __global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) ep_combine_kernel(EpArgs a, CombineArgs c, int num_tokens) {
-  pdl_wait();  // d, ids, inverse and weights of this call are complete
+  pdl_wait();  // d, ids, inverse and weights of this call are complete; ready[rank] is announced
   pdl_launch_dependents();
   const uint32_t epoch = *a.epoch;
   const int r = threadIdx.x;
-  if (r < a.world) {
-    // announce this rank's rows (d is complete: the producing grids finished)
-    __threadfence_system();
-    st_release_sys(a.peer_flags[r] + kEpReadyOffset + a.rank, epoch);
+  // every peer's rows of this call are complete (their announce kernels);
+  // the flags live in this rank's own memory, so the polls stay local
+  if (r < a.world && r != a.rank) {
     if (!wait_flag(a.flags + kEpReadyOffset + r, epoch, a.err)) record_error(a.err, kDevPeerTimeout);
   }
   __syncthreads();
@@ -142,7 +157,8 @@ __global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) ep_combine_kernel(EpAr
       }
       if (c.shared_out) {
         const float g = c.shared_gate ? c.shared_gate[t] : 1.0f;
-        const uint4 v = *reinterpret_cast<const uint4*>(c.shared_out + static_cast<size_t>(t) * c.hidden + col);
+        const uint4 v =
+            *reinterpret_cast<const uint4*>(c.shared_out + static_cast<size_t>(t - c.shared_row0) * c.hidden + col);
         acc[0] += g * bf16_lo(v.x); acc[1] += g * bf16_hi(v.x);
         acc[2] += g * bf16_lo(v.y); acc[3] += g * bf16_hi(v.y);
         acc[4] += g * bf16_lo(v.z); acc[5] += g * bf16_hi(v.z);
@@ -166,15 +182,17 @@ __global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) ep_combine_kernel(EpAr
   }
 
   // The last CTA to finish tells every peer that this rank is done reading
-  // and that its combined rows are in the peer's exchange.  Every thread
-  // fences its own peer stores before the CTA counts itself finished.
+  // and that its combined rows are in the peer's exchange.  The barrier
+  // orders the CTA's peer loads and stores before thread 0, whose one
+  // system-scope fence (cumulative) orders them before the CTA counts itself
+  // finished; the last CTA fences again before raising the flags.
   __shared__ bool s_last;
-  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const uint32_t total = gridDim.x * gridDim.y;
     s_last = atomicAdd(a.finished, 1u) == total - 1u;
-    __threadfence_system();
+    if (s_last) __threadfence_system();
   }
   __syncthreads();
   if (s_last) {
@@ -215,6 +233,10 @@ __global__ void __launch_bounds__(256) ep_gather_rows_kernel(EpArgs a, uint16_t*
 
 cudaError_t launch_ep_fence(const EpArgs& a, cudaStream_t st) {
   return launch_pdl(ep_fence_kernel, dim3(1), dim3(32), 0, st, a);
+}
+
+cudaError_t launch_ep_announce(const EpArgs& a, cudaStream_t st) {
+  return launch_pdl(ep_announce_kernel, dim3(1), dim3(32), 0, st, a);
 }
 
 cudaError_t launch_ep_combine(const EpArgs& a, const CombineArgs& c, int num_tokens, cudaStream_t st) {

@@ -259,7 +259,8 @@ __global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) combine_kernel(Combine
   }
   if (a.shared_out) {
     const float g = a.shared_gate ? a.shared_gate[t] : 1.0f;
-    const uint4 v = *reinterpret_cast<const uint4*>(a.shared_out + static_cast<size_t>(t) * a.hidden + col);
+    const uint4 v =
+        *reinterpret_cast<const uint4*>(a.shared_out + static_cast<size_t>(t - a.shared_row0) * a.hidden + col);
     acc[0] += g * bf16_lo(v.x); acc[1] += g * bf16_hi(v.x);
     acc[2] += g * bf16_lo(v.y); acc[3] += g * bf16_hi(v.y);
     acc[4] += g * bf16_lo(v.z); acc[5] += g * bf16_hi(v.z);

@@ -746,9 +746,17 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
                                                           const int32_t* __restrict__ perm, int k_div,
                                                           uint16_t* __restrict__ out, int num_slots, int hidden,
                                                           int* err, const int32_t* __restrict__ offsets, int eb,
-                                                          int ee, int order, float* __restrict__ group_sums) {
+                                                          int ee, int order, float* __restrict__ group_sums,
+                                                          int32_t* __restrict__ one_group) {
   pdl_wait();
   pdl_launch_dependents();
+  if (one_group && blockIdx.x == 0 && threadIdx.x == 0) {
+    // the consuming GEMMs' tile list: one group (local index 0) of num_slots slots
+    one_group[0] = 0;          // offsets[0]
+    one_group[1] = num_slots;  // offsets[1]
+    one_group[2] = 0;          // active[0]
+    one_group[3] = 1;          // active count
+  }
   const int s0 = blockIdx.x * kGatherSlots;
   int lo_slot = 0, hi_slot = num_slots;
   if (offsets) {  // expert parallelism: only this rank's slots
@@ -864,12 +872,13 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
 
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
                                int num_slots, int hidden, int* err, cudaStream_t st,
-                               const int32_t* offsets, int eb, int ee, int order, float* group_sums) {
+                               const int32_t* offsets, int eb, int ee, int order, float* group_sums,
+                               int32_t* one_group) {
   if (num_slots <= 0) return cudaSuccess;
   const int threads = hidden / 8 < 256 ? ((hidden / 8 + 31) / 32) * 32 : 256;
   const int grid = (num_slots + kGatherSlots - 1) / kGatherSlots;
   return launch_pdl(gather_rows_kernel, dim3(grid), dim3(threads), 0, st, x, perm, k_div, x_sorted, num_slots,
-                    hidden, err, offsets, eb, ee, order, order == kOrderMmaG4 ? group_sums : nullptr);
+                    hidden, err, offsets, eb, ee, order, order == kOrderMmaG4 ? group_sums : nullptr, one_group);
 }
 
 }  // namespace senmoe

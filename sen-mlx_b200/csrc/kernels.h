@@ -127,7 +127,8 @@ struct CombineArgs {
   const uint16_t* d;        // bf16 [P, H] expert outputs in slot order
   const int32_t* inverse;   // [T*K]
   const float* weights;     // [T*K]
-  const uint16_t* shared_out;  // bf16 [T, H] or null
+  const uint16_t* shared_out;  // bf16 [rows, H] or null; row i holds token shared_row0 + i
+  int shared_row0;
   const float* shared_gate;    // fp32 [T] gate per token (already sigmoid) or null
   const uint16_t* residual;    // bf16 [T, H] added before rounding (fused residual) or null
   uint16_t* y;              // bf16 [T, H]
@@ -177,11 +178,14 @@ enum ActivationOrder { kOrderTc = 0, kOrderMma = 1, kOrderMmaG4 = 2 };
 // With kOrderMmaG4 and `group_sums` non-null, group_sums[s * hidden/64 + G]
 // also receives 2^-24 * (the fp32 sum of x[perm[s]/k_div, 64 G .. 64 G + 63])
 // for every gathered slot: the group sums the group-scaled gate/up kernel
-// post-scales with.
+// post-scales with.  With `one_group` non-null (int32 [4]) the kernel also
+// writes a one-group tile list for the consuming GEMMs: offsets {0,
+// num_slots}, active {0}, count 1 (the shared expert as a grouped GEMM of
+// one expert over every gathered row).
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
                                int num_slots, int hidden, int* err, cudaStream_t st,
                                const int32_t* offsets = nullptr, int eb = 0, int ee = 0, int order = kOrderTc,
-                               float* group_sums = nullptr);
+                               float* group_sums = nullptr, int32_t* one_group = nullptr);
 
 // ------------------------------------------- warp-MMA expert GEMM (decode)
 // Same arguments as the tcgen05 GEMM (TcGemmArgs; out holds h as fp16 in
@@ -229,9 +233,12 @@ struct EpArgs {
 // Waits (bounded) until every peer has finished reading this rank's rows of
 // the previous call; advances the call epoch.  Launch before the expert kernels.
 cudaError_t launch_ep_fence(const EpArgs& a, cudaStream_t st);
-// Announces this rank's rows, waits (bounded) for every peer's, and runs the
-// weighted combine of this rank's tokens, reading each pair's row from its
-// owner (CombineArgs.d unused); every combined row goes to c.y and to each
+// Announces this rank's expert rows of the call (ready[rank] in every rank's
+// flags).  Launch right after the expert kernels.
+cudaError_t launch_ep_announce(const EpArgs& a, cudaStream_t st);
+// Waits (bounded) for every peer's rows and runs the weighted combine of
+// this rank's tokens, reading each pair's row from its owner
+// (CombineArgs.d unused); every combined row goes to c.y and to each
 // peer's exchange, and the last CTA raises rows[rank] in every peer's flags.
 cudaError_t launch_ep_combine(const EpArgs& a, const CombineArgs& c, int num_tokens, cudaStream_t st);
 // Waits (bounded) for every peer's combined rows and copies the tokens this

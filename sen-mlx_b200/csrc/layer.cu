@@ -17,6 +17,7 @@
 #include <cstring>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "../../include/senmoe.h"
 #include "kernels.h"
@@ -142,6 +143,16 @@ struct SenMoeLayer {
   // warp-MMA path
   bool mma_ok = false;
   CUtensorMap tm_xs8{}, tm_h8{};              // 8-slot activation tiles
+  // shared expert on the tensor-core kernels: a grouped GEMM of one expert
+  // over the rows gathered from x (sh_tc_ok / sh_mma_ok: the shapes allow it)
+  bool sh_tc_ok = false, sh_mma_ok = false;
+  uint16_t* xs_sh = nullptr;     // fp16 [Tmax, H] gathered rows of x
+  uint16_t* hsh16 = nullptr;     // fp16 [Tmax, Is] activation (B operand of the shared down GEMM)
+  float* xsum_sh = nullptr;      // [Tmax + 16, H/64] group sums (group-scaled form)
+  int32_t* sh_iota = nullptr;    // [Tmax] identity permutation
+  int32_t* sh_group = nullptr;   // [4] one-group tile list (written by the shared gather)
+  CUtensorMap tm_shg{}, tm_shu{}, tm_shd{};   // shared gate / up / down codes
+  CUtensorMap tm_xsh[4]{}, tm_hsh[4]{}, tm_xsh8{}, tm_hsh8{};
   // expert parallelism (senmoe_layer_connect_peers)
   size_t arena_bytes = 0, o_d = 0, o_flags = 0, o_yx = 0;
   uint32_t* ep_flags = nullptr;  // ready[8], done[8], rows[8]: written by peers
@@ -264,7 +275,9 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                o_shg = take(Is ? T * 4 : 0), o_zero = take(Is ? T * 4 : 0), o_xs = take(P * H * 2),
                o_h16 = take(P * I * 2), o_flags = take(kEpFlagBytes), o_local = take(8),
                o_route = take((T + 3) / 4 * 4), o_yx = take(T * H * 2),
-               o_xsum = take((P + 16) * (H / 64) * 4);
+               o_xsum = take((P + 16) * (H / 64) * 4), o_xssh = take(Is ? T * H * 2 : 0),
+               o_hsh = take(Is ? T * Is * 2 : 0), o_xsumsh = take(Is ? (T + 16) * (H / 64) * 4 : 0),
+               o_iota = take(Is ? T * 4 : 0), o_shgrp = take(Is ? 16 : 0);
   cudaError_t e = cudaMalloc(&L->arena, off);
   if (e != cudaSuccess) {
     delete L;
@@ -289,6 +302,11 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
     L->sh_out = reinterpret_cast<uint16_t*>(base + o_sho);
     L->sh_gate = reinterpret_cast<float*>(base + o_shg);
     L->zeros_idx = reinterpret_cast<uint32_t*>(base + o_zero);
+    L->xs_sh = reinterpret_cast<uint16_t*>(base + o_xssh);
+    L->hsh16 = reinterpret_cast<uint16_t*>(base + o_hsh);
+    L->xsum_sh = reinterpret_cast<float*>(base + o_xsumsh);
+    L->sh_iota = reinterpret_cast<int32_t*>(base + o_iota);
+    L->sh_group = reinterpret_cast<int32_t*>(base + o_shgrp);
   }
   L->xs = reinterpret_cast<uint16_t*>(base + o_xs);
   L->h16 = reinterpret_cast<uint16_t*>(base + o_h16);
@@ -336,10 +354,37 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                make_tmap_2d(&L->tm_down64, L->w.down_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, dw, uint64_t(El) * H,
                             dw * 4, 32, 64, true) == cudaSuccess;
   }
+  if (Is) {  // the shared expert on the warp-MMA / tcgen05 kernels (one expert, rows Is and H)
+    const int bits = c.bits;
+    const uint64_t gw = uint64_t(H) * bits / 32, dw = uint64_t(Is) * bits / 32;
+    bool maps = gw >= 32 && dw >= 32 && Is % 128 == 0 && H % 128 == 0 &&
+                make_tmap_2d(&L->tm_shg, L->w.shared_gate_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, gw, Is, gw * 4, 32,
+                             128, true) == cudaSuccess &&
+                make_tmap_2d(&L->tm_shu, L->w.shared_up_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, gw, Is, gw * 4, 32,
+                             128, true) == cudaSuccess &&
+                make_tmap_2d(&L->tm_shd, L->w.shared_down_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, dw, H, dw * 4, 32,
+                             128, true) == cudaSuccess;
+    for (int i = 0; i < 4 && maps; ++i)
+      maps = make_tmap_2d(&L->tm_xsh[i], L->xs_sh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, H, T, H * 2, 64, kTcTiles[i],
+                          true) == cudaSuccess &&
+             make_tmap_2d(&L->tm_hsh[i], L->hsh16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, Is, T, Is * 2, 64, kTcTiles[i],
+                          true) == cudaSuccess;
+    L->sh_tc_ok = maps && tc_supported(int(Is), int(H), bits, 2, 128) && tc_supported(int(H), int(Is), bits, 1, 128);
+    L->sh_mma_ok = maps && mma_supported(int(Is), int(H), bits) && mma_supported(int(H), int(Is), bits) &&
+                   make_tmap_2d(&L->tm_xsh8, L->xs_sh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, H, T, H * 2, 64, 8, true) ==
+                       cudaSuccess &&
+                   make_tmap_2d(&L->tm_hsh8, L->hsh16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, Is, T, Is * 2, 64, 8, true) ==
+                       cudaSuccess;
+  }
   L->rtc_ok = L->w.router_weight && router_tc_supported(int(H), int(E), int(K)) && E >= 128 &&
               make_tmap_2d(&L->tm_router, L->w.router_weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, E, H * 2, 64, 128,
                            true) == cudaSuccess;
   e = cudaMemset(L->arena, 0, off);
+  if (e == cudaSuccess && Is) {  // identity permutation of the shared expert's gather
+    std::vector<int32_t> iota(T);
+    for (size_t i = 0; i < T; ++i) iota[i] = static_cast<int32_t>(i);
+    e = cudaMemcpy(L->sh_iota, iota.data(), T * 4, cudaMemcpyHostToDevice);
+  }
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   cudaSetDevice(cur);
   if (e != cudaSuccess) {
@@ -650,39 +695,112 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     SENMOE_CUDA(mark(4));
   }
 
-  // 5. shared expert (deepseek_v2.rs:550-552), optionally sigmoid-gated
+  // expert parallelism: this rank's rows are complete; peers may read them
+  if (ep) SENMOE_CUDA(launch_ep_announce(ea, st));
+
+  // 5. shared expert (deepseek_v2.rs:550-552), optionally sigmoid-gated.
+  // On the tensor-core kernels it is a grouped GEMM of one expert over the
+  // rows of x this rank combines (all of them on one GPU): sh_out row i is
+  // token sh_t0 + i.  Otherwise the CUDA-core GEMV over every token.
+  int sh_t0 = 0;
   if (Is > 0) {
-    QGemvArgs sg{};
-    sg.x = static_cast<const uint16_t*>(x);
-    sg.w[0] = L->w.shared_gate_weight;
-    sg.s[0] = static_cast<const uint16_t*>(L->w.shared_gate_scales);
-    sg.b[0] = static_cast<const uint16_t*>(L->w.shared_gate_biases);
-    sg.w[1] = L->w.shared_up_weight;
-    sg.s[1] = static_cast<const uint16_t*>(L->w.shared_up_scales);
-    sg.b[1] = static_cast<const uint16_t*>(L->w.shared_up_biases);
-    sg.kdim = H;
-    sg.rows = Is;
-    sg.rows_per_cta = kGateUpRows;
-    sg.mode = kItemsGather;
-    sg.gather_idx = L->zeros_idx;
-    sg.rep = 1;
-    sg.num_experts = 1;
-    sg.out = L->sh_h;
-    sg.out_stride = Is;
-    sg.act = c.activation;
-    sg.err = L->err;
-    SENMOE_CUDA(launch_qgemv(sg, 2, c.bits, T, st));
-    QGemvArgs sd = sg;
-    sd.x = L->sh_h;
-    sd.w[0] = L->w.shared_down_weight;
-    sd.s[0] = static_cast<const uint16_t*>(L->w.shared_down_scales);
-    sd.b[0] = static_cast<const uint16_t*>(L->w.shared_down_biases);
-    sd.kdim = Is;
-    sd.rows = H;
-    sd.rows_per_cta = kDownRows;
-    sd.out = L->sh_out;
-    sd.out_stride = H;
-    SENMOE_CUDA(launch_qgemv(sd, 1, c.bits, T, st));
+    const int sh_n = ep ? ep_token_begin(T, L->ep_world, L->ep_rank + 1) - ep_token_begin(T, L->ep_world, L->ep_rank)
+                        : T;
+    const int own_t0 = ep ? ep_token_begin(T, L->ep_world, L->ep_rank) : 0;
+    const int forced = c.reserved[0];
+    int sh_path = kPathGemv;
+    if (forced == kPathTensorCore && L->sh_tc_ok) sh_path = kPathTensorCore;
+    else if (forced == kPathMma && L->sh_mma_ok) sh_path = kPathMma;
+    // kernel and tile width follow the call's token count T, the same on every
+    // expert-parallel rank and on one GPU, so each token's shared output is
+    // bit-identical however the tokens are split
+    else if (forced == kPathAuto)
+      sh_path = (T >= kTcMinTokensPerExpert && L->sh_tc_ok) ? kPathTensorCore
+                : L->sh_mma_ok                                  ? kPathMma
+                : L->sh_tc_ok                                   ? kPathTensorCore
+                                                                : kPathGemv;
+    if (sh_path != kPathGemv) {
+      sh_t0 = own_t0;  // the GEMV below writes every token's row instead
+      TcGemmArgs sa{};
+      sa.s[0] = static_cast<const uint16_t*>(L->w.shared_gate_scales);
+      sa.b[0] = static_cast<const uint16_t*>(L->w.shared_gate_biases);
+      sa.s[1] = static_cast<const uint16_t*>(L->w.shared_up_scales);
+      sa.b[1] = static_cast<const uint16_t*>(L->w.shared_up_biases);
+      sa.rows = Is;
+      sa.kdim = H;
+      sa.m_tiles = Is / 128;
+      sa.offsets = L->sh_group;       // {0, sh_n}, written by the gather below
+      sa.active = L->sh_group + 2;    // {0}
+      sa.active_count = L->sh_group + 3;
+      sa.expert_begin = 0;
+      sa.out = L->hsh16;
+      sa.out_stride = Is;
+      sa.act = c.activation;
+      sa.err = L->err;
+      sa.xsum = L->xsum_sh;
+      TcGemmArgs sd = sa;
+      sd.s[0] = sd.s[1] = static_cast<const uint16_t*>(L->w.shared_down_scales);
+      sd.b[0] = sd.b[1] = static_cast<const uint16_t*>(L->w.shared_down_biases);
+      sd.rows = H;
+      sd.kdim = Is;
+      sd.m_tiles = H / 128;
+      sd.out = L->sh_out;
+      sd.out_stride = H;
+      const uint16_t* xs_src = static_cast<const uint16_t*>(x) + static_cast<size_t>(sh_t0) * H;
+      if (sh_n > 0 && sh_path == kPathMma) {
+        const int nt = T <= 8 ? 1 : (T <= 16 ? 2 : 4);
+        const CUtensorMap& tb_x = nt == 1 ? L->tm_xsh8 : L->tm_xsh[nt == 2 ? 0 : 1];
+        const CUtensorMap& tb_h = nt == 1 ? L->tm_hsh8 : L->tm_hsh[nt == 2 ? 0 : 1];
+        const bool g4 = mma_g4_supported(c.bits, nt, sa) &&
+                        (c.reserved[1] == kMmaFormG4Single || (c.reserved[1] == kMmaFormAuto && nt == 1));
+        SENMOE_CUDA(launch_gather_rows(xs_src, L->sh_iota, 1, L->xs_sh, sh_n, H, L->err, st, nullptr, 0, 0,
+                                       g4 ? kOrderMmaG4 : kOrderMma, g4 ? L->xsum_sh : nullptr, L->sh_group));
+        SENMOE_CUDA(launch_mma_gemm(L->tm_shg, L->tm_shu, tb_x, sa, c.bits, 2, nt, g4,
+                                    (sh_n / (8 * nt) + 1) * sa.m_tiles, st));
+        SENMOE_CUDA(launch_mma_gemm(L->tm_shd, L->tm_shd, tb_h, sd, c.bits, 1, nt, g4,
+                                    (sh_n / (8 * nt) + 1) * sd.m_tiles, st));
+      } else if (sh_n > 0) {
+        const int ti = tc_tile_index(double(T)), bn = kTcTiles[ti];
+        SENMOE_CUDA(launch_gather_rows(xs_src, L->sh_iota, 1, L->xs_sh, sh_n, H, L->err, st, nullptr, 0, 0,
+                                       kOrderTc, nullptr, L->sh_group));
+        SENMOE_CUDA(launch_tc_gemm(L->tm_shg, L->tm_shu, L->tm_xsh[ti], sa, c.bits, 2, bn,
+                                   (sh_n / bn + 1) * sa.m_tiles, st));
+        SENMOE_CUDA(launch_tc_gemm(L->tm_shd, L->tm_shd, L->tm_hsh[ti], sd, c.bits, 1, bn,
+                                   (sh_n / bn + 1) * sd.m_tiles, st));
+      }
+    } else {
+      QGemvArgs sg{};
+      sg.x = static_cast<const uint16_t*>(x);
+      sg.w[0] = L->w.shared_gate_weight;
+      sg.s[0] = static_cast<const uint16_t*>(L->w.shared_gate_scales);
+      sg.b[0] = static_cast<const uint16_t*>(L->w.shared_gate_biases);
+      sg.w[1] = L->w.shared_up_weight;
+      sg.s[1] = static_cast<const uint16_t*>(L->w.shared_up_scales);
+      sg.b[1] = static_cast<const uint16_t*>(L->w.shared_up_biases);
+      sg.kdim = H;
+      sg.rows = Is;
+      sg.rows_per_cta = kGateUpRows;
+      sg.mode = kItemsGather;
+      sg.gather_idx = L->zeros_idx;
+      sg.rep = 1;
+      sg.num_experts = 1;
+      sg.out = L->sh_h;
+      sg.out_stride = Is;
+      sg.act = c.activation;
+      sg.err = L->err;
+      SENMOE_CUDA(launch_qgemv(sg, 2, c.bits, T, st));
+      QGemvArgs sd = sg;
+      sd.x = L->sh_h;
+      sd.w[0] = L->w.shared_down_weight;
+      sd.s[0] = static_cast<const uint16_t*>(L->w.shared_down_scales);
+      sd.b[0] = static_cast<const uint16_t*>(L->w.shared_down_biases);
+      sd.kdim = Is;
+      sd.rows = H;
+      sd.rows_per_cta = kDownRows;
+      sd.out = L->sh_out;
+      sd.out_stride = H;
+      SENMOE_CUDA(launch_qgemv(sd, 1, c.bits, T, st));
+    }
     if (c.shared_gate) {
       RouterArgs gr = ra;
       gr.weight = static_cast<const uint16_t*>(L->w.shared_gate_vector);
@@ -703,6 +821,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   ca.inverse = L->inv;
   ca.weights = wts;
   ca.shared_out = Is > 0 ? L->sh_out : nullptr;
+  ca.shared_row0 = sh_t0;
   ca.shared_gate = (Is > 0 && c.shared_gate) ? L->sh_gate : nullptr;
   ca.y = static_cast<uint16_t*>(y);
   ca.residual = residual ? static_cast<const uint16_t*>(x) : nullptr;
