@@ -67,6 +67,12 @@ __device__ __forceinline__ constexpr uint32_t idesc_f16_f32() {
   // D fp32 (bits 4-5 = 1), A and B fp16 (format 0), both K-major, N >> 3, M >> 4.
   return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
 }
+// The same with N chosen at run time: a tile's valid slots rounded up to 16
+// (M = 128 takes N = 16 .. 256 in steps of 16), so a partly filled last slot
+// tile of an expert costs MMA time in proportion to its slots.
+__device__ __forceinline__ uint32_t idesc_f16_f32_n(int n) {
+  return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+}
 
 // A from TMEM (row m in lane m, K pairs per 32-bit column), B from shared memory.
 __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
@@ -237,7 +243,6 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
   using S = TcShape<BITS, NPROJ, BN>;
   constexpr int SA = S::kA, SB = S::kB, SP = S::kP, KP = S::KP, KA = S::KA, ACC = S::kAcc;
   constexpr uint32_t kBTile = S::kBTile, kBBytes = S::kBBytes, kPBytes = S::kPBytes;
-  constexpr uint32_t kIdesc = idesc_f16_f32<BN>();
   static_assert(S::kSmem + 2048 <= 227 * 1024, "shared memory budget");
   static_assert(SA >= 2 && SP >= 2 && KP % KA == 0, "pipeline shape");
   static_assert(S::kACol0 + SA * S::kACols <= S::kCols, "TMEM budget");
@@ -362,6 +367,10 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
         if (!(ok = wait_or_abort(&bar_accempty[ab], accph ^ 1, &s_abort, a.err))) break;
         tc_fence_after();
         const uint32_t d = tmem + ab * S::kAccCols + iss * BN;  // this issuer's accumulator
+        // MMA width: the tile's valid slots rounded up to 16 (columns past
+        // them are never read by the epilogue)
+        const int n_mma = min(BN, (s_tiles[ti].w + 15) & ~15);
+        const uint32_t kIdesc = idesc_f16_f32_n(n_mma < 16 ? 16 : n_mma);
         for (int st = 0; st < nsteps; ++st, ++ai) {
           const int as = ai % SA, aph = (ai / SA) & 1;
           const int bs = ai % SB, bph = (ai / SB) & 1;
