@@ -476,29 +476,41 @@ def decode_point(g, spec, stk, lays, x, steps, warmup, hbm_peak, bounds, profile
     return out
 
 
-def prefill_point(g, spec, stk, lays, x, steps, warmup):
+def prefill_point(g, spec, stk, lays, x, steps, warmup, total_tokens=None):
     """One prefill pass of a stack: tokens/s and algorithmic TFLOP/s per GPU
     (routed experts' 6 H I flops per pair, the shared expert's per token, the
-    router's 2 H E per token) against the measured bf16 burst peak."""
-    T = x.shape[0]
+    router's 2 H E per token) against the measured bf16 burst peak.
+    total_tokens: token-local stack (x holds this rank's tokens, the call
+    all ranks' total_tokens); stage timings are then left out."""
+    T = x.shape[0] if total_tokens is None else total_tokens
     psteps = max(2, min(steps, 5))
     secs = timed_steps(g, stk, x, psteps, warmup)
     step = secs / psteps
     Hh, Ii = spec.hidden, spec.intermediate
     flops_layer = T * spec.top_k * 6 * Hh * Ii + T * 6 * Hh * spec.shared + 2 * T * Hh * spec.experts
     peak_t, src = tensor_peak()
-    pst = stage_profile(g, lays, x, 2)
-    gu_s = pst["gate_up"] / 1e3 / (2 * len(lays))
-    dn_s = pst["down"] / 1e3 / (2 * len(lays))
     per_gpu = flops_layer * len(lays) / step / 1e12 / g.world
-    return {"tokens": T, "tokens_per_s": T / step, "ms_per_step": step * 1e3, "tflops_per_gpu": per_gpu,
-            "frac": per_gpu / peak_t, "peak_tflops": peak_t, "peak_source": src,
-            # this rank's share of the expert pairs, over its gate/up and down stage times
-            "gate_up_tflops_per_gpu": T * spec.top_k * 4 * Hh * Ii / g.world / gu_s / 1e12,
-            "down_tflops_per_gpu": T * spec.top_k * 2 * Hh * Ii / g.world / dn_s / 1e12,
-            "expert_kernels": __import__("senmoe").PATH_NAMES[lays[0].expert_path(T)],
-            "stage_share": {k: v / max(sum(pst.values()), 1e-12) for k, v in pst.items()},
-            "scaling": "strong: the same tokens on every rank" if g.world > 1 else None}
+    out = {"tokens": T, "tokens_per_s": T / step, "ms_per_step": step * 1e3, "tflops_per_gpu": per_gpu,
+           "frac": per_gpu / peak_t, "peak_tflops": peak_t, "peak_source": src,
+           "expert_kernels": __import__("senmoe").PATH_NAMES[lays[0].expert_path(T)],
+           "scaling": None if g.world == 1 else "strong: the same tokens on every rank" if total_tokens is None
+           else f"weak, token-local: {x.shape[0]} own tokens per rank"}
+    if total_tokens is None:
+        pst = stage_profile(g, lays, x, 2)
+        gu_s = pst["gate_up"] / 1e3 / (2 * len(lays))
+        dn_s = pst["down"] / 1e3 / (2 * len(lays))
+        # this rank's share of the expert pairs, over its gate/up and down stage times
+        out["gate_up_tflops_per_gpu"] = T * spec.top_k * 4 * Hh * Ii / g.world / gu_s / 1e12
+        out["down_tflops_per_gpu"] = T * spec.top_k * 2 * Hh * Ii / g.world / dn_s / 1e12
+        out["stage_share"] = {k: v / max(sum(pst.values()), 1e-12) for k, v in pst.items()}
+    return out
+
+
+def arena_bytes(spec, max_tokens):
+    """About the scratch one layer allocates for max_tokens tokens (per pair:
+    gathered activations, h twice, d, group sums; per token: logits, rows)."""
+    H_, I_, K_, E_ = spec.hidden, spec.intermediate, spec.top_k, spec.experts
+    return int(max_tokens * K_ * (4 * H_ + 4 * I_ + H_ // 16 + 24) + max_tokens * (4 * E_ + 4 * H_) + (1 << 20))
 
 
 def free_stack(g, stk, lays):
@@ -630,10 +642,21 @@ def main():
     stage_share = {k: v / max(sum(stage_ms.values()), 1e-12) for k, v in stage_ms.items()}
     g.log(f"decode stage ms (sum over {nrep} steps x {len(layers)} layers): {stage_ms}")
 
-    strong = None
+    strong = token_local = None
     if world > 1:  # latency view: 64 tokens in all, each rank 1/N of the experts
         strong = decode_point(g, SPEC, stack, layers, x_all[:64], args.steps, args.warmup, hbm_peak, bounds)
         g.log(f"strong 64: {strong}")
+        # token-local form: each rank routes and combines only its own tokens
+        # (rank r: tokens [r * per_gpu, (r + 1) * per_gpu) of the same batch)
+        lstack = senmoe.MoeStack(layers, per_gpu, use_graph=True, tokens_per_rank=[per_gpu] * world)
+        secs = timed_steps(g, lstack, x_all[rank * per_gpu:(rank + 1) * per_gpu], args.steps, args.warmup)
+        step = secs / args.steps
+        alg = results[args.batch]["alg_bytes_per_step"]
+        token_local = {"tokens": args.batch, "tokens_per_s": args.batch / step, "ms_per_step": step * 1e3,
+                       "hbm_frac": alg / step / 1e9 / (world * hbm_peak),
+                       "form": f"token-local: {per_gpu} own tokens per rank (senmoe_layer_forward_tokens)"}
+        g.log(f"token-local decode: {token_local}")
+        lstack.release()
 
     # ---- e2e through the public API with host buffers
     x_host = x_all[:T].cpu().pin_memory()
@@ -664,6 +687,23 @@ def main():
         g.log(f"prefill {TP}: {prefill[str(TP)]}")
         free_stack(g, pstack, pl)
         del xp
+    # token-local prefill (N > 1): each rank its own sequence of TL tokens,
+    # TL = the first prefill size unless the 48 layers' scratch for all
+    # ranks' tokens would not fit the free device memory (then halved)
+    if world > 1 and args.prefill_tokens.strip():
+        TL = int(args.prefill_tokens.split(",")[0])
+        free_b = torch.cuda.mem_get_info(g.dev)[0]
+        while TL > 256 and args.layers * arena_bytes(SPEC, TL * world) > 0.7 * free_b:
+            TL //= 2
+        TL = int(-g.max_over_ranks(-TL))  # every rank takes the smallest
+        pl, _ = make_stack(torch, senmoe, local, SPEC, args.layers, TL * world, rank, world, weights=wts)
+        pstack = senmoe.MoeStack(pl, TL, use_graph=True, tokens_per_rank=[TL] * world)
+        xp = synth.spec_tokens(SPEC, TL, device=g.dev, first=rank * TL)
+        prefill[f"token_local_{TL}_per_gpu"] = prefill_point(g, SPEC, pstack, pl, xp, args.steps, args.warmup,
+                                                               total_tokens=TL * world)
+        g.log(f"token-local prefill {TL}/GPU: {prefill[f'token_local_{TL}_per_gpu']}")
+        free_stack(g, pstack, pl)
+        del xp
 
     head = results[args.batch]
     line = {
@@ -684,6 +724,7 @@ def main():
                      "step_hbm_gbs": head["hbm_gbs"], "step_frac": head["hbm_gbs"] / hbm_peak},
         "stage_share": stage_share,
         "strong": strong,
+        "token_local": token_local,
         "prefill": prefill,
         "gpu_launches": launches_per_forward(args.batch, head["expert_kernels"] != "gemv", world) * args.layers
         * args.steps,

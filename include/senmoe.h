@@ -205,6 +205,26 @@ typedef struct SenMoePeerInfo {
   int32_t reserved;
 } SenMoePeerInfo;
 
+/* Token-local expert parallelism (the prefill form of the expert split; no
+ * counterpart in the reference): each rank passes ITS OWN tokens x [T_r, H]
+ * -- data-parallel tokens, e.g. its own sequences -- and gets y [T_r, H] =
+ * DeepseekMoe::forward(x) (+ x when residual != 0, DecoderLayer::forward's
+ * residual add) for them.  tokens_per_rank[q] = T_q (host memory, the same
+ * array on every rank); the call's tokens are the ranks' tokens in rank
+ * order and sum(T_q) <= max_tokens.  Each rank routes only its own tokens,
+ * publishes its routing rows and token rows to the peers, runs its experts
+ * over every rank's pairs (reading each token's row from its owner over
+ * NVLink) and combines its own tokens in slot order, reading each pair's row
+ * from the expert's owner: the result is bit-identical to one GPU running
+ * the concatenated tokens whenever both take the same router kernel (it is
+ * picked by the token count routed: CUDA-core below 512 tokens, tensor-core
+ * from 512), within the block tolerance otherwise.  Needs the tensor-core
+ * expert kernels (SENMOE_ERR_UNSUPPORTED for the GEMV path).  A layer that
+ * is not connected runs it as senmoe_layer_forward (tokens_per_rank[0] ==
+ * num_tokens).  Same ordering rules as the replicated form. */
+int senmoe_layer_forward_tokens(SenMoeLayer* layer, const void* x, int64_t num_tokens, void* y,
+                                const int64_t* tokens_per_rank, int32_t residual, senmoe_stream_t stream);
+
 /* This rank's table entry. */
 int senmoe_layer_peer_info(const SenMoeLayer* layer, SenMoePeerInfo* out);
 

@@ -93,6 +93,58 @@ __global__ void ep_announce_kernel(EpArgs a) {
   if (r < a.world) st_release_sys(a.peer_flags[r] + kEpReadyOffset + a.rank, epoch);
 }
 
+// Token-local form: this rank's token rows -> its own exchange buffer (the
+// peers' gathers read them there), its routing rows (global pair rows
+// [tok_begin[rank] * K, ...)) -> every peer's routing arrays; the last CTA
+// to finish raises ids[rank] in every rank's flags.  Each CTA fences its
+// stores (one system-scope fence after a barrier) before it counts itself.
+__global__ void __launch_bounds__(256) ep_publish_kernel(EpArgs a, const uint16_t* __restrict__ x, int n_local,
+                                                         int hidden) {
+  pdl_wait();  // the router's ids / weights of this call are complete
+  pdl_launch_dependents();
+  const uint32_t epoch = *a.epoch;
+  const size_t nthreads = size_t(gridDim.x) * blockDim.x, tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t nvec = size_t(n_local) * hidden / 8;
+  const uint4* src = reinterpret_cast<const uint4*>(x);
+  uint4* dst = reinterpret_cast<uint4*>(a.peer_y[a.rank]);
+  for (size_t i = tid; i < nvec; i += nthreads) dst[i] = __ldcg(src + i);
+  const size_t p0 = size_t(a.tok_begin[a.rank]) * a.top_k, np = size_t(n_local) * a.top_k;
+  for (size_t i = tid; i < np; i += nthreads) {
+    const int32_t id = a.peer_ids[a.rank][p0 + i];
+    const float w = a.peer_wts[a.rank][p0 + i];
+    for (int q = 0; q < a.world; ++q) {
+      if (q == a.rank) continue;
+      a.peer_ids[q][p0 + i] = id;
+      a.peer_wts[q][p0 + i] = w;
+    }
+  }
+  __shared__ bool s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    s_last = atomicAdd(a.published, 1u) == gridDim.x - 1u;
+    if (s_last) __threadfence_system();
+  }
+  __syncthreads();
+  if (s_last) {
+    if (threadIdx.x == 0) *a.published = 0u;
+    const int r = threadIdx.x;
+    if (r < a.world) st_release_sys(a.peer_flags[r] + kEpIdsOffset + a.rank, epoch);
+  }
+}
+
+// Waits until every peer's routing and token rows of this call are here.
+__global__ void ep_wait_published_kernel(EpArgs a) {
+  pdl_wait();
+  const uint32_t epoch = *a.epoch;
+  const int r = threadIdx.x;
+  if (r < a.world && r != a.rank) {
+    if (!wait_flag(a.flags + kEpIdsOffset + r, epoch, a.err)) record_error(a.err, kDevPeerTimeout);
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+}
+
 // Expert-rows owner of expert e: the rank r with bounds[r] <= e < bounds[r+1].
 __device__ __forceinline__ int owner_of(const EpArgs& a, int e) {
   int r = 0;
@@ -119,8 +171,8 @@ __global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) ep_combine_kernel(EpAr
   __syncthreads();
 
   const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
-  const int t_begin = ep_token_begin(num_tokens, a.world, a.rank);
-  const int t_end = ep_token_begin(num_tokens, a.world, a.rank + 1);
+  const int t_begin = a.tok_begin[a.rank];
+  const int t_end = a.tok_begin[a.rank + 1];
   constexpr int kMaxK = KMAX;
   if (col < c.hidden) {
     for (int t = t_begin + blockIdx.y; t < t_end; t += gridDim.y) {
@@ -155,8 +207,9 @@ __global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) ep_combine_kernel(EpAr
           acc[6] += bf16_lo(v.w) * w; acc[7] += bf16_hi(v.w) * w;
         }
       }
+      const size_t lrow = static_cast<size_t>(t - c.local_row0);  // row of y / residual / shared_gate
       if (c.shared_out) {
-        const float g = c.shared_gate ? c.shared_gate[t] : 1.0f;
+        const float g = c.shared_gate ? c.shared_gate[lrow] : 1.0f;
         const uint4 v =
             *reinterpret_cast<const uint4*>(c.shared_out + static_cast<size_t>(t - c.shared_row0) * c.hidden + col);
         acc[0] += g * bf16_lo(v.x); acc[1] += g * bf16_hi(v.x);
@@ -165,7 +218,7 @@ __global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) ep_combine_kernel(EpAr
         acc[6] += g * bf16_lo(v.w); acc[7] += g * bf16_hi(v.w);
       }
       if (c.residual) {
-        const uint4 v = *reinterpret_cast<const uint4*>(c.residual + static_cast<size_t>(t) * c.hidden + col);
+        const uint4 v = *reinterpret_cast<const uint4*>(c.residual + lrow * c.hidden + col);
         acc[0] += bf16_lo(v.x); acc[1] += bf16_hi(v.x); acc[2] += bf16_lo(v.y); acc[3] += bf16_hi(v.y);
         acc[4] += bf16_lo(v.z); acc[5] += bf16_hi(v.z); acc[6] += bf16_lo(v.w); acc[7] += bf16_hi(v.w);
       }
@@ -174,10 +227,12 @@ __global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) ep_combine_kernel(EpAr
       o.y = uint32_t(f32_to_bf16_bits(acc[2])) | (uint32_t(f32_to_bf16_bits(acc[3])) << 16);
       o.z = uint32_t(f32_to_bf16_bits(acc[4])) | (uint32_t(f32_to_bf16_bits(acc[5])) << 16);
       o.w = uint32_t(f32_to_bf16_bits(acc[6])) | (uint32_t(f32_to_bf16_bits(acc[7])) << 16);
-      const size_t off = static_cast<size_t>(t) * c.hidden + col;
-      *reinterpret_cast<uint4*>(c.y + off) = o;
-      for (int q = 0; q < a.world; ++q)
-        if (q != a.rank) *reinterpret_cast<uint4*>(a.peer_y[q] + off) = o;
+      *reinterpret_cast<uint4*>(c.y + lrow * c.hidden + col) = o;
+      if (!a.local_tokens) {  // replicated form: every rank returns every token
+        const size_t off = static_cast<size_t>(t) * c.hidden + col;
+        for (int q = 0; q < a.world; ++q)
+          if (q != a.rank) *reinterpret_cast<uint4*>(a.peer_y[q] + off) = o;
+      }
     }
   }
 
@@ -199,7 +254,7 @@ __global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) ep_combine_kernel(EpAr
     if (threadIdx.x == 0) *a.finished = 0u;
     if (r < a.world) {
       st_release_sys(a.peer_flags[r] + kEpDoneOffset + a.rank, epoch);
-      if (r != a.rank) st_release_sys(a.peer_flags[r] + kEpRowsOffset + a.rank, epoch);
+      if (r != a.rank && !a.local_tokens) st_release_sys(a.peer_flags[r] + kEpRowsOffset + a.rank, epoch);
     }
   }
 }
@@ -209,8 +264,8 @@ __global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) ep_combine_kernel(EpAr
 __global__ void __launch_bounds__(256) ep_gather_rows_kernel(EpArgs a, uint16_t* y, int hidden, int num_tokens) {
   pdl_wait();  // y's previous readers have finished; this call's epoch is set
   pdl_launch_dependents();
-  const int t_begin = ep_token_begin(num_tokens, a.world, a.rank);
-  const int t_end = ep_token_begin(num_tokens, a.world, a.rank + 1);
+  const int t_begin = a.tok_begin[a.rank];
+  const int t_end = a.tok_begin[a.rank + 1];
   const int others = num_tokens - (t_end - t_begin);
   if (others == 0) return;
   const uint32_t epoch = *a.epoch;
@@ -239,8 +294,21 @@ cudaError_t launch_ep_announce(const EpArgs& a, cudaStream_t st) {
   return launch_pdl(ep_announce_kernel, dim3(1), dim3(32), 0, st, a);
 }
 
+cudaError_t launch_ep_publish(const EpArgs& a, const uint16_t* x, int n_local, int hidden, cudaStream_t st) {
+  // enough CTAs to stream the rows at full bandwidth; at least one raises the flags
+  const size_t vec = size_t(n_local) * hidden / 8;
+  int grid = static_cast<int>((vec + 255) / 256);
+  grid = grid < 1 ? 1 : (grid > 296 ? 296 : grid);
+  return launch_pdl(ep_publish_kernel, dim3(grid), dim3(256), 0, st, a, x, n_local, hidden);
+}
+
+cudaError_t launch_ep_wait_published(const EpArgs& a, cudaStream_t st) {
+  return launch_pdl(ep_wait_published_kernel, dim3(1), dim3(32), 0, st, a);
+}
+
 cudaError_t launch_ep_combine(const EpArgs& a, const CombineArgs& c, int num_tokens, cudaStream_t st) {
-  const int own = ep_token_begin(num_tokens, a.world, a.rank + 1) - ep_token_begin(num_tokens, a.world, a.rank);
+  (void)num_tokens;
+  const int own = a.tok_begin[a.rank + 1] - a.tok_begin[a.rank];
   const int threads = own < 256 ? 64 : 256;  // narrow CTAs for small batches (>= 8 ranks' flag threads)
   const int gx = (c.hidden / 8 + threads - 1) / threads;
   // enough CTAs to cover the rank's tokens of a decode batch in one wave;
@@ -252,7 +320,7 @@ cudaError_t launch_ep_combine(const EpArgs& a, const CombineArgs& c, int num_tok
 }
 
 cudaError_t launch_ep_gather_rows(const EpArgs& a, uint16_t* y, int hidden, int num_tokens, cudaStream_t st) {
-  const int own = ep_token_begin(num_tokens, a.world, a.rank + 1) - ep_token_begin(num_tokens, a.world, a.rank);
+  const int own = a.tok_begin[a.rank + 1] - a.tok_begin[a.rank];
   const int others = num_tokens - own;
   const int threads = others < 256 ? 64 : 256;
   const int gx = (hidden / 8 + threads - 1) / threads;

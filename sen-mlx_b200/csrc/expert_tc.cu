@@ -751,12 +751,22 @@ cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
 // odd columns divided by 16).  Each CTA copies kGatherSlots slots.
 constexpr int kGatherSlots = 4;
 
+// Row `token` of the gather's source: x, or its owner rank's exchange buffer.
+__device__ __forceinline__ const uint16_t* gather_src_row(const uint16_t* x, int token, int hidden,
+                                                          const PeerRows& pr) {
+  if (pr.world == 0) return x + static_cast<size_t>(token) * hidden;
+  int q = 0;
+#pragma unroll
+  for (int i = 1; i < kPeerRowsMax; ++i) q += (i < pr.world && token >= pr.begin[i]) ? 1 : 0;
+  return pr.base[q] + static_cast<size_t>(token - pr.begin[q]) * hidden;
+}
+
 __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __restrict__ x,
                                                           const int32_t* __restrict__ perm, int k_div,
                                                           uint16_t* __restrict__ out, int num_slots, int hidden,
                                                           int* err, const int32_t* __restrict__ offsets, int eb,
                                                           int ee, int order, float* __restrict__ group_sums,
-                                                          int32_t* __restrict__ one_group) {
+                                                          int32_t* __restrict__ one_group, const PeerRows pr) {
   pdl_wait();
   pdl_launch_dependents();
   if (one_group && blockIdx.x == 0 && threadIdx.x == 0) {
@@ -778,7 +788,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
   for (int j = 0; j < kGatherSlots; ++j) {
     const int s = s0 + j;
     live[j] = s < num_slots && s >= lo_slot && s < hi_slot;
-    src[j] = x + static_cast<size_t>(live[j] ? perm[s] / k_div : 0) * hidden;
+    src[j] = live[j] ? gather_src_row(x, perm[s] / k_div, hidden, pr) : x;
   }
   bool ok = true;
   if (order == kOrderMmaG4) {
@@ -789,11 +799,11 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
     for (int it = threadIdx.x; it < kGatherSlots * groups; it += blockDim.x) {
       const int j = it / groups, G = it - j * groups, s = s0 + j;
       if (!(s < num_slots && s >= lo_slot && s < hi_slot)) continue;
-      const uint4* in = reinterpret_cast<const uint4*>(x + static_cast<size_t>(perm[s] / k_div) * hidden + 64 * G);
+      const uint4* in = reinterpret_cast<const uint4*>(gather_src_row(x, perm[s] / k_div, hidden, pr) + 64 * G);
       uint32_t w[32];
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        const uint4 v = __ldg(in + q);
+        const uint4 v = __ldcg(in + q);
         w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
       }
       if (group_sums) {  // the group's sum of x (column order), in the MMA's 2^-24 units
@@ -882,12 +892,14 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
                                int num_slots, int hidden, int* err, cudaStream_t st,
                                const int32_t* offsets, int eb, int ee, int order, float* group_sums,
-                               int32_t* one_group) {
+                               int32_t* one_group, const PeerRows* peer_rows) {
   if (num_slots <= 0) return cudaSuccess;
   const int threads = hidden / 8 < 256 ? ((hidden / 8 + 31) / 32) * 32 : 256;
   const int grid = (num_slots + kGatherSlots - 1) / kGatherSlots;
+  PeerRows pr{};
+  if (peer_rows) pr = *peer_rows;
   return launch_pdl(gather_rows_kernel, dim3(grid), dim3(threads), 0, st, x, perm, k_div, x_sorted, num_slots,
-                    hidden, err, offsets, eb, ee, order, order == kOrderMmaG4 ? group_sums : nullptr, one_group);
+                    hidden, err, offsets, eb, ee, order, order == kOrderMmaG4 ? group_sums : nullptr, one_group, pr);
 }
 
 }  // namespace senmoe

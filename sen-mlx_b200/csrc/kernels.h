@@ -132,6 +132,9 @@ struct CombineArgs {
   const float* shared_gate;    // fp32 [T] gate per token (already sigmoid) or null
   const uint16_t* residual;    // bf16 [T, H] added before rounding (fused residual) or null
   uint16_t* y;              // bf16 [T, H]
+  // Token-local expert parallelism: y, residual and shared_gate hold only
+  // this rank's tokens, row i = global token local_row0 + i (0 otherwise).
+  int local_row0;
   float* y_f32;             // optional fp32 copy
   int hidden, top_k;
 };
@@ -175,6 +178,16 @@ cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
 // kOrderMmaG4 (warp-MMA group-scaled form, kperm_g4 with odd columns / 16;
 // hidden % 64 == 0).
 enum ActivationOrder { kOrderTc = 0, kOrderMma = 1, kOrderMmaG4 = 2 };
+// Where the gather finds token rows: x itself (world == 0), or, for
+// token-local expert parallelism, the owner rank's exchange buffer over
+// NVLink: token g of rank q (begin[q] <= g < begin[q+1]) is row g - begin[q]
+// of base[q] (plain peer loads; no TMA reads peer memory).
+constexpr int kPeerRowsMax = 8;
+struct PeerRows {
+  const uint16_t* base[kPeerRowsMax];
+  int begin[kPeerRowsMax + 1];
+  int world;
+};
 // With kOrderMmaG4 and `group_sums` non-null, group_sums[s * hidden/64 + G]
 // also receives 2^-24 * (the fp32 sum of x[perm[s]/k_div, 64 G .. 64 G + 63])
 // for every gathered slot: the group sums the group-scaled gate/up kernel
@@ -185,7 +198,8 @@ enum ActivationOrder { kOrderTc = 0, kOrderMma = 1, kOrderMmaG4 = 2 };
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
                                int num_slots, int hidden, int* err, cudaStream_t st,
                                const int32_t* offsets = nullptr, int eb = 0, int ee = 0, int order = kOrderTc,
-                               float* group_sums = nullptr, int32_t* one_group = nullptr);
+                               float* group_sums = nullptr, int32_t* one_group = nullptr,
+                               const PeerRows* peer_rows = nullptr);
 
 // ------------------------------------------- warp-MMA expert GEMM (decode)
 // Same arguments as the tcgen05 GEMM (TcGemmArgs; out holds h as fp16 in
@@ -212,7 +226,8 @@ constexpr int kEpMaxRanks = 8;
 constexpr int kEpReadyOffset = 0;   // u32 index of ready[0] in a rank's flag block
 constexpr int kEpDoneOffset = 8;    // u32 index of done[0]
 constexpr int kEpRowsOffset = 16;   // u32 index of rows[0]: rank r's combined rows are in this rank's exchange
-constexpr size_t kEpFlagBytes = 128; // ready[8], done[8], rows[8]
+constexpr int kEpIdsOffset = 24;    // u32 index of ids[0]: rank r's routing and token rows are published
+constexpr size_t kEpFlagBytes = 128; // ready[8], done[8], rows[8], ids[8]
 // Token ownership of the expert-parallel combine: rank r combines tokens
 // [ep_token_begin(T, world, r), ep_token_begin(T, world, r + 1)).
 __host__ __device__ inline int ep_token_begin(int num_tokens, int world, int r) {
@@ -221,13 +236,23 @@ __host__ __device__ inline int ep_token_begin(int num_tokens, int world, int r) 
 struct EpArgs {
   int rank, world;
   int bounds[kEpMaxRanks + 1];         // rank r owns experts [bounds[r], bounds[r+1])
+  // Tokens rank r combines: global tokens [tok_begin[r], tok_begin[r+1]).
+  // Replicated form: contiguous blocks of the shared batch (ep_token_begin);
+  // token-local form: each rank's own tokens, in rank order.
+  int tok_begin[kEpMaxRanks + 1];
+  int local_tokens;                    // 1: token-local form (no combined-row exchange)
   const uint16_t* peer_d[kEpMaxRanks]; // expert rows [P, H] of each rank, mapped here (own included)
   uint16_t* peer_y[kEpMaxRanks];       // combined-row exchange [Tmax, H] of each rank, mapped here (own included)
   uint32_t* peer_flags[kEpMaxRanks];   // flag block of each rank, mapped here (own included)
   uint32_t* flags;                     // this rank's flag block
   uint32_t* epoch;                     // this rank's call counter
   uint32_t* finished;                  // combine CTA completion counter
+  uint32_t* published;                 // publish CTA completion counter (token-local form)
   const int32_t* topk_ids;             // [T*K]
+  // token-local form: every rank's routing arrays (global pair rows), mapped here
+  int32_t* peer_ids[kEpMaxRanks];
+  float* peer_wts[kEpMaxRanks];
+  int top_k;
   int* err;
 };
 // Waits (bounded) until every peer has finished reading this rank's rows of
@@ -241,6 +266,15 @@ cudaError_t launch_ep_announce(const EpArgs& a, cudaStream_t st);
 // (CombineArgs.d unused); every combined row goes to c.y and to each
 // peer's exchange, and the last CTA raises rows[rank] in every peer's flags.
 cudaError_t launch_ep_combine(const EpArgs& a, const CombineArgs& c, int num_tokens, cudaStream_t st);
+// Token-local form, after the router of this rank's n_local tokens (routing
+// rows at global pair rows tok_begin[rank]*K ...): copies the token rows x
+// [n_local, H] into this rank's exchange (read by the peers' gathers) and the
+// routing rows into every peer's routing arrays, then raises ids[rank] in
+// every rank's flags.
+cudaError_t launch_ep_publish(const EpArgs& a, const uint16_t* x, int n_local, int hidden, cudaStream_t st);
+// Waits (bounded) until every peer has published (ids[*] >= epoch).  Launch
+// before the dispatch of the global pair list.
+cudaError_t launch_ep_wait_published(const EpArgs& a, cudaStream_t st);
 // Waits (bounded) for every peer's combined rows and copies the tokens this
 // rank does not own from its exchange into y [T, H].  Launch after the combine.
 cudaError_t launch_ep_gather_rows(const EpArgs& a, uint16_t* y, int hidden, int num_tokens, cudaStream_t st);

@@ -154,13 +154,16 @@ struct SenMoeLayer {
   CUtensorMap tm_shg{}, tm_shu{}, tm_shd{};   // shared gate / up / down codes
   CUtensorMap tm_xsh[4]{}, tm_hsh[4]{}, tm_xsh8{}, tm_hsh8{};
   // expert parallelism (senmoe_layer_connect_peers)
-  size_t arena_bytes = 0, o_d = 0, o_flags = 0, o_yx = 0;
+  size_t arena_bytes = 0, o_d = 0, o_flags = 0, o_yx = 0, o_ids = 0, o_wts = 0;
   uint32_t* ep_flags = nullptr;  // ready[8], done[8], rows[8]: written by peers
-  uint32_t* ep_local = nullptr;  // [0] call epoch, [1] combine CTA counter
+  uint32_t* ep_local = nullptr;  // [0] call epoch, [1] combine CTA counter, [2] publish CTA counter
   int ep_world = 0, ep_rank = 0; // ep_world 0: not connected
   int ep_bounds[kEpMaxRanks + 1] = {};
   const uint16_t* ep_peer_d[kEpMaxRanks] = {};
-  uint16_t* ep_peer_y[kEpMaxRanks] = {};     // combined-row exchanges [Tmax, H]
+  uint16_t* ep_peer_y[kEpMaxRanks] = {};     // row exchanges [Tmax, H]: combined rows (replicated
+                                             // form) or each rank's own token rows (token-local form)
+  int32_t* ep_peer_ids[kEpMaxRanks] = {};    // routing arrays [Tmax*K] of every rank (token-local form)
+  float* ep_peer_wts[kEpMaxRanks] = {};
   uint32_t* ep_peer_flags[kEpMaxRanks] = {};
   void* ep_opened[kEpMaxRanks] = {};  // IPC mappings to close
   // per-stage timing
@@ -273,7 +276,7 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                o_err = take(4), o_hist = take(size_t(L->nchunks_max) * E * 4), o_h = take(P * I * 2),
                o_d = take(P * H * 2), o_shh = take(Is ? T * Is * 2 : 0), o_sho = take(Is ? T * H * 2 : 0),
                o_shg = take(Is ? T * 4 : 0), o_zero = take(Is ? T * 4 : 0), o_xs = take(P * H * 2),
-               o_h16 = take(P * I * 2), o_flags = take(kEpFlagBytes), o_local = take(8),
+               o_h16 = take(P * I * 2), o_flags = take(kEpFlagBytes), o_local = take(16),
                o_route = take((T + 3) / 4 * 4), o_yx = take(T * H * 2),
                o_xsum = take((P + 16) * (H / 64) * 4), o_xssh = take(Is ? T * H * 2 : 0),
                o_hsh = take(Is ? T * Is * 2 : 0), o_xsumsh = take(Is ? (T + 16) * (H / 64) * 4 : 0),
@@ -318,6 +321,8 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
   L->o_d = o_d;
   L->o_flags = o_flags;
   L->o_yx = o_yx;
+  L->o_ids = o_ids;
+  L->o_wts = o_wts;
   {  // tensor maps for the tensor-core paths (host-side encoding only)
     const int bits = c.bits, El = c.expert_end - c.expert_begin;
     const uint64_t gw = uint64_t(H) * bits / 32, dw = uint64_t(I) * bits / 32;
@@ -439,25 +444,54 @@ static int expert_path_for(const SenMoeLayer* L, int64_t pairs) {
 
 // ext_ids / ext_w: routing [T, K] from the caller (Experts::forward), or
 // null to run the layer's router.
+// tokens_per_rank (host, [ep_world], token-local expert parallelism): x and
+// y hold this rank's num_tokens tokens only, which are global tokens
+// [sum of the earlier ranks' counts, + num_tokens) of the call.
 static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void* y, const SenMoeDebug* debug,
                          bool residual, senmoe_stream_t stream, const int32_t* ext_ids = nullptr,
-                         const float* ext_w = nullptr) {
+                         const float* ext_w = nullptr, const int64_t* tokens_per_rank = nullptr) {
   g_last_error.clear();
   if (!L) return fail(SENMOE_ERR_BAD_ARG, "layer is NULL");
   const SenMoeConfig& c = L->cfg;
-  if (num_tokens < 0 || num_tokens > c.max_tokens)
-    return fail(SENMOE_ERR_BAD_ARG, "num_tokens=%lld outside [0, max_tokens=%d]", (long long)num_tokens, c.max_tokens);
-  if (num_tokens == 0) return SENMOE_OK;
-  if (!x || !y) return fail(SENMOE_ERR_BAD_ARG, "x or y is NULL");
-  if (!aligned16(x) || !aligned16(y)) return fail(SENMOE_ERR_BAD_ARG, "x and y must be 16-byte aligned");
+  const bool local = tokens_per_rank != nullptr && L->ep_world > 0;
+  int tok_begin[kEpMaxRanks + 1] = {};
+  int64_t total = num_tokens;
+  if (local) {
+    total = 0;
+    for (int r = 0; r < L->ep_world; ++r) {
+      if (tokens_per_rank[r] < 0 || tokens_per_rank[r] > c.max_tokens)
+        return fail(SENMOE_ERR_BAD_ARG, "tokens_per_rank[%d]=%lld outside [0, max_tokens=%d]", r,
+                    (long long)tokens_per_rank[r], c.max_tokens);
+      tok_begin[r] = static_cast<int>(total);
+      total += tokens_per_rank[r];
+      tok_begin[r + 1] = static_cast<int>(total);
+    }
+    if (tokens_per_rank[L->ep_rank] != num_tokens)
+      return fail(SENMOE_ERR_BAD_ARG, "tokens_per_rank[%d]=%lld is not this rank's num_tokens=%lld", L->ep_rank,
+                  (long long)tokens_per_rank[L->ep_rank], (long long)num_tokens);
+    if (ext_ids || debug) return fail(SENMOE_ERR_UNSUPPORTED, "token-local forward takes no routing or debug outputs");
+  }
+  if (num_tokens < 0 || total > c.max_tokens)
+    return fail(SENMOE_ERR_BAD_ARG, "num_tokens=%lld (%lld in all) outside [0, max_tokens=%d]", (long long)num_tokens,
+                (long long)total, c.max_tokens);
+  if (total == 0) return SENMOE_OK;  // every rank sees the same total: all skip together
+  if (num_tokens > 0 && (!x || !y)) return fail(SENMOE_ERR_BAD_ARG, "x or y is NULL");
+  if ((x && !aligned16(x)) || (y && !aligned16(y))) return fail(SENMOE_ERR_BAD_ARG, "x and y must be 16-byte aligned");
   if (!ext_ids && !L->w.router_weight)
     return fail(SENMOE_ERR_BAD_ARG, "the layer has no router weight: use senmoe_layer_experts_forward");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   int32_t* const ids = ext_ids ? const_cast<int32_t*>(ext_ids) : L->ids;   // read-only when given
   float* const wts = ext_w ? const_cast<float*>(ext_w) : L->wts;
-  const int T = static_cast<int>(num_tokens), K = c.num_experts_per_tok, E = c.n_routed_experts;
+  // T: tokens of the call (all ranks' in the token-local form); T_loc, row0:
+  // the tokens x holds and the global index of its first row
+  const int T = static_cast<int>(total), K = c.num_experts_per_tok, E = c.n_routed_experts;
+  const int T_loc = static_cast<int>(num_tokens), row0 = local ? tok_begin[L->ep_rank] : 0;
   const int H = c.hidden_size, I = c.moe_intermediate_size, Is = c.shared_intermediate;
   const int P = T * K;
+  if (!local) tok_begin[0] = 0;
+  if (local && expert_path_for(L, P) == kPathGemv)
+    return fail(SENMOE_ERR_UNSUPPORTED, "token-local expert parallelism needs the tensor-core expert kernels (the "
+                                        "CUDA-core GEMV path reads tokens from x)");
   // Stage events are recorded only outside a stream capture (inside one a
   // plain record only links the capture's streams).
   bool profile = L->profiling;
@@ -469,14 +503,42 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   auto mark = [&](int stage) -> cudaError_t { return profile ? cudaEventRecord(L->ev[stage], st) : cudaSuccess; };
   SENMOE_CUDA(mark(0));
 
-  // 1. router (deepseek_v2.rs:528-543)
+  const bool ep = L->ep_world > 0;
+  EpArgs ea{};
+  if (ep) {
+    ea.rank = L->ep_rank;
+    ea.world = L->ep_world;
+    for (int r = 0; r <= L->ep_world; ++r) {
+      ea.bounds[r] = L->ep_bounds[r];
+      ea.tok_begin[r] = local ? tok_begin[r] : ep_token_begin(T, L->ep_world, r);
+    }
+    ea.local_tokens = local ? 1 : 0;
+    for (int r = 0; r < L->ep_world; ++r) {
+      ea.peer_d[r] = L->ep_peer_d[r];
+      ea.peer_y[r] = L->ep_peer_y[r];
+      ea.peer_flags[r] = L->ep_peer_flags[r];
+      ea.peer_ids[r] = L->ep_peer_ids[r];
+      ea.peer_wts[r] = L->ep_peer_wts[r];
+    }
+    ea.flags = L->ep_flags;
+    ea.epoch = L->ep_local;
+    ea.finished = L->ep_local + 1;
+    ea.published = L->ep_local + 2;
+    ea.topk_ids = ids;
+    ea.top_k = K;
+    ea.err = L->err;
+  }
+  // token-local form: the call epoch first (the publish below carries it)
+  if (local) SENMOE_CUDA(launch_ep_fence(ea, st));
+
+  // 1. router (deepseek_v2.rs:528-543), over the tokens x holds
   RouterArgs ra{};
   ra.x = static_cast<const uint16_t*>(x);
   ra.weight = static_cast<const uint16_t*>(L->w.router_weight);
   ra.logits = L->logits;
-  ra.topk_ids = L->ids;
-  ra.topk_weights = L->wts;
-  ra.num_tokens = T;
+  ra.topk_ids = L->ids + static_cast<size_t>(row0) * K;
+  ra.topk_weights = L->wts + static_cast<size_t>(row0) * K;
+  ra.num_tokens = T_loc;
   ra.hidden = H;
   ra.num_experts = E;
   ra.top_k = K;
@@ -499,26 +561,38 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   da.active_count = L->active_count;
   da.chunk_hist = L->chunk_hist;
   da.err = L->err;
-  const bool ep = L->ep_world > 0;
   da.keep_remote_slots = ep ? 1 : 0;  // the combine reads remote slots from their owners
+  // token-local form: every rank's routing rows are needed before the
+  // dispatch of the call's global pair list
+  auto exchange_routing = [&]() -> cudaError_t {
+    if (!local) return cudaSuccess;
+    cudaError_t e = launch_ep_publish(ea, static_cast<const uint16_t*>(x), T_loc, H, st);
+    return e == cudaSuccess ? launch_ep_wait_published(ea, st) : e;
+  };
   if (ext_ids) {
     SENMOE_CUDA(mark(1));  // routing given by the caller
     SENMOE_CUDA(launch_dispatch(da, st));
-  } else if (L->rtc_ok && T >= kRouterTcMinTokens) {
-    // prefill sizes: logits on the tensor cores and top-k in one launch
-    CUtensorMap tm_x;
-    SENMOE_CUDA(make_tmap_2d(&tm_x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, T, uint64_t(H) * 2, 64, 32, true));
-    SENMOE_CUDA(launch_router_tc(tm_x, L->tm_router, ra, st));
+  } else if (T_loc == 0) {  // token-local form, a rank with no tokens of its own
+    SENMOE_CUDA(exchange_routing());
     SENMOE_CUDA(mark(1));
     SENMOE_CUDA(launch_dispatch(da, st));
-  } else if (L->route_cnt && T >= kFusedTopkMinTokens) {
+  } else if (L->rtc_ok && T_loc >= kRouterTcMinTokens) {
+    // prefill sizes: logits on the tensor cores and top-k in one launch
+    CUtensorMap tm_x;
+    SENMOE_CUDA(make_tmap_2d(&tm_x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, T_loc, uint64_t(H) * 2, 64, 32, true));
+    SENMOE_CUDA(launch_router_tc(tm_x, L->tm_router, ra, st));
+    SENMOE_CUDA(exchange_routing());
+    SENMOE_CUDA(mark(1));
+    SENMOE_CUDA(launch_dispatch(da, st));
+  } else if (L->route_cnt && T_loc >= kFusedTopkMinTokens) {
     // one launch: logits, then top-k by the last CTA of each 4-token tile
     RouterArgs rf = ra;
     rf.tile_cnt = L->route_cnt;
     SENMOE_CUDA(launch_router_logits(rf, st));
+    SENMOE_CUDA(exchange_routing());
     SENMOE_CUDA(mark(1));
     SENMOE_CUDA(launch_dispatch(da, st));
-  } else if (router_topk_dispatch_supported(static_cast<int>(T), P, E)) {
+  } else if (!local && router_topk_dispatch_supported(static_cast<int>(T), P, E)) {
     // 1-8 tokens: logits, then top-k and the dispatch in one CTA
     SENMOE_CUDA(launch_router_logits(ra, st));
     SENMOE_CUDA(launch_router_topk_dispatch(ra, da, st));
@@ -526,27 +600,21 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   } else {
     SENMOE_CUDA(launch_router_logits(ra, st));
     SENMOE_CUDA(launch_router_topk(ra, st));
+    SENMOE_CUDA(exchange_routing());
     SENMOE_CUDA(mark(1));
     SENMOE_CUDA(launch_dispatch(da, st));
   }
-  EpArgs ea{};
-  if (ep) {
-    ea.rank = L->ep_rank;
-    ea.world = L->ep_world;
-    for (int r = 0; r <= L->ep_world; ++r) ea.bounds[r] = L->ep_bounds[r];
-    for (int r = 0; r < L->ep_world; ++r) {
-      ea.peer_d[r] = L->ep_peer_d[r];
-      ea.peer_y[r] = L->ep_peer_y[r];
-      ea.peer_flags[r] = L->ep_peer_flags[r];
-    }
-    ea.flags = L->ep_flags;
-    ea.epoch = L->ep_local;
-    ea.finished = L->ep_local + 1;
-    ea.topk_ids = ids;
-    ea.err = L->err;
-    // d is about to be overwritten: wait until the peers have read the last call's rows
-    SENMOE_CUDA(launch_ep_fence(ea, st));
+  // replicated form: d is about to be overwritten: wait until the peers have
+  // read the last call's rows (the token-local form did so first of all)
+  if (ep && !local) SENMOE_CUDA(launch_ep_fence(ea, st));
+  // token-local form: the gathers read each token's row from its owner's exchange
+  PeerRows prow{};
+  if (local) {
+    prow.world = L->ep_world;
+    for (int r = 0; r < L->ep_world; ++r) prow.base[r] = L->ep_peer_y[r];
+    for (int r = 0; r <= L->ep_world; ++r) prow.begin[r] = tok_begin[r];
   }
+  const PeerRows* prow_p = local ? &prow : nullptr;
 
   // 3-4. expert products over the touched local experts: h [P, I], d [P, H]
   const int E_local = c.expert_end - c.expert_begin;
@@ -585,7 +653,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     const bool q4 = g4 && nt == 1 && L->q4_ok && c.reserved[1] == kMmaFormAuto && max_items * (I / 128) < L->sms;
     SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
                                    L->offsets, c.expert_begin, c.expert_end,
-                                   g4 ? kOrderMmaG4 : kOrderMma, g4 ? L->xsum : nullptr));
+                                   g4 ? kOrderMmaG4 : kOrderMma, g4 ? L->xsum : nullptr, nullptr, prow_p));
     ga.xsum = L->xsum;
     SENMOE_CUDA(mark(2));
     if (q4) {
@@ -618,7 +686,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   } else if (path == kPathTensorCore) {
     const int ti = tc_tile_index(per_expert), bn = kTcTiles[ti];
     SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
-                                   L->offsets, c.expert_begin, c.expert_end));
+                                   L->offsets, c.expert_begin, c.expert_end, kOrderTc, nullptr, nullptr, prow_p));
     SENMOE_CUDA(mark(2));
     TcGemmArgs ga{};
     ga.s[0] = static_cast<const uint16_t*>(L->w.gate_scales);
@@ -704,9 +772,10 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   // token sh_t0 + i.  Otherwise the CUDA-core GEMV over every token.
   int sh_t0 = 0;
   if (Is > 0) {
-    const int sh_n = ep ? ep_token_begin(T, L->ep_world, L->ep_rank + 1) - ep_token_begin(T, L->ep_world, L->ep_rank)
-                        : T;
-    const int own_t0 = ep ? ep_token_begin(T, L->ep_world, L->ep_rank) : 0;
+    // the tokens this rank combines (global indices own_t0 ..); the
+    // token-local form holds exactly those in x
+    const int sh_n = local ? T_loc : ep ? ea.tok_begin[L->ep_rank + 1] - ea.tok_begin[L->ep_rank] : T;
+    const int own_t0 = local ? row0 : ep ? ea.tok_begin[L->ep_rank] : 0;
     const int forced = c.reserved[0];
     int sh_path = kPathGemv;
     if (forced == kPathTensorCore && L->sh_tc_ok) sh_path = kPathTensorCore;
@@ -746,7 +815,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
       sd.m_tiles = H / 128;
       sd.out = L->sh_out;
       sd.out_stride = H;
-      const uint16_t* xs_src = static_cast<const uint16_t*>(x) + static_cast<size_t>(sh_t0) * H;
+      const uint16_t* xs_src = static_cast<const uint16_t*>(x) + static_cast<size_t>(sh_t0 - row0) * H;
       if (sh_n > 0 && sh_path == kPathMma) {
         const int nt = T <= 8 ? 1 : (T <= 16 ? 2 : 4);
         const CUtensorMap& tb_x = nt == 1 ? L->tm_xsh8 : L->tm_xsh[nt == 2 ? 0 : 1];
@@ -769,6 +838,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
                                    (sh_n / bn + 1) * sd.m_tiles, st));
       }
     } else {
+      sh_t0 = row0;  // every token x holds, row i = global token row0 + i
       QGemvArgs sg{};
       sg.x = static_cast<const uint16_t*>(x);
       sg.w[0] = L->w.shared_gate_weight;
@@ -788,7 +858,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
       sg.out_stride = Is;
       sg.act = c.activation;
       sg.err = L->err;
-      SENMOE_CUDA(launch_qgemv(sg, 2, c.bits, T, st));
+      SENMOE_CUDA(launch_qgemv(sg, 2, c.bits, T_loc, st));
       QGemvArgs sd = sg;
       sd.x = L->sh_h;
       sd.w[0] = L->w.shared_down_weight;
@@ -799,7 +869,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
       sd.rows_per_cta = kDownRows;
       sd.out = L->sh_out;
       sd.out_stride = H;
-      SENMOE_CUDA(launch_qgemv(sd, 1, c.bits, T, st));
+      SENMOE_CUDA(launch_qgemv(sd, 1, c.bits, T_loc, st));
     }
     if (c.shared_gate) {
       RouterArgs gr = ra;
@@ -808,8 +878,10 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
       gr.num_experts = 1;
       gr.round_logits = 0;
       gr.tile_cnt = nullptr;  // a plain dot product: no top-k
-      SENMOE_CUDA(launch_router_logits(gr, st));
-      SENMOE_CUDA(launch_sigmoid_inplace(L->sh_gate, T, st));
+      if (T_loc > 0) {        // per token of x (combine: row t - local_row0)
+        SENMOE_CUDA(launch_router_logits(gr, st));
+        SENMOE_CUDA(launch_sigmoid_inplace(L->sh_gate, T_loc, st));
+      }
     }
   }
 
@@ -822,6 +894,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   ca.weights = wts;
   ca.shared_out = Is > 0 ? L->sh_out : nullptr;
   ca.shared_row0 = sh_t0;
+  ca.local_row0 = row0;
   ca.shared_gate = (Is > 0 && c.shared_gate) ? L->sh_gate : nullptr;
   ca.y = static_cast<uint16_t*>(y);
   ca.residual = residual ? static_cast<const uint16_t*>(x) : nullptr;
@@ -830,7 +903,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   ca.top_k = K;
   if (ep) {
     SENMOE_CUDA(launch_ep_combine(ea, ca, T, st));
-    SENMOE_CUDA(launch_ep_gather_rows(ea, ca.y, H, T, st));
+    if (!local) SENMOE_CUDA(launch_ep_gather_rows(ea, ca.y, H, T, st));
   } else
     SENMOE_CUDA(launch_combine(ca, T, st));
   SENMOE_CUDA(mark(6));
@@ -856,6 +929,20 @@ int senmoe_layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
 int senmoe_layer_forward_residual(SenMoeLayer* L, const void* x, int64_t num_tokens, void* h_out,
                                   senmoe_stream_t stream) {
   return layer_forward(L, x, num_tokens, h_out, nullptr, true, stream);
+}
+
+int senmoe_layer_forward_tokens(SenMoeLayer* L, const void* x, int64_t num_tokens, void* y,
+                                const int64_t* tokens_per_rank, int32_t residual, senmoe_stream_t stream) {
+  g_last_error.clear();
+  if (!L) return fail(SENMOE_ERR_BAD_ARG, "layer is NULL");
+  if (!tokens_per_rank) return fail(SENMOE_ERR_BAD_ARG, "tokens_per_rank is NULL");
+  if (L->ep_world == 0) {  // not connected: one rank holding every token
+    if (tokens_per_rank[0] != num_tokens)
+      return fail(SENMOE_ERR_BAD_ARG, "tokens_per_rank[0]=%lld is not num_tokens=%lld",
+                  (long long)tokens_per_rank[0], (long long)num_tokens);
+    return layer_forward(L, x, num_tokens, y, nullptr, residual != 0, stream);
+  }
+  return layer_forward(L, x, num_tokens, y, nullptr, residual != 0, stream, nullptr, nullptr, tokens_per_rank);
 }
 
 int senmoe_layer_expert_path(const SenMoeLayer* L, int64_t num_tokens) {
@@ -986,6 +1073,8 @@ int senmoe_layer_connect_peers(SenMoeLayer* L, int32_t rank, int32_t world_size,
     L->ep_peer_d[r] = reinterpret_cast<const uint16_t*>(bases[r] + L->o_d);
     L->ep_peer_y[r] = reinterpret_cast<uint16_t*>(bases[r] + L->o_yx);
     L->ep_peer_flags[r] = reinterpret_cast<uint32_t*>(bases[r] + L->o_flags);
+    L->ep_peer_ids[r] = reinterpret_cast<int32_t*>(bases[r] + L->o_ids);
+    L->ep_peer_wts[r] = reinterpret_cast<float*>(bases[r] + L->o_wts);
     L->ep_opened[r] = r == rank ? nullptr : bases[r];
     L->ep_bounds[r] = peers[r].expert_begin;
   }

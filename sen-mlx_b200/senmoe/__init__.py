@@ -98,6 +98,7 @@ SIGNATURES = {
     "senmoe_layer_peer_info": (C.c_int, [_P, C.POINTER(SenMoePeerInfo)]),
     "senmoe_layer_connect_peers": (C.c_int, [_P, _i32, _i32, C.POINTER(SenMoePeerInfo)]),
     "senmoe_layer_forward_residual": (C.c_int, [_P, _P, _i64, _P, _P]),
+    "senmoe_layer_forward_tokens": (C.c_int, [_P, _P, _i64, _P, C.POINTER(_i64), _i32, _P]),
     "senmoe_layer_set_profiling": (C.c_int, [_P, C.c_int]),
     "senmoe_layer_expert_path": (C.c_int, [_P, _i64]),
     "senmoe_layer_stage_times": (C.c_int, [_P, C.POINTER(C.c_float), C.c_int]),
@@ -329,6 +330,21 @@ class DeepseekMoe:
                                                    _ptr(h), _stream(stream)))
         return h
 
+    def forward_tokens(self, x: torch.Tensor, tokens_per_rank, residual: bool = False, stream=None,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+        """Token-local expert parallelism: ``x`` [T_r, H] holds this rank's
+        own tokens, ``tokens_per_rank[q]`` every rank's count (the same list
+        on every rank); returns forward(x) (+ x with ``residual``) for them."""
+        if x.dtype != torch.bfloat16 or not x.is_cuda or x.shape[-1] != self.args.hidden_size:
+            raise TypeError("x must be a CUDA bfloat16 tensor [..., hidden_size]")
+        xc = x.contiguous()
+        T = xc.numel() // self.args.hidden_size
+        counts = (C.c_int64 * max(len(tokens_per_rank), 1))(*[int(v) for v in tokens_per_rank])
+        y = torch.empty_like(xc) if out is None else out
+        _check(lib().senmoe_layer_forward_tokens(self._handle, _ptr(xc) if T else None, T, _ptr(y) if T else None,
+                                                 counts, int(residual), _stream(stream)))
+        return y
+
     def expert_path(self, num_tokens: int) -> int:
         """PATH_GEMV, PATH_MMA or PATH_TENSOR_CORE: the expert kernels a forward of num_tokens runs."""
         r = lib().senmoe_layer_expert_path(self._handle, int(num_tokens))
@@ -485,8 +501,11 @@ class MoeStack:
     graph launch instead of ~6 kernel launches per layer.
     """
 
-    def __init__(self, layers: list, max_tokens: int, use_graph: bool = True):
+    def __init__(self, layers: list, max_tokens: int, use_graph: bool = True, tokens_per_rank=None):
+        """``tokens_per_rank``: token-local expert parallelism (every rank
+        chains its own tokens; forward(x) takes this rank's count of them)."""
         self.layers = layers
+        self.tokens_per_rank = None if tokens_per_rank is None else [int(v) for v in tokens_per_rank]
         self.hidden = layers[0].args.hidden_size
         self.max_tokens = max_tokens
         self.use_graph = use_graph
@@ -500,7 +519,10 @@ class MoeStack:
     def _run(self, T: int) -> torch.Tensor:
         a, b = self.bufs
         for L in self.layers:
-            L.forward_residual(a[:T], stream=self.stream, out=b[:T])
+            if self.tokens_per_rank is not None:
+                L.forward_tokens(a[:T], self.tokens_per_rank, residual=True, stream=self.stream, out=b[:T])
+            else:
+                L.forward_residual(a[:T], stream=self.stream, out=b[:T])
             a, b = b, a
         return a[:T]
 

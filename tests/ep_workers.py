@@ -248,3 +248,63 @@ def ep_missing_rank(rank, world, H, I, E, K, bits, T, seed):
     epl.close()
     dist.barrier()
     return status
+
+
+def ep_tokens_forward(rank, world, H, I, E, K, bits, count_lists, shared, seed, expert_path):
+    """Token-local expert parallelism: rank r passes its own tokens (its
+    slice of the call's tokens, rank order) and must get back exactly what
+    one GPU returns for them when it runs every rank's tokens at once.
+    count_lists: per case, every rank's token count.  Returns per case the
+    bit-identity, repeatability and max abs vs the oracle, plus the same for
+    a graph-captured two-layer residual stack of the first case."""
+    import torch
+
+    import senmoe
+    from helpers import bf16_np_to_f32, moe_args, t_bf16, to_numpy_bf16
+    from oracle import oracle as O
+    from senmoe import ep
+
+    Tmax = max(sum(c) for c in count_lists)
+    cfg, mw, x_np, args, wd = _gpu_setup(rank, world, H, I, E, K, bits, Tmax, shared, seed)
+    args = moe_args(cfg, expert_path)
+    full = senmoe.DeepseekMoe(args, wd, max_tokens=Tmax)
+    epl = ep.make_layer(args, wd, Tmax, rank, world)
+    ep.connect([epl])
+    x = t_bf16(x_np, device=f"cuda:{rank}")
+    out = {}
+    for ci, counts in enumerate(count_lists):
+        T = sum(counts)
+        b = sum(counts[:rank])
+        n = counts[rank]
+        ref = full.forward(x[:T])[b:b + n]
+        y = epl.forward_tokens(x[b:b + n], counts)
+        y2 = epl.forward_tokens(x[b:b + n], counts)
+        epl.check()
+        full.check()
+        orc = O.moe_forward(cfg, mw, x_np[b:b + n]) if n else {"y_f32": np.zeros((0, H), np.float32)}
+        a = bf16_np_to_f32(to_numpy_bf16(y))
+        out[ci] = dict(exact=bool(torch.equal(y, ref)), repeat=bool(torch.equal(y, y2)),
+                       max_abs_full=float((y.float() - ref.float()).abs().max()) if n else 0.0,
+                       max_abs_oracle=float(np.abs(a - orc["y_f32"]).max()) if n else 0.0)
+    # a graph-captured two-layer residual stack over the first case's tokens
+    counts = count_lists[0]
+    T, b, n = sum(counts), sum(counts[:rank]), counts[rank]
+    epl2 = ep.make_layer(args, wd, Tmax, rank, world)
+    ep.connect([epl2])
+    full2 = senmoe.DeepseekMoe(args, wd, max_tokens=Tmax)
+    stack = senmoe.MoeStack([epl, epl2], max_tokens=Tmax, tokens_per_rank=counts)
+    ref_stack = senmoe.MoeStack([full, full2], max_tokens=Tmax, use_graph=False)
+    ys = [stack.forward(x[b:b + n]).clone() for _ in range(3)]
+    yr = ref_stack.forward(x[:T])[b:b + n]
+    epl.check()
+    epl2.check()
+    out["stack_repeat"] = all(bool(torch.equal(v, ys[0])) for v in ys)
+    out["stack_exact"] = bool(torch.equal(ys[0], yr))
+    stack.release()
+    torch.cuda.synchronize()
+    import torch.distributed as dist
+    dist.barrier()  # no rank frees its rows while a peer may still read them
+    for L in (epl, epl2, full, full2):
+        L.close()
+    dist.barrier()
+    return out

@@ -44,6 +44,42 @@ def test_expert_parallel_matches_one_gpu(world, case):
             assert r["max_abs_oracle"] <= MAX_ABS_TOL, f"rank {rank} T={T}: {r['max_abs_oracle']} vs oracle"
 
 
+TOKEN_CASES = {
+    # H, I, E, K, bits, shared, seed, expert_path
+    "config0": (2048, 768, 128, 8, 4, 0, 13, 0),
+    "shared8_tc": (256, 256, 16, 4, 8, 256, 15, 2),
+}
+
+
+def token_counts(world):
+    """Per case every rank's token count: equal small blocks, uneven blocks,
+    one rank without tokens, and prefill-size blocks (each case keeps the
+    same router kernel on the rank and on one GPU, so results are exact)."""
+    return [[16] * world, [8 + 7 * r for r in range(world)], [0] + [24] * (world - 1), [600] * world]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("case", sorted(TOKEN_CASES))
+def test_token_local_expert_parallel_matches_one_gpu(world, case):
+    """Token-local expert parallelism (each rank its own tokens; the prefill
+    form): every rank's output equals bit for bit what one GPU returns for
+    those tokens when it runs all ranks' tokens, on every call, and through a
+    graph-captured residual stack."""
+    if _ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
+    H, I, E, K, bits, shared, seed, path = TOKEN_CASES[case]
+    counts = token_counts(world)
+    res = spawn_ranks("ep_tokens_forward", world, H, I, E, K, bits, counts, shared, seed, path, timeout=600)
+    for rank, out in enumerate(res):
+        assert out["stack_repeat"], f"rank {rank}: graph replays of the token-local stack differ"
+        assert out["stack_exact"], f"rank {rank}: token-local stack differs from the one-GPU stack"
+        for ci in range(len(counts)):
+            r = out[ci]
+            assert r["repeat"], f"rank {rank} case {counts[ci]}: two calls differ"
+            assert r["exact"], f"rank {rank} case {counts[ci]}: differs from one GPU (max abs {r['max_abs_full']})"
+            assert r["max_abs_oracle"] <= MAX_ABS_TOL, f"rank {rank} case {counts[ci]}: {r['max_abs_oracle']}"
+
+
 def test_missing_rank_times_out_with_status():
     if _ngpu() < 2:
         pytest.skip("needs 2 GPUs")
