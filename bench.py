@@ -218,16 +218,17 @@ def pci_bus_id(torch, device: int) -> str | None:
 
 
 # --------------------------------------------------------------- weights
-def make_stack(torch, senmoe, device, spec, layers, max_tokens, rank=0, world=1, weights=None):
+def make_stack(torch, senmoe, device, spec, layers, max_tokens, rank=0, world=1, weights=None, expert_slots=0):
     """The rank's share of a synthetic `layers`-deep stack of `spec` on the
     device: this rank's experts of every layer (all of them on one GPU), the
-    router and shared expert whole.  `weights` reuses already built tensors."""
+    router and shared expert whole.  `weights` reuses already built tensors;
+    `expert_slots` caps each layer's per-pair scratch (expert parallelism)."""
     from senmoe import ep
     bnd = ep.expert_bounds(spec.experts, world)
     eb, ee = bnd[rank], bnd[rank + 1]
     if weights is None:
         weights = [synth.moe_weights(spec, l, device, experts=(eb, ee)) for l in range(layers)]
-    args = synth.moe_args(spec)
+    args = synth.moe_args(spec, expert_slots=expert_slots)
     blocks = [senmoe.DeepseekMoe(args, w, max_tokens=max_tokens, device=device, expert_range=(eb, ee))
               for w in weights]
     if world > 1:
@@ -506,11 +507,14 @@ def prefill_point(g, spec, stk, lays, x, steps, warmup, total_tokens=None):
     return out
 
 
-def arena_bytes(spec, max_tokens):
-    """About the scratch one layer allocates for max_tokens tokens (per pair:
-    gathered activations, h twice, d, group sums; per token: logits, rows)."""
+def arena_bytes(spec, max_tokens, expert_slots=0):
+    """About the scratch one layer allocates for max_tokens tokens (per
+    expert slot: gathered activations, h twice, d, group sums; per pair:
+    routing and permutation; per token: logits, rows)."""
     H_, I_, K_, E_ = spec.hidden, spec.intermediate, spec.top_k, spec.experts
-    return int(max_tokens * K_ * (4 * H_ + 4 * I_ + H_ // 16 + 24) + max_tokens * (4 * E_ + 4 * H_) + (1 << 20))
+    slots = expert_slots or max_tokens * K_
+    return int(slots * (4 * H_ + 4 * I_ + H_ // 16) + max_tokens * K_ * 24 + max_tokens * (4 * E_ + 4 * H_)
+               + (1 << 20))
 
 
 def free_stack(g, stk, lays):
@@ -693,10 +697,12 @@ def main():
     if world > 1 and args.prefill_tokens.strip():
         TL = int(args.prefill_tokens.split(",")[0])
         free_b = torch.cuda.mem_get_info(g.dev)[0]
-        while TL > 256 and args.layers * arena_bytes(SPEC, TL * world) > 0.7 * free_b:
+        # expert slots: twice a rank's even share of the pairs (TL * K)
+        while TL > 256 and args.layers * arena_bytes(SPEC, TL * world, 2 * TL * K) > 0.7 * free_b:
             TL //= 2
         TL = int(-g.max_over_ranks(-TL))  # every rank takes the smallest
-        pl, _ = make_stack(torch, senmoe, local, SPEC, args.layers, TL * world, rank, world, weights=wts)
+        pl, _ = make_stack(torch, senmoe, local, SPEC, args.layers, TL * world, rank, world, weights=wts,
+                           expert_slots=2 * TL * K)
         pstack = senmoe.MoeStack(pl, TL, use_graph=True, tokens_per_rank=[TL] * world)
         xp = synth.spec_tokens(SPEC, TL, device=g.dev, first=rank * TL)
         prefill[f"token_local_{TL}_per_gpu"] = prefill_point(g, SPEC, pstack, pl, xp, args.steps, args.warmup,

@@ -188,7 +188,10 @@ __global__ void __launch_bounds__(256, KMAX <= 8 ? 4 : 2) ep_combine_kernel(EpAr
           wj[j] = c.weights[p];
           if (slot >= 0) {
             const int e = a.topk_ids[p];
-            src[j] = a.peer_d[owner_of(a, e)] + static_cast<size_t>(slot) * c.hidden + col;
+            const int q = owner_of(a, e);
+            const int row = slot - a.offsets[a.bounds[q]];  // the owner's local row
+            if (a.slot_cap > 0 && row >= a.slot_cap) record_error(a.err, kDevSlotOverflow);
+            else src[j] = a.peer_d[q] + static_cast<size_t>(row) * c.hidden + col;
           }
         }
       }

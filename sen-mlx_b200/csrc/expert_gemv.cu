@@ -138,12 +138,13 @@ __global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(QGemvArgs a) {
   pdl_wait();  // the active list / offsets come from the dispatch kernel
   pdl_launch_dependents();
   // ---- which expert / slots does this CTA serve?
-  int expert, s_begin, s_end;
+  int expert, s_begin, s_end, s_local0 = 0;  // slot s is row s - s_local0 of out (and of x by slot)
   if (a.mode == kItemsGrouped) {
     if (blockIdx.x >= static_cast<unsigned>(*a.active_count)) return;
     expert = a.active[blockIdx.x];
     s_begin = a.offsets[expert];
     s_end = a.offsets[expert + 1];
+    s_local0 = a.offsets[a.expert_begin];  // this rank's first slot (0 on one GPU)
     expert -= a.expert_begin;
   } else {  // kItemsGather: one index per CTA row (no index list: expert 0, a dense linear)
     const uint32_t e = a.gather_idx ? a.gather_idx[blockIdx.x] : 0u;
@@ -193,10 +194,11 @@ __global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(QGemvArgs a) {
   }
 
   for (int s = s_begin; s < s_end; ++s) {
-    const int token = (a.mode == kItemsGather) ? static_cast<int>(s / a.rep) : (a.x_by_slot ? s : a.perm[s] / a.k_div);
+    const int token =
+        (a.mode == kItemsGather) ? static_cast<int>(s / a.rep) : (a.x_by_slot ? s - s_local0 : a.perm[s] / a.k_div);
     float xv[WPL][CPW], xs[WPL];
     load_x_slice<BITS, WPL>(a.x + static_cast<size_t>(token) * a.kdim, lane, words_per_row, xv, xs);
-    uint16_t* out = a.out + static_cast<size_t>(s) * a.out_stride + row0;
+    uint16_t* out = a.out + static_cast<size_t>(s - s_local0) * a.out_stride + row0;
     for (int r = warp; r < nrows; r += kGemvWarps) {
       float v0 = row_partial<BITS, WPL>(sw + static_cast<size_t>(r) * words_per_row, ss + r * groups,
                                         sb + r * groups, lane, words_per_row, xv, xs);

@@ -289,7 +289,7 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
   // until the producer starts: it is the list's scratch.
   {
     const int n = list_tiles(a.active, a.active_count, a.offsets, a.expert_begin, a.m_tiles, BM, BN, true, s_tiles,
-                             kMaxTilesPerCta, reinterpret_cast<int*>(sP), a.err);
+                             kMaxTilesPerCta, reinterpret_cast<int*>(sP), a.err, a.slot_cap);
     if (tid == 0) {
       s_ntiles = n;
       s_abort = 0;
@@ -766,7 +766,8 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
                                                           uint16_t* __restrict__ out, int num_slots, int hidden,
                                                           int* err, const int32_t* __restrict__ offsets, int eb,
                                                           int ee, int order, float* __restrict__ group_sums,
-                                                          int32_t* __restrict__ one_group, const PeerRows pr) {
+                                                          int32_t* __restrict__ one_group, const PeerRows pr,
+                                                          int slot_cap) {
   pdl_wait();
   pdl_launch_dependents();
   if (one_group && blockIdx.x == 0 && threadIdx.x == 0) {
@@ -782,6 +783,12 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
     lo_slot = offsets[eb];
     hi_slot = offsets[ee];
   }
+  // rows are local (slot - lo_slot) and the buffer holds slot_cap of them
+  if (slot_cap > 0 && hi_slot - lo_slot > slot_cap) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) record_error(err, kDevSlotOverflow);
+    hi_slot = lo_slot + slot_cap;
+  }
+  // slot s is row s - lo_slot of out (and of group_sums)
   const uint16_t* src[kGatherSlots];
   bool live[kGatherSlots];
 #pragma unroll
@@ -810,9 +817,9 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
         float sum = 0.f;
 #pragma unroll
         for (int q = 0; q < 32; ++q) sum += bf16_lo(w[q]) + bf16_hi(w[q]);
-        group_sums[static_cast<size_t>(s) * groups + G] = sum * 5.9604644775390625e-8f;  // 2^-24
+        group_sums[static_cast<size_t>(s - lo_slot) * groups + G] = sum * 5.9604644775390625e-8f;  // 2^-24
       }
-      uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(s) * hidden + 64 * G);
+      uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(s - lo_slot) * hidden + 64 * G);
 #pragma unroll
       for (int sg = 0; sg < 8; ++sg) {  // 16-byte segment: k-step sg / 2, kappa half sg % 2
         const int ks = sg >> 1, a2 = sg & 1;
@@ -856,7 +863,8 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
           const __half2 h = __floats2half2_rn(lo, hi);
           o[t] = *reinterpret_cast<const uint32_t*>(&h);
         }
-        reinterpret_cast<uint4*>(out + static_cast<size_t>(s0 + j) * hidden)[sg] = make_uint4(o[0], o[1], o[2], o[3]);
+        reinterpret_cast<uint4*>(out + static_cast<size_t>(s0 + j - lo_slot) * hidden)[sg] =
+            make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
   } else {
@@ -882,7 +890,8 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
           const __half2 h = __floats2half2_rn(f[k], f[k + 4]);
           o[k] = *reinterpret_cast<const uint32_t*>(&h);
         }
-        reinterpret_cast<uint4*>(out + static_cast<size_t>(s0 + j) * hidden)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+        reinterpret_cast<uint4*>(out + static_cast<size_t>(s0 + j - lo_slot) * hidden)[i] =
+            make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
   }
@@ -892,14 +901,15 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
                                int num_slots, int hidden, int* err, cudaStream_t st,
                                const int32_t* offsets, int eb, int ee, int order, float* group_sums,
-                               int32_t* one_group, const PeerRows* peer_rows) {
+                               int32_t* one_group, const PeerRows* peer_rows, int slot_cap) {
   if (num_slots <= 0) return cudaSuccess;
   const int threads = hidden / 8 < 256 ? ((hidden / 8 + 31) / 32) * 32 : 256;
   const int grid = (num_slots + kGatherSlots - 1) / kGatherSlots;
   PeerRows pr{};
   if (peer_rows) pr = *peer_rows;
   return launch_pdl(gather_rows_kernel, dim3(grid), dim3(threads), 0, st, x, perm, k_div, x_sorted, num_slots,
-                    hidden, err, offsets, eb, ee, order, order == kOrderMmaG4 ? group_sums : nullptr, one_group, pr);
+                    hidden, err, offsets, eb, ee, order, order == kOrderMmaG4 ? group_sums : nullptr, one_group, pr,
+                    slot_cap);
 }
 
 }  // namespace senmoe

@@ -16,6 +16,7 @@ enum DeviceError : int {
   kDevFp16Range = 3,    // an activation outside fp16 range met the tensor-core path
   kDevTileOverflow = 4, // a persistent CTA was handed more tiles than it can list
   kDevPeerTimeout = 5,  // a bounded wait on another rank's flag ran out
+  kDevSlotOverflow = 6, // more pairs reached this rank's experts than its expert-slot capacity
 };
 
 // -------------------------------------------------------------- dispatch
@@ -99,7 +100,8 @@ struct QGemvArgs {
   const uint16_t* b[2];
   int kdim, rows, rows_per_cta;
   int mode;                 // ItemMode
-  // grouped items: CTA x-index i serves active[i]'s slots offsets[e]..offsets[e+1]
+  // grouped items: CTA x-index i serves active[i]'s slots offsets[e]..offsets[e+1];
+  // slot s is row s - offsets[expert_begin] of out (and of x when x_by_slot)
   const int32_t* active;
   const int32_t* active_count;
   const int32_t* offsets;
@@ -157,6 +159,10 @@ struct TcGemmArgs {
   // group sums x 2^-24 ([slots + 16, kdim/64] fp32, from gather_rows); the
   // one-projection form computes its own.
   const float* xsum;
+  // Slots are local: slot s of the tile list is row s - offsets[expert_begin]
+  // of the activation, h and out buffers, which hold slot_cap rows (0: no
+  // limit); rows past slot_cap are not computed (kDevSlotOverflow).
+  int slot_cap;
 };
 size_t tc_smem_bytes(int bits, int nproj, int bn, int kdim);
 bool tc_supported(int rows, int kdim, int bits, int nproj, int bn);
@@ -167,8 +173,10 @@ cudaError_t launch_tc_gemm(const CUtensorMap& tA0, const CUtensorMap& tA1, const
 cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t inner,
                          uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                          bool swizzle128);
-// x_sorted[s, :] = fp16(x[perm[s] / k_div, :]) for s < num_slots (x bf16, rows of
-// `hidden`); a value outside fp16 range records kDevFp16Range in *err.
+// x_sorted[s - s0, :] = fp16(x[perm[s] / k_div, :]) for s < num_slots (x bf16, rows of
+// `hidden`; s0 = offsets[eb], 0 without offsets); a value outside fp16 range
+// records kDevFp16Range in *err.  With slot_cap > 0 rows past it are skipped
+// (kDevSlotOverflow).
 // With `offsets` non-null only the slots of experts [eb, ee), i.e. slots
 // offsets[eb] .. offsets[ee], are gathered (the layer always passes them:
 // slots past offsets[E] hold no placed pair when the dispatch rejected an
@@ -199,7 +207,7 @@ cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div
                                int num_slots, int hidden, int* err, cudaStream_t st,
                                const int32_t* offsets = nullptr, int eb = 0, int ee = 0, int order = kOrderTc,
                                float* group_sums = nullptr, int32_t* one_group = nullptr,
-                               const PeerRows* peer_rows = nullptr);
+                               const PeerRows* peer_rows = nullptr, int slot_cap = 0);
 
 // ------------------------------------------- warp-MMA expert GEMM (decode)
 // Same arguments as the tcgen05 GEMM (TcGemmArgs; out holds h as fp16 in
@@ -249,6 +257,10 @@ struct EpArgs {
   uint32_t* finished;                  // combine CTA completion counter
   uint32_t* published;                 // publish CTA completion counter (token-local form)
   const int32_t* topk_ids;             // [T*K]
+  // the call's expert offsets [E + 1] (the same on every rank): rank q's row
+  // of global slot s is s - offsets[bounds[q]], below slot_cap (0: no limit)
+  const int32_t* offsets;
+  int slot_cap;
   // token-local form: every rank's routing arrays (global pair rows), mapped here
   int32_t* peer_ids[kEpMaxRanks];
   float* peer_wts[kEpMaxRanks];

@@ -108,6 +108,7 @@ struct SenMoeLayer {
   int device = 0;
   int max_pairs = 0;
   int nchunks_max = 0;
+  int slot_cap = 0;  // rows of the per-pair buffers (local expert slots); max_pairs unless capped
   // scratch (one allocation, carved)
   void* arena = nullptr;
   float* logits = nullptr;       // [Tmax, E]
@@ -267,18 +268,22 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
   const size_t P = T * K;
   L->max_pairs = static_cast<int>(P);
   L->nchunks_max = static_cast<int>((P + kDispatchChunk - 1) / kDispatchChunk);
+  // per-pair buffers hold this rank's slots only: up to every pair, or the
+  // configured expert-slot capacity (expert parallelism)
+  const size_t C = (c.reserved[2] > 0 && size_t(c.reserved[2]) < P) ? size_t(c.reserved[2]) : P;
+  L->slot_cap = static_cast<int>(C);
 
   // carve one arena (256-byte aligned pieces)
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
   const size_t o_logits = take(T * E * 4), o_ids = take(P * 4), o_wts = take(P * 4), o_perm = take(P * 4),
                o_inv = take(P * 4), o_offs = take((E + 1) * 4), o_act = take(E * 4), o_cnt = take(4),
-               o_err = take(4), o_hist = take(size_t(L->nchunks_max) * E * 4), o_h = take(P * I * 2),
-               o_d = take(P * H * 2), o_shh = take(Is ? T * Is * 2 : 0), o_sho = take(Is ? T * H * 2 : 0),
-               o_shg = take(Is ? T * 4 : 0), o_zero = take(Is ? T * 4 : 0), o_xs = take(P * H * 2),
-               o_h16 = take(P * I * 2), o_flags = take(kEpFlagBytes), o_local = take(16),
+               o_err = take(4), o_hist = take(size_t(L->nchunks_max) * E * 4), o_h = take(C * I * 2),
+               o_d = take(C * H * 2), o_shh = take(Is ? T * Is * 2 : 0), o_sho = take(Is ? T * H * 2 : 0),
+               o_shg = take(Is ? T * 4 : 0), o_zero = take(Is ? T * 4 : 0), o_xs = take(C * H * 2),
+               o_h16 = take(C * I * 2), o_flags = take(kEpFlagBytes), o_local = take(16),
                o_route = take((T + 3) / 4 * 4), o_yx = take(T * H * 2),
-               o_xsum = take((P + 16) * (H / 64) * 4), o_xssh = take(Is ? T * H * 2 : 0),
+               o_xsum = take((C + 16) * (H / 64) * 4), o_xssh = take(Is ? T * H * 2 : 0),
                o_hsh = take(Is ? T * Is * 2 : 0), o_xsumsh = take(Is ? (T + 16) * (H / 64) * 4 : 0),
                o_iota = take(Is ? T * 4 : 0), o_shgrp = take(Is ? 16 : 0);
   cudaError_t e = cudaMalloc(&L->arena, off);
@@ -336,16 +341,16 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
     maps = maps && make_tmap_2d(&L->tm_down, L->w.down_weight, CU_TENSOR_MAP_DATA_TYPE_UINT32, dw,
                                 uint64_t(El) * H, dw * 4, 32, 128, true) == cudaSuccess;
     for (int i = 0; i < 4 && maps; ++i) {
-      maps = make_tmap_2d(&L->tm_xs[i], L->xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, H, P, H * 2, 64, kTcTiles[i],
+      maps = make_tmap_2d(&L->tm_xs[i], L->xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, H, C, H * 2, 64, kTcTiles[i],
                           true) == cudaSuccess &&
-             make_tmap_2d(&L->tm_h[i], L->h16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, I, P, I * 2, 64, kTcTiles[i],
+             make_tmap_2d(&L->tm_h[i], L->h16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, I, C, I * 2, 64, kTcTiles[i],
                           true) == cudaSuccess;
     }
     L->tc_ok = maps && tc_supported(int(I), int(H), bits, 2, 128) && tc_supported(int(H), int(I), bits, 1, 128);
     L->mma_ok = maps && mma_supported(int(I), int(H), bits) && mma_supported(int(H), int(I), bits) &&
-                make_tmap_2d(&L->tm_xs8, L->xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, H, P, H * 2, 64, 8, true) ==
+                make_tmap_2d(&L->tm_xs8, L->xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, H, C, H * 2, 64, 8, true) ==
                     cudaSuccess &&
-                make_tmap_2d(&L->tm_h8, L->h16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, I, P, I * 2, 64, 8, true) ==
+                make_tmap_2d(&L->tm_h8, L->h16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, I, C, I * 2, 64, 8, true) ==
                     cudaSuccess;
   }
   cudaDeviceGetAttribute(&L->sms, cudaDevAttrMultiProcessorCount, device);
@@ -492,6 +497,13 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   if (local && expert_path_for(L, P) == kPathGemv)
     return fail(SENMOE_ERR_UNSUPPORTED, "token-local expert parallelism needs the tensor-core expert kernels (the "
                                         "CUDA-core GEMV path reads tokens from x)");
+  // with a capped expert-slot buffer (fewer rows than pairs) only the
+  // expert-parallel tensor-core paths run: they skip and report rows past
+  // the cap, where the one-GPU combine and the GEMV would index past it
+  const int slot_cap = L->slot_cap < P ? L->slot_cap : 0;
+  if (slot_cap && (L->ep_world == 0 || expert_path_for(L, P) == kPathGemv))
+    return fail(SENMOE_ERR_UNSUPPORTED, "%d pairs with an expert-slot capacity of %d: a capped layer needs expert "
+                "parallelism and the tensor-core expert kernels", P, L->slot_cap);
   // Stage events are recorded only outside a stream capture (inside one a
   // plain record only links the capture's streams).
   bool profile = L->profiling;
@@ -525,6 +537,8 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     ea.finished = L->ep_local + 1;
     ea.published = L->ep_local + 2;
     ea.topk_ids = ids;
+    ea.offsets = L->offsets;
+    ea.slot_cap = slot_cap;
     ea.top_k = K;
     ea.err = L->err;
   }
@@ -653,8 +667,9 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     const bool q4 = g4 && nt == 1 && L->q4_ok && c.reserved[1] == kMmaFormAuto && max_items * (I / 128) < L->sms;
     SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
                                    L->offsets, c.expert_begin, c.expert_end,
-                                   g4 ? kOrderMmaG4 : kOrderMma, g4 ? L->xsum : nullptr, nullptr, prow_p));
+                                   g4 ? kOrderMmaG4 : kOrderMma, g4 ? L->xsum : nullptr, nullptr, prow_p, slot_cap));
     ga.xsum = L->xsum;
+    ga.slot_cap = slot_cap;
     SENMOE_CUDA(mark(2));
     if (q4) {
       ga.m_tiles = I / 64;
@@ -686,7 +701,8 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   } else if (path == kPathTensorCore) {
     const int ti = tc_tile_index(per_expert), bn = kTcTiles[ti];
     SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
-                                   L->offsets, c.expert_begin, c.expert_end, kOrderTc, nullptr, nullptr, prow_p));
+                                   L->offsets, c.expert_begin, c.expert_end, kOrderTc, nullptr, nullptr, prow_p,
+                                   slot_cap));
     SENMOE_CUDA(mark(2));
     TcGemmArgs ga{};
     ga.s[0] = static_cast<const uint16_t*>(L->w.gate_scales);
@@ -704,6 +720,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     ga.out_stride = I;
     ga.act = c.activation;
     ga.err = L->err;
+    ga.slot_cap = slot_cap;
     SENMOE_CUDA(launch_tc_gemm(L->tm_gate, L->tm_up, L->tm_xs[ti], ga, c.bits, 2, bn,
                                (P / bn + max_items) * ga.m_tiles, st));
     SENMOE_CUDA(mark(3));
@@ -996,6 +1013,9 @@ int senmoe_layer_check(SenMoeLayer* L, senmoe_stream_t stream) {
     if (host_err == kDevPeerTimeout)
       return fail(SENMOE_ERR_TIMEOUT, "a wait for another expert-parallel rank ran out (a rank missed a forward, "
                                       "or ran a different sequence of forwards)");
+    if (host_err == kDevSlotOverflow)
+      return fail(SENMOE_ERR_DEVICE, "more pairs reached this rank's experts than its expert-slot capacity (%d); "
+                                     "the excess was skipped", L->slot_cap);
     if (host_err == kDevFp16Range)
       return fail(SENMOE_ERR_DEVICE, "an activation outside fp16 range reached the tensor-core path (use the "
                                      "CUDA-core path, expert path 1, for such inputs)");

@@ -19,10 +19,12 @@ constexpr int kTileScratchInts = 4 * 512 + 64;  // per active expert: e, s0, cnt
 // memory; it ends with __syncthreads.  The loads of the active list and the
 // offsets are issued by all threads at once: a single thread walking the list
 // would wait on one dependent global load per expert.
+// Slots come out local: offsets[e] - offsets[expert_begin]; with slot_cap >
+// 0 an expert's slots past slot_cap are dropped (kDevSlotOverflow).
 __device__ __forceinline__ int list_tiles(const int32_t* __restrict__ active, const int32_t* __restrict__ active_count,
                                           const int32_t* __restrict__ offsets, int expert_begin, int m_tiles, int bm,
                                           int bn, bool chunk_major, int4* s_tiles, int max_tiles, int* scratch,
-                                          int* err) {
+                                          int* err, int slot_cap = 0) {
   int* s_e = scratch;
   int* s_s0 = scratch + 512;
   int* s_cnt = scratch + 1024;
@@ -33,7 +35,13 @@ __device__ __forceinline__ int list_tiles(const int32_t* __restrict__ active, co
   int v = 0;
   if (tid < nact) {
     const int e = active[tid];
-    const int s0 = offsets[e], cnt = offsets[e + 1] - s0;
+    const int base = offsets[expert_begin];
+    const int s0 = offsets[e] - base;
+    int cnt = offsets[e + 1] - offsets[e];
+    if (slot_cap > 0 && s0 + cnt > slot_cap) {
+      cnt = s0 < slot_cap ? slot_cap - s0 : 0;
+      record_error(err, kDevSlotOverflow);
+    }
     s_e[tid] = e;
     s_s0[tid] = s0;
     s_cnt[tid] = cnt;

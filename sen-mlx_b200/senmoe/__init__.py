@@ -205,6 +205,9 @@ class MoeArgs:
     # warp-MMA form: 0 group-scaled 4-bit where supported (two CTAs per SM at 8-slot tiles),
     # 1 dequantise every weight to fp16, 2 group-scaled with one CTA per SM at every tile width
     mma_form: int = 0
+    # expert parallelism: the most (token, expert) pairs this rank's experts take per call
+    # (per-pair scratch rows); 0 = max_tokens * num_experts_per_tok
+    expert_slots: int = 0
 
 
 @dataclass
@@ -260,6 +263,7 @@ class DeepseekMoe:
         cfg.expert_begin, cfg.expert_end = eb, ee
         cfg.reserved[0] = int(args.expert_path)
         cfg.reserved[1] = int(args.mma_form)
+        cfg.reserved[2] = int(args.expert_slots)
         self._cfg = cfg
         wt = SenMoeWeights()
         wt.router_weight = _ptr(weights.router_weight)

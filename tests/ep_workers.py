@@ -264,11 +264,16 @@ def ep_tokens_forward(rank, world, H, I, E, K, bits, count_lists, shared, seed, 
     from oracle import oracle as O
     from senmoe import ep
 
+    from dataclasses import replace
+
     Tmax = max(sum(c) for c in count_lists)
     cfg, mw, x_np, args, wd = _gpu_setup(rank, world, H, I, E, K, bits, Tmax, shared, seed)
     args = moe_args(cfg, expert_path)
     full = senmoe.DeepseekMoe(args, wd, max_tokens=Tmax)
-    epl = ep.make_layer(args, wd, Tmax, rank, world)
+    # expert-slot capacity: twice a rank's even share of the pairs (the scratch
+    # of an expert-parallel rank shrinks with the world size)
+    args_ep = replace(args, expert_slots=max(64, 2 * Tmax * K // world))
+    epl = ep.make_layer(args_ep, wd, Tmax, rank, world)
     ep.connect([epl])
     x = t_bf16(x_np, device=f"cuda:{rank}")
     out = {}
@@ -289,7 +294,7 @@ def ep_tokens_forward(rank, world, H, I, E, K, bits, count_lists, shared, seed, 
     # a graph-captured two-layer residual stack over the first case's tokens
     counts = count_lists[0]
     T, b, n = sum(counts), sum(counts[:rank]), counts[rank]
-    epl2 = ep.make_layer(args, wd, Tmax, rank, world)
+    epl2 = ep.make_layer(args_ep, wd, Tmax, rank, world)
     ep.connect([epl2])
     full2 = senmoe.DeepseekMoe(args, wd, max_tokens=Tmax)
     stack = senmoe.MoeStack([epl, epl2], max_tokens=Tmax, tokens_per_rank=counts)

@@ -270,3 +270,32 @@ def test_cuda_graph_capture_of_forward(senmoe, config0_layer):
     assert torch.equal(y, ref)
     del g
     blk.close()
+
+
+def test_expert_slot_capacity_overflow_is_reported(senmoe):
+    """An expert-slot capacity below the pairs a call sends to the rank's
+    experts: the kernels skip the excess and check() reports a device error
+    (the context stays usable); a capped layer without expert parallelism is
+    refused on the host."""
+    from dataclasses import replace
+
+    import torch
+    cfg = O.MoeConfig(hidden=256, intermediate=256, num_experts=16, top_k=4, bits=4)
+    mw = O.make_layer(cfg, seed=31)
+    args = replace(moe_args(cfg, PATHS["tc"]), expert_slots=32)
+    x = t_bf16(O.make_tokens(40, cfg.hidden, seed=2))
+    blk = senmoe.DeepseekMoe(args, device_weights(mw), max_tokens=64)
+    with pytest.raises(senmoe.SenMoeError) as e:
+        blk.forward(x)  # 160 pairs, capacity 32, one GPU
+    assert e.value.status == senmoe.ERR_UNSUPPORTED
+    blk.forward(x[:8])  # 32 pairs fit: runs
+    blk.check()
+    blk.connect_peers(0, [blk.peer_info()])  # expert parallelism of one rank
+    blk.forward(x)
+    with pytest.raises(senmoe.SenMoeError) as e:
+        blk.check()
+    assert e.value.status == senmoe.ERR_DEVICE and "capacity" in str(e.value)
+    y = blk.forward(x[:8])  # the context stays usable
+    blk.check()
+    assert torch.isfinite(y.float()).all()
+    blk.close()
