@@ -4,6 +4,8 @@ its owner GPU.  Every rank must return the same output, repeatably, equal bit
 for bit to the one-GPU layer's (same kernels, same expert rows, same slot
 order and fp32 sums) and within the parity tolerance of the oracle.  Skipped
 with fewer than 2 GPUs."""
+import os
+
 import pytest
 import torch
 
@@ -11,6 +13,10 @@ from ep_workers import spawn_ranks
 from helpers import MAX_ABS_TOL
 
 pytestmark = pytest.mark.gpu
+
+
+# world sizes to run (SENMOE_EP_WORLDS="8" runs only the 8-rank cases)
+WORLDS = [int(w) for w in os.environ.get("SENMOE_EP_WORLDS", "2,4,8").split(",")]
 
 
 def _ngpu() -> int:
@@ -25,7 +31,7 @@ CASES = {
 }
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("world", WORLDS)
 @pytest.mark.parametrize("case", sorted(CASES))
 def test_expert_parallel_matches_one_gpu(world, case):
     if _ngpu() < world:
@@ -58,7 +64,7 @@ def token_counts(world):
     return [[16] * world, [8 + 7 * r for r in range(world)], [0] + [24] * (world - 1), [600] * world]
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("world", WORLDS)
 @pytest.mark.parametrize("case", sorted(TOKEN_CASES))
 def test_token_local_expert_parallel_matches_one_gpu(world, case):
     """Token-local expert parallelism (each rank its own tokens; the prefill
