@@ -147,6 +147,25 @@ def decomposition(rank, world, bits):
 
 
 # ------------------------------------------------------------------ GPU ranks
+def two_cta_form(args, T, world, sms):
+    """Whether a forward of T tokens takes the warp-MMA kernel's two-CTA
+    (64-row) group-scaled form, by the layer's own choice (layer.cu: tokens
+    per touched local expert, slots per tile, and whether the 128-row gate/up
+    tiles fill the SMs).  An expert-parallel rank holds E / world experts, so
+    it can take that form where one GPU does not; the two forms add a row's
+    k-partitions in a different order (equal within the block tolerance, not
+    bit for bit)."""
+    K, E, I = args.num_experts_per_tok, args.n_routed_experts, args.moe_intermediate_size
+    P = T * K
+    e_local = E // world if world > 1 else E
+    pairs = P * e_local // E if world > 1 else P
+    pairs = max(pairs, 1)
+    pe = pairs / min(pairs, e_local)
+    if args.expert_path not in (0, 3) or (args.expert_path == 0 and pe >= 24.0):
+        return False  # not the warp-MMA path
+    return (args.bits == 4 and pe <= 8.0 and args.mma_form == 0 and min(P, e_local) * (I // 128) < sms)
+
+
 def _gpu_setup(rank, world, H, I, E, K, bits, T, shared, seed):
     import torch
 
@@ -189,7 +208,9 @@ def ep_forward(rank, world, H, I, E, K, bits, Ts, shared, seed, expert_path):
         full.check()
         orc = O.moe_forward(cfg, mw, x_np[:T])
         a, b2 = to_numpy_bf16(y), to_numpy_bf16(ref)
+        sms = torch.cuda.get_device_properties(rank).multi_processor_count
         out[T] = dict(exact=bool(torch.equal(y, ref)), repeat=bool(torch.equal(y, y2)),
+                      same_kernels=two_cta_form(args, T, world, sms) == two_cta_form(args, T, 1, sms),
                       digest=hashlib.sha256(a.tobytes()).hexdigest(),
                       max_abs=float(np.abs(bf16_np_to_f32(a) - bf16_np_to_f32(b2)).max()),
                       rel_l2=float(rel_l2(bf16_np_to_f32(a), bf16_np_to_f32(b2))),
@@ -209,6 +230,8 @@ def ep_forward(rank, world, H, I, E, K, bits, Ts, shared, seed, expert_path):
     out["stack_repeat"] = all(bool(torch.equal(v, ys[0])) for v in ys)
     out["stack_digest"] = hashlib.sha256(to_numpy_bf16(ys[0]).tobytes()).hexdigest()
     out["stack_max_abs"] = float((ys[0].float() - yr.float()).abs().max())
+    sms = torch.cuda.get_device_properties(rank).multi_processor_count
+    out["stack_same_kernels"] = two_cta_form(args, T, world, sms) == two_cta_form(args, T, 1, sms)
     stack.release()
     torch.cuda.synchronize()
     import torch.distributed as dist
@@ -288,7 +311,9 @@ def ep_tokens_forward(rank, world, H, I, E, K, bits, count_lists, shared, seed, 
         full.check()
         orc = O.moe_forward(cfg, mw, x_np[b:b + n]) if n else {"y_f32": np.zeros((0, H), np.float32)}
         a = bf16_np_to_f32(to_numpy_bf16(y))
+        sms = torch.cuda.get_device_properties(rank).multi_processor_count
         out[ci] = dict(exact=bool(torch.equal(y, ref)), repeat=bool(torch.equal(y, y2)),
+                       same_kernels=two_cta_form(args, T, world, sms) == two_cta_form(args, T, 1, sms),
                        max_abs_full=float((y.float() - ref.float()).abs().max()) if n else 0.0,
                        max_abs_oracle=float(np.abs(a - orc["y_f32"]).max()) if n else 0.0)
     # a graph-captured two-layer residual stack over the first case's tokens
@@ -305,6 +330,9 @@ def ep_tokens_forward(rank, world, H, I, E, K, bits, count_lists, shared, seed, 
     epl2.check()
     out["stack_repeat"] = all(bool(torch.equal(v, ys[0])) for v in ys)
     out["stack_exact"] = bool(torch.equal(ys[0], yr))
+    out["stack_max_abs"] = float((ys[0].float() - yr.float()).abs().max()) if n else 0.0
+    sms = torch.cuda.get_device_properties(rank).multi_processor_count
+    out["stack_same_kernels"] = two_cta_form(args, T, world, sms) == two_cta_form(args, T, 1, sms)
     stack.release()
     torch.cuda.synchronize()
     import torch.distributed as dist

@@ -41,12 +41,20 @@ def test_expert_parallel_matches_one_gpu(world, case):
     for rank, out in enumerate(res):
         assert out["stack_repeat"], f"rank {rank}: graph replays of the EP stack differ"
         assert out["stack_digest"] == res[0]["stack_digest"], f"rank {rank}: EP stack output differs across ranks"
-        assert out["stack_max_abs"] == 0.0, f"rank {rank}: EP stack differs from the one-GPU stack"
+        if out["stack_same_kernels"]:
+            assert out["stack_max_abs"] == 0.0, f"rank {rank}: EP stack differs from the one-GPU stack"
+        else:
+            assert out["stack_max_abs"] <= MAX_ABS_TOL, f"rank {rank}: EP stack {out['stack_max_abs']} from one GPU"
         for T in Ts:
             r = out[T]
             assert r["repeat"], f"rank {rank} T={T}: two EP calls differ"
             assert r["digest"] == res[0][T]["digest"], f"rank {rank} T={T}: ranks disagree"
-            assert r["exact"], f"rank {rank} T={T}: EP output differs from one GPU (max abs {r['max_abs']})"
+            # bit-identical to one GPU whenever both take the same kernels (the
+            # rank may pick the warp-MMA kernel's two-CTA form, holding fewer experts)
+            if r["same_kernels"]:
+                assert r["exact"], f"rank {rank} T={T}: EP output differs from one GPU (max abs {r['max_abs']})"
+            else:
+                assert r["max_abs"] <= MAX_ABS_TOL and r["rel_l2"] <= 1e-3, f"rank {rank} T={T}: {r}"
             assert r["max_abs_oracle"] <= MAX_ABS_TOL, f"rank {rank} T={T}: {r['max_abs_oracle']} vs oracle"
 
 
@@ -78,11 +86,17 @@ def test_token_local_expert_parallel_matches_one_gpu(world, case):
     res = spawn_ranks("ep_tokens_forward", world, H, I, E, K, bits, counts, shared, seed, path, timeout=600)
     for rank, out in enumerate(res):
         assert out["stack_repeat"], f"rank {rank}: graph replays of the token-local stack differ"
-        assert out["stack_exact"], f"rank {rank}: token-local stack differs from the one-GPU stack"
+        if out["stack_same_kernels"]:
+            assert out["stack_exact"], f"rank {rank}: token-local stack differs from the one-GPU stack"
+        else:
+            assert out["stack_max_abs"] <= MAX_ABS_TOL, f"rank {rank}: stack {out['stack_max_abs']} from one GPU"
         for ci in range(len(counts)):
             r = out[ci]
             assert r["repeat"], f"rank {rank} case {counts[ci]}: two calls differ"
-            assert r["exact"], f"rank {rank} case {counts[ci]}: differs from one GPU (max abs {r['max_abs_full']})"
+            if r["same_kernels"]:
+                assert r["exact"], f"rank {rank} case {counts[ci]}: differs from one GPU (max abs {r['max_abs_full']})"
+            else:
+                assert r["max_abs_full"] <= MAX_ABS_TOL, f"rank {rank} case {counts[ci]}: {r['max_abs_full']}"
             assert r["max_abs_oracle"] <= MAX_ABS_TOL, f"rank {rank} case {counts[ci]}: {r['max_abs_oracle']}"
 
 
