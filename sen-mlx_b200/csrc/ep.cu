@@ -93,22 +93,23 @@ __global__ void ep_announce_kernel(EpArgs a) {
   if (r < a.world) st_release_sys(a.peer_flags[r] + kEpReadyOffset + a.rank, epoch);
 }
 
-// Token-local form: this rank's token rows -> its own exchange buffer (the
-// peers' gathers read them there), its routing rows (global pair rows
-// [tok_begin[rank] * K, ...)) -> every peer's routing arrays; the last CTA
-// to finish raises ids[rank] in every rank's flags.  Each CTA fences its
+// Partitioned routing: this rank's routing rows (global pair rows
+// [tok_begin[rank] * K, + n_routed * K)) -> every peer's routing arrays and,
+// in the token-local form, its n_rows token rows -> its own exchange buffer
+// (the peers' gathers read them there); the last CTA to finish raises
+// ids[rank] in every rank's flags.  Each CTA fences its
 // stores (one system-scope fence after a barrier) before it counts itself.
-__global__ void __launch_bounds__(256) ep_publish_kernel(EpArgs a, const uint16_t* __restrict__ x, int n_local,
-                                                         int hidden) {
+__global__ void __launch_bounds__(256) ep_publish_kernel(EpArgs a, const uint16_t* __restrict__ x, int n_rows,
+                                                         int n_routed, int hidden) {
   pdl_wait();  // the router's ids / weights of this call are complete
   pdl_launch_dependents();
   const uint32_t epoch = *a.epoch;
   const size_t nthreads = size_t(gridDim.x) * blockDim.x, tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  const size_t nvec = size_t(n_local) * hidden / 8;
+  const size_t nvec = size_t(n_rows) * hidden / 8;
   const uint4* src = reinterpret_cast<const uint4*>(x);
   uint4* dst = reinterpret_cast<uint4*>(a.peer_y[a.rank]);
   for (size_t i = tid; i < nvec; i += nthreads) dst[i] = __ldcg(src + i);
-  const size_t p0 = size_t(a.tok_begin[a.rank]) * a.top_k, np = size_t(n_local) * a.top_k;
+  const size_t p0 = size_t(a.tok_begin[a.rank]) * a.top_k, np = size_t(n_routed) * a.top_k;
   for (size_t i = tid; i < np; i += nthreads) {
     const int32_t id = a.peer_ids[a.rank][p0 + i];
     const float w = a.peer_wts[a.rank][p0 + i];
@@ -297,12 +298,13 @@ cudaError_t launch_ep_announce(const EpArgs& a, cudaStream_t st) {
   return launch_pdl(ep_announce_kernel, dim3(1), dim3(32), 0, st, a);
 }
 
-cudaError_t launch_ep_publish(const EpArgs& a, const uint16_t* x, int n_local, int hidden, cudaStream_t st) {
+cudaError_t launch_ep_publish(const EpArgs& a, const uint16_t* x, int n_rows, int n_routed, int hidden,
+                              cudaStream_t st) {
   // enough CTAs to stream the rows at full bandwidth; at least one raises the flags
-  const size_t vec = size_t(n_local) * hidden / 8;
-  int grid = static_cast<int>((vec + 255) / 256);
+  const size_t work = size_t(n_rows) * hidden / 8 + size_t(n_routed) * a.top_k;
+  int grid = static_cast<int>((work + 255) / 256);
   grid = grid < 1 ? 1 : (grid > 296 ? 296 : grid);
-  return launch_pdl(ep_publish_kernel, dim3(grid), dim3(256), 0, st, a, x, n_local, hidden);
+  return launch_pdl(ep_publish_kernel, dim3(grid), dim3(256), 0, st, a, x, n_rows, n_routed, hidden);
 }
 
 cudaError_t launch_ep_wait_published(const EpArgs& a, cudaStream_t st) {

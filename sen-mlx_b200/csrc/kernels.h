@@ -278,12 +278,14 @@ cudaError_t launch_ep_announce(const EpArgs& a, cudaStream_t st);
 // (CombineArgs.d unused); every combined row goes to c.y and to each
 // peer's exchange, and the last CTA raises rows[rank] in every peer's flags.
 cudaError_t launch_ep_combine(const EpArgs& a, const CombineArgs& c, int num_tokens, cudaStream_t st);
-// Token-local form, after the router of this rank's n_local tokens (routing
-// rows at global pair rows tok_begin[rank]*K ...): copies the token rows x
-// [n_local, H] into this rank's exchange (read by the peers' gathers) and the
-// routing rows into every peer's routing arrays, then raises ids[rank] in
+// Partitioned routing, after the router of this rank's n_routed tokens
+// (routing rows at global pair rows tok_begin[rank]*K ...): copies the
+// routing rows into every peer's routing arrays and the token rows x
+// [n_rows, H] (token-local form; 0 rows in the replicated form) into this
+// rank's exchange, read by the peers' gathers, then raises ids[rank] in
 // every rank's flags.
-cudaError_t launch_ep_publish(const EpArgs& a, const uint16_t* x, int n_local, int hidden, cudaStream_t st);
+cudaError_t launch_ep_publish(const EpArgs& a, const uint16_t* x, int n_rows, int n_routed, int hidden,
+                              cudaStream_t st);
 // Waits (bounded) until every peer has published (ids[*] >= epoch).  Launch
 // before the dispatch of the global pair list.
 cudaError_t launch_ep_wait_published(const EpArgs& a, cudaStream_t st);

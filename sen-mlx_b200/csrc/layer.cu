@@ -93,6 +93,10 @@ constexpr int kRouterTcMinTokens = 512;
 // From this many tokens the CUDA-core router runs top-k in its own last CTAs
 // (measured: a separate top-k launch is as fast below that).
 constexpr int kFusedTopkMinTokens = 128;
+// Replicated expert parallelism routes each rank's own block of tokens and
+// exchanges the routing rows once a rank's block has this many tokens (below
+// it the exchange costs more than routing every token).
+constexpr int kPartitionMinTokensPerRank = 16;
 
 int tc_tile_index(double tokens_per_expert) {
   for (int i = 0; i < kTcMaxTile; ++i)
@@ -542,17 +546,27 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     ea.top_k = K;
     ea.err = L->err;
   }
-  // token-local form: the call epoch first (the publish below carries it)
-  if (local) SENMOE_CUDA(launch_ep_fence(ea, st));
+  // Routing is partitioned by token: the token-local form routes the tokens
+  // x holds; the replicated form, from kPartitionMinTokensPerRank tokens per
+  // rank, routes the block of tokens its combine owns.  Either way the rows
+  // are published to every rank before the dispatch of all pairs.
+  const bool part = local || (ep && !ext_ids && T / L->ep_world >= kPartitionMinTokensPerRank);
+  const int r_begin = local ? row0 : part ? ea.tok_begin[L->ep_rank] : 0;
+  const int r_count = local ? T_loc : part ? ea.tok_begin[L->ep_rank + 1] - r_begin : T;
+  const uint16_t* r_x = static_cast<const uint16_t*>(x) + static_cast<size_t>(local ? 0 : r_begin) * H;
+  // the call epoch first (the publish carries it)
+  if (part) SENMOE_CUDA(launch_ep_fence(ea, st));
 
-  // 1. router (deepseek_v2.rs:528-543), over the tokens x holds
+  // 1. router (deepseek_v2.rs:528-543), over the tokens routed here; the
+  // kernel is picked by the call's token count T, so each token's routing is
+  // bit-identical however the tokens are split across ranks
   RouterArgs ra{};
-  ra.x = static_cast<const uint16_t*>(x);
+  ra.x = r_x;
   ra.weight = static_cast<const uint16_t*>(L->w.router_weight);
   ra.logits = L->logits;
-  ra.topk_ids = L->ids + static_cast<size_t>(row0) * K;
-  ra.topk_weights = L->wts + static_cast<size_t>(row0) * K;
-  ra.num_tokens = T_loc;
+  ra.topk_ids = L->ids + static_cast<size_t>(r_begin) * K;
+  ra.topk_weights = L->wts + static_cast<size_t>(r_begin) * K;
+  ra.num_tokens = r_count;
   ra.hidden = H;
   ra.num_experts = E;
   ra.top_k = K;
@@ -579,26 +593,27 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   // token-local form: every rank's routing rows are needed before the
   // dispatch of the call's global pair list
   auto exchange_routing = [&]() -> cudaError_t {
-    if (!local) return cudaSuccess;
-    cudaError_t e = launch_ep_publish(ea, static_cast<const uint16_t*>(x), T_loc, H, st);
+    if (!part) return cudaSuccess;
+    // the token-local form also publishes its token rows (the peers' gathers read them)
+    cudaError_t e = launch_ep_publish(ea, static_cast<const uint16_t*>(x), local ? T_loc : 0, r_count, H, st);
     return e == cudaSuccess ? launch_ep_wait_published(ea, st) : e;
   };
   if (ext_ids) {
     SENMOE_CUDA(mark(1));  // routing given by the caller
     SENMOE_CUDA(launch_dispatch(da, st));
-  } else if (T_loc == 0) {  // token-local form, a rank with no tokens of its own
+  } else if (r_count == 0) {  // a rank with no tokens to route
     SENMOE_CUDA(exchange_routing());
     SENMOE_CUDA(mark(1));
     SENMOE_CUDA(launch_dispatch(da, st));
-  } else if (L->rtc_ok && T_loc >= kRouterTcMinTokens) {
+  } else if (L->rtc_ok && T >= kRouterTcMinTokens) {
     // prefill sizes: logits on the tensor cores and top-k in one launch
     CUtensorMap tm_x;
-    SENMOE_CUDA(make_tmap_2d(&tm_x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, T_loc, uint64_t(H) * 2, 64, 32, true));
+    SENMOE_CUDA(make_tmap_2d(&tm_x, r_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, r_count, uint64_t(H) * 2, 64, 32, true));
     SENMOE_CUDA(launch_router_tc(tm_x, L->tm_router, ra, st));
     SENMOE_CUDA(exchange_routing());
     SENMOE_CUDA(mark(1));
     SENMOE_CUDA(launch_dispatch(da, st));
-  } else if (L->route_cnt && T_loc >= kFusedTopkMinTokens) {
+  } else if (L->route_cnt && T >= kFusedTopkMinTokens) {
     // one launch: logits, then top-k by the last CTA of each 4-token tile
     RouterArgs rf = ra;
     rf.tile_cnt = L->route_cnt;
@@ -606,7 +621,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     SENMOE_CUDA(exchange_routing());
     SENMOE_CUDA(mark(1));
     SENMOE_CUDA(launch_dispatch(da, st));
-  } else if (!local && router_topk_dispatch_supported(static_cast<int>(T), P, E)) {
+  } else if (!part && router_topk_dispatch_supported(static_cast<int>(T), P, E)) {
     // 1-8 tokens: logits, then top-k and the dispatch in one CTA
     SENMOE_CUDA(launch_router_logits(ra, st));
     SENMOE_CUDA(launch_router_topk_dispatch(ra, da, st));
@@ -618,9 +633,9 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     SENMOE_CUDA(mark(1));
     SENMOE_CUDA(launch_dispatch(da, st));
   }
-  // replicated form: d is about to be overwritten: wait until the peers have
-  // read the last call's rows (the token-local form did so first of all)
-  if (ep && !local) SENMOE_CUDA(launch_ep_fence(ea, st));
+  // d is about to be overwritten: wait until the peers have read the last
+  // call's rows (a partitioned routing did so first of all)
+  if (ep && !part) SENMOE_CUDA(launch_ep_fence(ea, st));
   // token-local form: the gathers read each token's row from its owner's exchange
   PeerRows prow{};
   if (local) {
@@ -890,6 +905,8 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     }
     if (c.shared_gate) {
       RouterArgs gr = ra;
+      gr.x = static_cast<const uint16_t*>(x);  // every token x holds (combine: row t - local_row0)
+      gr.num_tokens = T_loc;
       gr.weight = static_cast<const uint16_t*>(L->w.shared_gate_vector);
       gr.logits = L->sh_gate;
       gr.num_experts = 1;
