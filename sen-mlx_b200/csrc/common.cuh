@@ -167,10 +167,23 @@ __device__ __forceinline__ float act_swiglu_mlx(float g, float u) {
   return round_bf16(a * u);
 }
 // gelu_approximate (tanh form) then the product, each rounded to bf16.
-__device__ __forceinline__ float act_geglu_mlx(float g, float u) {
+__device__ __forceinline__ float gelu_mlx(float g) {
   const float c = 0.7978845608028654f;  // sqrt(2/pi)
-  const float a = round_bf16(0.5f * g * (1.0f + tanhf(c * (g + 0.044715f * g * g * g))));
-  return round_bf16(a * u);
+  return round_bf16(0.5f * g * (1.0f + tanhf(c * (g + 0.044715f * g * g * g))));
+}
+__device__ __forceinline__ float act_geglu_mlx(float g, float u) { return round_bf16(gelu_mlx(g) * u); }
+
+// The same activations with the one transcendental step looked up: the gate
+// value g is a bf16 (the rounding MLX applies to the gate projection), so
+// bf16(sigmoid(g)) (SwiGLU) or bf16(gelu_approximate(g)) (GeGLU) has 65,536
+// possible inputs, and a table of them filled by these same functions
+// (fill_activation_table) gives bit-identical results.  g_bits: the bf16
+// bits of g.
+__device__ __forceinline__ float act_mlx_table(const uint16_t* __restrict__ table, int act, uint16_t g_bits,
+                                               float u) {
+  const float t = bf16_bits_to_f32(__ldg(table + g_bits));
+  if (act == 0) return round_bf16(round_bf16(bf16_bits_to_f32(g_bits) * t) * u);  // g * sigmoid(g), then * u
+  return round_bf16(t * u);                                                         // gelu(g) * u
 }
 
 

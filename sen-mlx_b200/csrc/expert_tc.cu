@@ -557,8 +557,11 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
         // flags an h outside fp16 range
         auto value = [&](int jj, bool& bad) -> uint16_t {
           if constexpr (NPROJ == 2) {
-            const float gg = round_bf16(__uint_as_float(g[jj])), uu = round_bf16(__uint_as_float(u[jj]));
-            const float v = a.act == 0 ? act_swiglu_mlx(gg, uu) : act_geglu_mlx(gg, uu);
+            const uint16_t gb = f32_to_bf16_bits(__uint_as_float(g[jj]));
+            const float uu = round_bf16(__uint_as_float(u[jj]));
+            const float v = a.act_table ? act_mlx_table(a.act_table, a.act, gb, uu)
+                            : a.act == 0 ? act_swiglu_mlx(bf16_bits_to_f32(gb), uu)
+                                         : act_geglu_mlx(bf16_bits_to_f32(gb), uu);
             bad = bad || !(fabsf(v) < 65504.0f);
             return __half_as_ushort(__float2half_rn(v));
           } else if constexpr (S::kIss == 1) {  // one accumulator: the whole sum

@@ -163,6 +163,9 @@ struct TcGemmArgs {
   // of the activation, h and out buffers, which hold slot_cap rows (0: no
   // limit); rows past slot_cap are not computed (kDevSlotOverflow).
   int slot_cap;
+  // Two-projection form: the activation table of `act` (launch_fill_activation_table),
+  // or null to evaluate the activation directly (same results).
+  const uint16_t* act_table;
 };
 size_t tc_smem_bytes(int bits, int nproj, int bn, int kdim);
 bool tc_supported(int rows, int kdim, int bits, int nproj, int bn);
@@ -321,5 +324,10 @@ cudaError_t ensure_dynamic_smem(const void* kernel, size_t bytes);
 
 // sigmoid of a per-token logit, in place.
 cudaError_t launch_sigmoid_inplace(float* v, int n, cudaStream_t st);
+// table[b] = bf16 bits of bf16(sigmoid(g)) (act 0, SwiGLU) or
+// bf16(gelu_approximate(g)) (act 1, GeGLU) for g = the bf16 with bits b,
+// b = 0 .. 65535: the expert epilogues' activation lookup.
+constexpr int kActTableEntries = 65536;
+cudaError_t launch_fill_activation_table(uint16_t* table, int act, cudaStream_t st);
 
 }  // namespace senmoe

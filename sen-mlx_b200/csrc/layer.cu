@@ -156,6 +156,7 @@ struct SenMoeLayer {
   float* xsum_sh = nullptr;      // [Tmax + 16, H/64] group sums (group-scaled form)
   int32_t* sh_iota = nullptr;    // [Tmax] identity permutation
   int32_t* sh_group = nullptr;   // [4] one-group tile list (written by the shared gather)
+  uint16_t* act_table = nullptr; // [65536] bf16 activation lookup of the gated expert MLPs
   CUtensorMap tm_shg{}, tm_shu{}, tm_shd{};   // shared gate / up / down codes
   CUtensorMap tm_xsh[4]{}, tm_hsh[4]{}, tm_xsh8{}, tm_hsh8{};
   // expert parallelism (senmoe_layer_connect_peers)
@@ -289,7 +290,8 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                o_route = take((T + 3) / 4 * 4), o_yx = take(T * H * 2),
                o_xsum = take((C + 16) * (H / 64) * 4), o_xssh = take(Is ? T * H * 2 : 0),
                o_hsh = take(Is ? T * Is * 2 : 0), o_xsumsh = take(Is ? (T + 16) * (H / 64) * 4 : 0),
-               o_iota = take(Is ? T * 4 : 0), o_shgrp = take(Is ? 16 : 0);
+               o_iota = take(Is ? T * 4 : 0), o_shgrp = take(Is ? 16 : 0),
+               o_acttab = take(size_t(kActTableEntries) * 2);
   cudaError_t e = cudaMalloc(&L->arena, off);
   if (e != cudaSuccess) {
     delete L;
@@ -324,6 +326,7 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
   L->h16 = reinterpret_cast<uint16_t*>(base + o_h16);
   L->route_cnt = reinterpret_cast<int*>(base + o_route);
   L->xsum = reinterpret_cast<float*>(base + o_xsum);
+  L->act_table = reinterpret_cast<uint16_t*>(base + o_acttab);
   L->ep_flags = reinterpret_cast<uint32_t*>(base + o_flags);
   L->ep_local = reinterpret_cast<uint32_t*>(base + o_local);
   L->arena_bytes = off;
@@ -394,6 +397,7 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
               make_tmap_2d(&L->tm_router, L->w.router_weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, E, H * 2, 64, 128,
                            true) == cudaSuccess;
   e = cudaMemset(L->arena, 0, off);
+  if (e == cudaSuccess) e = launch_fill_activation_table(L->act_table, c.activation, nullptr);
   if (e == cudaSuccess && Is) {  // identity permutation of the shared expert's gather
     std::vector<int32_t> iota(T);
     for (size_t i = 0; i < T; ++i) iota[i] = static_cast<int32_t>(i);
@@ -669,6 +673,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     ga.out = L->h16;
     ga.out_stride = I;
     ga.act = c.activation;
+    ga.act_table = L->act_table;
     ga.err = L->err;
     // group-scaled form (4-bit, up to 16 slots per tile) unless the
     // dequantising form is forced
@@ -734,6 +739,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     ga.out = L->h16;
     ga.out_stride = I;
     ga.act = c.activation;
+    ga.act_table = L->act_table;
     ga.err = L->err;
     ga.slot_cap = slot_cap;
     SENMOE_CUDA(launch_tc_gemm(L->tm_gate, L->tm_up, L->tm_xs[ti], ga, c.bits, 2, bn,
@@ -837,6 +843,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
       sa.out = L->hsh16;
       sa.out_stride = Is;
       sa.act = c.activation;
+      sa.act_table = L->act_table;
       sa.err = L->err;
       sa.xsum = L->xsum_sh;
       TcGemmArgs sd = sa;

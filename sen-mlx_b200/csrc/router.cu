@@ -403,6 +403,18 @@ cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st) {
   return cudaErrorNotSupported;
 }
 
+__global__ void fill_activation_table_kernel(uint16_t* table, int act) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= kActTableEntries) return;
+  const float g = bf16_bits_to_f32(static_cast<uint16_t>(b));
+  table[b] = f32_to_bf16_bits(act == 0 ? round_bf16(sigmoid_f(g)) : gelu_mlx(g));
+}
+
+cudaError_t launch_fill_activation_table(uint16_t* table, int act, cudaStream_t st) {
+  fill_activation_table_kernel<<<kActTableEntries / 256, 256, 0, st>>>(table, act);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_sigmoid_inplace(float* v, int n, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
   return launch_pdl(sigmoid_inplace_kernel, dim3((n + 255) / 256), dim3(256), 0, st, v, n);
