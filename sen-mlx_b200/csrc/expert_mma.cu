@@ -609,11 +609,8 @@ __global__ void __launch_bounds__(G4 ? kThreadsG4 : kThreads, 1)
         const size_t o = static_cast<size_t>(tl.z + n) * a.out_stride;
         constexpr float kUnit = G4 ? kG4Scale : 1.0f;  // accumulator units (exact power of two)
         if constexpr (NPROJ == 2) {
-          const uint16_t gb = f32_to_bf16_bits(acc[0][nt][i] * kUnit);
-          const float uv = round_bf16(acc[1][nt][i] * kUnit);
-          const float h = a.act_table ? act_mlx_table(a.act_table, a.act, gb, uv)
-                          : a.act == 0 ? act_swiglu_mlx(bf16_bits_to_f32(gb), uv)
-                                       : act_geglu_mlx(bf16_bits_to_f32(gb), uv);
+          const float gv = round_bf16(acc[0][nt][i] * kUnit), uv = round_bf16(acc[1][nt][i] * kUnit);
+          const float h = a.act == 0 ? act_swiglu_mlx(gv, uv) : act_geglu_mlx(gv, uv);
           range_ok &= fabsf(h) < 65504.0f;
           if constexpr (G4)
             a.out[o + kperm_g4(row)] = __half_as_ushort(__float2half_rn((row & 1) ? h * 0.0625f : h));
@@ -846,11 +843,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int row = tl.y + rA + 8 * (i >> 1);
       const size_t o = static_cast<size_t>(tl.z + n) * a.out_stride;
       if constexpr (NPROJ == 2) {
-        const uint16_t gb = f32_to_bf16_bits(acc[0][i] * kG4Scale);
-        const float uv = round_bf16(acc[1][i] * kG4Scale);
-        const float h = a.act_table ? act_mlx_table(a.act_table, a.act, gb, uv)
-                        : a.act == 0 ? act_swiglu_mlx(bf16_bits_to_f32(gb), uv)
-                                     : act_geglu_mlx(bf16_bits_to_f32(gb), uv);
+        const float gv = round_bf16(acc[0][i] * kG4Scale), uv = round_bf16(acc[1][i] * kG4Scale);
+        const float h = a.act == 0 ? act_swiglu_mlx(gv, uv) : act_geglu_mlx(gv, uv);
         range_ok &= fabsf(h) < 65504.0f;
         a.out[o + kperm_g4(row)] = __half_as_ushort(__float2half_rn((row & 1) ? h * 0.0625f : h));
       } else {

@@ -193,7 +193,9 @@ template <int BITS, int NPROJ, int BN> struct TcShape {
   // packed stages fill the rest of shared memory (at most 8)
   static constexpr int kPFit = int((200u * 1024u - kB * kBBytes - kEBytes) / (NPROJ * kPBytes));
   static constexpr int kP = kPFit > 8 ? 8 : kPFit;
-  static constexpr size_t kSmem = 1024 + size_t(kB) * kBBytes + size_t(kP) * NPROJ * kPBytes + kEBytes;
+  // gate/up: the activation lookup table (common.cuh, act_mlx_table) after the stages
+  static constexpr uint32_t kTabBytes = NPROJ == 2 ? uint32_t(kActTableBytes) : 0u;
+  static constexpr size_t kSmem = 1024 + size_t(kB) * kBBytes + size_t(kP) * NPROJ * kPBytes + kEBytes + kTabBytes;
 };
 
 constexpr int kMaxTilesPerCta = 64;
@@ -264,6 +266,7 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
   unsigned char* sB = base;                       // [SB][KA][BN*128]
   unsigned char* sP = sB + SB * kBBytes;          // [SP][NPROJ][16 KB]
   unsigned char* sE = sP + SP * NPROJ * kPBytes;  // [128 rows][kEStride] epilogue staging (kStage)
+  uint16_t* sTab = reinterpret_cast<uint16_t*>(sE + S::kEBytes);  // activation table (gate/up)
 
   // ---- barriers and TMEM first: they do not depend on the previous kernel
   if (warp == 0 && lane == 0) {
@@ -280,6 +283,12 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
                  "r"(S::kCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // the activation table: written at layer creation, not by the previous kernel
+  if constexpr (NPROJ == 2) {
+    if (a.act_table)
+      for (int i = tid; i < int(S::kTabBytes / 16); i += blockDim.x)
+        reinterpret_cast<uint4*>(sTab)[i] = __ldg(reinterpret_cast<const uint4*>(a.act_table) + i);
   }
   pdl_wait();  // the tile list comes from the dispatch kernel's active list / offsets
   pdl_launch_dependents();
@@ -559,7 +568,7 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
           if constexpr (NPROJ == 2) {
             const uint16_t gb = f32_to_bf16_bits(__uint_as_float(g[jj]));
             const float uu = round_bf16(__uint_as_float(u[jj]));
-            const float v = a.act_table ? act_mlx_table(a.act_table, a.act, gb, uu)
+            const float v = a.act_table ? act_mlx_table(sTab, a.act, gb, uu)
                             : a.act == 0 ? act_swiglu_mlx(bf16_bits_to_f32(gb), uu)
                                          : act_geglu_mlx(bf16_bits_to_f32(gb), uu);
             bad = bad || !(fabsf(v) < 65504.0f);

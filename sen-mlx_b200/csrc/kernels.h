@@ -163,8 +163,9 @@ struct TcGemmArgs {
   // of the activation, h and out buffers, which hold slot_cap rows (0: no
   // limit); rows past slot_cap are not computed (kDevSlotOverflow).
   int slot_cap;
-  // Two-projection form: the activation table of `act` (launch_fill_activation_table),
-  // or null to evaluate the activation directly (same results).
+  // tcgen05 two-projection form: the activation table of `act`
+  // (launch_fill_activation_table), or null to evaluate the activation
+  // directly (same results).  The warp-MMA kernels evaluate it directly.
   const uint16_t* act_table;
 };
 size_t tc_smem_bytes(int bits, int nproj, int bn, int kdim);
@@ -324,10 +325,11 @@ cudaError_t ensure_dynamic_smem(const void* kernel, size_t bytes);
 
 // sigmoid of a per-token logit, in place.
 cudaError_t launch_sigmoid_inplace(float* v, int n, cudaStream_t st);
-// table[b] = bf16 bits of bf16(sigmoid(g)) (act 0, SwiGLU) or
-// bf16(gelu_approximate(g)) (act 1, GeGLU) for g = the bf16 with bits b,
-// b = 0 .. 65535: the expert epilogues' activation lookup.
-constexpr int kActTableEntries = 65536;
+// The tcgen05 gate/up epilogue's activation table (common.cuh,
+// act_mlx_table): bf16(sigmoid(g)) (act 0, SwiGLU) or
+// bf16(gelu_approximate(g)) (act 1, GeGLU) for the bf16 g of each entry;
+// kActTableBytes of device memory, copied to shared memory by the kernel.
+constexpr size_t kActTableBytes = 16384;
 cudaError_t launch_fill_activation_table(uint16_t* table, int act, cudaStream_t st);
 
 }  // namespace senmoe

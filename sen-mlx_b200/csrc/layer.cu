@@ -291,7 +291,7 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                o_xsum = take((C + 16) * (H / 64) * 4), o_xssh = take(Is ? T * H * 2 : 0),
                o_hsh = take(Is ? T * Is * 2 : 0), o_xsumsh = take(Is ? (T + 16) * (H / 64) * 4 : 0),
                o_iota = take(Is ? T * 4 : 0), o_shgrp = take(Is ? 16 : 0),
-               o_acttab = take(size_t(kActTableEntries) * 2);
+               o_acttab = take(kActTableBytes);
   cudaError_t e = cudaMalloc(&L->arena, off);
   if (e != cudaSuccess) {
     delete L;
@@ -673,7 +673,6 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     ga.out = L->h16;
     ga.out_stride = I;
     ga.act = c.activation;
-    ga.act_table = L->act_table;
     ga.err = L->err;
     // group-scaled form (4-bit, up to 16 slots per tile) unless the
     // dequantising form is forced

@@ -404,14 +404,16 @@ cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st) {
 }
 
 __global__ void fill_activation_table_kernel(uint16_t* table, int act) {
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= kActTableEntries) return;
-  const float g = bf16_bits_to_f32(static_cast<uint16_t>(b));
-  table[b] = f32_to_bf16_bits(act == 0 ? round_bf16(sigmoid_f(g)) : gelu_mlx(g));
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= kActTabEntries) return;
+  // entry i <-> g bits: sign i >> 12, exponent kActTabELo + ((i >> 7) & 31), mantissa i & 127
+  const uint16_t bits = static_cast<uint16_t>(((i >> 12) << 15) | ((kActTabELo + ((i >> 7) & 31)) << 7) | (i & 127));
+  const float g = bf16_bits_to_f32(bits);
+  table[i] = f32_to_bf16_bits(act == 0 ? round_bf16(sigmoid_f(g)) : gelu_mlx(g));
 }
 
 cudaError_t launch_fill_activation_table(uint16_t* table, int act, cudaStream_t st) {
-  fill_activation_table_kernel<<<kActTableEntries / 256, 256, 0, st>>>(table, act);
+  fill_activation_table_kernel<<<kActTabEntries / 256, 256, 0, st>>>(table, act);
   return cudaGetLastError();
 }
 
