@@ -163,6 +163,12 @@ struct TcGemmArgs {
   // of the activation, h and out buffers, which hold slot_cap rows (0: no
   // limit); rows past slot_cap are not computed (kDevSlotOverflow).
   int slot_cap;
+  // tcgen05 kernels: with gather_perm set, the B operand's rows are
+  // gathered by TMA (tile::gather4) from per-token rows: local slot s reads
+  // row gather_perm[offsets[expert_begin] + s] / gather_k of tB, a map with
+  // one-row boxes (otherwise tB holds the slot-ordered rows, box BN rows).
+  const int32_t* gather_perm;
+  int gather_k;
   // tcgen05 two-projection form: the activation table of `act`
   // (launch_fill_activation_table), or null to evaluate the activation
   // directly (same results).  The warp-MMA kernels evaluate it directly.
@@ -177,7 +183,7 @@ cudaError_t launch_tc_gemm(const CUtensorMap& tA0, const CUtensorMap& tA1, const
 cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t inner,
                          uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                          bool swizzle128);
-// x_sorted[s - s0, :] = fp16(x[perm[s] / k_div, :]) for s < num_slots (x bf16, rows of
+// x_sorted[s - s0, :] = fp16(x[perm[s] / k_div, :]) for s < num_slots (perm null: row s; x bf16, rows of
 // `hidden`; s0 = offsets[eb], 0 without offsets); a value outside fp16 range
 // records kDevFp16Range in *err.  With slot_cap > 0 rows past it are skipped
 // (kDevSlotOverflow).
