@@ -167,35 +167,12 @@ __device__ __forceinline__ float act_swiglu_mlx(float g, float u) {
   return round_bf16(a * u);
 }
 // gelu_approximate (tanh form) then the product, each rounded to bf16.
-__device__ __forceinline__ float gelu_mlx(float g) {
+__device__ __forceinline__ float act_geglu_mlx(float g, float u) {
   const float c = 0.7978845608028654f;  // sqrt(2/pi)
-  return round_bf16(0.5f * g * (1.0f + tanhf(c * (g + 0.044715f * g * g * g))));
+  const float a = round_bf16(0.5f * g * (1.0f + tanhf(c * (g + 0.044715f * g * g * g))));
+  return round_bf16(a * u);
 }
-__device__ __forceinline__ float act_geglu_mlx(float g, float u) { return round_bf16(gelu_mlx(g) * u); }
 
-// The same activations with the one transcendental step looked up: the gate
-// value g is a bf16 (the rounding MLX applies to the gate projection), so
-// bf16(sigmoid(g)) (SwiGLU) or bf16(gelu_approximate(g)) (GeGLU) is a
-// function of g's 16 bits.  The table holds it for |g| in [2^-24, 2^8)
-// (exponent field 103 .. 134: 2 signs x 32 exponents x 128 mantissas = 8192
-// entries, 16 KB), filled by these same functions
-// (launch_fill_activation_table), so results are bit-identical; other g
-// (tiny, huge, inf, nan) take the direct evaluation.
-constexpr int kActTabELo = 103, kActTabExps = 32;
-constexpr int kActTabEntries = 2 * kActTabExps * 128;
-__device__ __forceinline__ int act_table_index(uint16_t g_bits) {
-  const int ei = ((g_bits >> 7) & 0xFF) - kActTabELo;
-  return static_cast<unsigned>(ei) < static_cast<unsigned>(kActTabExps)
-             ? ((g_bits >> 15) << 12) | (ei << 7) | (g_bits & 127)
-             : -1;
-}
-__device__ __forceinline__ float act_mlx_table(const uint16_t* table, int act, uint16_t g_bits, float u) {
-  const float g = bf16_bits_to_f32(g_bits);
-  const int i = act_table_index(g_bits);
-  const float t = i >= 0 ? bf16_bits_to_f32(table[i]) : (act == 0 ? round_bf16(sigmoid_f(g)) : gelu_mlx(g));
-  if (act == 0) return round_bf16(round_bf16(g * t) * u);  // g * sigmoid(g), then * u
-  return round_bf16(t * u);                                 // gelu(g) * u
-}
 
 // 2-D tiled TMA load (no multicast) completing on an mbarrier.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {

@@ -118,19 +118,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// TMA gather of four rows (tile::gather4, 2-D map with one-row boxes): rows
-// r0..r3 of columns [col, col + box) land one after another at dst, with the
-// map's swizzle applied by destination address like a tiled load.  No
-// multicast.
-__device__ __forceinline__ void tma_gather4_2d(void* dst, const CUtensorMap* map, int col, int r0, int r1, int r2,
-                                               int r3, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
-      "%4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // ------------------------------------------------------- dequantisation
 // Within every aligned block of 8 k-columns both MMA operands are stored in
 // the order (0,4,1,5,2,6,3,7): it is the order in which the 4-bit codes of a
@@ -206,9 +193,7 @@ template <int BITS, int NPROJ, int BN> struct TcShape {
   // packed stages fill the rest of shared memory (at most 8)
   static constexpr int kPFit = int((200u * 1024u - kB * kBBytes - kEBytes) / (NPROJ * kPBytes));
   static constexpr int kP = kPFit > 8 ? 8 : kPFit;
-  // gate/up: the activation lookup table (common.cuh, act_mlx_table) after the stages
-  static constexpr uint32_t kTabBytes = NPROJ == 2 ? uint32_t(kActTableBytes) : 0u;
-  static constexpr size_t kSmem = 1024 + size_t(kB) * kBBytes + size_t(kP) * NPROJ * kPBytes + kEBytes + kTabBytes;
+  static constexpr size_t kSmem = 1024 + size_t(kB) * kBBytes + size_t(kP) * NPROJ * kPBytes + kEBytes;
 };
 
 constexpr int kMaxTilesPerCta = 64;
@@ -279,7 +264,6 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
   unsigned char* sB = base;                       // [SB][KA][BN*128]
   unsigned char* sP = sB + SB * kBBytes;          // [SP][NPROJ][16 KB]
   unsigned char* sE = sP + SP * NPROJ * kPBytes;  // [128 rows][kEStride] epilogue staging (kStage)
-  uint16_t* sTab = reinterpret_cast<uint16_t*>(sE + S::kEBytes);  // activation table (gate/up)
 
   // ---- barriers and TMEM first: they do not depend on the previous kernel
   if (warp == 0 && lane == 0) {
@@ -296,12 +280,6 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
                  "r"(S::kCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  // the activation table: written at layer creation, not by the previous kernel
-  if constexpr (NPROJ == 2) {
-    if (a.act_table)
-      for (int i = tid; i < int(S::kTabBytes / 16); i += blockDim.x)
-        reinterpret_cast<uint4*>(sTab)[i] = __ldg(reinterpret_cast<const uint4*>(a.act_table) + i);
   }
   pdl_wait();  // the tile list comes from the dispatch kernel's active list / offsets
   pdl_launch_dependents();
@@ -328,51 +306,7 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
     return;
   }
 
-  if (warp == kBWarp && a.gather_perm) {
-    // ================================================= activation rows by gather
-    // The B tile of a slot block is gathered straight from the per-token
-    // fp16 rows (tmB: one-row boxes): lane l loads slots 4l .. 4l + 3 of
-    // every k-block with one tile::gather4; slots past the tile's count load
-    // row 0 (never stored).  Lane 0 owns the stage barriers.
-    const int slot_base = a.offsets[a.expert_begin];  // local slot 0 (expert parallelism)
-    int last_b[SB];
-#pragma unroll
-    for (int i = 0; i < SB; ++i) last_b[i] = -1;
-    bool ok = true;
-    int bi = 0;
-    for (int ti = 0; ti < ntiles && ok; ++ti) {
-      const int4 tl = s_tiles[ti];
-      int rows[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int sl = 4 * lane + j;
-        rows[j] = (4 * lane < BN && sl < tl.w) ? a.gather_perm[slot_base + tl.z + sl] / a.gather_k : 0;
-      }
-      for (int st = 0; st < nsteps; ++st) {
-        const int bs = bi % SB, bph = (bi / SB) & 1;
-        bool w = true;
-        if (lane == 0) {
-          w = wait_or_abort(&bar_bempty[bs], bph ^ 1, &s_abort, a.err);
-          if (w) mbar_arrive_expect_tx(&bar_bfull[bs], kBBytes);
-        }
-        if (!(ok = __shfl_sync(0xffffffffu, w, 0))) break;
-        if (4 * lane < BN) {
-#pragma unroll
-          for (int kk = 0; kk < KA; ++kk)
-            tma_gather4_2d(sB + bs * kBBytes + kk * kBTile + lane * 512, &tmB, (st * KA + kk) * BK, rows[0], rows[1],
-                           rows[2], rows[3], &bar_bfull[bs]);
-        }
-        last_b[bs] = bph;
-        ++bi;
-      }
-    }
-    if (!ok && lane == 0) {  // the copies already issued get a bounded chance to land before exit
-      volatile int never = 0;
-#pragma unroll
-      for (int i = 0; i < SB; ++i)
-        if (last_b[i] >= 0) wait_or_abort(&bar_bfull[i], last_b[i], &never, nullptr);
-    }
-  } else if (warp == 0 || warp == kBWarp) {
+  if (warp == 0 || warp == kBWarp) {
     // ================================================= TMA producers
     if (lane == 0) {
       const bool packed = warp == 0;  // warp 0: packed codes, warp kBWarp: activation tiles
@@ -623,11 +557,8 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
         // flags an h outside fp16 range
         auto value = [&](int jj, bool& bad) -> uint16_t {
           if constexpr (NPROJ == 2) {
-            const uint16_t gb = f32_to_bf16_bits(__uint_as_float(g[jj]));
-            const float uu = round_bf16(__uint_as_float(u[jj]));
-            const float v = a.act_table ? act_mlx_table(sTab, a.act, gb, uu)
-                            : a.act == 0 ? act_swiglu_mlx(bf16_bits_to_f32(gb), uu)
-                                         : act_geglu_mlx(bf16_bits_to_f32(gb), uu);
+            const float gg = round_bf16(__uint_as_float(g[jj])), uu = round_bf16(__uint_as_float(u[jj]));
+            const float v = a.act == 0 ? act_swiglu_mlx(gg, uu) : act_geglu_mlx(gg, uu);
             bad = bad || !(fabsf(v) < 65504.0f);
             return __half_as_ushort(__float2half_rn(v));
           } else if constexpr (S::kIss == 1) {  // one accumulator: the whole sum
@@ -864,7 +795,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
   for (int j = 0; j < kGatherSlots; ++j) {
     const int s = s0 + j;
     live[j] = s < num_slots && s >= lo_slot && s < hi_slot;
-    src[j] = live[j] ? gather_src_row(x, perm ? perm[s] / k_div : s, hidden, pr) : x;
+    src[j] = live[j] ? gather_src_row(x, perm[s] / k_div, hidden, pr) : x;
   }
   bool ok = true;
   if (order == kOrderMmaG4) {
@@ -875,8 +806,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
     for (int it = threadIdx.x; it < kGatherSlots * groups; it += blockDim.x) {
       const int j = it / groups, G = it - j * groups, s = s0 + j;
       if (!(s < num_slots && s >= lo_slot && s < hi_slot)) continue;
-      const uint4* in =
-          reinterpret_cast<const uint4*>(gather_src_row(x, perm ? perm[s] / k_div : s, hidden, pr) + 64 * G);
+      const uint4* in = reinterpret_cast<const uint4*>(gather_src_row(x, perm[s] / k_div, hidden, pr) + 64 * G);
       uint32_t w[32];
 #pragma unroll
       for (int q = 0; q < 8; ++q) {

@@ -163,16 +163,6 @@ struct TcGemmArgs {
   // of the activation, h and out buffers, which hold slot_cap rows (0: no
   // limit); rows past slot_cap are not computed (kDevSlotOverflow).
   int slot_cap;
-  // tcgen05 kernels: with gather_perm set, the B operand's rows are
-  // gathered by TMA (tile::gather4) from per-token rows: local slot s reads
-  // row gather_perm[offsets[expert_begin] + s] / gather_k of tB, a map with
-  // one-row boxes (otherwise tB holds the slot-ordered rows, box BN rows).
-  const int32_t* gather_perm;
-  int gather_k;
-  // tcgen05 two-projection form: the activation table of `act`
-  // (launch_fill_activation_table), or null to evaluate the activation
-  // directly (same results).  The warp-MMA kernels evaluate it directly.
-  const uint16_t* act_table;
 };
 size_t tc_smem_bytes(int bits, int nproj, int bn, int kdim);
 bool tc_supported(int rows, int kdim, int bits, int nproj, int bn);
@@ -183,7 +173,7 @@ cudaError_t launch_tc_gemm(const CUtensorMap& tA0, const CUtensorMap& tA1, const
 cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t inner,
                          uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                          bool swizzle128);
-// x_sorted[s - s0, :] = fp16(x[perm[s] / k_div, :]) for s < num_slots (perm null: row s; x bf16, rows of
+// x_sorted[s - s0, :] = fp16(x[perm[s] / k_div, :]) for s < num_slots (x bf16, rows of
 // `hidden`; s0 = offsets[eb], 0 without offsets); a value outside fp16 range
 // records kDevFp16Range in *err.  With slot_cap > 0 rows past it are skipped
 // (kDevSlotOverflow).
@@ -331,11 +321,5 @@ cudaError_t ensure_dynamic_smem(const void* kernel, size_t bytes);
 
 // sigmoid of a per-token logit, in place.
 cudaError_t launch_sigmoid_inplace(float* v, int n, cudaStream_t st);
-// The tcgen05 gate/up epilogue's activation table (common.cuh,
-// act_mlx_table): bf16(sigmoid(g)) (act 0, SwiGLU) or
-// bf16(gelu_approximate(g)) (act 1, GeGLU) for the bf16 g of each entry;
-// kActTableBytes of device memory, copied to shared memory by the kernel.
-constexpr size_t kActTableBytes = 16384;
-cudaError_t launch_fill_activation_table(uint16_t* table, int act, cudaStream_t st);
 
 }  // namespace senmoe

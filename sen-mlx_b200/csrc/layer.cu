@@ -156,10 +156,6 @@ struct SenMoeLayer {
   float* xsum_sh = nullptr;      // [Tmax + 16, H/64] group sums (group-scaled form)
   int32_t* sh_iota = nullptr;    // [Tmax] identity permutation
   int32_t* sh_group = nullptr;   // [4] one-group tile list (written by the shared gather)
-  uint16_t* act_table = nullptr; // bf16 activation lookup of the gated expert MLPs (kActTableBytes)
-  uint16_t* x16 = nullptr;       // fp16 [Tmax, H] token rows (kperm8 order) the tcgen05 gate/up gathers from
-  CUtensorMap tm_x16{};          // over x16, one-row boxes (tile::gather4)
-  bool gather_ok = false;
   CUtensorMap tm_shg{}, tm_shu{}, tm_shd{};   // shared gate / up / down codes
   CUtensorMap tm_xsh[4]{}, tm_hsh[4]{}, tm_xsh8{}, tm_hsh8{};
   // expert parallelism (senmoe_layer_connect_peers)
@@ -293,8 +289,7 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                o_route = take((T + 3) / 4 * 4), o_yx = take(T * H * 2),
                o_xsum = take((C + 16) * (H / 64) * 4), o_xssh = take(Is ? T * H * 2 : 0),
                o_hsh = take(Is ? T * Is * 2 : 0), o_xsumsh = take(Is ? (T + 16) * (H / 64) * 4 : 0),
-               o_iota = take(Is ? T * 4 : 0), o_shgrp = take(Is ? 16 : 0),
-               o_acttab = take(kActTableBytes), o_x16 = take(T * H * 2);
+               o_iota = take(Is ? T * 4 : 0), o_shgrp = take(Is ? 16 : 0);
   cudaError_t e = cudaMalloc(&L->arena, off);
   if (e != cudaSuccess) {
     delete L;
@@ -329,8 +324,6 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
   L->h16 = reinterpret_cast<uint16_t*>(base + o_h16);
   L->route_cnt = reinterpret_cast<int*>(base + o_route);
   L->xsum = reinterpret_cast<float*>(base + o_xsum);
-  L->act_table = reinterpret_cast<uint16_t*>(base + o_acttab);
-  L->x16 = reinterpret_cast<uint16_t*>(base + o_x16);
   L->ep_flags = reinterpret_cast<uint32_t*>(base + o_flags);
   L->ep_local = reinterpret_cast<uint32_t*>(base + o_local);
   L->arena_bytes = off;
@@ -358,9 +351,6 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                           true) == cudaSuccess;
     }
     L->tc_ok = maps && tc_supported(int(I), int(H), bits, 2, 128) && tc_supported(int(H), int(I), bits, 1, 128);
-    // the gate/up activation rows straight from per-token rows (tile::gather4: one-row boxes)
-    L->gather_ok = L->tc_ok && make_tmap_2d(&L->tm_x16, L->x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, H, T, H * 2, 64,
-                                            1, true) == cudaSuccess;
     L->mma_ok = maps && mma_supported(int(I), int(H), bits) && mma_supported(int(H), int(I), bits) &&
                 make_tmap_2d(&L->tm_xs8, L->xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, H, C, H * 2, 64, 8, true) ==
                     cudaSuccess &&
@@ -404,7 +394,6 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
               make_tmap_2d(&L->tm_router, L->w.router_weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, E, H * 2, 64, 128,
                            true) == cudaSuccess;
   e = cudaMemset(L->arena, 0, off);
-  if (e == cudaSuccess) e = launch_fill_activation_table(L->act_table, c.activation, nullptr);
   if (e == cudaSuccess && Is) {  // identity permutation of the shared expert's gather
     std::vector<int32_t> iota(T);
     for (size_t i = 0; i < T; ++i) iota[i] = static_cast<int32_t>(i);
@@ -726,17 +715,9 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     SENMOE_CUDA(mark(4));
   } else if (path == kPathTensorCore) {
     const int ti = tc_tile_index(per_expert), bn = kTcTiles[ti];
-    // the gate/up kernel gathers its activation rows by TMA from the tokens'
-    // fp16 rows (T rows converted once, instead of T*K slot rows copied);
-    // the token-local form's rows live in the owners' memory (no TMA there):
-    // it gathers them into slot order first
-    const bool gather = L->gather_ok && !local;
-    if (gather)
-      SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), nullptr, 1, L->x16, T, H, L->err, st));
-    else
-      SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
-                                     L->offsets, c.expert_begin, c.expert_end, kOrderTc, nullptr, nullptr, prow_p,
-                                     slot_cap));
+    SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
+                                   L->offsets, c.expert_begin, c.expert_end, kOrderTc, nullptr, nullptr, prow_p,
+                                   slot_cap));
     SENMOE_CUDA(mark(2));
     TcGemmArgs ga{};
     ga.s[0] = static_cast<const uint16_t*>(L->w.gate_scales);
@@ -753,18 +734,12 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     ga.out = L->h16;
     ga.out_stride = I;
     ga.act = c.activation;
-    ga.act_table = L->act_table;
     ga.err = L->err;
     ga.slot_cap = slot_cap;
-    if (gather) {
-      ga.gather_perm = L->perm;
-      ga.gather_k = K;
-    }
-    SENMOE_CUDA(launch_tc_gemm(L->tm_gate, L->tm_up, gather ? L->tm_x16 : L->tm_xs[ti], ga, c.bits, 2, bn,
+    SENMOE_CUDA(launch_tc_gemm(L->tm_gate, L->tm_up, L->tm_xs[ti], ga, c.bits, 2, bn,
                                (P / bn + max_items) * ga.m_tiles, st));
     SENMOE_CUDA(mark(3));
     TcGemmArgs gd = ga;
-    gd.gather_perm = nullptr;  // the down GEMM reads h in slot order
     gd.s[0] = static_cast<const uint16_t*>(L->w.down_scales);
     gd.b[0] = static_cast<const uint16_t*>(L->w.down_biases);
     gd.s[1] = gd.s[0];
@@ -862,7 +837,6 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
       sa.out = L->hsh16;
       sa.out_stride = Is;
       sa.act = c.activation;
-      sa.act_table = L->act_table;
       sa.err = L->err;
       sa.xsum = L->xsum_sh;
       TcGemmArgs sd = sa;

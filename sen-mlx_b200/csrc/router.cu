@@ -403,20 +403,6 @@ cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st) {
   return cudaErrorNotSupported;
 }
 
-__global__ void fill_activation_table_kernel(uint16_t* table, int act) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= kActTabEntries) return;
-  // entry i <-> g bits: sign i >> 12, exponent kActTabELo + ((i >> 7) & 31), mantissa i & 127
-  const uint16_t bits = static_cast<uint16_t>(((i >> 12) << 15) | ((kActTabELo + ((i >> 7) & 31)) << 7) | (i & 127));
-  const float g = bf16_bits_to_f32(bits);
-  table[i] = f32_to_bf16_bits(act == 0 ? round_bf16(sigmoid_f(g)) : gelu_mlx(g));
-}
-
-cudaError_t launch_fill_activation_table(uint16_t* table, int act, cudaStream_t st) {
-  fill_activation_table_kernel<<<kActTabEntries / 256, 256, 0, st>>>(table, act);
-  return cudaGetLastError();
-}
-
 cudaError_t launch_sigmoid_inplace(float* v, int n, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
   return launch_pdl(sigmoid_inplace_kernel, dim3((n + 255) / 256), dim3(256), 0, st, v, n);
