@@ -146,6 +146,11 @@ typedef struct SenMoeLayer SenMoeLayer;
 const char* senmoe_last_error(void);
 /* "senmoe <abi> sm_100a" */
 const char* senmoe_version(void);
+/* Self-check of the expert epilogues' sigmoid on the current device
+ * (synchronous): its fast form against 1 / (1 + expf(-g)) rounded to bf16,
+ * for every bf16 gate value g but NaNs.  *mismatches must come back 0;
+ * *exact_form counts the inputs that took the exact form. */
+int senmoe_selftest_sigmoid(int64_t* mismatches, int64_t* exact_form);
 
 /* Layer life cycle.  create validates the config, checks pointer alignment,
  * and allocates the layer's scratch on `device` for config->max_tokens. */

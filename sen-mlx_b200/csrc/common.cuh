@@ -161,10 +161,47 @@ __device__ __forceinline__ float warp_sum(float v) {
 // Activations with MLX's per-op bf16 rounding (nn::silu = x * sigmoid(x),
 // then the product with `up`, deepseek_v2.rs:472-474).
 __device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }
+// bf16(sigmoid_f(g)), bit for bit, at a fraction of the cost.  The intrinsic
+// form s' = __fdividef(1, 1 + __expf(-g)) differs from sigmoid_f(g) by at
+// most 53 fp32 units in the last place for |g| < 16, from the documented
+// bounds: __expf 2 + floor(1.173 |x|) ulp, expf 2 ulp, the two roundings of
+// 1 + e, __fdividef 2 ulp, IEEE division 0.5 ulp.  So where s' lies more than
+// 64 units from a bf16 rounding midpoint (its low 16 bits outside
+// 0x8000 +- 64), both round to the same bf16 value; elsewhere (about 0.2 % of
+// the values) and for |g| >= 16 the exact form runs.  senmoe_selftest_sigmoid
+// checks every bf16 input on the device.
+__device__ __forceinline__ float sigmoid_fast(float g) { return __fdividef(1.0f, 1.0f + __expf(-g)); }
+__device__ __forceinline__ bool sigmoid_fast_ok(float g, float sf) {
+  return fabsf(g) < 16.0f && (__float_as_uint(sf) & 0xffffu) - 0x7fc0u > 0x80u;
+}
+__device__ __forceinline__ float sigmoid_bf16(float g) {
+  const float sf = sigmoid_fast(g);
+  return round_bf16(sigmoid_fast_ok(g, sf) ? sf : sigmoid_f(g));
+}
 __device__ __forceinline__ float act_swiglu_mlx(float g, float u) {
-  const float sg = round_bf16(sigmoid_f(g));
+  const float sg = sigmoid_bf16(g);
   const float a = round_bf16(g * sg);
   return round_bf16(a * u);
+}
+// act_swiglu_mlx of N (gate, up) pairs: the N fast sigmoids run first as
+// straight-line chains that interleave, then the exact form for the few
+// that need it, so its rare branch does not split the chains.
+template <int N>
+__device__ __forceinline__ void act_swiglu_mlx_n(const float (&g)[N], const float (&u)[N], float (&h)[N]) {
+  float s[N];
+  uint32_t slow = 0;
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    s[j] = sigmoid_fast(g[j]);
+    slow |= sigmoid_fast_ok(g[j], s[j]) ? 0u : 1u << j;
+  }
+  if (slow) {
+#pragma unroll
+    for (int j = 0; j < N; ++j)
+      if (slow & (1u << j)) s[j] = sigmoid_f(g[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < N; ++j) h[j] = round_bf16(round_bf16(g[j] * round_bf16(s[j])) * u[j]);
 }
 // gelu_approximate (tanh form) then the product, each rounded to bf16.
 __device__ __forceinline__ float act_geglu_mlx(float g, float u) {

@@ -34,7 +34,8 @@
 //              8x-expanded fp16 weights never cross the shared-memory port
 //              (which would otherwise bound the kernel).
 //   warps 18-21 epilogue (TMEM accumulators -> global), warp 22 TMA of the
-//              activation tiles.
+//              activation tiles, warp 23 the second MMA issuer, warps 24-27
+//              (gate/up at 128 slots) epilogue helpers.
 // Every mbarrier wait is bounded; a timeout sets a CTA-wide abort flag, every
 // role drains and the CTA frees its TMEM and returns.
 
@@ -194,6 +195,9 @@ template <int BITS, int NPROJ, int BN> struct TcShape {
   static constexpr int kPFit = int((200u * 1024u - kB * kBBytes - kEBytes) / (NPROJ * kPBytes));
   static constexpr int kP = kPFit > 8 ? 8 : kPFit;
   static constexpr size_t kSmem = 1024 + size_t(kB) * kBBytes + size_t(kP) * NPROJ * kPBytes + kEBytes;
+  // Staged shapes add four helper warps that evaluate half of each staging
+  // row (see kHelpWarp0).
+  static constexpr int kThreads = (kStage ? 28 : 24) * 32;
 };
 
 constexpr int kMaxTilesPerCta = 64;
@@ -209,7 +213,13 @@ constexpr int kMaxTilesPerCta = 64;
 constexpr int kEpiWarp0 = 2 + kDqWarps;
 constexpr int kBWarp = kEpiWarp0 + 4;
 constexpr int kMma1Warp = kBWarp + 1;
-constexpr int kTcThreadsP = (kMma1Warp + 1) * 32;
+// Warps 24-27 (staged shapes only): epilogue helpers.  With the accumulator
+// staged, the activation math of a tile is the kernel's longest chain (one
+// warp per SM sub-partition evaluating 128 columns per row while four
+// dequant warps share its issue slots); the helper of lane quarter q takes
+// the upper half of the staging row of every thread of that quarter.
+constexpr int kHelpWarp0 = kMma1Warp + 1;
+constexpr int kHelpCol0 = 64;  // helpers evaluate slots [64, BN) of a 128-slot tile
 
 // Scale/bias of k-block j (0 <= j < KP) from KP bf16 values held as packed u32s.
 template <int KP>
@@ -237,7 +247,7 @@ __device__ __forceinline__ void load_group_params(const uint16_t* p, uint32_t (&
 // Persistent grouped GEMM: each CTA walks a strided list of (expert, 128-row
 // block, BN-slot block) tiles with one continuous pipeline across them.
 template <int BITS, int NPROJ, int BN>
-__global__ void __launch_bounds__(kTcThreadsP, 1)
+__global__ void __launch_bounds__(TcShape<BITS, NPROJ, BN>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                    const __grid_constant__ CUtensorMap tmB, TcGemmArgs a) {
   using S = TcShape<BITS, NPROJ, BN>;
@@ -249,7 +259,7 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
 
   extern __shared__ unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t bar_pfull[SP], bar_pempty[SP], bar_afull[SA], bar_aempty[SA], bar_bfull[SB],
-      bar_bempty[SB], bar_accfull[ACC], bar_accempty[ACC], bar_drain[S::kIss];
+      bar_bempty[SB], bar_accfull[ACC], bar_accempty[ACC], bar_drain[S::kIss], bar_stgfull, bar_stgempty;
   __shared__ uint32_t s_tmem;
   __shared__ int4 s_tiles[kMaxTilesPerCta];  // local expert, first weight row, first slot, valid slots
   __shared__ int s_ntiles;
@@ -273,6 +283,8 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
     for (int i = 0; i < SB; ++i) { mbar_init(&bar_bfull[i], 1); mbar_init(&bar_bempty[i], S::kIss); }
     for (int i = 0; i < ACC; ++i) { mbar_init(&bar_accfull[i], S::kIss); mbar_init(&bar_accempty[i], 4); }
     for (int i = 0; i < S::kIss; ++i) mbar_init(&bar_drain[i], 1);
+    mbar_init(&bar_stgfull, 4);   // staged: the four primary epilogue warps filled the staging rows
+    mbar_init(&bar_stgempty, 8);  // staged: all eight epilogue warps finished reading them
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -536,13 +548,18 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
         }
       }
     }
-  } else if (warp < kBWarp) {
+  } else if (warp < kBWarp || warp >= kHelpWarp0) {
     // ================================================= epilogue (TMEM -> global)
-    const int q = warp & 3;  // TMEM lane quarter this warp may read (warps 18..21 -> 2, 3, 0, 1)
+    // TMEM lane quarter of this warp (warps 18..21 -> 2, 3, 0, 1); a helper
+    // (warps 24..27, staged shapes only) reads the staging rows of quarter q
+    const int q = warp & 3;
+    const bool helper = warp >= kHelpWarp0;
     for (int ti = 0; ti < ntiles; ++ti) {
       const int ab = ti % ACC, accph = (ti / ACC) & 1;
-      if (!__all_sync(0xffffffffu, wait_or_abort(&bar_accfull[ab], accph, &s_abort, a.err))) break;
-      tc_fence_after();
+      if (!helper) {
+        if (!__all_sync(0xffffffffu, wait_or_abort(&bar_accfull[ab], accph, &s_abort, a.err))) break;
+        tc_fence_after();
+      }
       const int4 tl = s_tiles[ti];
       const int r = tl.y + q * 32 + lane;  // output row of this thread
       const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ab * S::kAccCols;
@@ -557,7 +574,9 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
         // flags an h outside fp16 range
         auto value = [&](int jj, bool& bad) -> uint16_t {
           if constexpr (NPROJ == 2) {
-            const float gg = round_bf16(__uint_as_float(g[jj])), uu = round_bf16(__uint_as_float(u[jj]));
+            // staged values are bf16 already (rounded on the way into the staging row)
+            const float gg = S::kStage ? __uint_as_float(g[jj]) : round_bf16(__uint_as_float(g[jj]));
+            const float uu = S::kStage ? __uint_as_float(u[jj]) : round_bf16(__uint_as_float(u[jj]));
             const float v = a.act == 0 ? act_swiglu_mlx(gg, uu) : act_geglu_mlx(gg, uu);
             bad = bad || !(fabsf(v) < 65504.0f);
             return __half_as_ushort(__float2half_rn(v));
@@ -572,8 +591,26 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
           // a full chunk (warp-uniform): 16 independent chains that interleave,
           // where a per-column exit would run them one after another
           uint16_t bits[16];
+          if (NPROJ == 2 && a.act == 0) {
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) bits[jj] = value(jj, bad);
+            for (int j0 = 0; j0 < 16; j0 += 8) {  // two batches of 8 chains
+              float gv[8], uv[8], hv[8];
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) {
+                gv[jj] = S::kStage ? __uint_as_float(g[j0 + jj]) : round_bf16(__uint_as_float(g[j0 + jj]));
+                uv[jj] = S::kStage ? __uint_as_float(u[j0 + jj]) : round_bf16(__uint_as_float(u[j0 + jj]));
+              }
+              act_swiglu_mlx_n<8>(gv, uv, hv);
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) {
+                bad = bad || !(fabsf(hv[jj]) < 65504.0f);
+                bits[j0 + jj] = __half_as_ushort(__float2half_rn(hv[jj]));
+              }
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) bits[jj] = value(jj, bad);
+          }
 #pragma unroll
           for (int jj = 0; jj < 16; ++jj) orow[static_cast<size_t>(jj) * a.out_stride] = bits[jj];
         } else {
@@ -592,25 +629,39 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
         // pairs, the rounding the activation applies first; then release the
         // accumulator and evaluate from the staging row
         unsigned char* erow = sE + static_cast<uint32_t>(q * 32 + lane) * S::kEStride;
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          if (c0 >= tl.w) break;  // uniform across the warp
-          uint32_t g[16], u[16];
-          tmem_ld16(lane_addr + c0, g);
-          tmem_ld16(lane_addr + BN + c0, u);
-          tmem_ld_wait();
-          uint32_t pk[16];
+        if (!helper) {
+          // the staging rows are free once all eight warps have evaluated the
+          // previous tile from them
+          if (ti > 0 && !__all_sync(0xffffffffu, wait_or_abort(&bar_stgempty, (ti - 1) & 1, &s_abort, a.err)))
+            break;
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            if (c0 >= tl.w) break;  // uniform across the warp
+            uint32_t g[16], u[16];
+            tmem_ld16(lane_addr + c0, g);
+            tmem_ld16(lane_addr + BN + c0, u);
+            tmem_ld_wait();
+            uint32_t pk[16];
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj)
-            pk[jj] = uint32_t(f32_to_bf16_bits(__uint_as_float(g[jj]))) |
-                     (uint32_t(f32_to_bf16_bits(__uint_as_float(u[jj]))) << 16);
-          uint4* dst = reinterpret_cast<uint4*>(erow + c0 * 4);
+            for (int jj = 0; jj < 16; ++jj)
+              pk[jj] = uint32_t(f32_to_bf16_bits(__uint_as_float(g[jj]))) |
+                       (uint32_t(f32_to_bf16_bits(__uint_as_float(u[jj]))) << 16);
+            uint4* dst = reinterpret_cast<uint4*>(erow + c0 * 4);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&bar_accempty[ab]);
+            mbar_arrive(&bar_stgfull);
+          }
+        } else if (!__all_sync(0xffffffffu, wait_or_abort(&bar_stgfull, ti & 1, &s_abort, a.err))) {
+          break;
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bar_accempty[ab]);
-        for (int c0 = 0; c0 < BN; c0 += 16) {
+        // primary warps slots [0, kHelpCol0), helpers [kHelpCol0, BN)
+        static_assert(!S::kStage || BN == 2 * kHelpCol0, "staged shapes split a 128-slot row in halves");
+        const int c_end = helper ? BN : kHelpCol0;
+        for (int c0 = helper ? kHelpCol0 : 0; c0 < c_end; c0 += 16) {
           if (c0 >= tl.w) break;
           const uint4* src = reinterpret_cast<const uint4*>(erow + c0 * 4);
           uint32_t g[16], u[16];
@@ -626,6 +677,8 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
           }
           emit_chunk(c0, g, u);
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_stgempty);
       } else {
         for (int c0 = 0; c0 < BN; c0 += 16) {
           if (c0 >= tl.w) break;  // uniform across the warp
@@ -691,7 +744,7 @@ static cudaError_t launch_tc_t(const CUtensorMap& tA0, const CUtensorMap& tA1, c
   // one persistent CTA per SM, enough CTAs that none owns more than kMaxTilesPerCta tiles
   int grid = tiles_upper < sm_count() ? tiles_upper : sm_count();
   if ((tiles_upper + grid - 1) / grid > kMaxTilesPerCta) grid = (tiles_upper + kMaxTilesPerCta - 1) / kMaxTilesPerCta;
-  return launch_pdl(kern, dim3(grid), dim3(kTcThreadsP), smem, st, tA0, tA1, tB, a);
+  return launch_pdl(kern, dim3(grid), dim3(TcShape<BITS, NPROJ, BN>::kThreads), smem, st, tA0, tA1, tB, a);
 }
 
 cudaError_t launch_tc_gemm(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,

@@ -55,10 +55,14 @@ cudaError_t launch_router_logits(const RouterArgs& a, cudaStream_t st);
 // rounded) and softmax / top-k in one launch, 32 tokens per CTA; logits are
 // not written to global memory.  tX: x bf16 [T, H], tW: Wg bf16 [E, H], both
 // 64-column boxes with SWIZZLE_128B (32 and 128 rows).  H % 64 == 0, E <= 512.
+// Each CTA streams all of Wg; up to one CTA per SM (the 8-stage ring).
+constexpr int kRouterTcTokensPerCta = 32;
 bool router_tc_supported(int hidden, int num_experts, int top_k);
 size_t router_tc_smem_bytes(int num_experts);
 cudaError_t launch_router_tc(const CUtensorMap& tX, const CUtensorMap& tW, const RouterArgs& a, cudaStream_t st);
 cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st);
+// sigmoid_bf16 against the exact form over every bf16 input (synchronous, current device).
+cudaError_t selftest_sigmoid(int64_t* mismatches, int64_t* exact_form);
 // Top-k of every token plus the single-chunk dispatch in one CTA, for small
 // batches (<= kTopkDispatchMaxTokens tokens, <= 2048 pairs); d.topk_ids must
 // be a.topk_ids.  Measured on the 48-layer decode stack: one launch fewer

@@ -93,10 +93,15 @@ constexpr int kRouterTcMinTokens = 512;
 // From this many tokens the CUDA-core router runs top-k in its own last CTAs
 // (measured: a separate top-k launch is as fast below that).
 constexpr int kFusedTopkMinTokens = 128;
-// Replicated expert parallelism routes each rank's own block of tokens and
-// exchanges the routing rows once a rank's block has this many tokens (below
-// it the exchange costs more than routing every token).
-constexpr int kPartitionMinTokensPerRank = 16;
+// Replicated expert parallelism routes each rank's own block of tokens (and
+// exchanges the routing rows) only where the tensor-core router over all
+// tokens takes more than one wave of CTAs: each CTA streams all of Wg, so
+// below that a smaller block is no faster, and the exchange adds a wait for
+// the slowest rank (measured at 2 GPUs with the split from 16 tokens per rank:
+// decode 128 tokens 25.1k -> 23.4k tokens/s, prefill 4096 180.5k -> 175.5k).
+bool partition_routing(int64_t tokens, int sms) {
+  return tokens >= kRouterTcMinTokens && (tokens + kRouterTcTokensPerCta - 1) / kRouterTcTokensPerCta > sms;
+}
 
 int tc_tile_index(double tokens_per_expert) {
   for (int i = 0; i < kTcMaxTile; ++i)
@@ -248,6 +253,14 @@ extern "C" {
 const char* senmoe_last_error(void) { return g_last_error.c_str(); }
 
 const char* senmoe_version(void) { return "senmoe 1 sm_100a"; }
+
+int senmoe_selftest_sigmoid(int64_t* mismatches, int64_t* exact_form) {
+  g_last_error.clear();
+  if (!mismatches || !exact_form) return fail(SENMOE_ERR_BAD_ARG, "output pointer is NULL");
+  const cudaError_t e = selftest_sigmoid(mismatches, exact_form);
+  if (e != cudaSuccess) return fail(SENMOE_ERR_CUDA, "selftest_sigmoid: %s", cudaGetErrorString(e));
+  return SENMOE_OK;
+}
 
 int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights, int device,
                         SenMoeLayer** out_layer) {
@@ -547,10 +560,10 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     ea.err = L->err;
   }
   // Routing is partitioned by token: the token-local form routes the tokens
-  // x holds; the replicated form, from kPartitionMinTokensPerRank tokens per
-  // rank, routes the block of tokens its combine owns.  Either way the rows
-  // are published to every rank before the dispatch of all pairs.
-  const bool part = local || (ep && !ext_ids && T / L->ep_world >= kPartitionMinTokensPerRank);
+  // x holds; the replicated form, where partition_routing says so, routes the
+  // block of tokens its combine owns.  Either way the rows are published to
+  // every rank before the dispatch of all pairs.
+  const bool part = local || (ep && !ext_ids && L->rtc_ok && partition_routing(T, L->sms));
   const int r_begin = local ? row0 : part ? ea.tok_begin[L->ep_rank] : 0;
   const int r_count = local ? T_loc : part ? ea.tok_begin[L->ep_rank + 1] - r_begin : T;
   const uint16_t* r_x = static_cast<const uint16_t*>(x) + static_cast<size_t>(local ? 0 : r_begin) * H;

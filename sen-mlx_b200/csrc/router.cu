@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(RouterArgs
 // logits stay in shared memory, and the same CTA runs softmax / top-k for its
 // tokens.  Experts come in chunks of 128 (E <= 512).
 namespace {
-constexpr int kRtTok = 32, kRtExp = 128, kRtStages = 8;
+constexpr int kRtTok = kRouterTcTokensPerCta, kRtExp = 128, kRtStages = 8;
 constexpr int kRtCompute = 8;                     // 2 token halves x 4 expert quarters
 constexpr int kRtThreads = (kRtCompute + 1) * 32; // + one TMA warp
 constexpr uint32_t kRtXBytes = kRtTok * 128, kRtWBytes = kRtExp * 128;
@@ -401,6 +401,31 @@ cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st) {
   SENMOE_TK_CASE(1) SENMOE_TK_CASE(2) SENMOE_TK_CASE(4) SENMOE_TK_CASE(8) SENMOE_TK_CASE(16)
 #undef SENMOE_TK_CASE
   return cudaErrorNotSupported;
+}
+
+// Every bf16 input of sigmoid_bf16 (NaNs aside) against the exact form:
+// counts[0] mismatches, counts[1] inputs that took the exact form.
+__global__ void selftest_sigmoid_kernel(unsigned int* counts) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= 65536u || ((i & 0x7f80u) == 0x7f80u && (i & 0x7fu) != 0)) return;
+  const float g = __uint_as_float(i << 16);
+  if (__float_as_uint(sigmoid_bf16(g)) != __float_as_uint(round_bf16(sigmoid_f(g)))) atomicAdd(&counts[0], 1u);
+  if (!sigmoid_fast_ok(g, sigmoid_fast(g))) atomicAdd(&counts[1], 1u);
+}
+
+cudaError_t selftest_sigmoid(int64_t* mismatches, int64_t* exact_form) {
+  unsigned int* d = nullptr;
+  unsigned int h[2] = {0, 0};
+  cudaError_t e = cudaMalloc(&d, sizeof(h));
+  if (e != cudaSuccess) return e;
+  if ((e = cudaMemset(d, 0, sizeof(h))) == cudaSuccess) {
+    selftest_sigmoid_kernel<<<256, 256>>>(d);
+    if ((e = cudaGetLastError()) == cudaSuccess) e = cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost);
+  }
+  cudaFree(d);
+  *mismatches = h[0];
+  *exact_form = h[1];
+  return e;
 }
 
 cudaError_t launch_sigmoid_inplace(float* v, int n, cudaStream_t st) {

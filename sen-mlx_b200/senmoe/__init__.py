@@ -91,6 +91,7 @@ _i64, _i32, _f32 = C.c_int64, C.c_int32, C.c_float
 SIGNATURES = {
     "senmoe_last_error": (C.c_char_p, []),
     "senmoe_version": (C.c_char_p, []),
+    "senmoe_selftest_sigmoid": (C.c_int, [C.POINTER(_i64), C.POINTER(_i64)]),
     "senmoe_layer_create": (C.c_int, [C.POINTER(SenMoeConfig), C.POINTER(SenMoeWeights), C.c_int, C.POINTER(_P)]),
     "senmoe_layer_destroy": (C.c_int, [_P]),
     "senmoe_layer_forward": (C.c_int, [_P, _P, _i64, _P, C.POINTER(SenMoeDebug), _P]),

@@ -26,7 +26,9 @@ def _ngpu() -> int:
 CASES = {
     # H, I, E, K, bits, Ts, shared, seed, expert_path
     "config0": (2048, 768, 128, 8, 4, [1, 8, 64, 256], 0, 3, 0),
-    "shared8": (256, 256, 16, 4, 8, [3, 40, 600], 256, 5, 0),
+    # 5000 tokens: the router takes more than one wave of CTAs, so each rank
+    # routes its own token block and the routing rows are exchanged
+    "shared8": (256, 256, 16, 4, 8, [3, 40, 600, 5000], 256, 5, 0),
     "config0_tc": (2048, 768, 128, 8, 4, [16, 512], 0, 7, 2),
 }
 

@@ -161,3 +161,17 @@ def test_quantized_linear_vs_oracle(senmoe, torch_cuda, bits, T, in_f, out_f):
     assert y.shape == (T, out_f)
     got = bf16_np_to_f32(to_numpy_bf16(y))
     assert np.all(np.abs(got - ref) <= 2.0 ** -7 * np.abs(ref) + 1e-5)
+
+
+def test_epilogue_sigmoid_fast_form_is_bit_identical(senmoe, torch_cuda):
+    """The expert epilogues' sigmoid (intrinsics away from bf16 rounding
+    midpoints, the exact form near them) rounds to the same bf16 value as
+    bf16(1 / (1 + expf(-g))) for every bf16 gate value g."""
+    import ctypes as C
+    torch_cuda.cuda.set_device(0)
+    mism, exact = C.c_int64(-1), C.c_int64(-1)
+    senmoe._check(senmoe.lib().senmoe_selftest_sigmoid(C.byref(mism), C.byref(exact)))
+    assert mism.value == 0
+    # the exact form: |g| >= 16 (about half of all bf16 patterns) and the
+    # inputs whose fast value sits near a midpoint
+    assert 0 < exact.value < 65536
