@@ -256,6 +256,9 @@ __global__ void __launch_bounds__(TcShape<BITS, NPROJ, BN>::kThreads, 1)
   static_assert(S::kSmem + 2048 <= 227 * 1024, "shared memory budget");
   static_assert(SA >= 2 && SP >= 2 && KP % KA == 0, "pipeline shape");
   static_assert(S::kACol0 + SA * S::kACols <= S::kCols, "TMEM budget");
+  // With rings of equal depth the A and B stages of a step free together:
+  // one commit (and one barrier) per step serves both producers.
+  constexpr bool kJointEmpty = SA == SB;
 
   extern __shared__ unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t bar_pfull[SP], bar_pempty[SP], bar_afull[SA], bar_aempty[SA], bar_bfull[SB],
@@ -346,7 +349,8 @@ __global__ void __launch_bounds__(TcShape<BITS, NPROJ, BN>::kThreads, 1)
         } else {
           for (int st = 0; st < nsteps; ++st) {  // activation stage: k-blocks [st*KA, st*KA + KA)
             const int bs = bi % SB, bph = (bi / SB) & 1;
-            if (!(ok = wait_or_abort(&bar_bempty[bs], bph ^ 1, &s_abort, a.err))) break;
+            if (!(ok = wait_or_abort(kJointEmpty ? &bar_aempty[bs] : &bar_bempty[bs], bph ^ 1, &s_abort, a.err)))
+              break;
             mbar_arrive_expect_tx(&bar_bfull[bs], kBBytes);
 #pragma unroll
             for (int kk = 0; kk < KA; ++kk)
@@ -369,14 +373,19 @@ __global__ void __launch_bounds__(TcShape<BITS, NPROJ, BN>::kThreads, 1)
   } else if (warp == 1 || warp == kMma1Warp) {
     // ================================================= MMA issuers
     // (a single-issuer shape leaves the second issuer warp without work; it
-    // goes straight to the teardown barrier)
-    if (lane == 0 && (warp == 1 || S::kIss == 2)) {
+    // goes straight to the teardown barrier).  The whole warp walks the
+    // pipeline and waits on the barriers, one elected lane issues the MMAs
+    // and commits: the loop stays warp-uniform, so its descriptor arithmetic
+    // is not a single diverged lane's (the issuer shares its sub-partition's
+    // issue slots with six busy warps).
+    if (warp == 1 || S::kIss == 2) {
       const int iss = warp == 1 ? 0 : 1;
+      const bool leader = elect_one();
       bool ok = true;
       int ai = 0;  // pipeline steps issued (A and B stages advance together)
       for (int ti = 0; ti < ntiles && ok; ++ti) {
         const int ab = ti % ACC, accph = (ti / ACC) & 1;
-        if (!(ok = wait_or_abort(&bar_accempty[ab], accph ^ 1, &s_abort, a.err))) break;
+        if (!(ok = __all_sync(0xffffffffu, wait_or_abort(&bar_accempty[ab], accph ^ 1, &s_abort, a.err)))) break;
         tc_fence_after();
         const uint32_t d = tmem + ab * S::kAccCols + iss * BN;  // this issuer's accumulator
         // MMA width: the tile's valid slots rounded up to 16 (columns past
@@ -386,33 +395,39 @@ __global__ void __launch_bounds__(TcShape<BITS, NPROJ, BN>::kThreads, 1)
         for (int st = 0; st < nsteps; ++st, ++ai) {
           const int as = ai % SA, aph = (ai / SA) & 1;
           const int bs = ai % SB, bph = (ai / SB) & 1;
-          ok = wait_or_abort(&bar_afull[as], aph, &s_abort, a.err) &&
-               wait_or_abort(&bar_bfull[bs], bph, &s_abort, a.err);
+          ok = __all_sync(0xffffffffu, wait_or_abort(&bar_afull[as], aph, &s_abort, a.err) &&
+                                           wait_or_abort(&bar_bfull[bs], bph, &s_abort, a.err));
           if (!ok) break;
           tc_fence_after();
           const uint64_t b_desc0 = sw128_kmajor_desc(smem_u32(sB + bs * kBBytes));
           const uint32_t a_stage = tmem + S::kACol0 + as * S::kACols;
-          if constexpr (NPROJ == 2) {  // projection iss, all K steps
+          if (leader) {
+            if constexpr (NPROJ == 2) {  // projection iss, all K steps
 #pragma unroll
-            for (int kk = 0; kk < KA; ++kk)
+              for (int kk = 0; kk < KA; ++kk)
 #pragma unroll
-              for (int k = 0; k < BK / 16; ++k)  // K = 16 per MMA: 8 TMEM columns of A, 32 bytes of B
-                umma_f16_ts(d, a_stage + (iss * KA + kk) * 32 + k * 8, b_desc0 + ((kk * kBTile + k * 32) >> 4),
-                            kIdesc, (st | kk | k) != 0);
-          } else {  // K steps iss, iss + kIss, ... into this issuer's partial sum
+                for (int k = 0; k < BK / 16; ++k)  // K = 16 per MMA: 8 TMEM columns of A, 32 bytes of B
+                  umma_f16_ts(d, a_stage + (iss * KA + kk) * 32 + k * 8, b_desc0 + ((kk * kBTile + k * 32) >> 4),
+                              kIdesc, (st | kk | k) != 0);
+            } else {  // K steps iss, iss + kIss, ... into this issuer's partial sum
 #pragma unroll
-            for (int kk = 0; kk < KA; ++kk)
+              for (int kk = 0; kk < KA; ++kk)
 #pragma unroll
-              for (int k = iss; k < BK / 16; k += S::kIss)
-                umma_f16_ts(d, a_stage + kk * 32 + k * 8, b_desc0 + ((kk * kBTile + k * 32) >> 4), kIdesc,
-                            (st | kk | (k - iss)) != 0);
+                for (int k = iss; k < BK / 16; k += S::kIss)
+                  umma_f16_ts(d, a_stage + kk * 32 + k * 8, b_desc0 + ((kk * kBTile + k * 32) >> 4), kIdesc,
+                              (st | kk | (k - iss)) != 0);
+            }
+            umma_commit(&bar_aempty[as]);
+            if constexpr (!kJointEmpty) umma_commit(&bar_bempty[bs]);
           }
-          umma_commit(&bar_aempty[as]);
-          umma_commit(&bar_bempty[bs]);
+          __syncwarp();
         }
-        if (ok) umma_commit(&bar_accfull[ab]);
+        if (ok && leader) umma_commit(&bar_accfull[ab]);
+        __syncwarp();
       }
-      umma_commit(&bar_drain[iss]);  // all MMAs issued by this thread have completed once it fires
+      // all MMAs issued by the leader have completed once this fires
+      if (leader) umma_commit(&bar_drain[iss]);
+      __syncwarp();
       volatile int never = 0;
       wait_or_abort(&bar_drain[iss], 0, &never, nullptr);
     }
