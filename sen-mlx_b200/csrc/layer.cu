@@ -180,6 +180,11 @@ struct SenMoeLayer {
   bool profiling = false;
   bool profiled_once = false;
   cudaEvent_t ev[SENMOE_NUM_STAGES + 1] = {};
+  // the shared expert runs on a side stream forked from the caller's at the
+  // start of a forward and joined before the combine (its kernels overlap
+  // the router, dispatch and routed experts)
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
 };
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -412,11 +417,15 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
     for (size_t i = 0; i < T; ++i) iota[i] = static_cast<int32_t>(i);
     e = cudaMemcpy(L->sh_iota, iota.data(), T * 4, cudaMemcpyHostToDevice);
   }
+  if (e == cudaSuccess && Is) {
+    e = cudaStreamCreateWithFlags(&L->side, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->fork_ev, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->join_ev, cudaEventDisableTiming);
+  }
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   cudaSetDevice(cur);
   if (e != cudaSuccess) {
-    cudaFree(L->arena);
-    delete L;
+    senmoe_layer_destroy(L);
     return fail(SENMOE_ERR_CUDA, "scratch initialisation failed: %s", cudaGetErrorString(e));
   }
   *out_layer = L;
@@ -431,6 +440,9 @@ int senmoe_layer_destroy(SenMoeLayer* layer) {
   cudaSetDevice(layer->device);
   for (auto& ev : layer->ev)
     if (ev) cudaEventDestroy(ev);
+  if (layer->fork_ev) cudaEventDestroy(layer->fork_ev);
+  if (layer->join_ev) cudaEventDestroy(layer->join_ev);
+  if (layer->side) cudaStreamDestroy(layer->side);
   for (void* p : layer->ep_opened)
     if (p) cudaIpcCloseMemHandle(p);
   cudaError_t e = cudaFree(layer->arena);
@@ -559,6 +571,143 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     ea.top_k = K;
     ea.err = L->err;
   }
+  // 5. shared expert (deepseek_v2.rs:550-552), optionally sigmoid-gated.
+  // On the tensor-core kernels it is a grouped GEMM of one expert over the
+  // rows of x this rank combines (all of them on one GPU): sh_out row i is
+  // token sh_t0 + i.  Otherwise the CUDA-core GEMV over every token.
+  int sh_t0 = 0;  // sh_out row i is token sh_t0 + i
+  auto run_shared = [&](cudaStream_t s5) -> int {
+    // the tokens this rank combines (global indices own_t0 ..); the
+    // token-local form holds exactly those in x
+    const int sh_n = local ? T_loc : ep ? ea.tok_begin[L->ep_rank + 1] - ea.tok_begin[L->ep_rank] : T;
+    const int own_t0 = local ? row0 : ep ? ea.tok_begin[L->ep_rank] : 0;
+    const int forced = c.reserved[0];
+    int sh_path = kPathGemv;
+    if (forced == kPathTensorCore && L->sh_tc_ok) sh_path = kPathTensorCore;
+    else if (forced == kPathMma && L->sh_mma_ok) sh_path = kPathMma;
+    // kernel and tile width follow the call's token count T, the same on every
+    // expert-parallel rank and on one GPU, so each token's shared output is
+    // bit-identical however the tokens are split
+    else if (forced == kPathAuto)
+      sh_path = (T >= kTcMinTokensPerExpert && L->sh_tc_ok) ? kPathTensorCore
+                : L->sh_mma_ok                                  ? kPathMma
+                : L->sh_tc_ok                                   ? kPathTensorCore
+                                                                : kPathGemv;
+    if (sh_path != kPathGemv) {
+      sh_t0 = own_t0;  // the GEMV below writes every token's row instead
+      TcGemmArgs sa{};
+      sa.s[0] = static_cast<const uint16_t*>(L->w.shared_gate_scales);
+      sa.b[0] = static_cast<const uint16_t*>(L->w.shared_gate_biases);
+      sa.s[1] = static_cast<const uint16_t*>(L->w.shared_up_scales);
+      sa.b[1] = static_cast<const uint16_t*>(L->w.shared_up_biases);
+      sa.rows = Is;
+      sa.kdim = H;
+      sa.m_tiles = Is / 128;
+      sa.offsets = L->sh_group;       // {0, sh_n}, written by the gather below
+      sa.active = L->sh_group + 2;    // {0}
+      sa.active_count = L->sh_group + 3;
+      sa.expert_begin = 0;
+      sa.out = L->hsh16;
+      sa.out_stride = Is;
+      sa.act = c.activation;
+      sa.err = L->err;
+      sa.xsum = L->xsum_sh;
+      TcGemmArgs sd = sa;
+      sd.s[0] = sd.s[1] = static_cast<const uint16_t*>(L->w.shared_down_scales);
+      sd.b[0] = sd.b[1] = static_cast<const uint16_t*>(L->w.shared_down_biases);
+      sd.rows = H;
+      sd.kdim = Is;
+      sd.m_tiles = H / 128;
+      sd.out = L->sh_out;
+      sd.out_stride = H;
+      const uint16_t* xs_src = static_cast<const uint16_t*>(x) + static_cast<size_t>(sh_t0 - row0) * H;
+      if (sh_n > 0 && sh_path == kPathMma) {
+        const int nt = T <= 8 ? 1 : (T <= 16 ? 2 : 4);
+        const CUtensorMap& tb_x = nt == 1 ? L->tm_xsh8 : L->tm_xsh[nt == 2 ? 0 : 1];
+        const CUtensorMap& tb_h = nt == 1 ? L->tm_hsh8 : L->tm_hsh[nt == 2 ? 0 : 1];
+        const bool g4 = mma_g4_supported(c.bits, nt, sa) &&
+                        (c.reserved[1] == kMmaFormG4Single || (c.reserved[1] == kMmaFormAuto && nt == 1));
+        SENMOE_CUDA(launch_gather_rows(xs_src, L->sh_iota, 1, L->xs_sh, sh_n, H, L->err, st, nullptr, 0, 0,
+                                       g4 ? kOrderMmaG4 : kOrderMma, g4 ? L->xsum_sh : nullptr, L->sh_group));
+        SENMOE_CUDA(launch_mma_gemm(L->tm_shg, L->tm_shu, tb_x, sa, c.bits, 2, nt, g4,
+                                    (sh_n / (8 * nt) + 1) * sa.m_tiles, s5));
+        SENMOE_CUDA(launch_mma_gemm(L->tm_shd, L->tm_shd, tb_h, sd, c.bits, 1, nt, g4,
+                                    (sh_n / (8 * nt) + 1) * sd.m_tiles, s5));
+      } else if (sh_n > 0) {
+        const int ti = tc_tile_index(double(T)), bn = kTcTiles[ti];
+        SENMOE_CUDA(launch_gather_rows(xs_src, L->sh_iota, 1, L->xs_sh, sh_n, H, L->err, st, nullptr, 0, 0,
+                                       kOrderTc, nullptr, L->sh_group));
+        SENMOE_CUDA(launch_tc_gemm(L->tm_shg, L->tm_shu, L->tm_xsh[ti], sa, c.bits, 2, bn,
+                                   (sh_n / bn + 1) * sa.m_tiles, s5));
+        SENMOE_CUDA(launch_tc_gemm(L->tm_shd, L->tm_shd, L->tm_hsh[ti], sd, c.bits, 1, bn,
+                                   (sh_n / bn + 1) * sd.m_tiles, s5));
+      }
+    } else {
+      sh_t0 = row0;  // every token x holds, row i = global token row0 + i
+      QGemvArgs sg{};
+      sg.x = static_cast<const uint16_t*>(x);
+      sg.w[0] = L->w.shared_gate_weight;
+      sg.s[0] = static_cast<const uint16_t*>(L->w.shared_gate_scales);
+      sg.b[0] = static_cast<const uint16_t*>(L->w.shared_gate_biases);
+      sg.w[1] = L->w.shared_up_weight;
+      sg.s[1] = static_cast<const uint16_t*>(L->w.shared_up_scales);
+      sg.b[1] = static_cast<const uint16_t*>(L->w.shared_up_biases);
+      sg.kdim = H;
+      sg.rows = Is;
+      sg.rows_per_cta = kGateUpRows;
+      sg.mode = kItemsGather;
+      sg.gather_idx = L->zeros_idx;
+      sg.rep = 1;
+      sg.num_experts = 1;
+      sg.out = L->sh_h;
+      sg.out_stride = Is;
+      sg.act = c.activation;
+      sg.err = L->err;
+      SENMOE_CUDA(launch_qgemv(sg, 2, c.bits, T_loc, s5));
+      QGemvArgs sd = sg;
+      sd.x = L->sh_h;
+      sd.w[0] = L->w.shared_down_weight;
+      sd.s[0] = static_cast<const uint16_t*>(L->w.shared_down_scales);
+      sd.b[0] = static_cast<const uint16_t*>(L->w.shared_down_biases);
+      sd.kdim = Is;
+      sd.rows = H;
+      sd.rows_per_cta = kDownRows;
+      sd.out = L->sh_out;
+      sd.out_stride = H;
+      SENMOE_CUDA(launch_qgemv(sd, 1, c.bits, T_loc, s5));
+    }
+    if (c.shared_gate) {
+      RouterArgs gr{};
+      gr.x = static_cast<const uint16_t*>(x);  // every token x holds (combine: row t - local_row0)
+      gr.hidden = H;
+      gr.top_k = K;
+      gr.err = L->err;
+      gr.num_tokens = T_loc;
+      gr.weight = static_cast<const uint16_t*>(L->w.shared_gate_vector);
+      gr.logits = L->sh_gate;
+      gr.num_experts = 1;
+      gr.round_logits = 0;
+      gr.tile_cnt = nullptr;  // a plain dot product: no top-k
+      if (T_loc > 0) {        // per token of x (combine: row t - local_row0)
+        SENMOE_CUDA(launch_router_logits(gr, s5));
+        SENMOE_CUDA(launch_sigmoid_inplace(L->sh_gate, T_loc, s5));
+      }
+    }
+    return SENMOE_OK;
+  };
+  // With stage profiling the shared expert runs in its own stage, after the
+  // routed experts; otherwise it is forked onto the layer's side stream
+  // here, so that its kernels overlap the router, dispatch and routed expert
+  // launches (it reads only x), and joined before the combine.
+  const bool overlap_shared = Is > 0 && !profile && L->side;
+  if (overlap_shared) {
+    SENMOE_CUDA(cudaEventRecord(L->fork_ev, st));
+    SENMOE_CUDA(cudaStreamWaitEvent(L->side, L->fork_ev, 0));
+    const int rc = run_shared(L->side);
+    if (rc != SENMOE_OK) return rc;
+    SENMOE_CUDA(cudaEventRecord(L->join_ev, L->side));
+  }
+
   // Routing is partitioned by token: the token-local form routes the tokens
   // x holds; the replicated form, where partition_routing says so, routes the
   // block of tokens its combine owns.  Either way the rows are published to
@@ -811,126 +960,12 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   // expert parallelism: this rank's rows are complete; peers may read them
   if (ep) SENMOE_CUDA(launch_ep_announce(ea, st));
 
-  // 5. shared expert (deepseek_v2.rs:550-552), optionally sigmoid-gated.
-  // On the tensor-core kernels it is a grouped GEMM of one expert over the
-  // rows of x this rank combines (all of them on one GPU): sh_out row i is
-  // token sh_t0 + i.  Otherwise the CUDA-core GEMV over every token.
-  int sh_t0 = 0;
-  if (Is > 0) {
-    // the tokens this rank combines (global indices own_t0 ..); the
-    // token-local form holds exactly those in x
-    const int sh_n = local ? T_loc : ep ? ea.tok_begin[L->ep_rank + 1] - ea.tok_begin[L->ep_rank] : T;
-    const int own_t0 = local ? row0 : ep ? ea.tok_begin[L->ep_rank] : 0;
-    const int forced = c.reserved[0];
-    int sh_path = kPathGemv;
-    if (forced == kPathTensorCore && L->sh_tc_ok) sh_path = kPathTensorCore;
-    else if (forced == kPathMma && L->sh_mma_ok) sh_path = kPathMma;
-    // kernel and tile width follow the call's token count T, the same on every
-    // expert-parallel rank and on one GPU, so each token's shared output is
-    // bit-identical however the tokens are split
-    else if (forced == kPathAuto)
-      sh_path = (T >= kTcMinTokensPerExpert && L->sh_tc_ok) ? kPathTensorCore
-                : L->sh_mma_ok                                  ? kPathMma
-                : L->sh_tc_ok                                   ? kPathTensorCore
-                                                                : kPathGemv;
-    if (sh_path != kPathGemv) {
-      sh_t0 = own_t0;  // the GEMV below writes every token's row instead
-      TcGemmArgs sa{};
-      sa.s[0] = static_cast<const uint16_t*>(L->w.shared_gate_scales);
-      sa.b[0] = static_cast<const uint16_t*>(L->w.shared_gate_biases);
-      sa.s[1] = static_cast<const uint16_t*>(L->w.shared_up_scales);
-      sa.b[1] = static_cast<const uint16_t*>(L->w.shared_up_biases);
-      sa.rows = Is;
-      sa.kdim = H;
-      sa.m_tiles = Is / 128;
-      sa.offsets = L->sh_group;       // {0, sh_n}, written by the gather below
-      sa.active = L->sh_group + 2;    // {0}
-      sa.active_count = L->sh_group + 3;
-      sa.expert_begin = 0;
-      sa.out = L->hsh16;
-      sa.out_stride = Is;
-      sa.act = c.activation;
-      sa.err = L->err;
-      sa.xsum = L->xsum_sh;
-      TcGemmArgs sd = sa;
-      sd.s[0] = sd.s[1] = static_cast<const uint16_t*>(L->w.shared_down_scales);
-      sd.b[0] = sd.b[1] = static_cast<const uint16_t*>(L->w.shared_down_biases);
-      sd.rows = H;
-      sd.kdim = Is;
-      sd.m_tiles = H / 128;
-      sd.out = L->sh_out;
-      sd.out_stride = H;
-      const uint16_t* xs_src = static_cast<const uint16_t*>(x) + static_cast<size_t>(sh_t0 - row0) * H;
-      if (sh_n > 0 && sh_path == kPathMma) {
-        const int nt = T <= 8 ? 1 : (T <= 16 ? 2 : 4);
-        const CUtensorMap& tb_x = nt == 1 ? L->tm_xsh8 : L->tm_xsh[nt == 2 ? 0 : 1];
-        const CUtensorMap& tb_h = nt == 1 ? L->tm_hsh8 : L->tm_hsh[nt == 2 ? 0 : 1];
-        const bool g4 = mma_g4_supported(c.bits, nt, sa) &&
-                        (c.reserved[1] == kMmaFormG4Single || (c.reserved[1] == kMmaFormAuto && nt == 1));
-        SENMOE_CUDA(launch_gather_rows(xs_src, L->sh_iota, 1, L->xs_sh, sh_n, H, L->err, st, nullptr, 0, 0,
-                                       g4 ? kOrderMmaG4 : kOrderMma, g4 ? L->xsum_sh : nullptr, L->sh_group));
-        SENMOE_CUDA(launch_mma_gemm(L->tm_shg, L->tm_shu, tb_x, sa, c.bits, 2, nt, g4,
-                                    (sh_n / (8 * nt) + 1) * sa.m_tiles, st));
-        SENMOE_CUDA(launch_mma_gemm(L->tm_shd, L->tm_shd, tb_h, sd, c.bits, 1, nt, g4,
-                                    (sh_n / (8 * nt) + 1) * sd.m_tiles, st));
-      } else if (sh_n > 0) {
-        const int ti = tc_tile_index(double(T)), bn = kTcTiles[ti];
-        SENMOE_CUDA(launch_gather_rows(xs_src, L->sh_iota, 1, L->xs_sh, sh_n, H, L->err, st, nullptr, 0, 0,
-                                       kOrderTc, nullptr, L->sh_group));
-        SENMOE_CUDA(launch_tc_gemm(L->tm_shg, L->tm_shu, L->tm_xsh[ti], sa, c.bits, 2, bn,
-                                   (sh_n / bn + 1) * sa.m_tiles, st));
-        SENMOE_CUDA(launch_tc_gemm(L->tm_shd, L->tm_shd, L->tm_hsh[ti], sd, c.bits, 1, bn,
-                                   (sh_n / bn + 1) * sd.m_tiles, st));
-      }
-    } else {
-      sh_t0 = row0;  // every token x holds, row i = global token row0 + i
-      QGemvArgs sg{};
-      sg.x = static_cast<const uint16_t*>(x);
-      sg.w[0] = L->w.shared_gate_weight;
-      sg.s[0] = static_cast<const uint16_t*>(L->w.shared_gate_scales);
-      sg.b[0] = static_cast<const uint16_t*>(L->w.shared_gate_biases);
-      sg.w[1] = L->w.shared_up_weight;
-      sg.s[1] = static_cast<const uint16_t*>(L->w.shared_up_scales);
-      sg.b[1] = static_cast<const uint16_t*>(L->w.shared_up_biases);
-      sg.kdim = H;
-      sg.rows = Is;
-      sg.rows_per_cta = kGateUpRows;
-      sg.mode = kItemsGather;
-      sg.gather_idx = L->zeros_idx;
-      sg.rep = 1;
-      sg.num_experts = 1;
-      sg.out = L->sh_h;
-      sg.out_stride = Is;
-      sg.act = c.activation;
-      sg.err = L->err;
-      SENMOE_CUDA(launch_qgemv(sg, 2, c.bits, T_loc, st));
-      QGemvArgs sd = sg;
-      sd.x = L->sh_h;
-      sd.w[0] = L->w.shared_down_weight;
-      sd.s[0] = static_cast<const uint16_t*>(L->w.shared_down_scales);
-      sd.b[0] = static_cast<const uint16_t*>(L->w.shared_down_biases);
-      sd.kdim = Is;
-      sd.rows = H;
-      sd.rows_per_cta = kDownRows;
-      sd.out = L->sh_out;
-      sd.out_stride = H;
-      SENMOE_CUDA(launch_qgemv(sd, 1, c.bits, T_loc, st));
-    }
-    if (c.shared_gate) {
-      RouterArgs gr = ra;
-      gr.x = static_cast<const uint16_t*>(x);  // every token x holds (combine: row t - local_row0)
-      gr.num_tokens = T_loc;
-      gr.weight = static_cast<const uint16_t*>(L->w.shared_gate_vector);
-      gr.logits = L->sh_gate;
-      gr.num_experts = 1;
-      gr.round_logits = 0;
-      gr.tile_cnt = nullptr;  // a plain dot product: no top-k
-      if (T_loc > 0) {        // per token of x (combine: row t - local_row0)
-        SENMOE_CUDA(launch_router_logits(gr, st));
-        SENMOE_CUDA(launch_sigmoid_inplace(L->sh_gate, T_loc, st));
-      }
-    }
+  // 5. the shared expert: joined from the side stream, or run now
+  if (Is > 0 && !overlap_shared) {
+    const int rc = run_shared(st);
+    if (rc != SENMOE_OK) return rc;
   }
+  if (overlap_shared) SENMOE_CUDA(cudaStreamWaitEvent(st, L->join_ev, 0));
 
   SENMOE_CUDA(mark(5));
 
