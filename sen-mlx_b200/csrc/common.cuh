@@ -127,6 +127,10 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 __device__ __forceinline__ void cp_async_8(uint32_t dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
 }
+// 4-byte asynchronous global -> shared copy (both addresses 4-byte aligned).
+__device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
 // Arrival on `bar` once all of this thread's earlier cp.async copies have
 // landed; counts as one of the barrier's expected arrivals (.noinc).
 __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {

@@ -22,10 +22,10 @@
 // projection (down) or two sharing the activation tile (gate and up, whose
 // epilogue applies SwiGLU/GeGLU with MLX's bf16 rounding and stores h as fp16
 // for the down GEMM's B operand).  Warp roles:
-//   warp 0     TMA producer: packed codes (2-D tensor map, no swizzle), the
-//              activation tile (2-D tensor map, SWIZZLE_128B), and once per
-//              tile the rows' scales and biases (1-D bulk copies).  No
-//              multicast anywhere.
+//   warp 0     producer of the packed codes (lane 0: 2-D TMA, no swizzle)
+//              and, per packed stage, its rows' scales and biases (all 32
+//              lanes, 4- or 8-byte cp.async into shared memory, arriving on
+//              the stage's barrier).  No multicast anywhere.
 //   warp 1     TMEM owner; one lane issues tcgen05.mma (kind::f16, fp16 x
 //              fp16 -> fp32, M=128, N=BN, K=16) and tcgen05.commit.
 //   warps 2-17 dequantise each 64-column k-block of codes to fp16
@@ -191,10 +191,17 @@ template <int BITS, int NPROJ, int BN> struct TcShape {
   static constexpr bool kStage = NPROJ == 2 && kAcc == 1;
   static constexpr uint32_t kEStride = BN * 4 + 16;
   static constexpr uint32_t kEBytes = kStage ? 128u * kEStride : 0u;
-  // packed stages fill the rest of shared memory (at most 8)
-  static constexpr int kPFit = int((200u * 1024u - kB * kBBytes - kEBytes) / (NPROJ * kPBytes));
+  // each packed stage carries its rows' scales and biases: [NPROJ][scale,
+  // bias][128 rows][KP bf16], copied by the producer warp's lanes
+  static constexpr uint32_t kSBRow = KP * 2;
+  static constexpr uint32_t kSBStage = NPROJ * 2 * 128 * kSBRow;
+  // packed stages fill the rest of shared memory (at most 8); staged shapes
+  // budget up to the 227 KB limit (static shared memory below 2 KB)
+  static constexpr uint32_t kBudget = (kStage ? 224u : 200u) * 1024u;
+  static constexpr int kPFit = int((kBudget - kB * kBBytes - kEBytes) / (NPROJ * kPBytes + kSBStage));
   static constexpr int kP = kPFit > 8 ? 8 : kPFit;
-  static constexpr size_t kSmem = 1024 + size_t(kB) * kBBytes + size_t(kP) * NPROJ * kPBytes + kEBytes;
+  static constexpr size_t kSmem =
+      1024 + size_t(kB) * kBBytes + size_t(kP) * (NPROJ * kPBytes + kSBStage) + kEBytes;
   // Staged shapes add four helper warps that evaluate half of each staging
   // row (see kHelpWarp0).
   static constexpr int kThreads = (kStage ? 28 : 24) * 32;
@@ -232,13 +239,13 @@ __device__ __forceinline__ uint16_t pick_bf16(const uint32_t (&v)[KP / 2], int j
 }
 
 template <int KP>
-__device__ __forceinline__ void load_group_params(const uint16_t* p, uint32_t (&v)[KP / 2]) {
+__device__ __forceinline__ void load_group_params_smem(const unsigned char* p, uint32_t (&v)[KP / 2]) {
   if constexpr (KP == 4) {
-    const uint2 t = __ldg(reinterpret_cast<const uint2*>(p));
+    const uint2 t = *reinterpret_cast<const uint2*>(p);
     v[0] = t.x;
     v[1] = t.y;
   } else {
-    v[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
+    v[0] = *reinterpret_cast<const uint32_t*>(p);
   }
 }
 
@@ -277,11 +284,13 @@ __global__ void __launch_bounds__(TcShape<BITS, NPROJ, BN>::kThreads, 1)
   unsigned char* sB = base;                       // [SB][KA][BN*128]
   unsigned char* sP = sB + SB * kBBytes;          // [SP][NPROJ][16 KB]
   unsigned char* sE = sP + SP * NPROJ * kPBytes;  // [128 rows][kEStride] epilogue staging (kStage)
+  unsigned char* sSB = sE + S::kEBytes;             // [SP] packed stages' scales and biases
 
   // ---- barriers and TMEM first: they do not depend on the previous kernel
   if (warp == 0 && lane == 0) {
     // consumer-side barriers count warps: each warp fences, syncs, and arrives once
-    for (int i = 0; i < SP; ++i) { mbar_init(&bar_pfull[i], 1); mbar_init(&bar_pempty[i], kDqWarps); }
+    // packed stage full: the TMA's expect_tx arrival plus one cp.async arrival per producer lane
+    for (int i = 0; i < SP; ++i) { mbar_init(&bar_pfull[i], 33); mbar_init(&bar_pempty[i], kDqWarps); }
     for (int i = 0; i < SA; ++i) { mbar_init(&bar_afull[i], kDqWarps); mbar_init(&bar_aempty[i], S::kIss); }
     for (int i = 0; i < SB; ++i) { mbar_init(&bar_bfull[i], 1); mbar_init(&bar_bempty[i], S::kIss); }
     for (int i = 0; i < ACC; ++i) { mbar_init(&bar_accfull[i], S::kIss); mbar_init(&bar_accempty[i], 4); }
@@ -323,8 +332,10 @@ __global__ void __launch_bounds__(TcShape<BITS, NPROJ, BN>::kThreads, 1)
 
   if (warp == 0 || warp == kBWarp) {
     // ================================================= TMA producers
-    if (lane == 0) {
-      const bool packed = warp == 0;  // warp 0: packed codes, warp kBWarp: activation tiles
+    // warp 0: packed codes (lane 0's TMA) and their scales / biases (every
+    // lane, cp.async); warp kBWarp: activation tiles (lane 0)
+    const bool packed = warp == 0;
+    if (packed || lane == 0) {
       int last_p[SP], last_b[SB];     // parity of the last load issued per stage (-1: none)
 #pragma unroll
       for (int i = 0; i < SP; ++i) last_p[i] = -1;
@@ -338,11 +349,29 @@ __global__ void __launch_bounds__(TcShape<BITS, NPROJ, BN>::kThreads, 1)
         if (packed) {
           for (int kt = 0; kt < ktiles; kt += KP) {  // packed stage: k-blocks [kt, kt + KP)
             const int ps = pi % SP, pph = (pi / SP) & 1;
-            if (!(ok = wait_or_abort(&bar_pempty[ps], pph ^ 1, &s_abort, a.err))) break;
-            mbar_arrive_expect_tx(&bar_pfull[ps], NPROJ * kPBytes);
-            tma_load_2d(sP + (ps * NPROJ + 0) * kPBytes, &tmA0, (kt / KP) * 32, row_base, &bar_pfull[ps]);
-            if constexpr (NPROJ == 2)
-              tma_load_2d(sP + (ps * NPROJ + 1) * kPBytes, &tmA1, (kt / KP) * 32, row_base, &bar_pfull[ps]);
+            if (!(ok = __all_sync(0xffffffffu, wait_or_abort(&bar_pempty[ps], pph ^ 1, &s_abort, a.err)))) break;
+            if (lane == 0) {
+              mbar_arrive_expect_tx(&bar_pfull[ps], NPROJ * kPBytes);
+              tma_load_2d(sP + (ps * NPROJ + 0) * kPBytes, &tmA0, (kt / KP) * 32, row_base, &bar_pfull[ps]);
+              if constexpr (NPROJ == 2)
+                tma_load_2d(sP + (ps * NPROJ + 1) * kPBytes, &tmA1, (kt / KP) * 32, row_base, &bar_pfull[ps]);
+            }
+            // the stage's scales and biases: KP bf16 per row and array, rows
+            // lane, lane + 32, lane + 64, lane + 96
+            const uint32_t sb0 = smem_u32(sSB + ps * S::kSBStage);
+#pragma unroll
+            for (int pa = 0; pa < 2 * NPROJ; ++pa) {  // array pa: scales (even) / biases (odd) of proj pa / 2
+              const uint16_t* src = ((pa & 1) ? a.b[pa >> 1] : a.s[pa >> 1]) + kt;
+#pragma unroll
+              for (int rr = 0; rr < 4; ++rr) {
+                const int r = lane + 32 * rr;
+                const uint32_t dst = sb0 + (pa * 128 + r) * S::kSBRow;
+                const uint16_t* g = src + static_cast<size_t>(row_base + r) * groups;
+                if constexpr (S::kSBRow == 8) cp_async_8(dst, g);
+                else cp_async_4(dst, g);
+              }
+            }
+            cp_async_arrive_noinc(&bar_pfull[ps]);
             last_p[ps] = pph;
             ++pi;
           }
@@ -448,29 +477,9 @@ __global__ void __launch_bounds__(TcShape<BITS, NPROJ, BN>::kThreads, 1)
         tmem + (static_cast<uint32_t>(q * 32) << 16) + S::kACol0 + proj * KA * 32 + slice * CPT;
     bool ok = true;
     int pi = 0, ai = 0;
-    // scales / biases of the next packed stage, prefetched one stage ahead,
-    // across tile boundaries too
-    // (sv, bv) this packed stage, (sn, bn) the next, (snn, bnn) the one after:
-    // prefetched two packed stages ahead, across tile boundaries too
-    uint32_t sv[KP / 2], bv[KP / 2], sn[KP / 2], bn[KP / 2], snn[KP / 2], bnn[KP / 2];
-    auto group_ptr = [&](int ti, const uint16_t* base_ptr) {
-      const int4 t = s_tiles[ti];
-      return base_ptr + static_cast<size_t>(t.x * a.rows + t.y + row) * groups;
-    };
-    // loads the parameters of the packed stage `ahead` stages after (ti, kt)
-    auto prefetch = [&](int ti, int kt, int ahead, uint32_t (&sd)[KP / 2], uint32_t (&bd)[KP / 2]) {
-      kt += ahead * KP;
-      while (kt >= ktiles && ti < ntiles) {
-        kt -= ktiles;
-        ++ti;
-      }
-      if (ti < ntiles) {
-        load_group_params<KP>(group_ptr(ti, a.s[proj]) + kt, sd);
-        load_group_params<KP>(group_ptr(ti, a.b[proj]) + kt, bd);
-      }
-    };
-    prefetch(0, 0, 0, sn, bn);
-    prefetch(0, 0, 1, snn, bnn);
+    // this packed stage's scales / biases of the thread's row, from the
+    // stage's copy in shared memory
+    uint32_t sv[KP / 2], bv[KP / 2];
     for (int ti = 0; ti < ntiles && ok; ++ti) {
       int ps = 0;
       for (int st = 0; st < nsteps; ++st, ++ai) {
@@ -480,14 +489,9 @@ __global__ void __launch_bounds__(TcShape<BITS, NPROJ, BN>::kThreads, 1)
           const int pph = (pi / SP) & 1;
           ok = __all_sync(0xffffffffu, wait_or_abort(&bar_pfull[ps], pph, &s_abort, a.err));
           if (!ok) break;
-#pragma unroll
-          for (int i = 0; i < KP / 2; ++i) {
-            sv[i] = sn[i];
-            bv[i] = bn[i];
-            sn[i] = snn[i];
-            bn[i] = bnn[i];
-          }
-          prefetch(ti, kt0, 2, snn, bnn);
+          const unsigned char* sbr = sSB + ps * S::kSBStage + (2 * proj * 128 + row) * S::kSBRow;
+          load_group_params_smem<KP>(sbr, sv);
+          load_group_params_smem<KP>(sbr + 128 * S::kSBRow, bv);
         }
         const int as = ai % SA, aph = (ai / SA) & 1;
         ok = __all_sync(0xffffffffu, wait_or_abort(&bar_aempty[as], aph ^ 1, &s_abort, a.err));

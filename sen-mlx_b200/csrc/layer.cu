@@ -75,11 +75,14 @@ constexpr int kDownRows = 64;
 // 256-token tile of gate and up would fill it with accumulators alone.
 constexpr int kTcTiles[4] = {16, 32, 64, 128};
 constexpr int kTcMaxTile = 3;  // index of the widest tile
-// Measured on B200 over the 48-layer config-1 stack: the warp-MMA kernel is
-// fastest up to at least 16 tokens per touched expert (batch 1-256), the
-// tcgen05 GEMM for prefill-size groups; the CUDA-core GEMV is kept for shapes
-// the tensor paths do not support and as the forced reference path.
-constexpr double kTcMinTokensPerExpert = 24.0;
+// Measured on B200 (4-layer config-1 and config-4 stacks, CUDA-graph replay,
+// each path forced): the warp-MMA kernel is fastest for decode-size groups,
+// the tcgen05 GEMM from 16 tokens per expert at 4 bits (config 1: 192 against
+// 200 us per layer at 256 tokens, 146 against 135 at 128) and from 24 at
+// 8 bits, whose dequantisation costs the tcgen05 kernel about twice the ALU
+// work; the CUDA-core GEMV is kept for shapes the tensor paths do not support
+// and as the forced reference path.
+inline double tc_min_tokens_per_expert(int bits) { return bits == 4 ? 16.0 : 24.0; }
 constexpr double kMmaMinTokensPerExpert = 0.0;
 enum ExpertPath { kPathAuto = 0, kPathGemv = 1, kPathTensorCore = 2, kPathMma = 3 };
 // SenMoeConfig.reserved[1]: warp-MMA form, 0 = group-scaled where supported
@@ -470,7 +473,7 @@ static int expert_path_for(const SenMoeLayer* L, int64_t pairs) {
   if (forced == kPathGemv) return kPathGemv;
   if (forced != kPathAuto) return kPathGemv;  // forced path not available for this shape
   const double pe = tokens_per_expert(L, pairs);
-  if (pe >= kTcMinTokensPerExpert && L->tc_ok) return kPathTensorCore;
+  if (pe >= tc_min_tokens_per_expert(L->cfg.bits) && L->tc_ok) return kPathTensorCore;
   if (pe >= kMmaMinTokensPerExpert && L->mma_ok) return kPathMma;
   if (pe >= kMmaMinTokensPerExpert && L->tc_ok) return kPathTensorCore;
   return kPathGemv;
@@ -589,7 +592,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     // expert-parallel rank and on one GPU, so each token's shared output is
     // bit-identical however the tokens are split
     else if (forced == kPathAuto)
-      sh_path = (T >= kTcMinTokensPerExpert && L->sh_tc_ok) ? kPathTensorCore
+      sh_path = (T >= tc_min_tokens_per_expert(c.bits) && L->sh_tc_ok) ? kPathTensorCore
                 : L->sh_mma_ok                                  ? kPathMma
                 : L->sh_tc_ok                                   ? kPathTensorCore
                                                                 : kPathGemv;

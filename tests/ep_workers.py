@@ -161,7 +161,8 @@ def two_cta_form(args, T, world, sms):
     pairs = P * e_local // E if world > 1 else P
     pairs = max(pairs, 1)
     pe = pairs / min(pairs, e_local)
-    if args.expert_path not in (0, 3) or (args.expert_path == 0 and pe >= 24.0):
+    tc_min = 16.0 if args.bits == 4 else 24.0  # layer.cu tc_min_tokens_per_expert
+    if args.expert_path not in (0, 3) or (args.expert_path == 0 and pe >= tc_min):
         return False  # not the warp-MMA path
     return (args.bits == 4 and pe <= 8.0 and args.mma_form == 0 and min(P, e_local) * (I // 128) < sms)
 
