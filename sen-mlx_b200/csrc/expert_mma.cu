@@ -265,7 +265,8 @@ __global__ void __launch_bounds__(G4 ? kThreadsG4 : kThreads, 1)
   pdl_launch_dependents();
   // the stage ring is free until the producer starts: use it as scratch
   const int nlisted = list_tiles(a.active, a.active_count, a.offsets, a.expert_begin, a.m_tiles, kRows, 8 * NT, false,
-                                 s_tiles, kMaxTiles, reinterpret_cast<int*>(sStage), a.err, a.slot_cap);
+                                 s_tiles, kMaxTiles, reinterpret_cast<int*>(sStage), a.err, a.slot_cap, a.cnt_lo,
+                                 a.cnt_hi);
   if (threadIdx.x == 0) s_ntiles = nlisted;
   __syncthreads();
   const int ntiles = s_ntiles;
@@ -695,7 +696,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   pdl_wait();  // active list / offsets (dispatch) and the activation rows (gather or gate/up)
   pdl_launch_dependents();
   const int nlisted = list_tiles(a.active, a.active_count, a.offsets, a.expert_begin, a.m_tiles, kQRows, 8, false,
-                                 s_tiles, kMaxTiles, reinterpret_cast<int*>(sStage), a.err, a.slot_cap);
+                                 s_tiles, kMaxTiles, reinterpret_cast<int*>(sStage), a.err, a.slot_cap, a.cnt_lo,
+                                 a.cnt_hi);
   if (threadIdx.x == 0) s_ntiles = nlisted;
   __syncthreads();
   const int ntiles = s_ntiles;

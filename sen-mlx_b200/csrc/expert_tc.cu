@@ -313,7 +313,8 @@ __global__ void __launch_bounds__(TcShape<BITS, NPROJ, BN>::kThreads, 1)
   // until the producer starts: it is the list's scratch.
   {
     const int n = list_tiles(a.active, a.active_count, a.offsets, a.expert_begin, a.m_tiles, BM, BN, true, s_tiles,
-                             kMaxTilesPerCta, reinterpret_cast<int*>(sP), a.err, a.slot_cap);
+                             kMaxTilesPerCta, reinterpret_cast<int*>(sP), a.err, a.slot_cap, a.cnt_lo,
+                             a.cnt_hi);
     if (tid == 0) {
       s_ntiles = n;
       s_abort = 0;
@@ -839,7 +840,8 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
                                                           int* err, const int32_t* __restrict__ offsets, int eb,
                                                           int ee, int order, float* __restrict__ group_sums,
                                                           int32_t* __restrict__ one_group, const PeerRows pr,
-                                                          int slot_cap) {
+                                                          int slot_cap, const int32_t* __restrict__ ids, int cnt_lo,
+                                                          int cnt_hi) {
   pdl_wait();
   pdl_launch_dependents();
   if (one_group && blockIdx.x == 0 && threadIdx.x == 0) {
@@ -867,6 +869,11 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
   for (int j = 0; j < kGatherSlots; ++j) {
     const int s = s0 + j;
     live[j] = s < num_slots && s >= lo_slot && s < hi_slot;
+    if (live[j] && cnt_hi > 0) {  // only the slots of experts with cnt_lo <= slots < cnt_hi
+      const int e = ids[perm[s]];
+      const int c = offsets[e + 1] - offsets[e];
+      live[j] = c >= cnt_lo && c < cnt_hi;
+    }
     src[j] = live[j] ? gather_src_row(x, perm[s] / k_div, hidden, pr) : x;
   }
   bool ok = true;
@@ -877,7 +884,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
     const int groups = hidden / 64;
     for (int it = threadIdx.x; it < kGatherSlots * groups; it += blockDim.x) {
       const int j = it / groups, G = it - j * groups, s = s0 + j;
-      if (!(s < num_slots && s >= lo_slot && s < hi_slot)) continue;
+      if (!live[j]) continue;
       const uint4* in = reinterpret_cast<const uint4*>(gather_src_row(x, perm[s] / k_div, hidden, pr) + 64 * G);
       uint32_t w[32];
 #pragma unroll
@@ -973,15 +980,17 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
                                int num_slots, int hidden, int* err, cudaStream_t st,
                                const int32_t* offsets, int eb, int ee, int order, float* group_sums,
-                               int32_t* one_group, const PeerRows* peer_rows, int slot_cap) {
+                               int32_t* one_group, const PeerRows* peer_rows, int slot_cap, const int32_t* ids,
+                               int cnt_lo, int cnt_hi) {
   if (num_slots <= 0) return cudaSuccess;
+  if (cnt_hi > 0 && (!ids || !offsets)) return cudaErrorInvalidValue;
   const int threads = hidden / 8 < 256 ? ((hidden / 8 + 31) / 32) * 32 : 256;
   const int grid = (num_slots + kGatherSlots - 1) / kGatherSlots;
   PeerRows pr{};
   if (peer_rows) pr = *peer_rows;
   return launch_pdl(gather_rows_kernel, dim3(grid), dim3(threads), 0, st, x, perm, k_div, x_sorted, num_slots,
                     hidden, err, offsets, eb, ee, order, order == kOrderMmaG4 ? group_sums : nullptr, one_group, pr,
-                    slot_cap);
+                    slot_cap, ids, cnt_lo, cnt_hi);
 }
 
 }  // namespace senmoe

@@ -167,6 +167,10 @@ struct TcGemmArgs {
   // of the activation, h and out buffers, which hold slot_cap rows (0: no
   // limit); rows past slot_cap are not computed (kDevSlotOverflow).
   int slot_cap;
+  // With cnt_hi > 0 only experts whose slot count c (before any slot_cap
+  // clipping) satisfies cnt_lo <= c < cnt_hi get tiles: a call splits its
+  // experts between the warp-MMA and the tcgen05 kernels by their load.
+  int cnt_lo, cnt_hi;
 };
 size_t tc_smem_bytes(int bits, int nproj, int bn, int kdim);
 bool tc_supported(int rows, int kdim, int bits, int nproj, int bn);
@@ -206,12 +210,16 @@ struct PeerRows {
 // post-scales with.  With `one_group` non-null (int32 [4]) the kernel also
 // writes a one-group tile list for the consuming GEMMs: offsets {0,
 // num_slots}, active {0}, count 1 (the shared expert as a grouped GEMM of
-// one expert over every gathered row).
+// one expert over every gathered row).  With cnt_hi > 0 (needs `ids`, the
+// [T, K] expert ids perm indexes, and `offsets`) only the slots of experts
+// with cnt_lo <= slots < cnt_hi are gathered: one call per kernel class when
+// a forward splits its experts between the warp-MMA and tcgen05 kernels.
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div, uint16_t* x_sorted,
                                int num_slots, int hidden, int* err, cudaStream_t st,
                                const int32_t* offsets = nullptr, int eb = 0, int ee = 0, int order = kOrderTc,
                                float* group_sums = nullptr, int32_t* one_group = nullptr,
-                               const PeerRows* peer_rows = nullptr, int slot_cap = 0);
+                               const PeerRows* peer_rows = nullptr, int slot_cap = 0,
+                               const int32_t* ids = nullptr, int cnt_lo = 0, int cnt_hi = 0);
 
 // ------------------------------------------- warp-MMA expert GEMM (decode)
 // Same arguments as the tcgen05 GEMM (TcGemmArgs; out holds h as fp16 in

@@ -83,6 +83,15 @@ constexpr int kTcMaxTile = 3;  // index of the widest tile
 // work; the CUDA-core GEMV is kept for shapes the tensor paths do not support
 // and as the forced reference path.
 inline double tc_min_tokens_per_expert(int bits) { return bits == 4 ? 16.0 : 24.0; }
+// The per-call choice above sees only the mean load per expert.  Skewed
+// routing (a few experts holding most pairs) is better served by both
+// kernels at once: from kHybridMinPairs pairs, a call on the warp-MMA path
+// sends experts with at least kHybridHotSlots slots to the tcgen05 GEMM
+// (128-slot tiles, so their weights stream once) and the rest to the
+// warp-MMA kernel; each kernel lists only its own experts.  Below that size
+// the two extra launches cost more than any skew recovers.
+constexpr int kHybridMinPairs = 2048;
+constexpr int kHybridHotSlots = 32;
 constexpr double kMmaMinTokensPerExpert = 0.0;
 enum ExpertPath { kPathAuto = 0, kPathGemv = 1, kPathTensorCore = 2, kPathMma = 3 };
 // SenMoeConfig.reserved[1]: warp-MMA form, 0 = group-scaled where supported
@@ -845,11 +854,26 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     const bool g4 = mma_g4_supported(c.bits, nt, ga) &&
                     (c.reserved[1] == kMmaFormG4Single || (c.reserved[1] == kMmaFormAuto && nt == 1));
     const bool q4 = g4 && nt == 1 && L->q4_ok && c.reserved[1] == kMmaFormAuto && max_items * (I / 128) < L->sms;
+    const bool hybrid = P >= kHybridMinPairs && L->tc_ok && c.reserved[0] == kPathAuto && !q4;
+    const int hot = kHybridHotSlots, hot_max = 0x7fffffff;
+    ga.cnt_lo = 0;
+    ga.cnt_hi = hybrid ? hot : 0;
     SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
                                    L->offsets, c.expert_begin, c.expert_end,
-                                   g4 ? kOrderMmaG4 : kOrderMma, g4 ? L->xsum : nullptr, nullptr, prow_p, slot_cap));
+                                   g4 ? kOrderMmaG4 : kOrderMma, g4 ? L->xsum : nullptr, nullptr, prow_p, slot_cap,
+                                   ids, ga.cnt_lo, ga.cnt_hi));
+    if (hybrid)  // the loaded experts' slots, in the tcgen05 kernel's order
+      SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
+                                     L->offsets, c.expert_begin, c.expert_end, kOrderTc, nullptr, nullptr, prow_p,
+                                     slot_cap, ids, hot, hot_max));
     ga.xsum = L->xsum;
     ga.slot_cap = slot_cap;
+    // the loaded experts on the tcgen05 GEMM (gate/up, then down)
+    TcGemmArgs ha = ga;
+    ha.m_tiles = I / 128;
+    ha.cnt_lo = hot;
+    ha.cnt_hi = hot_max;
+    const int hot_upper = P / kTcTiles[kTcMaxTile] + P / hot;  // slot tiles of the loaded experts, at most
     SENMOE_CUDA(mark(2));
     if (q4) {
       ga.m_tiles = I / 64;
@@ -858,6 +882,9 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
       SENMOE_CUDA(launch_mma_gemm(L->tm_gate, L->tm_up, tb_x, ga, c.bits, 2, nt, g4,
                                   (P / (8 * nt) + max_items) * ga.m_tiles, st));
     }
+    if (hybrid)
+      SENMOE_CUDA(launch_tc_gemm(L->tm_gate, L->tm_up, L->tm_xs[kTcMaxTile], ha, c.bits, 2, kTcTiles[kTcMaxTile],
+                                 hot_upper * ha.m_tiles, st));
     SENMOE_CUDA(mark(3));
     TcGemmArgs gd = ga;
     gd.s[0] = static_cast<const uint16_t*>(L->w.down_scales);
@@ -876,6 +903,14 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     } else {
       SENMOE_CUDA(launch_mma_gemm(L->tm_down, L->tm_down, tb_h, gd, c.bits, 1, nt, g4,
                                   (P / (8 * nt) + max_items) * gd.m_tiles, st));
+    }
+    if (hybrid) {
+      TcGemmArgs hd = gd;
+      hd.m_tiles = H / 128;
+      hd.cnt_lo = hot;
+      hd.cnt_hi = hot_max;
+      SENMOE_CUDA(launch_tc_gemm(L->tm_down, L->tm_down, L->tm_h[kTcMaxTile], hd, c.bits, 1, kTcTiles[kTcMaxTile],
+                                 hot_upper * hd.m_tiles, st));
     }
     SENMOE_CUDA(mark(4));
   } else if (path == kPathTensorCore) {

@@ -20,11 +20,12 @@ constexpr int kTileScratchInts = 4 * 512 + 64;  // per active expert: e, s0, cnt
 // offsets are issued by all threads at once: a single thread walking the list
 // would wait on one dependent global load per expert.
 // Slots come out local: offsets[e] - offsets[expert_begin]; with slot_cap >
-// 0 an expert's slots past slot_cap are dropped (kDevSlotOverflow).
+// 0 an expert's slots past slot_cap are dropped (kDevSlotOverflow).  With
+// cnt_hi > 0 only experts of cnt_lo <= slots < cnt_hi are listed.
 __device__ __forceinline__ int list_tiles(const int32_t* __restrict__ active, const int32_t* __restrict__ active_count,
                                           const int32_t* __restrict__ offsets, int expert_begin, int m_tiles, int bm,
                                           int bn, bool chunk_major, int4* s_tiles, int max_tiles, int* scratch,
-                                          int* err, int slot_cap = 0) {
+                                          int* err, int slot_cap = 0, int cnt_lo = 0, int cnt_hi = 0) {
   int* s_e = scratch;
   int* s_s0 = scratch + 512;
   int* s_cnt = scratch + 1024;
@@ -38,6 +39,7 @@ __device__ __forceinline__ int list_tiles(const int32_t* __restrict__ active, co
     const int base = offsets[expert_begin];
     const int s0 = offsets[e] - base;
     int cnt = offsets[e + 1] - offsets[e];
+    if (cnt_hi > 0 && (cnt < cnt_lo || cnt >= cnt_hi)) cnt = 0;  // the other kernel's expert
     if (slot_cap > 0 && s0 + cnt > slot_cap) {
       cnt = s0 < slot_cap ? slot_cap - s0 : 0;
       record_error(err, kDevSlotOverflow);

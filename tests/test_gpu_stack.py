@@ -155,14 +155,18 @@ def test_bench_stack_residual_graph_vs_oracle(env, T):
 
 
 @pytest.mark.parametrize("name,T", [("CONFIG1", 4096), ("CONFIG1", 16384), ("CONFIG3", 64), ("CONFIG3", 2048),
-                                    ("CONFIG4", 256), ("CONFIG4", 8192)])
+                                    ("CONFIG4", 256), ("CONFIG4", 8192), ("HYBRID4", 384)])
 def test_baseline_config_sizes_vs_oracle(env, name, T):
     """One layer of each BASELINE config at its token counts on the path the
     layer picks: config 2 (config 1's layer at 4096 and 16,384 tokens),
     config 3 (E=512, K=10, gated shared expert) at 64 and 2048, config 4
-    (8-bit, Zipf-skewed router) at 256 and 8192."""
+    (8-bit, Zipf-skewed router) at 256 and 8192.  Config 4 at 256 tokens and
+    HYBRID4 (4-bit, E=256, skewed, 384 tokens) split their experts between
+    the warp-MMA kernel and the tcgen05 GEMM (at least 2048 pairs on the
+    warp-MMA path: experts with 32 or more slots go to the tcgen05 GEMM)."""
     torch, senmoe, synth = env
-    spec = getattr(synth, name)
+    spec = (synth.LayerSpec("hybrid4", 1024, 256, 8, 512, 4, zipf=True, seed=9) if name == "HYBRID4"
+            else getattr(synth, name))
     w = synth.moe_weights(spec, 1, 0)
     blk = senmoe.DeepseekMoe(synth.moe_args(spec), w, max_tokens=T, device=0)
     x = synth.spec_tokens(spec, T, device="cuda")
@@ -172,6 +176,8 @@ def test_baseline_config_sizes_vs_oracle(env, name, T):
         counts = np.diff(dbg["offsets"])
         top = np.sort(counts)[::-1][:spec.experts // 10].sum()
         assert top > 0.5 * counts.sum(), "the skewed router should send most pairs to the top 10 % of experts"
+        if T * spec.top_k < 4096:  # the split sizes: both kernels get experts
+            assert (counts >= 32).any() and ((counts > 0) & (counts < 32)).any()
     cfg, mw = oracle_layer(spec, w)
     check_sampled(cfg, mw, to_numpy_bf16(x), y, dbg["topk_ids"], sample_rows(T, seed=7))
     blk.close()
