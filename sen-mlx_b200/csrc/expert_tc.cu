@@ -495,12 +495,14 @@ __global__ void __launch_bounds__(TcShape<BITS, NPROJ, BN>::kThreads, 1)
           load_group_params_smem<KP>(sbr + 128 * S::kSBRow, bv);
         }
         const int as = ai % SA, aph = (ai / SA) & 1;
-        ok = __all_sync(0xffffffffu, wait_or_abort(&bar_aempty[as], aph ^ 1, &s_abort, a.err));
-        if (!ok) break;
-        tc_fence_after();  // the MMAs that read this A stage have completed
+        // the step's fp16 values are computed into registers first, then the
+        // A stage is awaited and stored: the arithmetic overlaps the wait for
+        // the MMAs that still read the stage
         const unsigned char* prow = sP + (ps * NPROJ + proj) * kPBytes + row * 128;
+        uint32_t outs[KA][CPT];
 #pragma unroll
         for (int kk = 0; kk < KA; ++kk) {
+          uint32_t (&out)[CPT] = outs[kk];
           const int kt = kt0 + kk;
           const uint16_t sb = pick_bf16<KP>(sv, kt % KP), bb = pick_bf16<KP>(bv, kt % KP);
           // this thread's words start at word (kt % KP) * W + slice * WPT of the
@@ -519,7 +521,6 @@ __global__ void __launch_bounds__(TcShape<BITS, NPROJ, BN>::kThreads, 1)
               wd[i] = v.x; wd[i + 1] = v.y;
             }
           }
-          uint32_t out[CPT];
           if constexpr (BITS == 4) {  // one word (8 codes) -> four columns
             const float sf = bf16_bits_to_f32(sb);
             const __half2 b2 = __float2half2_rn(bf16_bits_to_f32(bb));
@@ -554,9 +555,15 @@ __global__ void __launch_bounds__(TcShape<BITS, NPROJ, BN>::kThreads, 1)
               out[2 * i] = v.x; out[2 * i + 1] = v.y; out[2 * i + 2] = v.z; out[2 * i + 3] = v.w;
             }
           }
+        }
+        ok = __all_sync(0xffffffffu, wait_or_abort(&bar_aempty[as], aph ^ 1, &s_abort, a.err));
+        if (!ok) break;
+        tc_fence_after();  // the MMAs that read this A stage have completed
+#pragma unroll
+        for (int kk = 0; kk < KA; ++kk) {
           const uint32_t taddr = lane_base + as * S::kACols + kk * 32;
-          if constexpr (CPT == 16) tmem_st16(taddr, out);
-          else tmem_st8(taddr, out);
+          if constexpr (CPT == 16) tmem_st16(taddr, outs[kk]);
+          else tmem_st8(taddr, outs[kk]);
         }
         tmem_st_wait();
         tc_fence_before();
@@ -834,6 +841,9 @@ __device__ __forceinline__ const uint16_t* gather_src_row(const uint16_t* x, int
   return pr.base[q] + static_cast<size_t>(token - pr.begin[q]) * hidden;
 }
 
+// kFilter: only the slots of experts with cnt_lo <= slots < cnt_hi (a
+// separate instance, so the unfiltered gather carries no per-slot lookup)
+template <bool kFilter>
 __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __restrict__ x,
                                                           const int32_t* __restrict__ perm, int k_div,
                                                           uint16_t* __restrict__ out, int num_slots, int hidden,
@@ -869,7 +879,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
   for (int j = 0; j < kGatherSlots; ++j) {
     const int s = s0 + j;
     live[j] = s < num_slots && s >= lo_slot && s < hi_slot;
-    if (live[j] && cnt_hi > 0) {  // only the slots of experts with cnt_lo <= slots < cnt_hi
+    if (kFilter && live[j]) {  // only the slots of experts with cnt_lo <= slots < cnt_hi
       const int e = ids[perm[s]];
       const int c = offsets[e + 1] - offsets[e];
       live[j] = c >= cnt_lo && c < cnt_hi;
@@ -988,9 +998,10 @@ cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div
   const int grid = (num_slots + kGatherSlots - 1) / kGatherSlots;
   PeerRows pr{};
   if (peer_rows) pr = *peer_rows;
-  return launch_pdl(gather_rows_kernel, dim3(grid), dim3(threads), 0, st, x, perm, k_div, x_sorted, num_slots,
-                    hidden, err, offsets, eb, ee, order, order == kOrderMmaG4 ? group_sums : nullptr, one_group, pr,
-                    slot_cap, ids, cnt_lo, cnt_hi);
+  auto kern = cnt_hi > 0 ? gather_rows_kernel<true> : gather_rows_kernel<false>;
+  return launch_pdl(kern, dim3(grid), dim3(threads), 0, st, x, perm, k_div, x_sorted, num_slots, hidden, err,
+                    offsets, eb, ee, order, order == kOrderMmaG4 ? group_sums : nullptr, one_group, pr, slot_cap, ids,
+                    cnt_lo, cnt_hi);
 }
 
 }  // namespace senmoe
