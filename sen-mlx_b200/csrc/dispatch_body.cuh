@@ -122,5 +122,81 @@ __device__ __forceinline__ void dispatch_single_body(const DispatchArgs& a, int*
   for (int c = 0; c < nchunks; ++c) place_chunk(a, c, cnt, whist);
 }
 
+// The whole dispatch of at most 128 pairs by one warp, with the same result
+// as dispatch_single_body: a shared-memory histogram, per-lane prefix sums
+// over E/32 consecutive experts (offsets, active list), then stable
+// placement 32 pairs at a time in pair order (match_any rank within the 32
+// plus each expert's running cursor).  cnt: shared [E], E <= 512.
+__device__ __forceinline__ void dispatch_warp_body(const DispatchArgs& a, int* cnt, int lane) {
+  const int E = a.num_experts, P = a.num_pairs;
+  for (int e = lane; e < E; e += 32) cnt[e] = 0;
+  __syncwarp();
+  for (int p = lane; p < P; p += 32) {
+    const int e = __ldcg(a.topk_ids + p);
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+  }
+  __syncwarp();
+  const int epl = (E + 31) / 32, e0 = lane * epl;
+  int mine = 0;
+  uint32_t act = 0;  // bit i: expert e0 + i is local and has pairs
+  for (int i = 0; i < epl; ++i) {
+    const int e = e0 + i;
+    if (e < E) {
+      const int c = cnt[e];
+      mine += c;
+      if (c > 0 && e >= a.expert_begin && e < a.expert_end) act |= 1u << i;
+    }
+  }
+  int incl = mine, ainc = __popc(act);
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, incl, o), v = __shfl_up_sync(0xffffffffu, ainc, o);
+    if (lane >= o) {
+      incl += u;
+      ainc += v;
+    }
+  }
+  int run = incl - mine, apos = ainc - __popc(act);
+  for (int i = 0; i < epl; ++i) {
+    const int e = e0 + i;
+    if (e < E) {
+      const int c = cnt[e];
+      a.offsets[e] = run;
+      cnt[e] = run;  // from here on: the expert's next free slot
+      run += c;
+      if (act & (1u << i)) a.active[apos++] = e;
+    }
+  }
+  if (lane == 31) {
+    a.offsets[E] = incl;
+    *a.active_count = ainc;
+  }
+  __syncwarp();
+  for (int c0 = 0; c0 < P; c0 += 32) {
+    const int p = c0 + lane;
+    int e = -1;
+    if (p < P) {
+      e = __ldcg(a.topk_ids + p);
+      if (e < 0 || e >= E) {
+        record_error(a.err, kDevBadExpert);
+        e = -1;
+      }
+    }
+    const unsigned mask = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(mask & ((1u << lane) - 1u));
+    if (e >= 0) {
+      const int slot = cnt[e] + rank;
+      a.perm[slot] = p;
+      a.inverse[p] = (a.keep_remote_slots || (e >= a.expert_begin && e < a.expert_end)) ? slot : -1;
+    } else if (p < P) {
+      a.inverse[p] = -1;  // rejected id: the combine skips the pair
+    }
+    __syncwarp();
+    if (e >= 0 && lane == __ffs(mask) - 1) cnt[e] += __popc(mask);
+    __syncwarp();
+  }
+}
+constexpr int kWarpDispatchMaxPairs = 128;
+
 }  // namespace dispatch_detail
 }  // namespace senmoe

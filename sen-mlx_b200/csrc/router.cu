@@ -372,6 +372,20 @@ __global__ void __launch_bounds__(dispatch_detail::kThreads) router_topk_dispatc
   dispatch_detail::dispatch_single_body(d, sm_disp);
 }
 
+// Up to 8 tokens and 128 pairs: the same in one CTA of 8 warps, the
+// dispatch by one warp (no block-wide scans or barriers).
+template <int EPL>
+__global__ void __launch_bounds__(kTopkDispatchMaxTokens * 32)
+    router_topk_dispatch_small_kernel(RouterArgs a, DispatchArgs d) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ int sm_small[];  // [E]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (warp < a.num_tokens) topk_row<EPL, false>(a, a.logits + static_cast<size_t>(warp) * a.num_experts, warp, lane);
+  __syncthreads();
+  if (warp == 0) dispatch_detail::dispatch_warp_body(d, sm_small, lane);
+}
+
 bool router_topk_dispatch_supported(int num_tokens, int num_pairs, int num_experts) {
   return num_tokens > 0 && num_tokens <= kTopkDispatchMaxTokens && num_pairs <= dispatch_detail::kThreads * 2 &&
          num_experts <= 512;
@@ -379,8 +393,18 @@ bool router_topk_dispatch_supported(int num_tokens, int num_pairs, int num_exper
 
 cudaError_t launch_router_topk_dispatch(const RouterArgs& a, const DispatchArgs& d, cudaStream_t st) {
   if (!router_topk_dispatch_supported(a.num_tokens, d.num_pairs, a.num_experts)) return cudaErrorNotSupported;
-  const size_t smem = dispatch_smem_bytes(d.num_experts);
   const int epl = (a.num_experts + 31) / 32;
+  if (d.num_pairs <= dispatch_detail::kWarpDispatchMaxPairs) {
+    const size_t smem_small = static_cast<size_t>(d.num_experts) * 4;
+#define SENMOE_TDS_CASE(V)                                                                                  \
+  if (epl <= V)                                                                                            \
+    return launch_pdl(router_topk_dispatch_small_kernel<V>, dim3(1), dim3(kTopkDispatchMaxTokens * 32), smem_small, \
+                      st, a, d);
+    SENMOE_TDS_CASE(1) SENMOE_TDS_CASE(2) SENMOE_TDS_CASE(4) SENMOE_TDS_CASE(8) SENMOE_TDS_CASE(16)
+#undef SENMOE_TDS_CASE
+    return cudaErrorNotSupported;
+  }
+  const size_t smem = dispatch_smem_bytes(d.num_experts);
 #define SENMOE_TD_CASE(V)                                                                                   \
   if (epl <= V) {                                                                                         \
     cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(router_topk_dispatch_kernel<V>), smem); \
