@@ -830,6 +830,7 @@ cudaError_t make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
 // (kperm8), or in one of the warp-MMA kernel's orders (kperm256; kperm_g4,
 // odd columns divided by 16).  Each CTA copies kGatherSlots slots.
 constexpr int kGatherSlots = 4;
+constexpr int kGatherCtasPerSm = 8;
 
 // Row `token` of the gather's source: x, or its owner rank's exchange buffer.
 __device__ __forceinline__ const uint16_t* gather_src_row(const uint16_t* x, int token, int hidden,
@@ -861,7 +862,6 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
     one_group[2] = 0;          // active[0]
     one_group[3] = 1;          // active count
   }
-  const int s0 = blockIdx.x * kGatherSlots;
   int lo_slot = 0, hi_slot = num_slots;
   if (offsets) {  // expert parallelism: only this rank's slots
     lo_slot = offsets[eb];
@@ -872,115 +872,119 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
     if (blockIdx.x == 0 && threadIdx.x == 0) record_error(err, kDevSlotOverflow);
     hi_slot = lo_slot + slot_cap;
   }
-  // slot s is row s - lo_slot of out (and of group_sums)
-  const uint16_t* src[kGatherSlots];
-  bool live[kGatherSlots];
-#pragma unroll
-  for (int j = 0; j < kGatherSlots; ++j) {
-    const int s = s0 + j;
-    live[j] = s < num_slots && s >= lo_slot && s < hi_slot;
-    if (kFilter && live[j]) {  // only the slots of experts with cnt_lo <= slots < cnt_hi
-      const int e = ids[perm[s]];
-      const int c = offsets[e + 1] - offsets[e];
-      live[j] = c >= cnt_lo && c < cnt_hi;
-    }
-    src[j] = live[j] ? gather_src_row(x, perm[s] / k_div, hidden, pr) : x;
-  }
+  // slot s is row s - lo_slot of out (and of group_sums).  The grid strides
+  // over groups of kGatherSlots slots (at most kGatherCtasPerSm CTAs per SM),
+  // so a CTA's next group starts while its earlier stores drain.
   bool ok = true;
-  if (order == kOrderMmaG4) {
-    // kperm_g4, one thread per (slot, 64-column group): output position
-    // 16 s + kappa (kappa = 8 a2 + 2 t + h) holds column
-    // 8 (t + 4 (s / 2)) + (s & 1) + 2 a2 + 4 h, divided by 16 for odd s
-    const int groups = hidden / 64;
-    for (int it = threadIdx.x; it < kGatherSlots * groups; it += blockDim.x) {
-      const int j = it / groups, G = it - j * groups, s = s0 + j;
-      if (!live[j]) continue;
-      const uint4* in = reinterpret_cast<const uint4*>(gather_src_row(x, perm[s] / k_div, hidden, pr) + 64 * G);
-      uint32_t w[32];
+  for (int s0 = blockIdx.x * kGatherSlots; s0 < num_slots; s0 += gridDim.x * kGatherSlots) {
+    const uint16_t* src[kGatherSlots];
+    bool live[kGatherSlots];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const uint4 v = __ldcg(in + q);
-        w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+    for (int j = 0; j < kGatherSlots; ++j) {
+      const int s = s0 + j;
+      live[j] = s < num_slots && s >= lo_slot && s < hi_slot;
+      if (kFilter && live[j]) {  // only the slots of experts with cnt_lo <= slots < cnt_hi
+        const int e = ids[perm[s]];
+        const int c = offsets[e + 1] - offsets[e];
+        live[j] = c >= cnt_lo && c < cnt_hi;
       }
-      if (group_sums) {  // the group's sum of x (column order), in the MMA's 2^-24 units
-        float sum = 0.f;
-#pragma unroll
-        for (int q = 0; q < 32; ++q) sum += bf16_lo(w[q]) + bf16_hi(w[q]);
-        group_sums[static_cast<size_t>(s - lo_slot) * groups + G] = sum * 5.9604644775390625e-8f;  // 2^-24
-      }
-      uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(s - lo_slot) * hidden + 64 * G);
-#pragma unroll
-      for (int sg = 0; sg < 8; ++sg) {  // 16-byte segment: k-step sg / 2, kappa half sg % 2
-        const int ks = sg >> 1, a2 = sg & 1;
-        const float sc = (ks & 1) ? 0.0625f : 1.0f;
-        uint32_t o[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int u0 = 8 * (t + 4 * (ks >> 1)) + (ks & 1) + 2 * a2, u1 = u0 + 4;
-          const float f0 = (u0 & 1) ? bf16_hi(w[u0 >> 1]) : bf16_lo(w[u0 >> 1]);
-          const float f1 = (u1 & 1) ? bf16_hi(w[u1 >> 1]) : bf16_lo(w[u1 >> 1]);
-          ok &= fabsf(f0) < 65504.0f && fabsf(f1) < 65504.0f;
-          const __half2 hv = __floats2half2_rn(f0 * sc, f1 * sc);
-          o[t] = *reinterpret_cast<const uint32_t*>(&hv);
-        }
-        dst[sg] = make_uint4(o[0], o[1], o[2], o[3]);
-      }
+      src[j] = live[j] ? gather_src_row(x, perm[s] / k_div, hidden, pr) : x;
     }
-  } else if (order == kOrderMma) {
-    // kperm256 (warp-MMA operand order): output segment sg (8 halves) of
-    // stage st = sg / 32 holds, at half 2t + h, column
-    // 256 st + 32 (2t + kh) + 8 b + p + 4h with sg % 32 = 16 kh + 4 b + p
-    for (int sg = threadIdx.x; sg < hidden / 8; sg += blockDim.x) {
-      const int st = sg >> 5, sp = sg & 31, kh = sp >> 4, b = (sp >> 2) & 3, p = sp & 3;
-      const int c0 = st * 256 + 32 * kh + 8 * b + p;
-      uint16_t v[kGatherSlots][8];
-#pragma unroll
-      for (int j = 0; j < kGatherSlots; ++j)
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          v[j][2 * t] = live[j] ? src[j][c0 + 64 * t] : 0;
-          v[j][2 * t + 1] = live[j] ? src[j][c0 + 64 * t + 4] : 0;
-        }
-#pragma unroll
-      for (int j = 0; j < kGatherSlots; ++j) {
+    if (order == kOrderMmaG4) {
+      // kperm_g4, one thread per (slot, 64-column group): output position
+      // 16 s + kappa (kappa = 8 a2 + 2 t + h) holds column
+      // 8 (t + 4 (s / 2)) + (s & 1) + 2 a2 + 4 h, divided by 16 for odd s
+      const int groups = hidden / 64;
+      for (int it = threadIdx.x; it < kGatherSlots * groups; it += blockDim.x) {
+        const int j = it / groups, G = it - j * groups, s = s0 + j;
         if (!live[j]) continue;
-        uint32_t o[4];
+        const uint4* in = reinterpret_cast<const uint4*>(gather_src_row(x, perm[s] / k_div, hidden, pr) + 64 * G);
+        uint32_t w[32];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float lo = bf16_bits_to_f32(v[j][2 * t]), hi = bf16_bits_to_f32(v[j][2 * t + 1]);
-          ok &= fabsf(lo) < 65504.0f && fabsf(hi) < 65504.0f;
-          const __half2 h = __floats2half2_rn(lo, hi);
-          o[t] = *reinterpret_cast<const uint32_t*>(&h);
+        for (int q = 0; q < 8; ++q) {
+          const uint4 v = __ldcg(in + q);
+          w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
         }
-        reinterpret_cast<uint4*>(out + static_cast<size_t>(s0 + j - lo_slot) * hidden)[sg] =
-            make_uint4(o[0], o[1], o[2], o[3]);
+        if (group_sums) {  // the group's sum of x (column order), in the MMA's 2^-24 units
+          float sum = 0.f;
+#pragma unroll
+          for (int q = 0; q < 32; ++q) sum += bf16_lo(w[q]) + bf16_hi(w[q]);
+          group_sums[static_cast<size_t>(s - lo_slot) * groups + G] = sum * 5.9604644775390625e-8f;  // 2^-24
+        }
+        uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(s - lo_slot) * hidden + 64 * G);
+#pragma unroll
+        for (int sg = 0; sg < 8; ++sg) {  // 16-byte segment: k-step sg / 2, kappa half sg % 2
+          const int ks = sg >> 1, a2 = sg & 1;
+          const float sc = (ks & 1) ? 0.0625f : 1.0f;
+          uint32_t o[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int u0 = 8 * (t + 4 * (ks >> 1)) + (ks & 1) + 2 * a2, u1 = u0 + 4;
+            const float f0 = (u0 & 1) ? bf16_hi(w[u0 >> 1]) : bf16_lo(w[u0 >> 1]);
+            const float f1 = (u1 & 1) ? bf16_hi(w[u1 >> 1]) : bf16_lo(w[u1 >> 1]);
+            ok &= fabsf(f0) < 65504.0f && fabsf(f1) < 65504.0f;
+            const __half2 hv = __floats2half2_rn(f0 * sc, f1 * sc);
+            o[t] = *reinterpret_cast<const uint32_t*>(&hv);
+          }
+          dst[sg] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
       }
-    }
-  } else {
-    for (int i = threadIdx.x; i < hidden / 8; i += blockDim.x) {
-      uint4 v[kGatherSlots];
+    } else if (order == kOrderMma) {
+      // kperm256 (warp-MMA operand order): output segment sg (8 halves) of
+      // stage st = sg / 32 holds, at half 2t + h, column
+      // 256 st + 32 (2t + kh) + 8 b + p + 4h with sg % 32 = 16 kh + 4 b + p
+      for (int sg = threadIdx.x; sg < hidden / 8; sg += blockDim.x) {
+        const int st = sg >> 5, sp = sg & 31, kh = sp >> 4, b = (sp >> 2) & 3, p = sp & 3;
+        const int c0 = st * 256 + 32 * kh + 8 * b + p;
+        uint16_t v[kGatherSlots][8];
 #pragma unroll
-      for (int j = 0; j < kGatherSlots; ++j)
-        v[j] = live[j] ? reinterpret_cast<const uint4*>(src[j])[i] : make_uint4(0, 0, 0, 0);
+        for (int j = 0; j < kGatherSlots; ++j)
 #pragma unroll
-      for (int j = 0; j < kGatherSlots; ++j) {
-        if (!live[j]) continue;
-        const uint32_t in[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-        float f[8];
+          for (int t = 0; t < 4; ++t) {
+            v[j][2 * t] = live[j] ? src[j][c0 + 64 * t] : 0;
+            v[j][2 * t + 1] = live[j] ? src[j][c0 + 64 * t + 4] : 0;
+          }
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          f[2 * k] = bf16_lo(in[k]);
-          f[2 * k + 1] = bf16_hi(in[k]);
+        for (int j = 0; j < kGatherSlots; ++j) {
+          if (!live[j]) continue;
+          uint32_t o[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const float lo = bf16_bits_to_f32(v[j][2 * t]), hi = bf16_bits_to_f32(v[j][2 * t + 1]);
+            ok &= fabsf(lo) < 65504.0f && fabsf(hi) < 65504.0f;
+            const __half2 h = __floats2half2_rn(lo, hi);
+            o[t] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          reinterpret_cast<uint4*>(out + static_cast<size_t>(s0 + j - lo_slot) * hidden)[sg] =
+              make_uint4(o[0], o[1], o[2], o[3]);
         }
-        uint32_t o[4];
+      }
+    } else {
+      for (int i = threadIdx.x; i < hidden / 8; i += blockDim.x) {
+        uint4 v[kGatherSlots];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {  // k-permuted pairs (k, k + 4), see kperm8
-          ok &= fabsf(f[k]) < 65504.0f && fabsf(f[k + 4]) < 65504.0f;
-          const __half2 h = __floats2half2_rn(f[k], f[k + 4]);
-          o[k] = *reinterpret_cast<const uint32_t*>(&h);
+        for (int j = 0; j < kGatherSlots; ++j)
+          v[j] = live[j] ? reinterpret_cast<const uint4*>(src[j])[i] : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int j = 0; j < kGatherSlots; ++j) {
+          if (!live[j]) continue;
+          const uint32_t in[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+          float f[8];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            f[2 * k] = bf16_lo(in[k]);
+            f[2 * k + 1] = bf16_hi(in[k]);
+          }
+          uint32_t o[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {  // k-permuted pairs (k, k + 4), see kperm8
+            ok &= fabsf(f[k]) < 65504.0f && fabsf(f[k + 4]) < 65504.0f;
+            const __half2 h = __floats2half2_rn(f[k], f[k + 4]);
+            o[k] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          reinterpret_cast<uint4*>(out + static_cast<size_t>(s0 + j - lo_slot) * hidden)[i] =
+              make_uint4(o[0], o[1], o[2], o[3]);
         }
-        reinterpret_cast<uint4*>(out + static_cast<size_t>(s0 + j - lo_slot) * hidden)[i] =
-            make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
   }
@@ -995,7 +999,8 @@ cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* perm, int k_div
   if (num_slots <= 0) return cudaSuccess;
   if (cnt_hi > 0 && (!ids || !offsets)) return cudaErrorInvalidValue;
   const int threads = hidden / 8 < 256 ? ((hidden / 8 + 31) / 32) * 32 : 256;
-  const int grid = (num_slots + kGatherSlots - 1) / kGatherSlots;
+  int grid = (num_slots + kGatherSlots - 1) / kGatherSlots;
+  if (grid > kGatherCtasPerSm * sm_count()) grid = kGatherCtasPerSm * sm_count();
   PeerRows pr{};
   if (peer_rows) pr = *peer_rows;
   auto kern = cnt_hi > 0 ? gather_rows_kernel<true> : gather_rows_kernel<false>;
