@@ -61,6 +61,35 @@ bool router_tc_supported(int hidden, int num_experts, int top_k);
 size_t router_tc_smem_bytes(int num_experts);
 cudaError_t launch_router_tc(const CUtensorMap& tX, const CUtensorMap& tW, const RouterArgs& a, cudaStream_t st);
 cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st);
+// ------------------------------------- single-token fused layer (batch 1)
+struct SingleTokenArgs {
+  const uint16_t* x;              // bf16 [H]
+  const uint16_t* router_weight;  // bf16 [E, H]
+  const uint32_t* w[3];           // gate, up, down codes (MLX layout, 4-bit)
+  const uint16_t* s[3];           // bf16 scales
+  const uint16_t* b[3];           // bf16 biases
+  const uint16_t* residual;       // bf16 [H] added before rounding, or null
+  uint16_t* y;                    // bf16 [H]
+  float* logits;                  // fp32 [E]: bf16-rounded router logits
+  int32_t* topk_ids;              // [K]
+  float* topk_weights;            // [K]
+  uint16_t* h;                    // bf16 [K, I] scratch
+  unsigned int* grid_bar;         // grid barrier word, zero before the first call
+  int* err;
+  int hidden, inter, num_experts, top_k, bits;
+  int norm_topk_prob;
+  float routed_scaling_factor;
+  int act;
+  // filled by single_token_plan: row split units, the most rows per CTA,
+  // shared-memory bytes (gate/up part, down part, total with h)
+  int unit_c, unit_d, rows_c, rows_d, smem_c, smem_d, smem;
+};
+// Fills the plan fields; false if the shape is not supported (4-bit, H with
+// 8 code words per lane, I with 2 or 3, E <= 512, K <= 16 and <= sms, the
+// shared memory within 200 KB).
+bool single_token_plan(SingleTokenArgs& a, int sms);
+// One persistent grid of `sms` CTAs (all resident: the caller gives the SM count).
+cudaError_t launch_single_token_layer(const SingleTokenArgs& a, int sms, cudaStream_t st);
 // sigmoid_bf16 against the exact form over every bf16 input (synchronous, current device).
 cudaError_t selftest_sigmoid(int64_t* mismatches, int64_t* exact_form);
 // Top-k of every token plus the single-chunk dispatch in one CTA, for small

@@ -197,6 +197,10 @@ struct SenMoeLayer {
   // the router, dispatch and routed experts)
   cudaStream_t side = nullptr;
   cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
+  // one token on one GPU: the fused single-launch block (layer_single.cu)
+  bool single_ok = false;
+  SingleTokenArgs single{};
+  unsigned int* gbar = nullptr;  // its grid-barrier word
 };
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -319,7 +323,7 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                o_route = take((T + 3) / 4 * 4), o_yx = take(T * H * 2),
                o_xsum = take((C + 16) * (H / 64) * 4), o_xssh = take(Is ? T * H * 2 : 0),
                o_hsh = take(Is ? T * Is * 2 : 0), o_xsumsh = take(Is ? (T + 16) * (H / 64) * 4 : 0),
-               o_iota = take(Is ? T * 4 : 0), o_shgrp = take(Is ? 16 : 0);
+               o_iota = take(Is ? T * 4 : 0), o_shgrp = take(Is ? 16 : 0), o_gbar = take(16);
   cudaError_t e = cudaMalloc(&L->arena, off);
   if (e != cudaSuccess) {
     delete L;
@@ -356,6 +360,7 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
   L->xsum = reinterpret_cast<float*>(base + o_xsum);
   L->ep_flags = reinterpret_cast<uint32_t*>(base + o_flags);
   L->ep_local = reinterpret_cast<uint32_t*>(base + o_local);
+  L->gbar = reinterpret_cast<unsigned int*>(base + o_gbar);
   L->arena_bytes = off;
   L->o_d = o_d;
   L->o_flags = o_flags;
@@ -419,6 +424,34 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
                        cudaSuccess &&
                    make_tmap_2d(&L->tm_hsh8, L->hsh16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, Is, T, Is * 2, 64, 8, true) ==
                        cudaSuccess;
+  }
+  if (L->w.router_weight && !Is && c.expert_begin == 0 && c.expert_end == c.n_routed_experts) {
+    SingleTokenArgs& sa = L->single;
+    sa.router_weight = static_cast<const uint16_t*>(L->w.router_weight);
+    sa.w[0] = static_cast<const uint32_t*>(L->w.gate_weight);
+    sa.w[1] = static_cast<const uint32_t*>(L->w.up_weight);
+    sa.w[2] = static_cast<const uint32_t*>(L->w.down_weight);
+    sa.s[0] = static_cast<const uint16_t*>(L->w.gate_scales);
+    sa.s[1] = static_cast<const uint16_t*>(L->w.up_scales);
+    sa.s[2] = static_cast<const uint16_t*>(L->w.down_scales);
+    sa.b[0] = static_cast<const uint16_t*>(L->w.gate_biases);
+    sa.b[1] = static_cast<const uint16_t*>(L->w.up_biases);
+    sa.b[2] = static_cast<const uint16_t*>(L->w.down_biases);
+    sa.logits = L->logits;
+    sa.topk_ids = L->ids;
+    sa.topk_weights = L->wts;
+    sa.h = L->h;
+    sa.grid_bar = L->gbar;
+    sa.err = L->err;
+    sa.hidden = int(H);
+    sa.inter = int(I);
+    sa.num_experts = int(E);
+    sa.top_k = int(K);
+    sa.bits = c.bits;
+    sa.norm_topk_prob = c.norm_topk_prob;
+    sa.routed_scaling_factor = c.routed_scaling_factor;
+    sa.act = c.activation;
+    L->single_ok = single_token_plan(sa, L->sms);
   }
   L->rtc_ok = L->w.router_weight && router_tc_supported(int(H), int(E), int(K)) && E >= 128 &&
               make_tmap_2d(&L->tm_router, L->w.router_weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, H, E, H * 2, 64, 128,
@@ -555,6 +588,20 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   }
   auto mark = [&](int stage) -> cudaError_t { return profile ? cudaEventRecord(L->ev[stage], st) : cudaSuccess; };
   SENMOE_CUDA(mark(0));
+
+  // One token on one GPU: the whole block in one persistent launch
+  // (layer_single.cu), equal bit for bit to the CUDA-core GEMV path.  Stage
+  // profiling, debug outputs, forced kernels and capped slots keep the
+  // staged launches.
+  if (T == 1 && L->single_ok && L->ep_world == 0 && !local && !ext_ids && !debug && !profile &&
+      c.reserved[0] == kPathAuto && c.reserved[1] == kMmaFormAuto && slot_cap == 0) {
+    SingleTokenArgs sa = L->single;
+    sa.x = static_cast<const uint16_t*>(x);
+    sa.residual = residual ? static_cast<const uint16_t*>(x) : nullptr;
+    sa.y = static_cast<uint16_t*>(y);
+    SENMOE_CUDA(launch_single_token_layer(sa, L->sms, st));
+    return SENMOE_OK;
+  }
 
   const bool ep = L->ep_world > 0;
   EpArgs ea{};

@@ -15,6 +15,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "dispatch_body.cuh"
+#include "router_core.cuh"
 
 namespace senmoe {
 
@@ -24,79 +25,7 @@ constexpr int kRouterTokTile = 4;      // tokens per CTA (x tile in shared memor
                                        // work per warp, E/4 x T/4 CTAs
 static_assert(kRouterTokTile <= kRouterWarps, "fused top-k runs one warp per token of a tile");
 constexpr int kTopkWarps = 4;          // tokens per CTA in the top-k kernel
-constexpr int kMaxTopK = 16;
 }  // namespace
-
-// One warp per token: softmax over E (fp32), scores rounded to bf16, K rounds
-// of warp arg-max (score desc, id asc), then renorm / scaling in fp32.
-// lg is token t's logits row, in global memory (kShared false) or shared.
-template <int EPL, bool kShared>  // experts per lane = ceil(E / 32)
-__device__ __forceinline__ void topk_row(const RouterArgs& a, const float* lg, int t, int lane) {
-  float p[EPL];
-  float m = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < EPL; ++j) {
-    const int e = lane + 32 * j;
-    p[j] = e < a.num_experts ? (kShared ? lg[e] : __ldcg(lg + e)) : -INFINITY;
-    m = fmaxf(m, p[j]);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  float sum = 0.f;
-#pragma unroll
-  for (int j = 0; j < EPL; ++j) {
-    const int e = lane + 32 * j;
-    p[j] = e < a.num_experts ? expf(p[j] - m) : 0.f;
-    sum += p[j];
-  }
-  sum = warp_sum(sum);
-#pragma unroll
-  for (int j = 0; j < EPL; ++j) {
-    const int e = lane + 32 * j;
-    p[j] = e < a.num_experts ? round_bf16(p[j] / sum) : -1.0f;
-  }
-
-  // K rounds of a warp-wide max over packed keys: bf16 score bits (scores are
-  // non-negative, so their bit patterns order like the values) above the
-  // inverted expert id, so the max picks the highest score and, on ties, the
-  // lowest id -- one redux.sync per round.
-  uint32_t key[EPL];
-#pragma unroll
-  for (int j = 0; j < EPL; ++j) {
-    const int e = lane + 32 * j;
-    key[j] = e < a.num_experts ? (static_cast<uint32_t>(f32_to_bf16_bits(p[j])) << 16) | (0xffffu - e) : 0u;
-  }
-  float sel_w[kMaxTopK];
-  int sel_e[kMaxTopK];
-#pragma unroll
-  for (int k = 0; k < kMaxTopK; ++k) {
-    if (k >= a.top_k) break;
-    uint32_t best = 0;
-#pragma unroll
-    for (int j = 0; j < EPL; ++j) best = max(best, key[j]);
-    best = __reduce_max_sync(0xffffffffu, best);
-    const int be = 0xffff - static_cast<int>(best & 0xffffu);
-#pragma unroll
-    for (int j = 0; j < EPL; ++j)
-      if (key[j] == best) key[j] = 0u;  // unique: the id is part of the key
-    sel_w[k] = bf16_bits_to_f32(static_cast<uint16_t>(best >> 16));
-    sel_e[k] = be;
-  }
-  if (lane == 0) {
-    if (a.norm_topk_prob) {
-      float s = 0.f;
-      for (int k = 0; k < a.top_k; ++k) s += sel_w[k];
-      const float den = round_bf16(s) + 1e-20f;
-      for (int k = 0; k < a.top_k; ++k) sel_w[k] = sel_w[k] / den;
-    }
-    if (fabsf(a.routed_scaling_factor - 1.0f) > 1.1920929e-7f)
-      for (int k = 0; k < a.top_k; ++k) sel_w[k] *= a.routed_scaling_factor;
-    for (int k = 0; k < a.top_k; ++k) {
-      a.topk_ids[static_cast<size_t>(t) * a.top_k + k] = sel_e[k];
-      a.topk_weights[static_cast<size_t>(t) * a.top_k + k] = sel_w[k];
-    }
-  }
-}
 
 // top-k of token t for any E <= 512 (logits row in global memory).
 __device__ __forceinline__ void topk_any(const RouterArgs& a, int t, int lane) {
@@ -126,14 +55,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_logits_kernel(Router
   // The router weights do not depend on the previous kernel: load them before
   // waiting for it (programmatic dependent launch).
   float wv[VPL][8];
-  const uint4* wrow = reinterpret_cast<const uint4*>(a.weight + static_cast<size_t>(e < a.num_experts ? e : 0) *
-                                                                    a.hidden);
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const uint4 v = (32 * i + lane < vec_per_row) ? wrow[32 * i + lane] : make_uint4(0, 0, 0, 0);
-    wv[i][0] = bf16_lo(v.x); wv[i][1] = bf16_hi(v.x); wv[i][2] = bf16_lo(v.y); wv[i][3] = bf16_hi(v.y);
-    wv[i][4] = bf16_lo(v.z); wv[i][5] = bf16_hi(v.z); wv[i][6] = bf16_lo(v.w); wv[i][7] = bf16_hi(v.w);
-  }
+  router_load_wrow<VPL>(a.weight + static_cast<size_t>(e < a.num_experts ? e : 0) * a.hidden, lane, vec_per_row, wv);
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
@@ -150,16 +72,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_logits_kernel(Router
   const bool ok = mbar_wait(&bar, 0, a.err);
   if (ok && e < a.num_experts) {
     for (int t = 0; t < nt; ++t) {
-    float acc = 0.f;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      if (32 * i + lane >= vec_per_row) break;
-      const uint4 v = xs[t * vec_per_row + 32 * i + lane];
-      acc = fmaf(bf16_lo(v.x), wv[i][0], acc); acc = fmaf(bf16_hi(v.x), wv[i][1], acc);
-      acc = fmaf(bf16_lo(v.y), wv[i][2], acc); acc = fmaf(bf16_hi(v.y), wv[i][3], acc);
-      acc = fmaf(bf16_lo(v.z), wv[i][4], acc); acc = fmaf(bf16_hi(v.z), wv[i][5], acc);
-      acc = fmaf(bf16_lo(v.w), wv[i][6], acc); acc = fmaf(bf16_hi(v.w), wv[i][7], acc);
-    }
+      float acc = router_dot_lane<VPL>(wv, xs + t * vec_per_row, lane, vec_per_row);
       acc = warp_sum(acc);
       if (lane == 0)
         a.logits[static_cast<size_t>(t0 + t) * a.num_experts + e] = a.round_logits ? round_bf16(acc) : acc;
