@@ -183,8 +183,12 @@ int senmoe_layer_stage_times(SenMoeLayer* layer, float* ms, int n);
 
 /* Which expert-product kernels a forward of num_tokens tokens runs: 1 = the
  * CUDA-core dequant-GEMV, 2 = the tcgen05 grouped GEMM (prefill-size groups of
- * tokens per expert), 3 = the warp-MMA grouped GEMM (decode-size groups);
- * SenMoeConfig.reserved[0] can force one (0 = choose by tokens per expert). */
+ * tokens per expert), 3 = the warp-MMA grouped GEMM (decode-size groups),
+ * 4 = one token on one GPU: the whole block in one fused launch whose expert
+ * products use the GEMV's arithmetic (a forward with debug outputs or stage
+ * profiling runs the staged kernels of path 3 instead);
+ * SenMoeConfig.reserved[0] can force one of 1-3 (0 = choose by tokens per
+ * expert). */
 int senmoe_layer_expert_path(const SenMoeLayer* layer, int64_t num_tokens);
 
 /* Synchronises `stream` and reports any error a kernel recorded on the

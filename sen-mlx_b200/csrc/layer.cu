@@ -93,7 +93,8 @@ inline double tc_min_tokens_per_expert(int bits) { return bits == 4 ? 16.0 : 24.
 constexpr int kHybridMinPairs = 2048;
 constexpr int kHybridHotSlots = 32;
 constexpr double kMmaMinTokensPerExpert = 0.0;
-enum ExpertPath { kPathAuto = 0, kPathGemv = 1, kPathTensorCore = 2, kPathMma = 3 };
+enum ExpertPath { kPathAuto = 0, kPathGemv = 1, kPathTensorCore = 2, kPathMma = 3,
+                  kPathSingleToken = 4 /* reported only: the one-token fused launch */ };
 // SenMoeConfig.reserved[1]: warp-MMA form, 0 = group-scaled where supported
 // (4-bit, up to 16 slots per tile; two CTAs per SM at 8 slots), 1 = always
 // dequantise to fp16, 2 = group-scaled, one CTA per SM at every tile width
@@ -508,6 +509,14 @@ static double tokens_per_expert(const SenMoeLayer* L, int64_t pairs) {
 }
 
 // Expert-product kernels one forward of `pairs` pairs takes (ExpertPath).
+// One token on one GPU with the automatic kernel choice takes the fused
+// single-launch block (layer_single.cu); a forward with debug outputs or
+// stage profiling keeps the staged kernels.
+static bool single_token_path(const SenMoeLayer* L, int64_t tokens) {
+  return tokens == 1 && L->single_ok && L->ep_world == 0 && L->cfg.reserved[0] == kPathAuto &&
+         L->cfg.reserved[1] == kMmaFormAuto;
+}
+
 static int expert_path_for(const SenMoeLayer* L, int64_t pairs) {
   const int forced = L->cfg.reserved[0];
   if (forced == kPathTensorCore && L->tc_ok) return kPathTensorCore;
@@ -593,8 +602,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
   // (layer_single.cu), equal bit for bit to the CUDA-core GEMV path.  Stage
   // profiling, debug outputs, forced kernels and capped slots keep the
   // staged launches.
-  if (T == 1 && L->single_ok && L->ep_world == 0 && !local && !ext_ids && !debug && !profile &&
-      c.reserved[0] == kPathAuto && c.reserved[1] == kMmaFormAuto && slot_cap == 0) {
+  if (single_token_path(L, T) && !local && !ext_ids && !debug && !profile && slot_cap == 0) {
     SingleTokenArgs sa = L->single;
     sa.x = static_cast<const uint16_t*>(x);
     sa.residual = residual ? static_cast<const uint16_t*>(x) : nullptr;
@@ -1116,6 +1124,7 @@ int senmoe_layer_expert_path(const SenMoeLayer* L, int64_t num_tokens) {
   g_last_error.clear();
   if (!L) return -fail(SENMOE_ERR_BAD_ARG, "layer is NULL");
   if (num_tokens <= 0) return kPathGemv;
+  if (single_token_path(L, num_tokens)) return kPathSingleToken;
   return expert_path_for(L, num_tokens * L->cfg.num_experts_per_tok);
 }
 

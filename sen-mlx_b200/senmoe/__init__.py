@@ -33,7 +33,8 @@ ROUTER_SOFTMAX_TOPK = 0
 ACT_SWIGLU, ACT_GEGLU = 0, 1
 # expert-product kernels (SenMoeConfig.reserved[0]): CUDA-core GEMV, tcgen05 GEMM, warp-MMA GEMM
 PATH_AUTO, PATH_GEMV, PATH_TENSOR_CORE, PATH_MMA = 0, 1, 2, 3
-PATH_NAMES = {PATH_GEMV: "gemv", PATH_TENSOR_CORE: "tcgen05", PATH_MMA: "mma"}
+PATH_SINGLE_TOKEN = 4  # reported only: one token on one GPU, the whole block in one launch
+PATH_NAMES = {PATH_GEMV: "gemv", PATH_TENSOR_CORE: "tcgen05", PATH_MMA: "mma", PATH_SINGLE_TOKEN: "single-token"}
 
 
 class SenMoeError(RuntimeError):

@@ -211,7 +211,8 @@ def ep_forward(rank, world, H, I, E, K, bits, Ts, shared, seed, expert_path):
         a, b2 = to_numpy_bf16(y), to_numpy_bf16(ref)
         sms = torch.cuda.get_device_properties(rank).multi_processor_count
         out[T] = dict(exact=bool(torch.equal(y, ref)), repeat=bool(torch.equal(y, y2)),
-                      same_kernels=two_cta_form(args, T, world, sms) == two_cta_form(args, T, 1, sms),
+                      same_kernels=(two_cta_form(args, T, world, sms) == two_cta_form(args, T, 1, sms)
+                                    and full.expert_path(T) == epl.expert_path(T)),
                       digest=hashlib.sha256(a.tobytes()).hexdigest(),
                       max_abs=float(np.abs(bf16_np_to_f32(a) - bf16_np_to_f32(b2)).max()),
                       rel_l2=float(rel_l2(bf16_np_to_f32(a), bf16_np_to_f32(b2))),
@@ -232,7 +233,8 @@ def ep_forward(rank, world, H, I, E, K, bits, Ts, shared, seed, expert_path):
     out["stack_digest"] = hashlib.sha256(to_numpy_bf16(ys[0]).tobytes()).hexdigest()
     out["stack_max_abs"] = float((ys[0].float() - yr.float()).abs().max())
     sms = torch.cuda.get_device_properties(rank).multi_processor_count
-    out["stack_same_kernels"] = two_cta_form(args, T, world, sms) == two_cta_form(args, T, 1, sms)
+    out["stack_same_kernels"] = (two_cta_form(args, T, world, sms) == two_cta_form(args, T, 1, sms)
+                                 and full.expert_path(T) == epl.expert_path(T))
     stack.release()
     torch.cuda.synchronize()
     import torch.distributed as dist
@@ -314,7 +316,8 @@ def ep_tokens_forward(rank, world, H, I, E, K, bits, count_lists, shared, seed, 
         a = bf16_np_to_f32(to_numpy_bf16(y))
         sms = torch.cuda.get_device_properties(rank).multi_processor_count
         out[ci] = dict(exact=bool(torch.equal(y, ref)), repeat=bool(torch.equal(y, y2)),
-                       same_kernels=two_cta_form(args, T, world, sms) == two_cta_form(args, T, 1, sms),
+                       same_kernels=(two_cta_form(args, T, world, sms) == two_cta_form(args, T, 1, sms)
+                                    and full.expert_path(T) == epl.expert_path(T)),
                        max_abs_full=float((y.float() - ref.float()).abs().max()) if n else 0.0,
                        max_abs_oracle=float(np.abs(a - orc["y_f32"]).max()) if n else 0.0)
     # a graph-captured two-layer residual stack over the first case's tokens
@@ -333,7 +336,8 @@ def ep_tokens_forward(rank, world, H, I, E, K, bits, count_lists, shared, seed, 
     out["stack_exact"] = bool(torch.equal(ys[0], yr))
     out["stack_max_abs"] = float((ys[0].float() - yr.float()).abs().max()) if n else 0.0
     sms = torch.cuda.get_device_properties(rank).multi_processor_count
-    out["stack_same_kernels"] = two_cta_form(args, T, world, sms) == two_cta_form(args, T, 1, sms)
+    out["stack_same_kernels"] = (two_cta_form(args, T, world, sms) == two_cta_form(args, T, 1, sms)
+                                 and full.expert_path(T) == epl.expert_path(T))
     stack.release()
     torch.cuda.synchronize()
     import torch.distributed as dist

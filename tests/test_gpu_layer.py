@@ -313,6 +313,7 @@ def test_single_token_fused_layer_equals_gemv_path(senmoe, config0_layer, activa
     cfg = O.MoeConfig(**{**cfg.__dict__, "activation": activation}) if activation else cfg
     fused = senmoe.DeepseekMoe(moe_args(cfg, 0), device_weights(mw), max_tokens=1)
     gemv = senmoe.DeepseekMoe(moe_args(cfg, PATHS["gemv"]), device_weights(mw), max_tokens=1)
+    assert fused.expert_path(1) == senmoe.PATH_SINGLE_TOKEN and gemv.expert_path(1) == PATHS["gemv"]
     for seed in range(6):
         x = O.make_tokens(1, cfg.hidden, seed=300 + seed)
         xt = t_bf16(x)
