@@ -103,10 +103,11 @@ __global__ void __launch_bounds__(kSingleThreads, 1) single_token_kernel(SingleT
   }
   pdl_wait();  // x and the residual come from the previous kernel
 
-  // ---- A. router logits, one expert per warp of the grid
+  // ---- A. router logits, one expert per warp of the grid, spread over the
+  // CTAs first (expert e on CTA e mod G) so each SM loads only a few rows
   {
     const int vec = H / 8;
-    for (int e = cta * kSingleWarps + warp; e < E; e += G * kSingleWarps) {
+    for (int e = warp * G + cta; e < E; e += G * kSingleWarps) {
       // H / 256 16-byte vectors per lane: WPL_GU at 4 bits (H / 8 words of 8 codes)
       float wv[WPL_GU][8];
       router_load_wrow<WPL_GU>(a.router_weight + static_cast<size_t>(e) * H, lane, vec, wv);
