@@ -95,7 +95,9 @@ typedef struct SenMoeConfig {
   int32_t reserved[3];             /* [0]: expert kernels, 0 auto, 1 CUDA-core GEMV, 2 tcgen05 GEMM,
                                       3 warp-MMA GEMM; [1]: warp-MMA form, 0 group-scaled where
                                       supported (4-bit), 1 dequantise every weight, 2 group-scaled
-                                      with one CTA per SM; [2]: expert-slot capacity, the most
+                                      with one CTA per SM, 3 as 2 with 128-row down tiles instead
+                                      of 256-row ones (same results); [2]: expert-slot
+                                      capacity, the most
                                       (token, expert) pairs that reach this rank's experts in one
                                       call (0: max_tokens * K).  Under expert parallelism a rank
                                       holds only its own experts' pairs, about 1/world of them, so

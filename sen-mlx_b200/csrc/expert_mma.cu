@@ -63,8 +63,11 @@ constexpr int kThreadsG4 = (kComputeWarps + kLoaderWarps) * 32;
 constexpr int kMaxTiles = 128;       // per CTA
 constexpr int kSmemBudget = 226 * 1024;
 
-template <int BITS, int NPROJ, int NT, bool G4>
+// DP (group-scaled down): the tile is two 128-row blocks of the one
+// projection, laid out as the two projections of a gate/up tile.
+template <int BITS, int NPROJ, int NT, bool G4, bool DP = false>
 struct MmaShape {
+  static_assert(!DP || (G4 && NPROJ == 2), "row-block pairs: group-scaled, two blocks");
   static constexpr int kABoxes = BITS / 4;                   // 128-byte boxes per row per stage
   static constexpr int kABox = kRows * 128;                  // 16 KB
   static constexpr int kABytes = NPROJ * kABoxes * kABox;
@@ -77,7 +80,7 @@ struct MmaShape {
   static constexpr int kSBBytes = G4 ? NPROJ * 2 * kRows * 8 : 0;
   // group-scaled gate/up: the stage's activation group sums, [slot][4 groups] fp32
   static constexpr int kXOff = kSBOff + kSBBytes;
-  static constexpr int kXBytes = (G4 && NPROJ == 2) ? 8 * NT * 16 : 0;
+  static constexpr int kXBytes = (G4 && NPROJ == 2 && !DP) ? 8 * NT * 16 : 0;
   static constexpr int kStageBytes = (kTmaBytes + kSBBytes + kXBytes + 1023) / 1024 * 1024;
   static constexpr int kRedBytes = 8 * 32 * NPROJ * NT * 4 * 4;
   static constexpr int kMisc = 4096;                         // barriers + tile list
@@ -228,11 +231,18 @@ __device__ __forceinline__ int kperm256(int col) {
 
 // G4: the group-scaled 4-bit form (kperm_g4 activations); otherwise every
 // weight is dequantised to fp16 (kperm256 activations).
-template <int BITS, int NPROJ, int NT, bool G4>
+// DP (group-scaled down, NPROJ = 2): a tile is 256 rows of the down
+// projection, taken as two 128-row blocks in the places of gate and up
+// (tA0 for both, the second block 128 rows on), so every warp runs two
+// independent MMA chains, as in gate/up, instead of one, and the four MMAs
+// of each group's activation sums serve both blocks.  Each output is the
+// same fp32 chain as in a 128-row down tile, so both give the same bits.
+template <int BITS, int NPROJ, int NT, bool G4, bool DP>
 __global__ void __launch_bounds__(G4 ? kThreadsG4 : kThreads, 1)
     qmma_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ CUtensorMap tA1,
                 const __grid_constant__ CUtensorMap tB, TcGemmArgs a) {
-  using S = MmaShape<BITS, NPROJ, NT, G4>;
+  using S = MmaShape<BITS, NPROJ, NT, G4, DP>;
+  constexpr bool kGateUp = NPROJ == 2 && !DP;  // two projections with the activation epilogue
   static_assert(!G4 || BITS == 4, "group-scaled form is 4-bit");
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
@@ -264,7 +274,7 @@ __global__ void __launch_bounds__(G4 ? kThreadsG4 : kThreads, 1)
   pdl_wait();  // active list / offsets (dispatch) and the activation rows (gather or gate/up)
   pdl_launch_dependents();
   // the stage ring is free until the producer starts: use it as scratch
-  const int nlisted = list_tiles(a.active, a.active_count, a.offsets, a.expert_begin, a.m_tiles, kRows, 8 * NT, false,
+  const int nlisted = list_tiles(a.active, a.active_count, a.offsets, a.expert_begin, a.m_tiles, DP ? 2 * kRows : kRows, 8 * NT, false,
                                  s_tiles, kMaxTiles, reinterpret_cast<int*>(sStage), a.err, a.slot_cap, a.cnt_lo,
                                  a.cnt_hi);
   if (threadIdx.x == 0) s_ntiles = nlisted;
@@ -301,8 +311,8 @@ __global__ void __launch_bounds__(G4 ? kThreadsG4 : kThreads, 1)
             for (int p = 0; p < NPROJ; ++p)
 #pragma unroll
               for (int bx = 0; bx < S::kABoxes; ++bx)
-                tma_load_2d(base + (p * S::kABoxes + bx) * S::kABox, p ? &tA1 : &tA0, (st * S::kABoxes + bx) * 32,
-                            arow, &bar_full[slot]);
+                tma_load_2d(base + (p * S::kABoxes + bx) * S::kABox, (p && !DP) ? &tA1 : &tA0,
+                            (st * S::kABoxes + bx) * 32, DP ? arow + p * kRows : arow, &bar_full[slot]);
 #pragma unroll
             for (int j = 0; j < 4; ++j)
               tma_load_2d(base + S::kABytes + j * S::kBBox, &tB, st * kStageCols + j * 64, tl.z, &bar_full[slot]);
@@ -311,9 +321,14 @@ __global__ void __launch_bounds__(G4 ? kThreadsG4 : kThreads, 1)
             static_assert(32 * kLoaderWarps == kRows, "one loader lane per weight row");
             const uint32_t dst = smem_u32(base + S::kSBOff) + ll * 8;
 #pragma unroll
-            for (int pa = 0; pa < 2 * NPROJ; ++pa)  // array pa: scales (even) / biases (odd) of proj pa / 2
-              cp_async_8(dst + pa * kRows * 8, ((pa & 1) ? a.b[pa >> 1] : a.s[pa >> 1]) + sb_row0 + 4 * st);
-            if constexpr (NPROJ == 2) {
+            for (int pa = 0; pa < 2 * NPROJ; ++pa) {  // array pa: scales (even) / biases (odd) of proj pa / 2
+              if constexpr (DP)  // block pa / 2: rows 128 (pa / 2) on, of the one projection
+                cp_async_8(dst + pa * kRows * 8,
+                           ((pa & 1) ? a.b[0] : a.s[0]) + sb_row0 + static_cast<size_t>(pa >> 1) * kRows * groups + 4 * st);
+              else
+                cp_async_8(dst + pa * kRows * 8, ((pa & 1) ? a.b[pa >> 1] : a.s[pa >> 1]) + sb_row0 + 4 * st);
+            }
+            if constexpr (kGateUp) {
               // the group sums of the stage's 4 groups: 16 bytes per slot,
               // two 8-byte halves per loader lane (rows past the valid slots
               // exist: the buffer has 16 spare rows)
@@ -428,7 +443,7 @@ __global__ void __launch_bounds__(G4 ? kThreadsG4 : kThreads, 1)
         // gate/up: group sums of slots 2t (c0, c2) and 2t + 1 (c1, c3) for
         // this k-half's groups 2kh, 2kh + 1
         float xlo[NT][2], xhi[NT][2];
-        if constexpr (NPROJ == 2) {
+        if constexpr (kGateUp) {
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             const float2 v0 = *reinterpret_cast<const float2*>(base + S::kXOff + (8 * nt + 2 * t) * 16 + kh * 8);
@@ -451,7 +466,7 @@ __global__ void __launch_bounds__(G4 ? kThreadsG4 : kThreads, 1)
           float xs[NT][4];
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            if constexpr (NPROJ == 2) {
+            if constexpr (kGateUp) {
               xs[nt][0] = xs[nt][2] = xlo[nt][gi];
               xs[nt][1] = xs[nt][3] = xhi[nt][gi];
             } else {
@@ -609,7 +624,7 @@ __global__ void __launch_bounds__(G4 ? kThreadsG4 : kThreads, 1)
         const int row = tl.y + rA + 8 * (i >> 1);
         const size_t o = static_cast<size_t>(tl.z + n) * a.out_stride;
         constexpr float kUnit = G4 ? kG4Scale : 1.0f;  // accumulator units (exact power of two)
-        if constexpr (NPROJ == 2) {
+        if constexpr (kGateUp) {
           const float gv = round_bf16(acc[0][nt][i] * kUnit), uv = round_bf16(acc[1][nt][i] * kUnit);
           const float h = a.act == 0 ? act_swiglu_mlx(gv, uv) : act_geglu_mlx(gv, uv);
           range_ok &= fabsf(h) < 65504.0f;
@@ -618,7 +633,9 @@ __global__ void __launch_bounds__(G4 ? kThreadsG4 : kThreads, 1)
           else
             a.out[o + kperm256(row)] = __half_as_ushort(__float2half_rn(h));
         } else {
-          a.out[o + row] = f32_to_bf16_bits(acc[0][nt][i] * kUnit);
+#pragma unroll
+          for (int p = 0; p < NPROJ; ++p)  // row blocks (DP: 128 rows apart)
+            a.out[o + row + p * kRows] = f32_to_bf16_bits(acc[p][nt][i] * kUnit);
         }
       }
     }
@@ -860,11 +877,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 }  // namespace
 
 // ------------------------------------------------------------------ host
-template <int BITS, int NPROJ, int NT, bool G4>
+template <int BITS, int NPROJ, int NT, bool G4, bool DP = false>
 static cudaError_t launch_mma_t(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
                                 const TcGemmArgs& a, int tiles_upper, cudaStream_t st) {
-  using S = MmaShape<BITS, NPROJ, NT, G4>;
-  auto kern = qmma_kernel<BITS, NPROJ, NT, G4>;
+  using S = MmaShape<BITS, NPROJ, NT, G4, DP>;
+  auto kern = qmma_kernel<BITS, NPROJ, NT, G4, DP>;
   constexpr int threads = G4 ? kThreadsG4 : kThreads;
   cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), S::kSmem);
   if (e != cudaSuccess) return e;
@@ -924,6 +941,16 @@ bool mma_g4_supported(int bits, int nt, const TcGemmArgs& a) {
   bool ok = bits == 4 && (nt == 1 || nt == 2);
   for (int p = 0; p < 2; ++p) ok = ok && aligned4(a.s[p]) && aligned4(a.b[p]);
   return ok;
+}
+
+bool mma_down_pair_supported(int bits, int nt, const TcGemmArgs& a) {
+  return nt == 1 && mma_g4_supported(bits, nt, a) && a.rows % (2 * kRows) == 0 && a.m_tiles * 2 * kRows == a.rows;
+}
+
+cudaError_t launch_mma_down_pair(const CUtensorMap& tA, const CUtensorMap& tB, const TcGemmArgs& a, int bits, int nt,
+                                 int tiles_upper, cudaStream_t st) {
+  if (!mma_down_pair_supported(bits, nt, a)) return cudaErrorInvalidValue;
+  return launch_mma_t<4, 2, 1, true, true>(tA, tA, tB, a, tiles_upper, st);
 }
 
 cudaError_t launch_mma_gemm(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,

@@ -265,6 +265,12 @@ bool mma_g4_supported(int bits, int nt, const TcGemmArgs& a);
 cudaError_t launch_mma_gemm(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,
                             const TcGemmArgs& a, int bits, int nproj, int nt, bool g4, int tiles_upper,
                             cudaStream_t st);
+// Group-scaled down (4-bit, 8 slots per tile) in tiles of two 128-row blocks
+// (a.m_tiles = rows / 256; tA with 128-row boxes): the same bits as
+// launch_mma_gemm's 128-row tiles, two MMA chains per warp.
+bool mma_down_pair_supported(int bits, int nt, const TcGemmArgs& a);
+cudaError_t launch_mma_down_pair(const CUtensorMap& tA, const CUtensorMap& tB, const TcGemmArgs& a, int bits, int nt,
+                                 int tiles_upper, cudaStream_t st);
 // Group-scaled form at two CTAs per SM: 64-row tiles (a.m_tiles = rows / 64;
 // tA* with 64-row boxes), 8 slots per tile, 4-bit.
 cudaError_t launch_mma_q4(const CUtensorMap& tA0, const CUtensorMap& tA1, const CUtensorMap& tB,

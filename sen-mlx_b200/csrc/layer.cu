@@ -97,8 +97,10 @@ enum ExpertPath { kPathAuto = 0, kPathGemv = 1, kPathTensorCore = 2, kPathMma = 
                   kPathSingleToken = 4 /* reported only: the one-token fused launch */ };
 // SenMoeConfig.reserved[1]: warp-MMA form, 0 = group-scaled where supported
 // (4-bit, up to 16 slots per tile; two CTAs per SM at 8 slots), 1 = always
-// dequantise to fp16, 2 = group-scaled, one CTA per SM at every tile width
-enum MmaForm { kMmaFormAuto = 0, kMmaFormDequant = 1, kMmaFormG4Single = 2 };
+// dequantise to fp16, 2 = group-scaled, one CTA per SM at every tile width,
+// 3 = as 2 with 128-row down tiles instead of 256-row ones at 8 slots (same
+// bits)
+enum MmaForm { kMmaFormAuto = 0, kMmaFormDequant = 1, kMmaFormG4Single = 2, kMmaFormG4Down128 = 3 };
 // From this many tokens the router runs as one tensor-core launch (logits
 // and top-k, 32 tokens per CTA, so at least 16 CTAs) instead of the CUDA-core
 // logits + top-k pair.
@@ -693,7 +695,8 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
         const CUtensorMap& tb_x = nt == 1 ? L->tm_xsh8 : L->tm_xsh[nt == 2 ? 0 : 1];
         const CUtensorMap& tb_h = nt == 1 ? L->tm_hsh8 : L->tm_hsh[nt == 2 ? 0 : 1];
         const bool g4 = mma_g4_supported(c.bits, nt, sa) &&
-                        (c.reserved[1] == kMmaFormG4Single || (c.reserved[1] == kMmaFormAuto && nt == 1));
+                        (c.reserved[1] == kMmaFormG4Single || c.reserved[1] == kMmaFormG4Down128 ||
+                         (c.reserved[1] == kMmaFormAuto && nt == 1));
         SENMOE_CUDA(launch_gather_rows(xs_src, L->sh_iota, 1, L->xs_sh, sh_n, H, L->err, st, nullptr, 0, 0,
                                        g4 ? kOrderMmaG4 : kOrderMma, g4 ? L->xsum_sh : nullptr, L->sh_group));
         SENMOE_CUDA(launch_mma_gemm(L->tm_shg, L->tm_shu, tb_x, sa, c.bits, 2, nt, g4,
@@ -907,8 +910,16 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     // does not); the two-CTA kernel only while the 128-row gate/up tiles
     // cannot fill the SMs (about one token per expert).
     const bool g4 = mma_g4_supported(c.bits, nt, ga) &&
-                    (c.reserved[1] == kMmaFormG4Single || (c.reserved[1] == kMmaFormAuto && nt == 1));
+                    (c.reserved[1] == kMmaFormG4Single || c.reserved[1] == kMmaFormG4Down128 ||
+                     (c.reserved[1] == kMmaFormAuto && nt == 1));
     const bool q4 = g4 && nt == 1 && L->q4_ok && c.reserved[1] == kMmaFormAuto && max_items * (I / 128) < L->sms;
+    // down in 256-row tiles (two 128-row blocks per warp: two MMA chains, as
+    // in gate/up, where a 128-row down tile gives each warp only one) from two
+    // tokens per expert; below that the half as many tiles fill the SMs worse
+    // (measured, 48-layer config-1 graphs: -3 % per layer at 32-128 tokens,
+    // +1.4 % at 8)
+    const bool down_pair = g4 && nt == 1 && !q4 && H % 256 == 0 && per_expert >= 2.0 &&
+                           c.reserved[1] != kMmaFormG4Down128;
     const bool hybrid = P >= kHybridMinPairs && L->tc_ok && c.reserved[0] == kPathAuto && !q4;
     const int hot = kHybridHotSlots, hot_max = 0x7fffffff;
     ga.cnt_lo = 0;
@@ -955,6 +966,9 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
       gd.m_tiles = H / 64;
       SENMOE_CUDA(launch_mma_q4(L->tm_down64, L->tm_down64, tb_h, gd, c.bits, 1, (P / 8 + max_items) * gd.m_tiles,
                                 st));
+    } else if (down_pair) {
+      gd.m_tiles = H / 256;
+      SENMOE_CUDA(launch_mma_down_pair(L->tm_down, tb_h, gd, c.bits, nt, (P / (8 * nt) + max_items) * gd.m_tiles, st));
     } else {
       SENMOE_CUDA(launch_mma_gemm(L->tm_down, L->tm_down, tb_h, gd, c.bits, 1, nt, g4,
                                   (P / (8 * nt) + max_items) * gd.m_tiles, st));

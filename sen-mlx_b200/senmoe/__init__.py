@@ -205,7 +205,8 @@ class MoeArgs:
     shared_gate: bool = False  # sigmoid-gated shared expert (no reference counterpart)
     expert_path: int = PATH_AUTO  # AUTO: GEMV (~1 token per expert), warp MMA (decode), tcgen05 (prefill)
     # warp-MMA form: 0 group-scaled 4-bit where supported (two CTAs per SM at 8-slot tiles),
-    # 1 dequantise every weight to fp16, 2 group-scaled with one CTA per SM at every tile width
+    # 1 dequantise every weight to fp16, 2 group-scaled with one CTA per SM at every tile width,
+    # 3 as 2 with 128-row down tiles instead of 256-row ones (same results)
     mma_form: int = 0
     # expert parallelism: the most (token, expert) pairs this rank's experts take per call
     # (per-pair scratch rows); 0 = max_tokens * num_experts_per_tok

@@ -162,6 +162,24 @@ def test_warp_mma_group_scaled_wide_scales(senmoe, T, form):
     assert rel_l2(y, yr) <= REL_L2_TOL
 
 
+@pytest.mark.parametrize("T", [32, 64])
+def test_warp_mma_down_row_pairs_equal_single_rows(senmoe, config0_layer, T):
+    """Group-scaled down at 8-slot tiles in 256-row tiles (two 128-row blocks
+    per warp: forms 0 and 2 from two tokens per expert) against 128-row tiles
+    (form 3), config 0's layer at decode batches: every output is the same
+    fp32 chain in both tilings, so the block outputs are bit-identical; the
+    pairs also against the oracle."""
+    cfg, mw = config0_layer
+    x = O.make_tokens(T, cfg.hidden, seed=500 + T)
+    single = run_block(senmoe, cfg, mw, x, path=PATHS["mma"], mma_form=3)
+    pair = run_block(senmoe, cfg, mw, x, path=PATHS["mma"], mma_form=2)
+    auto = run_block(senmoe, cfg, mw, x, path=PATHS["mma"], mma_form=0)
+    np.testing.assert_array_equal(pair["topk_ids"], single["topk_ids"])
+    np.testing.assert_array_equal(pair["y"], single["y"])
+    np.testing.assert_array_equal(auto["y"], single["y"])
+    check_against_oracle(cfg, mw, x, pair)
+
+
 @pytest.mark.parametrize("path", ["gemv", "tc", "mma"])
 def test_block_8bit_shared_gated_large_e(senmoe, path):
     """Config-3-like: E=512, K=10, I=512, sigmoid-gated shared expert (I_s=512)."""
