@@ -914,11 +914,13 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
                      (c.reserved[1] == kMmaFormAuto && nt == 1));
     const bool q4 = g4 && nt == 1 && L->q4_ok && c.reserved[1] == kMmaFormAuto && max_items * (I / 128) < L->sms;
     // down in 256-row tiles (two 128-row blocks per warp: two MMA chains, as
-    // in gate/up, where a 128-row down tile gives each warp only one) from two
-    // tokens per expert; below that the half as many tiles fill the SMs worse
-    // (measured, 48-layer config-1 graphs: -3 % per layer at 32-128 tokens,
-    // +1.4 % at 8)
-    const bool down_pair = g4 && nt == 1 && !q4 && H % 256 == 0 && per_expert >= 2.0 &&
+    // in gate/up, where a 128-row down tile gives each warp only one) while
+    // the expected tiles (uniform routing) still give every SM five or more;
+    // with fewer the half as many tiles fill the SMs worse (measured, 48-layer
+    // config-1 graphs: -3 % per layer at 32-128 tokens, +1.4 % at 8)
+    const int64_t local_pairs = ep ? static_cast<int64_t>(P) * E_local / c.n_routed_experts : P;
+    const double touched = E_local * (1.0 - std::pow(1.0 - 1.0 / E_local, static_cast<double>(local_pairs)));
+    const bool down_pair = g4 && nt == 1 && !q4 && H % 256 == 0 && touched * (H / 256) >= 5.0 * L->sms &&
                            c.reserved[1] != kMmaFormG4Down128;
     const bool hybrid = P >= kHybridMinPairs && L->tc_ok && c.reserved[0] == kPathAuto && !q4;
     const int hot = kHybridHotSlots, hot_max = 0x7fffffff;

@@ -165,10 +165,10 @@ def test_warp_mma_group_scaled_wide_scales(senmoe, T, form):
 @pytest.mark.parametrize("T", [32, 64])
 def test_warp_mma_down_row_pairs_equal_single_rows(senmoe, config0_layer, T):
     """Group-scaled down at 8-slot tiles in 256-row tiles (two 128-row blocks
-    per warp: forms 0 and 2 from two tokens per expert) against 128-row tiles
-    (form 3), config 0's layer at decode batches: every output is the same
-    fp32 chain in both tilings, so the block outputs are bit-identical; the
-    pairs also against the oracle."""
+    per warp: forms 0 and 2 once the expected tiles give every SM five)
+    against 128-row tiles (form 3), config 0's layer at decode batches: every
+    output is the same fp32 chain in both tilings, so the block outputs are
+    bit-identical; the pairs also against the oracle."""
     cfg, mw = config0_layer
     x = O.make_tokens(T, cfg.hidden, seed=500 + T)
     single = run_block(senmoe, cfg, mw, x, path=PATHS["mma"], mma_form=3)
