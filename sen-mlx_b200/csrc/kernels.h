@@ -55,10 +55,13 @@ cudaError_t launch_router_logits(const RouterArgs& a, cudaStream_t st);
 // rounded) and softmax / top-k in one launch, 32 tokens per CTA; logits are
 // not written to global memory.  tX: x bf16 [T, H], tW: Wg bf16 [E, H], both
 // 64-column boxes with SWIZZLE_128B (32 and 128 rows).  H % 64 == 0, E <= 512.
-// Each CTA streams all of Wg; up to one CTA per SM (the 8-stage ring).
+// Each CTA streams all of Wg; up to one CTA per SM (the 8-stage ring).  With
+// more than 128 experts and fewer 32-token tiles than SMs, one CTA per (tile,
+// 128-expert chunk) writes the logits to a.logits [T, E] and a top-k launch
+// follows (same results).
 constexpr int kRouterTcTokensPerCta = 32;
 bool router_tc_supported(int hidden, int num_experts, int top_k);
-size_t router_tc_smem_bytes(int num_experts);
+size_t router_tc_smem_bytes(int num_experts, bool split = false);
 cudaError_t launch_router_tc(const CUtensorMap& tX, const CUtensorMap& tW, const RouterArgs& a, cudaStream_t st);
 cudaError_t launch_router_topk(const RouterArgs& a, cudaStream_t st);
 // ------------------------------------- single-token fused layer (batch 1)

@@ -110,7 +110,11 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(RouterArgs
 // no multicast), warps take bf16 m16n8k16 MMA fragments from the stages with
 // ldmatrix (products exact in fp32, fp32 accumulation), the bf16-rounded
 // logits stay in shared memory, and the same CTA runs softmax / top-k for its
-// tokens.  Experts come in chunks of 128 (E <= 512).
+// tokens.  Experts come in chunks of 128 (E <= 512).  SPLIT (more than one
+// chunk, fewer 32-token tiles than SMs): CTA (tile, chunk) computes one chunk,
+// writes its logits to global memory, and router_topk_kernel follows; every
+// CTA otherwise streams all of Wg (2 MB at 512 experts) and only
+// T / 32 SMs work.  Same logits, same top-k code: same results.
 namespace {
 constexpr int kRtTok = kRouterTcTokensPerCta, kRtExp = 128, kRtStages = 8;
 constexpr int kRtCompute = 8;                     // 2 token halves x 4 expert quarters
@@ -132,11 +136,11 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], 
 }
 }  // namespace
 
-size_t router_tc_smem_bytes(int num_experts) {
-  return 1024 + size_t(kRtStages) * kRtStageBytes + size_t(kRtTok) * num_experts * 4;
+size_t router_tc_smem_bytes(int num_experts, bool split) {
+  return 1024 + size_t(kRtStages) * kRtStageBytes + (split ? 0 : size_t(kRtTok) * num_experts * 4);
 }
 
-template <int EPL>
+template <int EPL, bool SPLIT>
 __global__ void __launch_bounds__(kRtThreads, 1)
     router_tc_kernel(const __grid_constant__ CUtensorMap tX, const __grid_constant__ CUtensorMap tW, RouterArgs a) {
   extern __shared__ unsigned char smem_raw[];
@@ -147,7 +151,9 @@ __global__ void __launch_bounds__(kRtThreads, 1)
   __shared__ int s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kRtTok;
-  const int nk = a.hidden / 64, nchunk = (a.num_experts + kRtExp - 1) / kRtExp;
+  const int nk = a.hidden / 64;
+  const int c_begin = SPLIT ? static_cast<int>(blockIdx.y) : 0;
+  const int c_end = SPLIT ? c_begin + 1 : (a.num_experts + kRtExp - 1) / kRtExp;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRtStages; ++i) {
       mbar_init(&bar_full[i], 1);
@@ -165,7 +171,7 @@ __global__ void __launch_bounds__(kRtThreads, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int c = 0; c < nchunk && ok; ++c)
+      for (int c = c_begin; c < c_end && ok; ++c)
         for (int k = 0; k < nk; ++k, ++it) {
           const int slot = it % kRtStages, ph = (it / kRtStages) & 1;
           if (!(ok = wait_or_abort(&bar_empty[slot], ph ^ 1, &s_abort, a.err))) break;
@@ -186,7 +192,7 @@ __global__ void __launch_bounds__(kRtThreads, 1)
   const uint32_t base = smem_u32(smem);
   int it = 0;
   bool ok = true;
-  for (int c = 0; c < nchunk && ok; ++c) {
+  for (int c = c_begin; c < c_end && ok; ++c) {
     float acc[4][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j)
@@ -227,9 +233,16 @@ __global__ void __launch_bounds__(kRtThreads, 1)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int tok = 16 * mi + g + 8 * (i >> 1), e = c * kRtExp + 32 * nq + 8 * j + 2 * tq + (i & 1);
-        if (e < a.num_experts) s_logits[tok * a.num_experts + e] = a.round_logits ? round_bf16(acc[j][i]) : acc[j][i];
+        const float v = a.round_logits ? round_bf16(acc[j][i]) : acc[j][i];
+        if constexpr (SPLIT) {
+          if (e < a.num_experts && t0 + tok < a.num_tokens)
+            a.logits[static_cast<size_t>(t0 + tok) * a.num_experts + e] = v;
+        } else {
+          if (e < a.num_experts) s_logits[tok * a.num_experts + e] = v;
+        }
       }
   }
+  if constexpr (SPLIT) return;  // router_topk_kernel follows
   ok = __all_sync(0xffffffffu, ok);
   // all compute warps' logits are in place (named barrier: the TMA warp has left)
   asm volatile("bar.sync 1, %0;" ::"r"(kRtCompute * 32) : "memory");
@@ -378,13 +391,26 @@ cudaError_t launch_router_tc(const CUtensorMap& tX, const CUtensorMap& tW, const
   if (a.num_tokens == 0) return cudaSuccess;
   if (!router_tc_supported(a.hidden, a.num_experts, a.top_k)) return cudaErrorNotSupported;
   const int epl = (a.num_experts + 31) / 32;
-  const size_t smem = router_tc_smem_bytes(a.num_experts);
-  const dim3 grid((a.num_tokens + kRtTok - 1) / kRtTok);
+  const int tiles = (a.num_tokens + kRtTok - 1) / kRtTok, nchunk = (a.num_experts + kRtExp - 1) / kRtExp;
+  int sms = 0, dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  if (nchunk > 1 && tiles < sms) {
+    // one chunk per CTA, logits through global memory, then the top-k launch
+    const size_t smem = router_tc_smem_bytes(a.num_experts, true);
+    auto kern = router_tc_kernel<1, true>;
+    if ((e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem)) != cudaSuccess) return e;
+    if ((e = launch_pdl(kern, dim3(tiles, nchunk), dim3(kRtThreads), smem, st, tX, tW, a)) != cudaSuccess) return e;
+    return launch_router_topk(a, st);
+  }
+  const size_t smem = router_tc_smem_bytes(a.num_experts, false);
+  const dim3 grid(tiles);
 #define SENMOE_RT_CASE(V)                                                                              \
   if (epl <= V) {                                                                                    \
-    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(router_tc_kernel<V>), smem);     \
+    e = ensure_dynamic_smem(reinterpret_cast<const void*>(router_tc_kernel<V, false>), smem);          \
     if (e != cudaSuccess) return e;                                                                  \
-    return launch_pdl(router_tc_kernel<V>, grid, dim3(kRtThreads), smem, st, tX, tW, a);             \
+    return launch_pdl(router_tc_kernel<V, false>, grid, dim3(kRtThreads), smem, st, tX, tW, a);      \
   }
   SENMOE_RT_CASE(1) SENMOE_RT_CASE(2) SENMOE_RT_CASE(4) SENMOE_RT_CASE(8) SENMOE_RT_CASE(16)
 #undef SENMOE_RT_CASE

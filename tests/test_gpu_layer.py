@@ -202,6 +202,26 @@ def test_prefill_router_large_e(senmoe):
     check_against_oracle(cfg, mw, x, got)
 
 
+def test_prefill_router_chunk_split_equals_fused(senmoe):
+    """E=512 prefill router: below one 32-token tile per SM (2048 tokens) each
+    CTA takes one 128-expert chunk and a top-k launch follows; from one tile
+    per SM one CTA runs all chunks and its own top-k.  Routing is per token,
+    so the first 2048 tokens get the same ids and weights both ways, bit for
+    bit, and the ids match the oracle except at router ties."""
+    import torch
+    cfg = O.MoeConfig(hidden=2048, intermediate=512, num_experts=512, top_k=10, bits=4)
+    mw = O.make_layer(cfg, seed=15, router_std=1.0 / np.sqrt(2048))
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    x = O.make_tokens(32 * sms + 64, cfg.hidden, seed=16)
+    big = run_block(senmoe, cfg, mw, x)
+    small = run_block(senmoe, cfg, mw, x[:2048])
+    np.testing.assert_array_equal(small["topk_ids"], big["topk_ids"][:2048])
+    np.testing.assert_array_equal(small["topk_weights"], big["topk_weights"][:2048])
+    ids_ref, _, scores = O.router(cfg, mw, x[:64])
+    ok, _ = topk_match_except_ties(small["topk_ids"][:64], ids_ref, scores)
+    assert ok, "top-k ids differ from the oracle beyond router ties"
+
+
 @pytest.mark.parametrize("path", ["gemv", "tc", "mma"])
 def test_block_8bit_skewed(senmoe, path):
     """Config-4-like: 8-bit weights, Zipf-biased router (many tokens on few experts)."""
