@@ -200,6 +200,11 @@ struct SenMoeLayer {
   // the router, dispatch and routed experts)
   cudaStream_t side = nullptr;
   cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
+  // a skewed batch split between the warp-MMA and tcgen05 kernels runs the
+  // tcgen05 part (its gather and both products) on this stream, so each
+  // kernel's last-round SMs take the other's tiles
+  cudaStream_t hyb = nullptr;
+  cudaEvent_t hyb_fork = nullptr, hyb_join = nullptr;
   // one token on one GPU: the fused single-launch block (layer_single.cu)
   bool single_ok = false;
   SingleTokenArgs single{};
@@ -470,6 +475,11 @@ int senmoe_layer_create(const SenMoeConfig* config, const SenMoeWeights* weights
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->fork_ev, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->join_ev, cudaEventDisableTiming);
   }
+  if (e == cudaSuccess && L->tc_ok && L->mma_ok) {
+    e = cudaStreamCreateWithFlags(&L->hyb, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->hyb_fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->hyb_join, cudaEventDisableTiming);
+  }
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   cudaSetDevice(cur);
   if (e != cudaSuccess) {
@@ -491,6 +501,9 @@ int senmoe_layer_destroy(SenMoeLayer* layer) {
   if (layer->fork_ev) cudaEventDestroy(layer->fork_ev);
   if (layer->join_ev) cudaEventDestroy(layer->join_ev);
   if (layer->side) cudaStreamDestroy(layer->side);
+  if (layer->hyb_fork) cudaEventDestroy(layer->hyb_fork);
+  if (layer->hyb_join) cudaEventDestroy(layer->hyb_join);
+  if (layer->hyb) cudaStreamDestroy(layer->hyb);
   for (void* p : layer->ep_opened)
     if (p) cudaIpcCloseMemHandle(p);
   cudaError_t e = cudaFree(layer->arena);
@@ -926,12 +939,21 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     const int hot = kHybridHotSlots, hot_max = 0x7fffffff;
     ga.cnt_lo = 0;
     ga.cnt_hi = hybrid ? hot : 0;
+    // the loaded experts' gather and products on the layer's second stream,
+    // beside the warp-MMA kernels (disjoint slots of xs, h and d); joined
+    // before the combine.  Stage profiling keeps them in line.
+    const bool overlap_hybrid = hybrid && !profile && L->hyb;
+    cudaStream_t hs = overlap_hybrid ? L->hyb : st;
+    if (overlap_hybrid) {
+      SENMOE_CUDA(cudaEventRecord(L->hyb_fork, st));
+      SENMOE_CUDA(cudaStreamWaitEvent(hs, L->hyb_fork, 0));
+    }
     SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
                                    L->offsets, c.expert_begin, c.expert_end,
                                    g4 ? kOrderMmaG4 : kOrderMma, g4 ? L->xsum : nullptr, nullptr, prow_p, slot_cap,
                                    ids, ga.cnt_lo, ga.cnt_hi));
     if (hybrid)  // the loaded experts' slots, in the tcgen05 kernel's order
-      SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, st,
+      SENMOE_CUDA(launch_gather_rows(static_cast<const uint16_t*>(x), L->perm, K, L->xs, P, H, L->err, hs,
                                      L->offsets, c.expert_begin, c.expert_end, kOrderTc, nullptr, nullptr, prow_p,
                                      slot_cap, ids, hot, hot_max));
     ga.xsum = L->xsum;
@@ -952,7 +974,7 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
     }
     if (hybrid)
       SENMOE_CUDA(launch_tc_gemm(L->tm_gate, L->tm_up, L->tm_xs[kTcMaxTile], ha, c.bits, 2, kTcTiles[kTcMaxTile],
-                                 hot_upper * ha.m_tiles, st));
+                                 hot_upper * ha.m_tiles, hs));
     SENMOE_CUDA(mark(3));
     TcGemmArgs gd = ga;
     gd.s[0] = static_cast<const uint16_t*>(L->w.down_scales);
@@ -981,7 +1003,11 @@ static int layer_forward(SenMoeLayer* L, const void* x, int64_t num_tokens, void
       hd.cnt_lo = hot;
       hd.cnt_hi = hot_max;
       SENMOE_CUDA(launch_tc_gemm(L->tm_down, L->tm_down, L->tm_h[kTcMaxTile], hd, c.bits, 1, kTcTiles[kTcMaxTile],
-                                 hot_upper * hd.m_tiles, st));
+                                 hot_upper * hd.m_tiles, hs));
+    }
+    if (overlap_hybrid) {
+      SENMOE_CUDA(cudaEventRecord(L->hyb_join, hs));
+      SENMOE_CUDA(cudaStreamWaitEvent(st, L->hyb_join, 0));
     }
     SENMOE_CUDA(mark(4));
   } else if (path == kPathTensorCore) {
