@@ -167,7 +167,7 @@ def two_cta_form(args, T, world, sms):
     return (args.bits == 4 and pe <= 8.0 and args.mma_form == 0 and min(P, e_local) * (I // 128) < sms)
 
 
-def _gpu_setup(rank, world, H, I, E, K, bits, T, shared, seed):
+def _gpu_setup(rank, world, H, I, E, K, bits, T, shared, seed, skew=False):
     import torch
 
     from helpers import device_weights, moe_args
@@ -178,10 +178,19 @@ def _gpu_setup(rank, world, H, I, E, K, bits, T, shared, seed):
                       shared_intermediate=shared, shared_gate=bool(shared))
     mw = O.make_layer(cfg, seed=seed, router_std=1.0 / np.sqrt(H))
     x = O.make_tokens(T, H, seed=seed + 1)
+    if skew:
+        # Zipf(1.2) pull toward the low expert ids: x's column 0 is the
+        # constant 1 and Wg's column 0 holds the per-expert offset, so a few
+        # experts get many more slots than the mean (the hybrid split)
+        x = x.copy()
+        x[:, 0] = O.f32_to_bf16(np.ones(T, dtype=np.float32))
+        rw = O.bf16_to_f32(mw.router_w)
+        rw[:, 0] = 3.0 / np.arange(1, E + 1, dtype=np.float32) ** 1.2
+        mw.router_w = O.f32_to_bf16(rw.astype(np.float32))
     return cfg, mw, x, moe_args(cfg), device_weights(mw, device=f"cuda:{rank}")
 
 
-def ep_forward(rank, world, H, I, E, K, bits, Ts, shared, seed, expert_path):
+def ep_forward(rank, world, H, I, E, K, bits, Ts, shared, seed, expert_path, skew=False):
     """EP layer vs the one-GPU layer on every rank, for several batch sizes
     (also through a CUDA-graph stack).  Returns per T: bit-identity with the
     one-GPU layer, repeatability, a digest of the output (compared across
@@ -194,7 +203,7 @@ def ep_forward(rank, world, H, I, E, K, bits, Ts, shared, seed, expert_path):
     from senmoe import ep
 
     Tmax = max(Ts)
-    cfg, mw, x_np, args, wd = _gpu_setup(rank, world, H, I, E, K, bits, Tmax, shared, seed)
+    cfg, mw, x_np, args, wd = _gpu_setup(rank, world, H, I, E, K, bits, Tmax, shared, seed, skew)
     args = moe_args(cfg, expert_path)
     full = senmoe.DeepseekMoe(args, wd, max_tokens=Tmax)
     epl = ep.make_layer(args, wd, Tmax, rank, world)

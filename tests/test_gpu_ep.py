@@ -30,6 +30,9 @@ CASES = {
     # routes its own token block and the routing rows are exchanged
     "shared8": (256, 256, 16, 4, 8, [3, 40, 600, 5000], 256, 5, 0),
     "config0_tc": (2048, 768, 128, 8, 4, [16, 512], 0, 7, 2),
+    # 8-bit, skewed router, 2048 pairs at 16 per expert: the warp-MMA path
+    # with the loaded experts split off to the tcgen05 GEMM (second stream)
+    "skew8": (512, 256, 128, 8, 8, [256], 0, 11, 0, True),
 }
 
 
@@ -38,8 +41,9 @@ CASES = {
 def test_expert_parallel_matches_one_gpu(world, case):
     if _ngpu() < world:
         pytest.skip(f"needs {world} GPUs")
-    H, I, E, K, bits, Ts, shared, seed, path = CASES[case]
-    res = spawn_ranks("ep_forward", world, H, I, E, K, bits, Ts, shared, seed, path, timeout=600)
+    H, I, E, K, bits, Ts, shared, seed, path, *skew = CASES[case]
+    res = spawn_ranks("ep_forward", world, H, I, E, K, bits, Ts, shared, seed, path, bool(skew and skew[0]),
+                      timeout=600)
     for rank, out in enumerate(res):
         assert out["stack_repeat"], f"rank {rank}: graph replays of the EP stack differ"
         assert out["stack_digest"] == res[0]["stack_digest"], f"rank {rank}: EP stack output differs across ranks"
